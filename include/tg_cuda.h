@@ -1,0 +1,179 @@
+/* tg_cuda.h -- C ABI of libtgcuda, the B200 (sm_100a) batch backend for Technograd.
+ *
+ * Plain C: pointers, sizes and status codes only. Every entry point returns
+ * TG_CUDA_OK (0) or a negative status; the text of the last error on the
+ * calling thread is tg_cuda_error(). The library never exits the process and
+ * never prints; the caller (the `tgc batch --device cuda` branch) turns a
+ * status into its own die() before it creates any output file, which keeps
+ * the reference's atomic-failure rule (src/main.c:414-419, docs/SPEC.md:282-285).
+ *
+ * Reference interfaces replaced (paths inside IlumCI/Technograd):
+ *   tg_cuda_batch      <- the par_for(batch_rows) loop of the batch branch,
+ *                         src/main.c:421-441, and vm_run_into per row, src/vm.c:475-481
+ *   tg_cuda_matmul_q   <- tg_matmul_qa / tg_matmul_qb, runtime/tg_rt.h:132-151
+ *   tg_cuda_load       <- the planned Module handed to the VM, src/tg.h:177-200, src/plan.c:154
+ *   tg_cuda_lm_*       <- `tgc batch` over the Qwen3 program that examples/qwen3/import.py:51-131
+ *                         emits (per-head tg_matmul_qb, rmsnorm, softmax, take), run per sequence
+ *   tg_cuda_quantize_rtn <- the RTN branch of quantize_param, src/quant.c:176-200,258-316
+ */
+#ifndef TG_CUDA_H
+#define TG_CUDA_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status ------------------------------------------------------------- */
+#define TG_CUDA_OK            0
+#define TG_CUDA_EINVAL       -1 /* bad argument (shape, pointer, size) */
+#define TG_CUDA_ENODEV       -2 /* no usable CUDA device, or not initialised */
+#define TG_CUDA_ECUDA        -3 /* a CUDA runtime call failed */
+#define TG_CUDA_EUNSUPPORTED -4 /* op or model form the GPU path does not run (no CPU fallback) */
+#define TG_CUDA_ENOMEM       -5 /* device or pinned host allocation failed */
+#define TG_CUDA_EFAULT       -6 /* failure injected through TG_CUDA_FAULT (host-side tests) */
+#define TG_CUDA_EDEVICE      -7 /* a kernel reported an error in its device status word */
+
+/* Last error text of the calling thread ("" if none). */
+const char *tg_cuda_error(void);
+
+/* ---- devices -------------------------------------------------------------- */
+/* Select the GPUs rows are sharded over. ngpus <= 0 or devices == NULL: every
+ * visible device (or the first ngpus). Idempotent for the same set. */
+int tg_cuda_init(int ngpus, const int *devices);
+/* Number of devices selected by tg_cuda_init (0 before it). */
+int tg_cuda_ngpus(void);
+/* Release every device resource the library holds. */
+void tg_cuda_shutdown(void);
+
+/* ---- kernel-level drop-in --------------------------------------------------
+ * axis 0 (tg_matmul_qa, runtime/tg_rt.h:132-140): o[m,n] = s[i] * sum_p code(q, i*k+p) * act[p*n+j]
+ * axis 1 (tg_matmul_qb, runtime/tg_rt.h:143-151): o[m,n] = s[j] * sum_p act[i*k+p] * code(q, p*n+j)
+ * Codes: bits 8 = one signed byte per element; bits 4 = two per byte, element
+ * e in byte e/2, low nibble first, sign-extended (runtime/tg_rt.h:124-129).
+ * All pointers are DEVICE pointers on the current device; the call is
+ * asynchronous on `stream` (NULL = the legacy default stream). Scratch for the
+ * tensor-core path (m*k or k*n large) is cached per device by the library. */
+int tg_cuda_matmul_q(int axis, float *o, const float *act, const signed char *q, int bits, const float *s, int m,
+		     int k, int n, void *stream);
+
+/* Per-channel RTN quantization on the device, bit-exact with quant.c: w is the
+ * f32 matrix [rows, cols] (device), axis 0 = one scale per row, 1 = per column;
+ * q receives (bits 8) rows*cols bytes or (bits 4) (rows*cols+1)/2 bytes, s one
+ * f32 scale per channel. */
+int tg_cuda_quantize_rtn(const float *w, int rows, int cols, int axis, int bits, signed char *q, float *s, void *stream);
+
+/* ---- programs ------------------------------------------------------------- */
+/* A planned TGIR program, flattened. The host builds it from its Module
+ * (src/tg.h:112-200); the numbering of ops is the reference's enum Op. */
+enum {
+	TG_CUDA_OP_CONST, TG_CUDA_OP_ADD, TG_CUDA_OP_SUB, TG_CUDA_OP_MUL, TG_CUDA_OP_DIV, TG_CUDA_OP_MAX, TG_CUDA_OP_MIN,
+	TG_CUDA_OP_NEG, TG_CUDA_OP_TANH, TG_CUDA_OP_RELU, TG_CUDA_OP_SIGMOID, TG_CUDA_OP_EXP, TG_CUDA_OP_SQRT, TG_CUDA_OP_GELU,
+	TG_CUDA_OP_SILU, TG_CUDA_OP_SOFTPLUS, TG_CUDA_OP_LOG, TG_CUDA_OP_MATMUL, TG_CUDA_OP_SOFTMAX, TG_CUDA_OP_RMSNORM,
+	TG_CUDA_OP_SUM, TG_CUDA_OP_MEAN, TG_CUDA_OP_TRANSPOSE, TG_CUDA_OP_OUTER, TG_CUDA_OP_STEP, TG_CUDA_OP_SPMM,
+	TG_CUDA_OP_SPMM_T, TG_CUDA_OP_SPMM_DX, TG_CUDA_OP_ACTIVE, TG_CUDA_OP_TAKE, TG_CUDA_OP_TAKE_T, TG_CUDA_OP_SPMM_TC,
+	TG_CUDA_OP_SIN, TG_CUDA_OP_COS, TG_CUDA_OP_RESHAPE, TG_CUDA_OP_FLOOR, TG_CUDA_OP_SUM_TO, TG_CUDA_OP_TOPK,
+	TG_CUDA_OP_MEMSCAN, TG_CUDA_OP_MEMSCAN_T, TG_CUDA_OP_SUFMATCH, TG_CUDA_OP_THINK, TG_CUDA_OP_SCAN, TG_CUDA_OP_COUNT
+};
+
+enum { TG_CUDA_PARAM, TG_CUDA_INPUT, TG_CUDA_TMP, TG_CUDA_STATE }; /* VKind, src/tg.h:114 */
+
+typedef struct {
+	int kind;                /* TG_CUDA_PARAM / INPUT / TMP / STATE */
+	int rank, dim[4];        /* Shape, src/tg.h:36-39 */
+	const float *data;       /* params: f32 values (host memory, copied at load) */
+	int qbits, qaxis;        /* quantized params: 8 or 4, axis 0 (rows) or 1 (columns); qbits 0 = f32 */
+	const signed char *q;    /* codes in the reference packing (host memory) */
+	const float *qs;         /* one scale per channel (host memory) */
+	int index;               /* inputs: position in the entry signature */
+} tg_cuda_value;
+
+typedef struct {
+	int T, reverse, tid;     /* Scan, src/tg.h:140-147 */
+	int nc; const int *c, *init, *next;
+	int nx; const int *x, *xt;
+	int ny; const int *y, *ys;
+} tg_cuda_scan;
+
+typedef struct {
+	int op;                  /* TG_CUDA_OP_* */
+	int out, a[3], na;       /* value indices */
+	float k;                 /* const */
+	int init, maxit;         /* think: initial state, budget */
+	float eps;               /* think: delta threshold, < 0 = none */
+	int yield, tid, halt;    /* think: next state, steps slot, halting scalar or -1 */
+	float hthr;              /* think: learned-halt threshold */
+	int body, nbody;         /* think/scan: body = ins[body .. body + nbody) */
+	int scan;                /* scan: index into tg_cuda_program.scans, else -1 */
+} tg_cuda_ins;
+
+typedef struct {
+	int nval; const tg_cuda_value *val;
+	int nins; const tg_cuda_ins *ins;
+	int ntop;                /* the top-level block is ins[0 .. ntop) */
+	int nscan; const tg_cuda_scan *scans;
+	int ninputs; const int *inputs; /* value index of each entry input, in order */
+	int output;
+	int nthink;              /* steps slots per row */
+	int nupd;                /* state updates; > 0 is rejected (rows would not be independent) */
+} tg_cuda_program;
+
+typedef struct tg_cuda_model tg_cuda_model;
+
+/* Validate a program, plan its device arena and upload its params to every
+ * selected GPU. TG_CUDA_EUNSUPPORTED for stateful models (nupd > 0) and ops the
+ * device executor does not implement. */
+int tg_cuda_load(const tg_cuda_program *p, tg_cuda_model **out);
+/* Run rows independent samples. all: rows * per floats (host), each row the
+ * concatenated inputs; out: rows * n floats; steps: rows * nt ints (nt >= the
+ * program's nthink, may be NULL when nthink == 0). Rows keep input order; the
+ * call blocks until out and steps are written. Rows are sharded across the
+ * selected GPUs in contiguous blocks. */
+int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int per, float *out, int n, int *steps, int nt);
+/* Same, with every buffer already on device 0 of the selection (device pointers,
+ * asynchronous on stream). Used for measurements with inputs resident in HBM. */
+int tg_cuda_batch_device(tg_cuda_model *g, const float *all, long rows, float *out, int *steps, void *stream);
+void tg_cuda_free(tg_cuda_model *g);
+
+/* ---- decoder language models (the Qwen3 import) ---------------------------
+ * Weights follow examples/qwen3/import.py:37-60: every linear weight is stored
+ * as W^T [in, out] and used as x @ W, so it is quantized on axis 1 (one scale
+ * per output column, src/ops.c:310-320). Per-head projections are separate
+ * params in the program; here they arrive concatenated along the output axis
+ * (q: head h at columns h*HD..), which keeps each head's own column scales.
+ * Wo arrives as the per-head params stacked along the input axis ([NQ*HD, D]);
+ * its scales are per head and column: wo_s[h*D + n]. */
+typedef struct {
+	const signed char *q;    /* codes, reference packing over the [in, out] matrix */
+	const float *s;          /* scales, one per output column (wo: per head and column) */
+} tg_cuda_qmat;
+
+typedef struct {
+	int layers, hidden, nq, nkv, head_dim, ffn, vocab;
+	int bits;                /* 8 or 4 */
+	float eps;               /* rmsnorm epsilon of the program (1e-6, runtime/tg_rt.h:172) */
+	float attn_scale;        /* the f32 constant the program multiplies scores by */
+	double rope_theta;
+	const float *embed;      /* E [vocab, hidden] f32 (take operand, never quantized) */
+	const float *final_norm; /* lnf [hidden] */
+	tg_cuda_qmat lm_head;    /* LM [hidden, vocab] */
+	const float *const *ln1, *const *ln2, *const *qn, *const *kn; /* per layer */
+	const tg_cuda_qmat *wq, *wk, *wv, *wo, *wg, *wu, *wd;          /* per layer */
+} tg_cuda_lm_desc;
+
+typedef struct tg_cuda_lm tg_cuda_lm;
+
+int tg_cuda_lm_load(const tg_cuda_lm_desc *d, int max_seqs, int max_len, tg_cuda_lm **out);
+/* Prefill nseq sequences of T token ids each (ids as f32, the program's input
+ * type) and return the logits of the last position, [nseq, vocab]. */
+int tg_cuda_lm_forward(tg_cuda_lm *g, const float *ids, long nseq, int T, float *logits);
+/* Greedy decode: prefill, then nnew argmax tokens per sequence (tokens [nseq, nnew]),
+ * each step feeding the previous token back through a per-sequence KV cache. */
+int tg_cuda_lm_generate(tg_cuda_lm *g, const float *ids, long nseq, int T, int nnew, int *tokens);
+void tg_cuda_lm_free(tg_cuda_lm *g);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,665 @@
+/* tgo.c -- CPU oracle (TEST INFRASTRUCTURE ONLY; see tgo.h).
+ *
+ * Restates, in this project's own code, the arithmetic of the reference
+ * (IlumCI/Technograd) on the batch path. Each function names the reference
+ * lines it follows. Build: oracle/Makefile (-O2 -ffp-contract=off). */
+#include "tgo.h"
+
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ---- kernels: runtime/tg_rt.h ------------------------------------------------ */
+
+/* runtime/tg_rt.h:124-129: int8 one per byte; int4 element i in byte i/2, low
+ * nibble first, each nibble sign-extended. */
+int tgo_qget(const signed char *q, int bits, long i)
+{
+	if (bits == 8) return q[i];
+	int byte = q[i >> 1];
+	if (i & 1) return byte >> 4; /* arithmetic shift of the signed byte */
+	return (int)(signed char)(unsigned char)((unsigned)byte << 4) >> 4;
+}
+
+/* runtime/tg_rt.h:81-116: every output sums its k products in order p = 0..k-1
+ * starting from 0 (the narrow-n specialisations keep that order). */
+void tgo_matmul(float *o, const float *a, const float *b, int m, int k, int n)
+{
+	for (int i = 0; i < m; i++)
+		for (int j = 0; j < n; j++) {
+			float acc = 0.0f;
+			for (int p = 0; p < k; p++) acc += a[(long)i * k + p] * b[(long)p * n + j];
+			o[(long)i * n + j] = acc;
+		}
+}
+
+/* runtime/tg_rt.h:132-140: f32 sum of code * b, then one multiply by the row scale. */
+void tgo_matmul_qa(float *o, const signed char *q, int bits, const float *s, const float *b, int m, int k, int n)
+{
+	for (int i = 0; i < m; i++)
+		for (int j = 0; j < n; j++) {
+			float acc = 0.0f;
+			for (int p = 0; p < k; p++) acc += (float)tgo_qget(q, bits, (long)i * k + p) * b[(long)p * n + j];
+			o[(long)i * n + j] = s[i] * acc;
+		}
+}
+
+/* runtime/tg_rt.h:143-151: column scale after the sum. */
+void tgo_matmul_qb(float *o, const float *a, const signed char *q, int bits, const float *s, int m, int k, int n)
+{
+	for (int i = 0; i < m; i++)
+		for (int j = 0; j < n; j++) {
+			float acc = 0.0f;
+			for (int p = 0; p < k; p++) acc += a[(long)i * k + p] * (float)tgo_qget(q, bits, (long)p * n + j);
+			o[(long)i * n + j] = s[j] * acc;
+		}
+}
+
+/* runtime/tg_rt.h:165-175: eps 1e-6f inside the root, reciprocal then multiply. */
+void tgo_rmsnorm(float *o, const float *a, int rows, int cols)
+{
+	for (int r = 0; r < rows; r++) {
+		const float *x = a + (long)r * cols;
+		float *y = o + (long)r * cols;
+		float ss = 0.0f;
+		for (int i = 0; i < cols; i++) ss += x[i] * x[i];
+		float inv = 1.0f / sqrtf(ss / (float)cols + 1e-6f);
+		for (int i = 0; i < cols; i++) y[i] = x[i] * inv;
+	}
+}
+
+/* runtime/tg_rt.h:154-164: max-subtract, expf, then a division by the sum. */
+void tgo_softmax(float *o, const float *a, int rows, int cols)
+{
+	for (int r = 0; r < rows; r++) {
+		const float *x = a + (long)r * cols;
+		float *y = o + (long)r * cols;
+		float mx = x[0], sum = 0.0f;
+		for (int i = 1; i < cols; i++)
+			if (x[i] > mx) mx = x[i];
+		for (int i = 0; i < cols; i++) {
+			y[i] = expf(x[i] - mx);
+			sum += y[i];
+		}
+		for (int i = 0; i < cols; i++) y[i] /= sum;
+	}
+}
+
+/* runtime/tg_rt.h:39-75 (and :73-75 step): the same float expressions. */
+static float un1(int op, float x)
+{
+	switch (op) {
+	case TG_CUDA_OP_NEG: return -x;
+	case TG_CUDA_OP_TANH: return tanhf(x);
+	case TG_CUDA_OP_RELU: return x > 0.0f ? x : 0.0f;
+	case TG_CUDA_OP_SIGMOID: return 1.0f / (1.0f + expf(-x));
+	case TG_CUDA_OP_EXP: return expf(x);
+	case TG_CUDA_OP_SQRT: return sqrtf(x);
+	case TG_CUDA_OP_GELU: return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
+	case TG_CUDA_OP_SILU: return x / (1.0f + expf(-x));
+	case TG_CUDA_OP_SOFTPLUS: return (x > 0.0f ? x : 0.0f) + log1pf(expf(-fabsf(x)));
+	case TG_CUDA_OP_LOG: return logf(x);
+	case TG_CUDA_OP_STEP: return x > 0.0f ? 1.0f : 0.0f;
+	case TG_CUDA_OP_SIN: return sinf(x);
+	case TG_CUDA_OP_COS: return cosf(x);
+	case TG_CUDA_OP_FLOOR: return floorf(x);
+	}
+	return NAN;
+}
+
+void tgo_unary(int op, float *o, const float *a, int n)
+{
+	for (int i = 0; i < n; i++) o[i] = un1(op, a[i]);
+}
+
+static float bin1(int op, float x, float y)
+{
+	switch (op) {
+	case TG_CUDA_OP_ADD: return x + y;
+	case TG_CUDA_OP_SUB: return x - y;
+	case TG_CUDA_OP_MUL: return x * y;
+	case TG_CUDA_OP_DIV: return x / y;
+	case TG_CUDA_OP_MAX: return x > y ? x : y; /* runtime/tg_rt.h:34-35 */
+	case TG_CUDA_OP_MIN: return x < y ? x : y;
+	}
+	return NAN;
+}
+
+/* ---- rand(seed, scale): src/lower.c:661-668, 766-775 ----------------------------- */
+void tgo_rand(unsigned seed, float scale, float *out, long n)
+{
+	uint32_t s = seed ? seed : 0x9e3779b9u;
+	for (long i = 0; i < n; i++) {
+		s ^= s << 13;
+		s ^= s >> 17;
+		s ^= s << 5;
+		float u = (float)(s >> 8) / 16777216.0f;
+		out[i] = (2.0f * u - 1.0f) * scale;
+	}
+}
+
+/* ---- quantizer: src/quant.c ------------------------------------------------------ */
+
+/* src/quant.c:176-181 */
+static int code_of(double w, double s, int lim)
+{
+	if (s <= 0) return 0;
+	double r = nearbyint(w / s);
+	return (int)(r > lim ? lim : r < -lim ? -lim : r);
+}
+
+/* src/quant.c:183-200: 10-point clipping grid, first minimum wins. */
+static double best_scale(const double *w, int K, const double *hd, int lim)
+{
+	double amax = 0;
+	for (int j = 0; j < K; j++)
+		if (fabs(w[j]) > amax) amax = fabs(w[j]);
+	if (amax == 0) return 1e-8;
+	double best = INFINITY, bs = amax / lim;
+	for (int g = 0; g < 10; g++) {
+		double s = amax * (1.0 - 0.05 * g) / lim, e = 0;
+		for (int j = 0; j < K; j++) {
+			double d = w[j] - s * code_of(w[j], s, lim);
+			e += d * d * (hd ? hd[j] : 1.0);
+		}
+		if (e < best) {
+			best = e;
+			bs = s;
+		}
+	}
+	return bs;
+}
+
+/* src/quant.c:202-220: in-place lower Cholesky, upper triangle zeroed. */
+static int cholesky(double *A, int n)
+{
+	for (int j = 0; j < n; j++) {
+		double d = A[(long)j * n + j];
+		for (int k = 0; k < j; k++) d -= A[(long)j * n + k] * A[(long)j * n + k];
+		if (d <= 0) return 0;
+		d = sqrt(d);
+		A[(long)j * n + j] = d;
+		for (int i = j + 1; i < n; i++) {
+			double s = A[(long)i * n + j];
+			for (int k = 0; k < j; k++) s -= A[(long)i * n + k] * A[(long)j * n + k];
+			A[(long)i * n + j] = s / d;
+		}
+		for (int k = j + 1; k < n; k++) A[(long)j * n + k] = 0;
+	}
+	return 1;
+}
+
+/* src/quant.c:222-253: U with H^-1 = U^T U, through L^-1 and a second factorisation. */
+static int inv_chol_upper(const double *H, int n, double *U)
+{
+	size_t nn = (size_t)n * (size_t)n;
+	double *L = malloc(nn * sizeof *L), *Li = malloc(nn * sizeof *Li);
+	memcpy(L, H, nn * sizeof *L);
+	int ok = cholesky(L, n);
+	if (ok) {
+		for (size_t i = 0; i < nn; i++) Li[i] = 0;
+		for (int c = 0; c < n; c++)
+			for (int i = c; i < n; i++) {
+				double s = i == c ? 1.0 : 0.0;
+				for (int k = c; k < i; k++) s -= L[(long)i * n + k] * Li[(long)k * n + c];
+				Li[(long)i * n + c] = s / L[(long)i * n + i];
+			}
+		for (int i = 0; i < n; i++)
+			for (int j = i; j < n; j++) {
+				double s = 0;
+				for (int k = j; k < n; k++) s += Li[(long)k * n + i] * Li[(long)k * n + j];
+				U[(long)i * n + j] = U[(long)j * n + i] = s;
+			}
+		ok = cholesky(U, n);
+		if (ok)
+			for (int i = 0; i < n; i++)
+				for (int j = i + 1; j < n; j++) {
+					U[(long)i * n + j] = U[(long)j * n + i];
+					U[(long)j * n + i] = 0;
+				}
+	}
+	free(L);
+	free(Li);
+	return ok;
+}
+
+/* src/quant.c:158-174 set_code */
+static void set_code(signed char *q, int bits, long i, int code)
+{
+	if (bits == 8) {
+		q[i] = (signed char)code;
+		return;
+	}
+	unsigned char b = (unsigned char)q[i / 2];
+	b = i % 2 ? (unsigned char)((b & 0x0f) | (unsigned char)((unsigned)code << 4)) : (unsigned char)((b & 0xf0) | (code & 0x0f));
+	q[i / 2] = (signed char)b;
+}
+
+/* src/quant.c:92-118: H[r][c] += x_r x_c in double, zero inputs skipped. */
+void tgo_hessian_add(double *H, const float *x, int nrows, int K)
+{
+	for (int r0 = 0; r0 < nrows; r0++) {
+		const float *v = x + (long)r0 * K;
+		for (int r = 0; r < K; r++) {
+			double xr = v[r];
+			if (xr == 0) continue;
+			for (int c = 0; c < K; c++) H[(long)r * K + c] += xr * v[c];
+		}
+	}
+}
+
+/* src/quant.c:258-302: channels on `axis`, RTN scale per channel, GPTQ error
+ * feedback through U when H is given and positive definite. */
+int tgo_quantize(const float *w, int rows, int cols, int axis, int bits, double *H, signed char *q, float *s)
+{
+	int lim = bits == 8 ? 127 : 7;
+	int C = axis == 0 ? rows : cols, K = axis == 0 ? cols : rows;
+	long n = (long)C * K;
+	memset(q, 0, (size_t)(bits == 8 ? n : (n + 1) / 2));
+	double *W = malloc((size_t)n * sizeof *W), *hd = NULL, *U = NULL;
+	for (int c = 0; c < C; c++)
+		for (int j = 0; j < K; j++) W[(long)c * K + j] = axis == 0 ? w[(long)c * K + j] : w[(long)j * C + c];
+	if (H) {
+		double mean = 0;
+		hd = malloc((size_t)K * sizeof *hd);
+		for (int j = 0; j < K; j++) mean += H[(long)j * K + j];
+		mean /= K;
+		for (int j = 0; j < K; j++) {
+			if (H[(long)j * K + j] == 0) {
+				H[(long)j * K + j] = 1;
+				for (int c = 0; c < C; c++) W[(long)c * K + j] = 0;
+			}
+			H[(long)j * K + j] += 0.01 * mean;
+			hd[j] = H[(long)j * K + j];
+		}
+		U = malloc((size_t)K * (size_t)K * sizeof *U);
+		if (!inv_chol_upper(H, K, U)) {
+			free(U);
+			U = NULL;
+		}
+	}
+	for (int c = 0; c < C; c++) {
+		double *wc = W + (long)c * K;
+		double sc = best_scale(wc, K, hd, lim);
+		s[c] = (float)sc;
+		for (int j = 0; j < K; j++) {
+			int code = code_of(wc[j], sc, lim);
+			set_code(q, bits, axis == 0 ? (long)c * K + j : (long)j * C + c, code);
+			if (U) {
+				double err = (wc[j] - sc * code) / U[(long)j * K + j];
+				for (int jj = j + 1; jj < K; jj++) wc[jj] -= err * U[(long)j * K + jj];
+			}
+		}
+	}
+	int used = U != NULL;
+	free(W);
+	free(hd);
+	free(U);
+	return used;
+}
+
+/* ---- program VM: src/vm.c ----------------------------------------------------- */
+
+typedef struct {
+	const tg_cuda_program *p;
+	const float *row;
+	float *arena;
+	long *slot; /* per value: arena offset, or input offset into the row */
+	int *steps;
+	float *margin; /* per think loop: min over iterations of |delta - eps|, or NULL */
+} OVM;
+
+static long numel(const tg_cuda_value *v)
+{
+	long n = 1;
+	for (int i = 0; i < v->rank; i++) n *= v->dim[i];
+	return n;
+}
+
+static float *optr(OVM *vm, int v)
+{
+	const tg_cuda_value *x = &vm->p->val[v];
+	if (x->kind == TG_CUDA_PARAM || x->kind == TG_CUDA_STATE) return (float *)x->data;
+	if (x->kind == TG_CUDA_INPUT) return (float *)vm->row + vm->slot[v];
+	return vm->arena + vm->slot[v];
+}
+
+static void ocopy(float *o, const float *a, long n)
+{
+	if (o != a) memmove(o, a, (size_t)n * sizeof *o);
+}
+
+/* NumPy broadcasting (src/util.c shape_broadcast): dimensions aligned from the right. */
+static void obin(int op, float *o, const tg_cuda_value *vo, const float *a, const tg_cuda_value *va, const float *b,
+		 const tg_cuda_value *vb)
+{
+	int r = vo->rank;
+	long n = numel(vo);
+	long sa[4] = { 0 }, sb[4] = { 0 };
+	long st = 1;
+	for (int d = va->rank - 1; d >= 0; d--) {
+		int od = r - va->rank + d;
+		sa[od] = va->dim[d] == 1 ? 0 : st;
+		st *= va->dim[d];
+	}
+	st = 1;
+	for (int d = vb->rank - 1; d >= 0; d--) {
+		int od = r - vb->rank + d;
+		sb[od] = vb->dim[d] == 1 ? 0 : st;
+		st *= vb->dim[d];
+	}
+	for (long i = 0; i < n; i++) {
+		long rem = i, ia = 0, ib = 0;
+		for (int d = r - 1; d >= 0; d--) {
+			long idx = rem % vo->dim[d];
+			rem /= vo->dim[d];
+			ia += idx * sa[d];
+			ib += idx * sb[d];
+		}
+		o[i] = bin1(op, a[ia], b[ib]);
+	}
+}
+
+static int oexec(OVM *vm, int from, int count);
+
+/* src/ops.c:60-73 matmul_dims / matmul_groups, src/ops.c:310-320 q_axis_for,
+ * src/vm.c:262-290 dispatch. */
+static void omatmul(OVM *vm, const tg_cuda_ins *in)
+{
+	const tg_cuda_program *p = vm->p;
+	const tg_cuda_value *A = &p->val[in->a[0]], *B = &p->val[in->a[1]];
+	int g = A->rank == 3 && B->rank == 3 ? A->dim[0] : 1;
+	int m = A->rank == 3 ? (g > 1 || B->rank == 3 ? A->dim[1] : A->dim[0] * A->dim[1]) : A->rank == 2 ? A->dim[0] : 1;
+	int k = A->dim[A->rank - 1];
+	int n = B->rank >= 2 ? B->dim[B->rank - 1] : 1;
+	float *o = optr(vm, in->out);
+	const float *a = optr(vm, in->a[0]), *b = optr(vm, in->a[1]);
+	if (g > 1) {
+		for (int i = 0; i < g; i++)
+			tgo_matmul(o + (long)i * m * n, a + (long)i * m * k, b + (long)i * k * n, m, k, n);
+		return;
+	}
+	int qa_axis = A->rank == 2 && in->a[0] != in->a[1] ? 0 : -1;
+	int qb_axis = B->rank == 2 && in->a[0] != in->a[1] ? 1 : -1;
+	if (A->qbits && qa_axis == A->qaxis) tgo_matmul_qa(o, A->q, A->qbits, A->qs, b, m, k, n);
+	else if (B->qbits && qb_axis == B->qaxis) tgo_matmul_qb(o, a, B->q, B->qbits, B->qs, m, k, n);
+	else tgo_matmul(o, a, b, m, k, n);
+}
+
+static int oone(OVM *vm, const tg_cuda_ins *in)
+{
+	const tg_cuda_program *p = vm->p;
+	const tg_cuda_value *vo = &p->val[in->out];
+	long n = numel(vo);
+	float *o = optr(vm, in->out);
+	const float *a = in->na > 0 ? optr(vm, in->a[0]) : NULL;
+	const float *c = in->na > 1 ? optr(vm, in->a[1]) : NULL;
+	switch (in->op) {
+	case TG_CUDA_OP_CONST:
+		o[0] = in->k;
+		return 0;
+	case TG_CUDA_OP_ADD: case TG_CUDA_OP_SUB: case TG_CUDA_OP_MUL: case TG_CUDA_OP_DIV: case TG_CUDA_OP_MAX: case TG_CUDA_OP_MIN:
+		obin(in->op, o, vo, a, &p->val[in->a[0]], c, &p->val[in->a[1]]);
+		return 0;
+	case TG_CUDA_OP_NEG: case TG_CUDA_OP_TANH: case TG_CUDA_OP_RELU: case TG_CUDA_OP_SIGMOID: case TG_CUDA_OP_EXP:
+	case TG_CUDA_OP_SQRT: case TG_CUDA_OP_GELU: case TG_CUDA_OP_SILU: case TG_CUDA_OP_SOFTPLUS: case TG_CUDA_OP_LOG:
+	case TG_CUDA_OP_STEP: case TG_CUDA_OP_SIN: case TG_CUDA_OP_COS: case TG_CUDA_OP_FLOOR:
+		tgo_unary(in->op, o, a, (int)n);
+		return 0;
+	case TG_CUDA_OP_MATMUL:
+		omatmul(vm, in);
+		return 0;
+	case TG_CUDA_OP_SOFTMAX: case TG_CUDA_OP_RMSNORM: { /* src/ops.c:75-79 row_dims */
+		const tg_cuda_value *x = &p->val[in->a[0]];
+		int cols = x->rank ? x->dim[x->rank - 1] : 1, rows = (int)(numel(x) / cols);
+		if (in->op == TG_CUDA_OP_SOFTMAX) tgo_softmax(o, a, rows, cols);
+		else tgo_rmsnorm(o, a, rows, cols);
+		return 0;
+	}
+	case TG_CUDA_OP_SUM: case TG_CUDA_OP_MEAN: { /* runtime/tg_rt.h:178-181 */
+		long k = numel(&p->val[in->a[0]]);
+		float s = 0.0f;
+		for (long i = 0; i < k; i++) s += a[i];
+		o[0] = in->op == TG_CUDA_OP_SUM ? s : s / (float)k;
+		return 0;
+	}
+	case TG_CUDA_OP_TRANSPOSE: { /* runtime/tg_rt.h:183-187, :443-446 */
+		const tg_cuda_value *x = &p->val[in->a[0]];
+		int g = x->rank == 3 ? x->dim[0] : 1, r = x->dim[x->rank - 2], cc = x->dim[x->rank - 1];
+		for (int q = 0; q < g; q++)
+			for (int i = 0; i < r; i++)
+				for (int j = 0; j < cc; j++) o[(long)q * r * cc + (long)j * r + i] = a[(long)q * r * cc + (long)i * cc + j];
+		return 0;
+	}
+	case TG_CUDA_OP_OUTER: { /* runtime/tg_rt.h:190-194 */
+		long m = numel(&p->val[in->a[0]]), nn = numel(&p->val[in->a[1]]);
+		for (long i = 0; i < m; i++)
+			for (long j = 0; j < nn; j++) o[i * nn + j] = a[i] * c[j];
+		return 0;
+	}
+	case TG_CUDA_OP_TAKE: { /* runtime/tg_rt.h:316-322 with tg_ell_idx :200-204 */
+		const tg_cuda_value *w = &p->val[in->a[0]];
+		int d = w->dim[0];
+		long h = numel(w) / d;
+		int cnt = p->val[in->a[1]].dim[0];
+		for (int i = 0; i < cnt; i++) {
+			float r = floorf(c[i] + 0.5f);
+			int t = r >= 0.0f && r < (float)d ? (int)r : -1;
+			for (long j = 0; j < h; j++) o[(long)i * h + j] = t >= 0 ? a[(long)t * h + j] : 0.0f;
+		}
+		return 0;
+	}
+	case TG_CUDA_OP_RESHAPE:
+		ocopy(o, a, n);
+		return 0;
+	case TG_CUDA_OP_THINK: { /* src/vm.c:383-411 */
+		ocopy(o, optr(vm, in->init), n);
+		int it = 0;
+		float survive = 1.0f;
+		while (it < in->maxit) {
+			if (oexec(vm, in->body, in->nbody)) return -1;
+			it++;
+			const float *y = optr(vm, in->yield);
+			float d = 0.0f; /* runtime/tg_rt.h:361-366 tg_delta */
+			for (long i = 0; i < n; i++) {
+				float e = fabsf(y[i] - o[i]);
+				if (e > d) d = e;
+			}
+			ocopy(o, y, n);
+			if (vm->margin && in->eps >= 0 && fabsf(d - in->eps) < vm->margin[in->tid]) vm->margin[in->tid] = fabsf(d - in->eps);
+			if (in->eps >= 0 && d <= in->eps) break;
+			if (in->halt >= 0) {
+				float pr = *optr(vm, in->halt);
+				survive *= 1.0f - (pr < 0.0f ? 0.0f : pr > 1.0f ? 1.0f : pr);
+				if (1.0f - survive > in->hthr) break;
+			}
+		}
+		vm->steps[in->tid] = it;
+		return 0;
+	}
+	case TG_CUDA_OP_SCAN: { /* src/vm.c:364-382 */
+		const tg_cuda_scan *s = &p->scans[in->scan];
+		for (int k = 0; k < s->nc; k++) ocopy(optr(vm, s->c[k]), optr(vm, s->init[k]), numel(&p->val[s->c[k]]));
+		for (int step = 0; step < s->T; step++) {
+			int t = s->reverse ? s->T - 1 - step : step;
+			for (int j = 0; j < s->nx; j++) {
+				long w = numel(&p->val[s->xt[j]]);
+				ocopy(optr(vm, s->xt[j]), optr(vm, s->x[j]) + (long)t * w, w);
+			}
+			if (oexec(vm, in->body, in->nbody)) return -1;
+			for (int y = 0; y < s->ny; y++) {
+				long w = numel(&p->val[s->y[y]]);
+				ocopy(optr(vm, s->ys[y]) + (long)t * w, optr(vm, s->y[y]), w);
+			}
+			for (int k = 0; k < s->nc; k++) ocopy(optr(vm, s->c[k]), optr(vm, s->next[k]), numel(&p->val[s->c[k]]));
+		}
+		if (s->tid >= 0) vm->steps[s->tid] = s->T;
+		return 0;
+	}
+	}
+	return -1;
+}
+
+static int oexec(OVM *vm, int from, int count)
+{
+	for (int i = from; i < from + count; i++)
+		if (oone(vm, &vm->p->ins[i])) return -1;
+	return 0;
+}
+
+/* One slot per temporary (no sharing): the oracle favours plainness over size. */
+static long oplan(const tg_cuda_program *p, long *slot)
+{
+	long off = 0, in = 0;
+	for (int i = 0; i < p->ninputs; i++) {
+		slot[p->inputs[i]] = in;
+		in += numel(&p->val[p->inputs[i]]);
+	}
+	for (int v = 0; v < p->nval; v++)
+		if (p->val[v].kind == TG_CUDA_TMP) {
+			slot[v] = off;
+			off += (numel(&p->val[v]) + 3) / 4 * 4;
+		}
+	return off ? off : 1;
+}
+
+long tgo_program_arena(const tg_cuda_program *p)
+{
+	long *slot = calloc((size_t)p->nval + 1, sizeof *slot);
+	long a = oplan(p, slot);
+	free(slot);
+	return a;
+}
+
+int tgo_program_run(const tg_cuda_program *p, const float *row, float *out, int *steps, float *arena, float *margin)
+{
+	long *slot = calloc((size_t)p->nval + 1, sizeof *slot);
+	oplan(p, slot);
+	if (margin)
+		for (int t = 0; t < p->nthink; t++) margin[t] = INFINITY;
+	OVM vm = { p, row, arena, slot, steps, margin };
+	int rc = oexec(&vm, 0, p->ntop);
+	if (!rc) ocopy(out, optr(&vm, p->output), numel(&p->val[p->output]));
+	free(slot);
+	return rc;
+}
+
+/* ---- the Qwen3 program: examples/qwen3/import.py:90-132 ---------------------------- */
+
+static void rowmul(float *x, const float *w, int rows, int cols) /* x * w, w broadcast over rows */
+{
+	for (int r = 0; r < rows; r++)
+		for (int i = 0; i < cols; i++) x[(long)r * cols + i] = x[(long)r * cols + i] * w[i];
+}
+
+/* Column block [c0, c0+nc) of a quantized [K, N] matrix applied as x @ W (tg_matmul_qb on
+ * the per-head param the program holds). */
+static void qb_block(float *o, const float *x, const tg_cuda_qmat *w, int bits, int T, int K, int N, int c0, int nc,
+		     const float *s)
+{
+	for (int t = 0; t < T; t++)
+		for (int j = 0; j < nc; j++) {
+			float acc = 0.0f;
+			for (int p = 0; p < K; p++) acc += x[(long)t * K + p] * (float)tgo_qget(w->q, bits, (long)p * N + c0 + j);
+			o[(long)t * nc + j] = s[j] * acc;
+		}
+}
+
+/* rotary(x) = x * cosT + (x @ Rot) * sinT with Rot the rotate-half matrix
+ * (import.py:79-84,96-97); x @ Rot sums exactly one nonzero product. */
+static void rotary(float *x, const float *cosT, const float *sinT, int T, int HD)
+{
+	float *r = malloc((size_t)HD * sizeof *r);
+	for (int t = 0; t < T; t++) {
+		float *v = x + (long)t * HD;
+		for (int i = 0; i < HD / 2; i++) {
+			r[i] = -v[i + HD / 2];
+			r[i + HD / 2] = v[i];
+		}
+		for (int i = 0; i < HD; i++) {
+			float a = v[i] * cosT[(long)t * HD + i], b = r[i] * sinT[(long)t * HD + i];
+			v[i] = a + b;
+		}
+	}
+	free(r);
+}
+
+int tgo_lm_forward(const tg_cuda_lm_desc *d, const float *ids, int T, float *logits)
+{
+	int D = d->hidden, HD = d->head_dim, NQ = d->nq, NKV = d->nkv, FF = d->ffn, V = d->vocab, grp = NQ / NKV;
+	size_t TD = (size_t)T * D;
+	float *h = malloc(TD * sizeof *h), *n = malloc(TD * sizeof *n), *acc = malloc(TD * sizeof *acc);
+	float *k = malloc((size_t)NKV * T * HD * sizeof *k), *v = malloc((size_t)NKV * T * HD * sizeof *v);
+	float *q = malloc((size_t)T * HD * sizeof *q), *sc = malloc((size_t)T * T * sizeof *sc);
+	float *sv = malloc((size_t)T * HD * sizeof *sv), *oh = malloc(TD * sizeof *oh);
+	float *g = malloc((size_t)T * FF * sizeof *g), *u = malloc((size_t)T * FF * sizeof *u), *m = malloc(TD * sizeof *m);
+	float *cosT = malloc((size_t)T * HD * sizeof *cosT), *sinT = malloc((size_t)T * HD * sizeof *sinT);
+	/* RoPE tables in double, stored as f32 (import.py:76-78) */
+	for (int t = 0; t < T; t++)
+		for (int i = 0; i < HD / 2; i++) {
+			double inv = pow(d->rope_theta, -((double)(2 * i) / HD)), ang = (double)t * inv;
+			cosT[(long)t * HD + i] = cosT[(long)t * HD + i + HD / 2] = (float)cos(ang);
+			sinT[(long)t * HD + i] = sinT[(long)t * HD + i + HD / 2] = (float)sin(ang);
+		}
+	for (int t = 0; t < T; t++) { /* h = take(E, ids) */
+		float r = floorf(ids[t] + 0.5f);
+		int row = r >= 0.0f && r < (float)V ? (int)r : -1;
+		for (int i = 0; i < D; i++) h[(long)t * D + i] = row >= 0 ? d->embed[(long)row * D + i] : 0.0f;
+	}
+	for (int l = 0; l < d->layers; l++) {
+		tgo_rmsnorm(n, h, T, D); /* n = rmsnorm(h) * ln1 */
+		rowmul(n, d->ln1[l], T, D);
+		for (int j = 0; j < NKV; j++) {
+			float *kj = k + (size_t)j * T * HD, *vj = v + (size_t)j * T * HD;
+			qb_block(kj, n, &d->wk[l], d->bits, T, D, NKV * HD, j * HD, HD, d->wk[l].s + j * HD);
+			tgo_rmsnorm(kj, kj, T, HD);
+			rowmul(kj, d->kn[l], T, HD);
+			rotary(kj, cosT, sinT, T, HD);
+			qb_block(vj, n, &d->wv[l], d->bits, T, D, NKV * HD, j * HD, HD, d->wv[l].s + j * HD);
+		}
+		for (int hh = 0; hh < NQ; hh++) {
+			const float *kj = k + (size_t)(hh / grp) * T * HD, *vj = v + (size_t)(hh / grp) * T * HD;
+			qb_block(q, n, &d->wq[l], d->bits, T, D, NQ * HD, hh * HD, HD, d->wq[l].s + hh * HD);
+			tgo_rmsnorm(q, q, T, HD);
+			rowmul(q, d->qn[l], T, HD);
+			rotary(q, cosT, sinT, T, HD);
+			/* s = softmax((q @ transpose(k)) * scale + mask), mask 0 / -1e9 (import.py:85) */
+			for (int t = 0; t < T; t++)
+				for (int s2 = 0; s2 < T; s2++) {
+					float dot = 0.0f;
+					for (int p = 0; p < HD; p++) dot += q[(long)t * HD + p] * kj[(long)s2 * HD + p];
+					sc[(long)t * T + s2] = dot * d->attn_scale + (s2 <= t ? 0.0f : -1e9f);
+				}
+			tgo_softmax(sc, sc, T, T);
+			tgo_matmul(sv, sc, vj, T, T, HD);
+			/* o_h = (s @ v) @ Wo_h: rows h*HD.. of the stacked Wo, per-head column scales */
+			const tg_cuda_qmat *wo = &d->wo[l];
+			for (int t = 0; t < T; t++)
+				for (int c = 0; c < D; c++) {
+					float a = 0.0f;
+					for (int p = 0; p < HD; p++)
+						a += sv[(long)t * HD + p] * (float)tgo_qget(wo->q, d->bits, (long)(hh * HD + p) * D + c);
+					oh[(long)t * D + c] = wo->s[(long)hh * D + c] * a;
+				}
+			if (hh == 0) memcpy(acc, oh, TD * sizeof *acc); /* o0 + o1 + ... left to right */
+			else
+				for (size_t i = 0; i < TD; i++) acc[i] = acc[i] + oh[i];
+		}
+		for (size_t i = 0; i < TD; i++) h[i] = h[i] + acc[i];
+		tgo_rmsnorm(n, h, T, D); /* n = rmsnorm(h) * ln2 */
+		rowmul(n, d->ln2[l], T, D);
+		qb_block(g, n, &d->wg[l], d->bits, T, D, FF, 0, FF, d->wg[l].s);
+		qb_block(u, n, &d->wu[l], d->bits, T, D, FF, 0, FF, d->wu[l].s);
+		for (size_t i = 0; i < (size_t)T * FF; i++) g[i] = (g[i] / (1.0f + expf(-g[i]))) * u[i];
+		qb_block(m, g, &d->wd[l], d->bits, T, FF, D, 0, D, d->wd[l].s);
+		for (size_t i = 0; i < TD; i++) h[i] = h[i] + m[i];
+	}
+	/* logits = (rmsnorm(h) * lnf) @ LM; take(logits, lastidx) keeps row T-1 */
+	tgo_rmsnorm(n, h + (size_t)(T - 1) * D, 1, D);
+	rowmul(n, d->final_norm, 1, D);
+	qb_block(logits, n, &d->lm_head, d->bits, 1, D, V, 0, V, d->lm_head.s);
+	free(h); free(n); free(acc); free(k); free(v); free(q); free(sc); free(sv); free(oh);
+	free(g); free(u); free(m); free(cosT); free(sinT);
+	return 0;
+}

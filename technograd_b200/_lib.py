@@ -1,0 +1,125 @@
+"""ctypes binding of libtgcuda (include/tg_cuda.h).
+
+The structures mirror the header field for field. Loading fails loudly when
+the library is missing: the package has no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libtgcuda.so")
+
+OK, EINVAL, ENODEV, ECUDA, EUNSUPPORTED, ENOMEM, EFAULT, EDEVICE = 0, -1, -2, -3, -4, -5, -6, -7
+
+# enum Op of the reference (src/tg.h:68-112), the numbering of TG_CUDA_OP_*
+OPS = ["const", "add", "sub", "mul", "div", "max", "min", "neg", "tanh", "relu", "sigmoid", "exp", "sqrt",
+       "gelu", "silu", "softplus", "log", "matmul", "softmax", "rmsnorm", "sum", "mean", "transpose", "outer",
+       "step", "spmm", "spmm_t", "spmm_dx", "active", "take", "take_t", "spmm_tc", "sin", "cos", "reshape",
+       "floor", "sum_to", "topk", "memscan", "memscan_t", "sufmatch", "think", "scan"]
+OP = {name: i for i, name in enumerate(OPS)}
+PARAM, INPUT, TMP, STATE = 0, 1, 2, 3
+
+# Every entry point include/tg_cuda.h declares.
+SYMBOLS = ["tg_cuda_error", "tg_cuda_init", "tg_cuda_ngpus", "tg_cuda_shutdown", "tg_cuda_matmul_q",
+           "tg_cuda_quantize_rtn", "tg_cuda_load", "tg_cuda_batch", "tg_cuda_batch_device", "tg_cuda_free",
+           "tg_cuda_lm_load", "tg_cuda_lm_forward", "tg_cuda_lm_generate", "tg_cuda_lm_free"]
+
+
+class TgCudaError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"tg_cuda status {status}: {msg}")
+        self.status = status
+
+
+class Value(C.Structure):
+    _fields_ = [("kind", C.c_int), ("rank", C.c_int), ("dim", C.c_int * 4), ("data", C.POINTER(C.c_float)),
+                ("qbits", C.c_int), ("qaxis", C.c_int), ("q", C.POINTER(C.c_byte)), ("qs", C.POINTER(C.c_float)),
+                ("index", C.c_int)]
+
+
+class Scan(C.Structure):
+    _fields_ = [("T", C.c_int), ("reverse", C.c_int), ("tid", C.c_int),
+                ("nc", C.c_int), ("c", C.POINTER(C.c_int)), ("init", C.POINTER(C.c_int)), ("next", C.POINTER(C.c_int)),
+                ("nx", C.c_int), ("x", C.POINTER(C.c_int)), ("xt", C.POINTER(C.c_int)),
+                ("ny", C.c_int), ("y", C.POINTER(C.c_int)), ("ys", C.POINTER(C.c_int))]
+
+
+class Ins(C.Structure):
+    _fields_ = [("op", C.c_int), ("out", C.c_int), ("a", C.c_int * 3), ("na", C.c_int), ("k", C.c_float),
+                ("init", C.c_int), ("maxit", C.c_int), ("eps", C.c_float), ("yield_", C.c_int), ("tid", C.c_int),
+                ("halt", C.c_int), ("hthr", C.c_float), ("body", C.c_int), ("nbody", C.c_int), ("scan", C.c_int)]
+
+
+class Program(C.Structure):
+    _fields_ = [("nval", C.c_int), ("val", C.POINTER(Value)), ("nins", C.c_int), ("ins", C.POINTER(Ins)),
+                ("ntop", C.c_int), ("nscan", C.c_int), ("scans", C.POINTER(Scan)), ("ninputs", C.c_int),
+                ("inputs", C.POINTER(C.c_int)), ("output", C.c_int), ("nthink", C.c_int), ("nupd", C.c_int)]
+
+
+class QMat(C.Structure):
+    _fields_ = [("q", C.POINTER(C.c_byte)), ("s", C.POINTER(C.c_float))]
+
+
+FP = C.POINTER(C.c_float)
+FPP = C.POINTER(FP)
+QP = C.POINTER(QMat)
+
+
+class LmDesc(C.Structure):
+    _fields_ = [("layers", C.c_int), ("hidden", C.c_int), ("nq", C.c_int), ("nkv", C.c_int), ("head_dim", C.c_int),
+                ("ffn", C.c_int), ("vocab", C.c_int), ("bits", C.c_int), ("eps", C.c_float),
+                ("attn_scale", C.c_float), ("rope_theta", C.c_double), ("embed", FP), ("final_norm", FP),
+                ("lm_head", QMat), ("ln1", FPP), ("ln2", FPP), ("qn", FPP), ("kn", FPP),
+                ("wq", QP), ("wk", QP), ("wv", QP), ("wo", QP), ("wg", QP), ("wu", QP), ("wd", QP)]
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The loaded library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"libtgcuda is not built ({LIB_PATH}); run __graft_entry__.build()")
+        L = C.CDLL(LIB_PATH)
+        vp, i, l = C.c_void_p, C.c_int, C.c_long
+        sigs = {
+            "tg_cuda_error": ([], C.c_char_p),
+            "tg_cuda_init": ([i, C.POINTER(i)], i),
+            "tg_cuda_ngpus": ([], i),
+            "tg_cuda_shutdown": ([], None),
+            "tg_cuda_matmul_q": ([i, vp, vp, vp, i, vp, i, i, i, vp], i),
+            "tg_cuda_quantize_rtn": ([vp, i, i, i, i, vp, vp, vp], i),
+            "tg_cuda_load": ([C.POINTER(Program), C.POINTER(vp)], i),
+            "tg_cuda_batch": ([vp, vp, l, i, vp, i, vp, i], i),
+            "tg_cuda_batch_device": ([vp, vp, l, vp, vp, vp], i),
+            "tg_cuda_free": ([vp], None),
+            "tg_cuda_lm_load": ([C.POINTER(LmDesc), i, i, C.POINTER(vp)], i),
+            "tg_cuda_lm_forward": ([vp, vp, l, i, vp], i),
+            "tg_cuda_lm_generate": ([vp, vp, l, i, i, vp], i),
+            "tg_cuda_lm_free": ([vp], None),
+        }
+        for name, (args, res) in sigs.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = res
+        _lib = L
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != OK:
+        raise TgCudaError(status, lib().tg_cuda_error().decode(errors="replace"))
+
+
+def init(ngpus: int = 0, devices=None) -> int:
+    L = lib()
+    if devices:
+        arr = (C.c_int * len(devices))(*devices)
+        check(L.tg_cuda_init(len(devices), arr))
+    else:
+        check(L.tg_cuda_init(ngpus, None))
+    return L.tg_cuda_ngpus()

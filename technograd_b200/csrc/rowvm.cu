@@ -1,0 +1,965 @@
+// rowvm.cu -- the batch executor: a planned TGIR program run over many rows at
+// once (tg_cuda_load / tg_cuda_batch). Replaces the par_for(batch_rows) loop of
+// the batch branch (src/main.c:421-441) and vm_run_into per row (src/vm.c:475-481).
+//
+// Layout. The host compiles the program into a tape of device ops. Each thread
+// executes the tape for one row. Its arena (the temporaries, planned with
+// liveness sharing like src/plan.c) lives in shared memory in SoA form,
+// arena[slot * ROWS_PER_CTA + thread], so the 32 lanes of a warp touch 32
+// consecutive words: conflict-free. Params live once per CTA in shared memory
+// (quantized params as their exact codes in f32 plus the channel scales), or in
+// global memory when they do not fit. Think loops run on the device: at the end
+// of a body each lane applies the halting test of src/vm.c:383-411 to its own
+// row, the warp repeats the body while any lane is still iterating, and a lane
+// that halted is masked off until the loop ends for the whole warp.
+//
+// Arithmetic follows the reference kernels (runtime/tg_rt.h) operation by
+// operation: products and sums in the same order with explicit rounding
+// (__fmul_rn/__fadd_rn, no contraction), scale after the sum for quantized
+// matmuls, division by the sum in softmax. Transcendentals are CUDA's libm,
+// which differs from glibc by a few ulp.
+#include <limits.h>
+#include <string.h>
+
+#include <algorithm>
+#include <memory>
+#include <thread>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace tgc {
+
+// ---- device tape ----------------------------------------------------------------------
+
+enum : int {
+	D_CONST = 1, D_BIN, D_UN, D_MATMUL, D_ROW, D_RED, D_TRANS, D_OUTER, D_TAKE, D_COPY,
+	D_THINK_BEGIN, D_THINK_END, D_SCAN_BEGIN, D_SCAN_SLICE, D_SCAN_END,
+};
+
+// An operand: >= 0 an arena slot (per row), < 0 a param offset -(loc + 1) in the param blob.
+struct DOp {
+	int code, sub;        // tape opcode; TG op (bin/un/row/red) or variant
+	int out, a, b, c;     // operand locations
+	int n;                // element count of out (elementwise), etc.
+	int dims[4], sa[4], sb[4]; // broadcast: out dims (rank in sub2), operand strides
+	int rank;
+	int m, k, nn, g;      // matmul dims, groups
+	int scale;            // matmul: 0 none, 1 per row (qa), 2 per column (qb); c = scale location
+	int depth, target;    // loops: depth, jump target
+	int tid, maxit, yield, halt;
+	float f, eps, hthr;
+	int cnt, len;         // copies / scans: count and lengths
+};
+
+struct Prog {
+	std::vector<DOp> tape;
+	std::vector<float> blob; // params
+	int arena = 0;           // floats per row
+	int per = 0, nout = 0, nthink = 0, out_loc = 0;
+	std::vector<int> in_off, in_len; // input i: arena location, length
+	int max_depth = 0;
+};
+
+constexpr int VM_ROWS = 128; // rows (threads) per CTA
+constexpr int VM_MAXDEPTH = 4;
+
+struct Loc {
+	float *p;
+	int st;
+};
+
+__device__ __forceinline__ Loc loc(int l, float *ar, const float *pb)
+{
+	if (l >= 0) return { ar + (long)l * VM_ROWS, VM_ROWS };
+	return { (float *)pb + (-(l + 1)), 1 };
+}
+
+__device__ float un_op(int op, float x)
+{
+	switch (op) {
+	case TG_CUDA_OP_NEG: return -x;
+	case TG_CUDA_OP_TANH: return tanhf(x);
+	case TG_CUDA_OP_RELU: return x > 0.0f ? x : 0.0f;
+	case TG_CUDA_OP_SIGMOID: return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+	case TG_CUDA_OP_EXP: return expf(x);
+	case TG_CUDA_OP_SQRT: return __fsqrt_rn(x);
+	case TG_CUDA_OP_GELU: {
+		float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+		float t = tanhf(__fmul_rn(0.7978845608f, __fadd_rn(x, x3)));
+		return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
+	}
+	case TG_CUDA_OP_SILU: return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+	case TG_CUDA_OP_SOFTPLUS: return __fadd_rn(x > 0.0f ? x : 0.0f, log1pf(expf(-fabsf(x))));
+	case TG_CUDA_OP_LOG: return logf(x);
+	case TG_CUDA_OP_STEP: return x > 0.0f ? 1.0f : 0.0f;
+	case TG_CUDA_OP_SIN: return sinf(x);
+	case TG_CUDA_OP_COS: return cosf(x);
+	case TG_CUDA_OP_FLOOR: return floorf(x);
+	}
+	return 0.0f;
+}
+
+__device__ __forceinline__ float bin_op(int op, float x, float y)
+{
+	switch (op) {
+	case TG_CUDA_OP_ADD: return __fadd_rn(x, y);
+	case TG_CUDA_OP_SUB: return __fsub_rn(x, y);
+	case TG_CUDA_OP_MUL: return __fmul_rn(x, y);
+	case TG_CUDA_OP_DIV: return __fdiv_rn(x, y);
+	case TG_CUDA_OP_MAX: return x > y ? x : y;
+	case TG_CUDA_OP_MIN: return x < y ? x : y;
+	}
+	return 0.0f;
+}
+
+// o[i,j] (+ per-group offsets) = sum_p a[i,p] b[p,j], in p order, scale after the sum.
+__device__ void vm_matmul(const DOp &op, float *ar, const float *pb)
+{
+	Loc o = loc(op.out, ar, pb), a = loc(op.a, ar, pb), b = loc(op.b, ar, pb);
+	const float *sc = op.scale ? loc(op.c, ar, pb).p : nullptr;
+	const int m = op.m, k = op.k, n = op.nn;
+	for (int g = 0; g < op.g; g++) {
+		long oo = (long)g * m * n, ao = (long)g * m * k, bo = (long)g * k * n;
+		for (int i = 0; i < m; i++)
+			for (int j = 0; j < n; j++) {
+				float acc = 0.0f;
+				for (int p = 0; p < k; p++)
+					acc = __fadd_rn(acc, __fmul_rn(a.p[(ao + (long)i * k + p) * a.st], b.p[(bo + (long)p * n + j) * b.st]));
+				if (op.scale == 1) acc = __fmul_rn(sc[i], acc);
+				else if (op.scale == 2) acc = __fmul_rn(sc[j], acc);
+				o.p[(oo + (long)i * n + j) * o.st] = acc;
+			}
+	}
+}
+
+__global__ void __launch_bounds__(VM_ROWS) vm_kernel(const DOp *__restrict__ tape, int ntape,
+						    const float *__restrict__ gblob, int nblob, int blob_in_smem, int arena,
+						    const float *__restrict__ in, int per, long rows, float *__restrict__ out,
+						    int nout, int out_loc, int *__restrict__ steps, int nt,
+						    const int *__restrict__ in_loc, const int *__restrict__ in_len, int ninputs,
+						    float *__restrict__ gar)
+{
+	extern __shared__ float sm[];
+	float *blob = blob_in_smem ? sm : (float *)gblob;
+	float *arsm = sm + (blob_in_smem ? (nblob + 3) / 4 * 4 : 0);
+	if (blob_in_smem)
+		for (int i = threadIdx.x; i < nblob; i += blockDim.x) sm[i] = gblob[i];
+	// per-thread arena base: column threadIdx.x of a [arena][VM_ROWS] table
+	float *ar = gar ? gar + (long)blockIdx.x * arena * VM_ROWS + threadIdx.x : arsm + threadIdx.x;
+	__syncthreads();
+	const long row = (long)blockIdx.x * VM_ROWS + threadIdx.x;
+	const bool live = row < rows;
+	// inputs -> arena
+	if (live)
+		for (int i = 0, o = 0; i < ninputs; i++) {
+			const float *src = in + row * per + o;
+			float *dst = ar + (long)in_loc[i] * VM_ROWS;
+			for (int e = 0; e < in_len[i]; e++) dst[(long)e * VM_ROWS] = src[e];
+			o += in_len[i];
+		}
+	unsigned done = live ? 0u : 1u << VM_MAXDEPTH; // bit d: halted in the loop at depth d
+	int it[VM_MAXDEPTH];
+	float surv[VM_MAXDEPTH];
+	for (int pc = 0; pc < ntape;) {
+		const DOp &op = tape[pc];
+		const bool act = done == 0;
+		switch (op.code) {
+		case D_CONST:
+			if (act) ar[(long)op.out * VM_ROWS] = op.f;
+			break;
+		case D_BIN:
+			if (act) {
+				Loc o = loc(op.out, ar, blob), a = loc(op.a, ar, blob), b = loc(op.b, ar, blob);
+				if (op.rank == 0) { // equal shapes or scalars: sa/sb[0] are 1 or 0
+					for (int e = 0; e < op.n; e++)
+						o.p[(long)e * o.st] = bin_op(op.sub, a.p[(long)e * op.sa[0] * a.st], b.p[(long)e * op.sb[0] * b.st]);
+				} else {
+					for (int e = 0; e < op.n; e++) {
+						int rem = e, ia = 0, ib = 0;
+						for (int d = op.rank - 1; d >= 0; d--) {
+							int idx = rem % op.dims[d];
+							rem /= op.dims[d];
+							ia += idx * op.sa[d];
+							ib += idx * op.sb[d];
+						}
+						o.p[(long)e * o.st] = bin_op(op.sub, a.p[(long)ia * a.st], b.p[(long)ib * b.st]);
+					}
+				}
+			}
+			break;
+		case D_UN:
+			if (act) {
+				Loc o = loc(op.out, ar, blob), a = loc(op.a, ar, blob);
+				for (int e = 0; e < op.n; e++) o.p[(long)e * o.st] = un_op(op.sub, a.p[(long)e * a.st]);
+			}
+			break;
+		case D_MATMUL:
+			if (act) vm_matmul(op, ar, blob);
+			break;
+		case D_ROW:
+			if (act) {
+				Loc o = loc(op.out, ar, blob), a = loc(op.a, ar, blob);
+				for (int r = 0; r < op.m; r++) {
+					const long base = (long)r * op.k;
+					if (op.sub == TG_CUDA_OP_SOFTMAX) { // runtime/tg_rt.h:154-164
+						float mx = a.p[base * a.st], s = 0.0f;
+						for (int i = 1; i < op.k; i++) {
+							float v = a.p[(base + i) * a.st];
+							if (v > mx) mx = v;
+						}
+						for (int i = 0; i < op.k; i++) {
+							float y = expf(__fsub_rn(a.p[(base + i) * a.st], mx));
+							o.p[(base + i) * o.st] = y;
+							s = __fadd_rn(s, y);
+						}
+						for (int i = 0; i < op.k; i++) o.p[(base + i) * o.st] = __fdiv_rn(o.p[(base + i) * o.st], s);
+					} else { // rmsnorm, runtime/tg_rt.h:165-175
+						float s = 0.0f;
+						for (int i = 0; i < op.k; i++) {
+							float x = a.p[(base + i) * a.st];
+							s = __fadd_rn(s, __fmul_rn(x, x));
+						}
+						float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)op.k), 1e-6f)));
+						for (int i = 0; i < op.k; i++) o.p[(base + i) * o.st] = __fmul_rn(a.p[(base + i) * a.st], inv);
+					}
+				}
+			}
+			break;
+		case D_RED:
+			if (act) {
+				Loc o = loc(op.out, ar, blob), a = loc(op.a, ar, blob);
+				float s = 0.0f;
+				for (int e = 0; e < op.n; e++) s = __fadd_rn(s, a.p[(long)e * a.st]);
+				o.p[0] = op.sub == TG_CUDA_OP_MEAN ? __fdiv_rn(s, (float)op.n) : s;
+			}
+			break;
+		case D_TRANS:
+			if (act) {
+				Loc o = loc(op.out, ar, blob), a = loc(op.a, ar, blob);
+				for (int g = 0; g < op.g; g++)
+					for (int i = 0; i < op.m; i++)
+						for (int j = 0; j < op.k; j++)
+							o.p[((long)g * op.m * op.k + (long)j * op.m + i) * o.st] = a.p[((long)g * op.m * op.k + (long)i * op.k + j) * a.st];
+			}
+			break;
+		case D_OUTER:
+			if (act) {
+				Loc o = loc(op.out, ar, blob), a = loc(op.a, ar, blob), b = loc(op.b, ar, blob);
+				for (int i = 0; i < op.m; i++)
+					for (int j = 0; j < op.k; j++) o.p[((long)i * op.k + j) * o.st] = __fmul_rn(a.p[(long)i * a.st], b.p[(long)j * b.st]);
+			}
+			break;
+		case D_TAKE: // runtime/tg_rt.h:316-322, rows of a [d, h] by rounded index
+			if (act) {
+				Loc o = loc(op.out, ar, blob), a = loc(op.a, ar, blob), b = loc(op.b, ar, blob);
+				for (int i = 0; i < op.m; i++) {
+					float r = floorf(__fadd_rn(b.p[(long)i * b.st], 0.5f));
+					int t = r >= 0.0f && r < (float)op.k ? (int)r : -1;
+					for (int j = 0; j < op.nn; j++)
+						o.p[((long)i * op.nn + j) * o.st] = t >= 0 ? a.p[((long)t * op.nn + j) * a.st] : 0.0f;
+				}
+			}
+			break;
+		case D_COPY:
+			if (act && op.out != op.a) {
+				Loc o = loc(op.out, ar, blob), a = loc(op.a, ar, blob);
+				for (int e = 0; e < op.n; e++) o.p[(long)e * o.st] = a.p[(long)e * a.st];
+			}
+			break;
+		case D_THINK_BEGIN: // copy init into the state, reset this depth's counters
+			if (act) {
+				Loc o = loc(op.out, ar, blob), a = loc(op.a, ar, blob);
+				if (op.out != op.a)
+					for (int e = 0; e < op.n; e++) o.p[(long)e * o.st] = a.p[(long)e * a.st];
+				it[op.depth] = 0;
+				surv[op.depth] = 1.0f;
+			}
+			break;
+		case D_THINK_END: { // src/vm.c:389-409
+			if (act) {
+				Loc o = loc(op.out, ar, blob), y = loc(op.yield, ar, blob);
+				it[op.depth]++;
+				float d = 0.0f;
+				for (int e = 0; e < op.n; e++) {
+					float v = fabsf(__fsub_rn(y.p[(long)e * y.st], o.p[(long)e * o.st]));
+					if (v > d) d = v;
+				}
+				for (int e = 0; e < op.n; e++) o.p[(long)e * o.st] = y.p[(long)e * y.st];
+				bool stop = it[op.depth] >= op.maxit;
+				if (op.eps >= 0 && d <= op.eps) stop = true;
+				if (op.halt != INT_MIN) {
+					float p = loc(op.halt, ar, blob).p[0];
+					surv[op.depth] = __fmul_rn(surv[op.depth], __fsub_rn(1.0f, p < 0.0f ? 0.0f : p > 1.0f ? 1.0f : p));
+					if (__fsub_rn(1.0f, surv[op.depth]) > op.hthr) stop = true;
+				}
+				if (stop) {
+					done |= 1u << op.depth;
+					if (live && op.tid < nt) steps[row * nt + op.tid] = it[op.depth];
+				}
+			}
+			if (__any_sync(0xffffffffu, done == 0)) {
+				pc = op.target;
+				continue;
+			}
+			done &= ~(1u << op.depth);
+			break;
+		}
+		case D_SCAN_BEGIN: // carries <- init (cnt copies listed in the following D_COPY ops)
+			it[op.depth] = 0;
+			break;
+		case D_SCAN_SLICE: // sub bit 0: reverse; bit 1 clear: xt <- row t of x, set: row t of ys <- y
+			if (act) {
+				int t = (op.sub & 1) ? op.len - 1 - it[op.depth] : it[op.depth];
+				Loc o = loc(op.out, ar, blob), a = loc(op.a, ar, blob);
+				if (op.sub & 2)
+					for (int e = 0; e < op.n; e++) o.p[((long)t * op.n + e) * o.st] = a.p[(long)e * a.st];
+				else
+					for (int e = 0; e < op.n; e++) o.p[(long)e * o.st] = a.p[((long)t * op.n + e) * a.st];
+			}
+			break;
+		case D_SCAN_END: // ys[t] <- y (sub-ops follow as D_COPY with a per-step offset)
+			it[op.depth]++;
+			if (it[op.depth] < op.len) {
+				pc = op.target;
+				continue;
+			}
+			if (act && op.tid >= 0 && op.tid < nt && live) steps[row * nt + op.tid] = op.len;
+			break;
+		}
+		pc++;
+	}
+	if (live) {
+		Loc o = loc(out_loc, ar, blob);
+		for (int e = 0; e < nout; e++) out[row * nout + e] = o.p[(long)e * o.st];
+	}
+}
+
+// ---- host: program -> tape -------------------------------------------------------------------
+
+struct Model {
+	Prog prog;
+	struct PerDev {
+		DevBuf tape, blob, inloc, inlen, gar;
+		long gar_rows = 0;
+	};
+	std::vector<std::unique_ptr<PerDev>> dev;
+	bool blob_in_smem = true;
+	size_t smem = 0;
+	bool global_arena = false;
+};
+
+static long numel(const tg_cuda_value &v)
+{
+	long n = 1;
+	for (int i = 0; i < v.rank; i++) n *= v.dim[i];
+	return n;
+}
+
+struct Compiler {
+	const tg_cuda_program *p;
+	Prog *out;
+	std::vector<int> slot;     // arena slot of each temporary
+	std::vector<int> pslot;    // blob offset of each param (f32 values or exact codes)
+	std::vector<int> sslot;    // blob offset of each quantized param's scales
+	std::vector<int> inloc;    // arena slot of each input value
+	std::string err;
+	int status = TG_CUDA_OK;
+
+	int fail(int st, const char *msg, int v = -1)
+	{
+		if (status == TG_CUDA_OK) {
+			status = st;
+			char b[256];
+			snprintf(b, sizeof b, "%s%s%d", msg, v >= 0 ? " (instruction " : "", v);
+			err = b;
+			if (v >= 0) err += ")";
+		}
+		return st;
+	}
+
+	int L(int v) // location of a value
+	{
+		const tg_cuda_value &x = p->val[v];
+		if (x.kind == TG_CUDA_PARAM || x.kind == TG_CUDA_STATE) return -(pslot[v] + 1);
+		if (x.kind == TG_CUDA_INPUT) return inloc[v];
+		return slot[v];
+	}
+};
+
+// Liveness over a linear numbering of instructions, a loop body's reads of outer values
+// extended to the loop end (the algorithm of src/plan.c: lifetimes, then greedy by size).
+struct Life {
+	int def = -1, last = -1;
+};
+
+static void number_ins(const tg_cuda_program *p, int from, int cnt, int &pos, std::vector<int> &beg, std::vector<int> &end)
+{
+	for (int i = from; i < from + cnt; i++) {
+		const tg_cuda_ins &in = p->ins[i];
+		beg[i] = pos++;
+		bool loop = in.op == TG_CUDA_OP_THINK || in.op == TG_CUDA_OP_SCAN;
+		if (loop) number_ins(p, in.body, in.nbody, pos, beg, end);
+		end[i] = loop ? pos++ : beg[i];
+	}
+}
+
+static void lives(const tg_cuda_program *p, int from, int cnt, const std::vector<int> &beg, const std::vector<int> &end,
+		  std::vector<int> &loops, std::vector<Life> &life)
+{
+	auto use = [&](int v, int at) {
+		if (v < 0 || p->val[v].kind != TG_CUDA_TMP) return;
+		int last = at;
+		for (int li : loops)
+			if (life[v].def < beg[li] && end[li] > last) last = end[li];
+		if (last > life[v].last) life[v].last = last;
+	};
+	auto def = [&](int v, int at) {
+		if (v < 0 || p->val[v].kind != TG_CUDA_TMP) return;
+		if (life[v].def < 0 || at < life[v].def) life[v].def = at;
+		if (life[v].last < at) life[v].last = at;
+	};
+	for (int i = from; i < from + cnt; i++) {
+		const tg_cuda_ins &in = p->ins[i];
+		if (in.op == TG_CUDA_OP_THINK) {
+			use(in.init, beg[i]);
+			def(in.out, beg[i]);
+			loops.push_back(i);
+			lives(p, in.body, in.nbody, beg, end, loops, life);
+			use(in.yield, end[i]);
+			if (in.halt >= 0) use(in.halt, end[i]);
+			loops.pop_back();
+			use(in.out, end[i]);
+		} else if (in.op == TG_CUDA_OP_SCAN) {
+			const tg_cuda_scan &s = p->scans[in.scan];
+			for (int k = 0; k < s.nc; k++) {
+				use(s.init[k], beg[i]);
+				def(s.c[k], beg[i]);
+			}
+			for (int j = 0; j < s.nx; j++) {
+				use(s.x[j], end[i]);
+				def(s.xt[j], beg[i]);
+			}
+			for (int y = 0; y < s.ny; y++) def(s.ys[y], beg[i]);
+			loops.push_back(i);
+			lives(p, in.body, in.nbody, beg, end, loops, life);
+			for (int k = 0; k < s.nc; k++) use(s.next[k], end[i]);
+			for (int y = 0; y < s.ny; y++) use(s.y[y], end[i]);
+			loops.pop_back();
+			for (int k = 0; k < s.nc; k++) use(s.c[k], end[i]);
+			for (int j = 0; j < s.nx; j++) use(s.xt[j], end[i]);
+			for (int y = 0; y < s.ny; y++) use(s.ys[y], end[i]);
+		} else {
+			for (int j = 0; j < in.na; j++) use(in.a[j], beg[i]);
+			def(in.out, beg[i]);
+		}
+	}
+}
+
+static int plan_arena(Compiler &C)
+{
+	const tg_cuda_program *p = C.p;
+	std::vector<int> beg(p->nins, 0), end(p->nins, 0);
+	int pos = 0;
+	number_ins(p, 0, p->ntop, pos, beg, end);
+	std::vector<Life> life(p->nval);
+	std::vector<int> loops;
+	lives(p, 0, p->ntop, beg, end, loops, life);
+	if (p->val[p->output].kind == TG_CUDA_TMP) life[p->output].last = pos;
+	// inputs occupy their own slots for the whole run
+	int top = 0;
+	C.inloc.assign(p->nval, -1);
+	for (int i = 0; i < p->ninputs; i++) {
+		int v = p->inputs[i];
+		C.inloc[v] = top;
+		top += (int)((numel(p->val[v]) + 3) / 4 * 4);
+	}
+	std::vector<int> order;
+	for (int v = 0; v < p->nval; v++)
+		if (p->val[v].kind == TG_CUDA_TMP && life[v].def >= 0) order.push_back(v);
+	auto asz = [&](int v) { return (int)((numel(p->val[v]) + 3) / 4 * 4); };
+	std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+		if (asz(a) != asz(b)) return asz(a) > asz(b);
+		return life[a].def < life[b].def;
+	});
+	C.slot.assign(p->nval, -1);
+	std::vector<int> placed;
+	int arena = top;
+	for (int v : order) {
+		std::vector<std::pair<int, int>> busy; // [off, off+size) of overlapping placed values
+		for (int w : placed)
+			if (life[w].def <= life[v].last && life[v].def <= life[w].last) busy.push_back({ C.slot[w], C.slot[w] + asz(w) });
+		std::sort(busy.begin(), busy.end());
+		int off = top, sz = asz(v);
+		for (auto &b : busy) {
+			if (off + sz <= b.first) break;
+			if (b.second > off) off = b.second;
+		}
+		C.slot[v] = off;
+		arena = std::max(arena, off + sz);
+		placed.push_back(v);
+	}
+	C.out->arena = arena ? arena : 4;
+	return TG_CUDA_OK;
+}
+
+static int emit_block(Compiler &C, int from, int cnt, int depth);
+
+static void bcast(const tg_cuda_value &o, const tg_cuda_value &a, const tg_cuda_value &b, DOp &d)
+{
+	long n = numel(o), na = numel(a), nb = numel(b);
+	d.n = (int)n;
+	if ((na == n || na == 1) && (nb == n || nb == 1)) {
+		d.rank = 0;
+		d.sa[0] = na == n ? 1 : 0;
+		d.sb[0] = nb == n ? 1 : 0;
+		return;
+	}
+	d.rank = o.rank;
+	for (int i = 0; i < 4; i++) d.dims[i] = i < o.rank ? o.dim[i] : 1;
+	long st = 1;
+	for (int x = 0; x < 4; x++) d.sa[x] = d.sb[x] = 0;
+	for (int i = a.rank - 1; i >= 0; i--) {
+		int od = o.rank - a.rank + i;
+		d.sa[od] = a.dim[i] == 1 ? 0 : (int)st;
+		st *= a.dim[i];
+	}
+	st = 1;
+	for (int i = b.rank - 1; i >= 0; i--) {
+		int od = o.rank - b.rank + i;
+		d.sb[od] = b.dim[i] == 1 ? 0 : (int)st;
+		st *= b.dim[i];
+	}
+}
+
+static int emit_ins(Compiler &C, int idx, int depth)
+{
+	const tg_cuda_program *p = C.p;
+	const tg_cuda_ins &in = p->ins[idx];
+	std::vector<DOp> &T = C.out->tape;
+	DOp d;
+	memset(&d, 0, sizeof d);
+	d.out = in.out >= 0 ? C.L(in.out) : 0;
+	d.a = in.na > 0 ? C.L(in.a[0]) : 0;
+	d.b = in.na > 1 ? C.L(in.a[1]) : 0;
+	const tg_cuda_value &vo = p->val[in.out];
+	switch (in.op) {
+	case TG_CUDA_OP_CONST:
+		d.code = D_CONST;
+		d.f = in.k;
+		T.push_back(d);
+		return 0;
+	case TG_CUDA_OP_ADD: case TG_CUDA_OP_SUB: case TG_CUDA_OP_MUL: case TG_CUDA_OP_DIV: case TG_CUDA_OP_MAX: case TG_CUDA_OP_MIN:
+		d.code = D_BIN;
+		d.sub = in.op;
+		bcast(vo, p->val[in.a[0]], p->val[in.a[1]], d);
+		T.push_back(d);
+		return 0;
+	case TG_CUDA_OP_NEG: case TG_CUDA_OP_TANH: case TG_CUDA_OP_RELU: case TG_CUDA_OP_SIGMOID: case TG_CUDA_OP_EXP:
+	case TG_CUDA_OP_SQRT: case TG_CUDA_OP_GELU: case TG_CUDA_OP_SILU: case TG_CUDA_OP_SOFTPLUS: case TG_CUDA_OP_LOG:
+	case TG_CUDA_OP_STEP: case TG_CUDA_OP_SIN: case TG_CUDA_OP_COS: case TG_CUDA_OP_FLOOR:
+		d.code = D_UN;
+		d.sub = in.op;
+		d.n = (int)numel(vo);
+		T.push_back(d);
+		return 0;
+	case TG_CUDA_OP_MATMUL: { // src/ops.c:60-73 dims, src/vm.c:262-290 dispatch, src/ops.c:310-320 axes
+		const tg_cuda_value &A = p->val[in.a[0]], &B = p->val[in.a[1]];
+		int g = A.rank == 3 && B.rank == 3 ? A.dim[0] : 1;
+		d.code = D_MATMUL;
+		d.m = A.rank == 3 ? (g > 1 || B.rank == 3 ? A.dim[1] : A.dim[0] * A.dim[1]) : A.rank == 2 ? A.dim[0] : 1;
+		d.k = A.dim[A.rank - 1];
+		d.nn = B.rank >= 2 ? B.dim[B.rank - 1] : 1;
+		d.g = g;
+		if (g == 1) {
+			bool distinct = in.a[0] != in.a[1];
+			if (A.qbits && A.rank == 2 && distinct && A.qaxis == 0) {
+				d.scale = 1;
+				d.c = -(C.sslot[in.a[0]] + 1);
+			} else if (B.qbits && B.rank == 2 && distinct && B.qaxis == 1) {
+				d.scale = 2;
+				d.c = -(C.sslot[in.a[1]] + 1);
+			}
+			// a quantized param used on another axis reads its dequantized values
+			if (A.qbits && d.scale != 1) d.a = -(C.pslot[in.a[0]] + 1 + (int)numel(A) + A.dim[A.qaxis]);
+			if (B.qbits && d.scale != 2) d.b = -(C.pslot[in.a[1]] + 1 + (int)numel(B) + B.dim[B.qaxis]);
+		}
+		T.push_back(d);
+		return 0;
+	}
+	case TG_CUDA_OP_SOFTMAX: case TG_CUDA_OP_RMSNORM: {
+		const tg_cuda_value &x = p->val[in.a[0]];
+		d.code = D_ROW;
+		d.sub = in.op;
+		d.k = x.rank ? x.dim[x.rank - 1] : 1;
+		d.m = (int)(numel(x) / d.k);
+		T.push_back(d);
+		return 0;
+	}
+	case TG_CUDA_OP_SUM: case TG_CUDA_OP_MEAN:
+		d.code = D_RED;
+		d.sub = in.op;
+		d.n = (int)numel(p->val[in.a[0]]);
+		T.push_back(d);
+		return 0;
+	case TG_CUDA_OP_TRANSPOSE: {
+		const tg_cuda_value &x = p->val[in.a[0]];
+		d.code = D_TRANS;
+		d.g = x.rank == 3 ? x.dim[0] : 1;
+		d.m = x.dim[x.rank - 2];
+		d.k = x.dim[x.rank - 1];
+		T.push_back(d);
+		return 0;
+	}
+	case TG_CUDA_OP_OUTER:
+		d.code = D_OUTER;
+		d.m = (int)numel(p->val[in.a[0]]);
+		d.k = (int)numel(p->val[in.a[1]]);
+		T.push_back(d);
+		return 0;
+	case TG_CUDA_OP_TAKE: {
+		const tg_cuda_value &w = p->val[in.a[0]];
+		d.code = D_TAKE;
+		d.k = w.dim[0];
+		d.nn = (int)(numel(w) / w.dim[0]);
+		d.m = p->val[in.a[1]].dim[0];
+		if (w.qbits) d.a = -(C.pslot[in.a[0]] + 1 + (int)numel(w) + w.dim[w.qaxis]);
+		T.push_back(d);
+		return 0;
+	}
+	case TG_CUDA_OP_RESHAPE:
+		d.code = D_COPY;
+		d.n = (int)numel(vo);
+		if (p->val[in.a[0]].qbits) d.a = -(C.pslot[in.a[0]] + 1 + (int)numel(p->val[in.a[0]]) + p->val[in.a[0]].dim[p->val[in.a[0]].qaxis]);
+		T.push_back(d);
+		return 0;
+	case TG_CUDA_OP_THINK: {
+		if (depth >= VM_MAXDEPTH) return C.fail(TG_CUDA_EUNSUPPORTED, "think/scan nesting deeper than 4", idx);
+		C.out->max_depth = std::max(C.out->max_depth, depth + 1);
+		d.code = D_THINK_BEGIN;
+		d.a = C.L(in.init);
+		d.n = (int)numel(vo);
+		d.depth = depth;
+		T.push_back(d);
+		int body = (int)T.size();
+		if (emit_block(C, in.body, in.nbody, depth + 1)) return C.status;
+		DOp e;
+		memset(&e, 0, sizeof e);
+		e.code = D_THINK_END;
+		e.out = C.L(in.out);
+		e.yield = C.L(in.yield);
+		e.n = (int)numel(vo);
+		e.depth = depth;
+		e.target = body;
+		e.maxit = in.maxit;
+		e.eps = in.eps;
+		e.tid = in.tid;
+		e.halt = in.halt >= 0 ? C.L(in.halt) : INT_MIN;
+		e.hthr = in.hthr;
+		T.push_back(e);
+		return 0;
+	}
+	case TG_CUDA_OP_SCAN: {
+		if (depth >= VM_MAXDEPTH) return C.fail(TG_CUDA_EUNSUPPORTED, "think/scan nesting deeper than 4", idx);
+		C.out->max_depth = std::max(C.out->max_depth, depth + 1);
+		const tg_cuda_scan &s = p->scans[in.scan];
+		for (int k = 0; k < s.nc; k++) { // carries <- init
+			DOp c;
+			memset(&c, 0, sizeof c);
+			c.code = D_COPY;
+			c.out = C.L(s.c[k]);
+			c.a = C.L(s.init[k]);
+			c.n = (int)numel(p->val[s.c[k]]);
+			T.push_back(c);
+		}
+		DOp b0;
+		memset(&b0, 0, sizeof b0);
+		b0.code = D_SCAN_BEGIN;
+		b0.depth = depth;
+		T.push_back(b0);
+		int body = (int)T.size();
+		for (int j = 0; j < s.nx; j++) {
+			DOp c;
+			memset(&c, 0, sizeof c);
+			c.code = D_SCAN_SLICE;
+			c.sub = s.reverse;
+			c.len = s.T;
+			c.out = C.L(s.xt[j]);
+			c.a = C.L(s.x[j]);
+			c.n = (int)numel(p->val[s.xt[j]]);
+			c.depth = depth;
+			T.push_back(c);
+		}
+		if (emit_block(C, in.body, in.nbody, depth + 1)) return C.status;
+		// ys[t] <- y: a slice op in reverse (out is the stack): encode as a strided copy
+		for (int y = 0; y < s.ny; y++) {
+			DOp c;
+			memset(&c, 0, sizeof c);
+			c.code = D_SCAN_SLICE;
+			c.sub = s.reverse | 2; // bit 1: write into the stack
+			c.len = s.T;
+			c.out = C.L(s.ys[y]);
+			c.a = C.L(s.y[y]);
+			c.n = (int)numel(p->val[s.y[y]]);
+			c.depth = depth;
+			T.push_back(c);
+		}
+		for (int k = 0; k < s.nc; k++) {
+			DOp c;
+			memset(&c, 0, sizeof c);
+			c.code = D_COPY;
+			c.out = C.L(s.c[k]);
+			c.a = C.L(s.next[k]);
+			c.n = (int)numel(p->val[s.c[k]]);
+			T.push_back(c);
+		}
+		DOp e;
+		memset(&e, 0, sizeof e);
+		e.code = D_SCAN_END;
+		e.depth = depth;
+		e.target = body;
+		e.len = s.T;
+		e.tid = s.tid;
+		T.push_back(e);
+		return 0;
+	}
+	}
+	return C.fail(TG_CUDA_EUNSUPPORTED, "op not implemented by the device executor", idx);
+}
+
+static int emit_block(Compiler &C, int from, int cnt, int depth)
+{
+	for (int i = from; i < from + cnt; i++)
+		if (emit_ins(C, i, depth)) return C.status;
+	return 0;
+}
+
+static int compile(const tg_cuda_program *p, Prog &out, std::string &err)
+{
+	Compiler C;
+	C.p = p;
+	C.out = &out;
+	if (p->nupd > 0) {
+		err = "stateful model (update statements): rows are not independent, the GPU batch path rejects it";
+		return TG_CUDA_EUNSUPPORTED;
+	}
+	if (p->nval <= 0 || !p->val || p->nins < 0 || p->ntop < 0 || p->ntop > p->nins || p->output < 0 || p->output >= p->nval) {
+		err = "malformed program";
+		return TG_CUDA_EINVAL;
+	}
+	for (int i = 0; i < p->nins; i++) {
+		const tg_cuda_ins &in = p->ins[i];
+		if (in.out < -1 || in.out >= p->nval || in.na < 0 || in.na > 3) {
+			err = "malformed instruction";
+			return TG_CUDA_EINVAL;
+		}
+		for (int j = 0; j < in.na; j++)
+			if (in.a[j] < 0 || in.a[j] >= p->nval) {
+				err = "operand out of range";
+				return TG_CUDA_EINVAL;
+			}
+	}
+	// params: f32 values; quantized params additionally keep codes (exact, in f32) and scales
+	C.pslot.assign(p->nval, -1);
+	C.sslot.assign(p->nval, -1);
+	for (int v = 0; v < p->nval; v++) {
+		const tg_cuda_value &x = p->val[v];
+		if (x.kind == TG_CUDA_STATE) {
+			err = "state values are not supported on the GPU batch path";
+			return TG_CUDA_EUNSUPPORTED;
+		}
+		if (x.kind != TG_CUDA_PARAM) continue;
+		long n = numel(x);
+		C.pslot[v] = (int)out.blob.size();
+		if (x.qbits) {
+			if (!x.q || !x.qs || (x.qbits != 8 && x.qbits != 4) || x.rank != 2) {
+				err = "malformed quantized param";
+				return TG_CUDA_EINVAL;
+			}
+			int nch = x.dim[x.qaxis];
+			for (long e = 0; e < n; e++) {
+				int c;
+				if (x.qbits == 8) c = x.q[e];
+				else {
+					int b = x.q[e >> 1];
+					c = (e & 1) ? (b >> 4) : ((int)(signed char)(b << 4) >> 4);
+				}
+				out.blob.push_back((float)c);
+			}
+			C.sslot[v] = (int)out.blob.size();
+			for (int c = 0; c < nch; c++) out.blob.push_back(x.qs[c]);
+			// dequantized values for uses on another axis: data = code * scale (src/ir.c:503-507)
+			for (long e = 0; e < n; e++) {
+				int ch = x.qaxis == 0 ? (int)(e / x.dim[1]) : (int)(e % x.dim[1]);
+				out.blob.push_back(x.data ? x.data[e] : out.blob[C.pslot[v] + e] * x.qs[ch]);
+			}
+		} else {
+			if (!x.data) {
+				err = "param without data";
+				return TG_CUDA_EINVAL;
+			}
+			for (long e = 0; e < n; e++) out.blob.push_back(x.data[e]);
+		}
+		while (out.blob.size() % 4) out.blob.push_back(0.0f);
+	}
+	if (plan_arena(C)) {
+		err = C.err;
+		return C.status;
+	}
+	if (emit_block(C, 0, p->ntop, 0)) {
+		err = C.err;
+		return C.status;
+	}
+	out.nout = (int)numel(p->val[p->output]);
+	out.out_loc = C.L(p->output);
+	out.nthink = p->nthink;
+	out.per = 0;
+	for (int i = 0; i < p->ninputs; i++) {
+		int v = p->inputs[i];
+		out.in_off.push_back(C.inloc[v]);
+		out.in_len.push_back((int)numel(p->val[v]));
+		out.per += (int)numel(p->val[v]);
+	}
+	return TG_CUDA_OK;
+}
+
+} // namespace tgc
+
+using namespace tgc;
+
+struct tg_cuda_model {
+	Model m;
+};
+
+extern "C" int tg_cuda_load(const tg_cuda_program *p, tg_cuda_model **out)
+{
+	clear_err();
+	if (!p || !out) return set_err(TG_CUDA_EINVAL, "tg_cuda_load: NULL argument");
+	*out = nullptr;
+	if (!inited()) return set_err(TG_CUDA_ENODEV, "tg_cuda_load: call tg_cuda_init first");
+	tg_cuda_model *g = new tg_cuda_model;
+	std::string err;
+	int rc = compile(p, g->m.prog, err);
+	if (rc) {
+		delete g;
+		return set_err(rc, "tg_cuda_load: %s", err.c_str());
+	}
+	Prog &P = g->m.prog;
+	size_t blob_bytes = (P.blob.size() + 3) / 4 * 4 * sizeof(float);
+	size_t arena_bytes = (size_t)P.arena * VM_ROWS * sizeof(float);
+	g->m.blob_in_smem = blob_bytes <= 96 * 1024;
+	g->m.global_arena = arena_bytes + (g->m.blob_in_smem ? blob_bytes : 0) > 200 * 1024;
+	g->m.smem = (g->m.blob_in_smem ? blob_bytes : 0) + (g->m.global_arena ? 0 : arena_bytes);
+	for (size_t i = 0; i < devices().size(); i++) g->m.dev.emplace_back(new Model::PerDev);
+	for (size_t i = 0; i < devices().size(); i++) {
+		auto &D = *g->m.dev[i];
+		int id = devices()[i].id;
+		if ((rc = D.tape.alloc(P.tape.size() * sizeof(DOp), id)) || (rc = D.blob.alloc(blob_bytes, id)) ||
+		    (rc = D.inloc.alloc(P.in_off.size() * sizeof(int) + 4, id)) || (rc = D.inlen.alloc(P.in_len.size() * sizeof(int) + 4, id))) {
+			delete g;
+			return rc;
+		}
+		cudaSetDevice(id);
+		if (fault("h2d")) {
+			delete g;
+			return set_err(TG_CUDA_EFAULT, "injected copy failure (TG_CUDA_FAULT=h2d)");
+		}
+		TGC_CUDA(cudaMemcpy(D.tape.p, P.tape.data(), P.tape.size() * sizeof(DOp), cudaMemcpyHostToDevice));
+		TGC_CUDA(cudaMemcpy(D.blob.p, P.blob.data(), P.blob.size() * sizeof(float), cudaMemcpyHostToDevice));
+		TGC_CUDA(cudaMemcpy(D.inloc.p, P.in_off.data(), P.in_off.size() * sizeof(int), cudaMemcpyHostToDevice));
+		TGC_CUDA(cudaMemcpy(D.inlen.p, P.in_len.data(), P.in_len.size() * sizeof(int), cudaMemcpyHostToDevice));
+		TGC_CUDA(cudaFuncSetAttribute(vm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+	}
+	cudaSetDevice(devices()[0].id);
+	*out = g;
+	return TG_CUDA_OK;
+}
+
+static int run_rows(Model &M, size_t di, const float *d_in, long rows, float *d_out, int *d_steps, int nt, cudaStream_t st)
+{
+	Prog &P = M.prog;
+	auto &D = *M.dev[di];
+	if (rows <= 0) return TG_CUDA_OK;
+	long ctas = (rows + VM_ROWS - 1) / VM_ROWS;
+	float *gar = nullptr;
+	if (M.global_arena) {
+		size_t need = (size_t)ctas * P.arena * VM_ROWS * sizeof(float);
+		int rc = D.gar.ensure(need, devices()[di].id);
+		if (rc) return rc;
+		gar = D.gar.as<float>();
+	}
+	if (fault("launch")) return set_err(TG_CUDA_EFAULT, "injected launch failure (TG_CUDA_FAULT=launch)");
+	vm_kernel<<<(unsigned)ctas, VM_ROWS, M.smem, st>>>(D.tape.as<DOp>(), (int)P.tape.size(), D.blob.as<float>(),
+							   (int)P.blob.size(), M.blob_in_smem ? 1 : 0, P.arena, d_in, P.per,
+							   rows, d_out, P.nout, P.out_loc, d_steps, nt, D.inloc.as<int>(),
+							   D.inlen.as<int>(), (int)P.in_off.size(), gar);
+	TGC_LAUNCH_CHECK();
+	return TG_CUDA_OK;
+}
+
+extern "C" int tg_cuda_batch_device(tg_cuda_model *g, const float *all, long rows, float *out, int *steps, void *stream)
+{
+	clear_err();
+	if (!g || (rows > 0 && (!all || !out))) return set_err(TG_CUDA_EINVAL, "tg_cuda_batch_device: NULL argument");
+	if (g->m.prog.nthink > 0 && rows > 0 && !steps) return set_err(TG_CUDA_EINVAL, "tg_cuda_batch_device: steps is NULL");
+	cudaSetDevice(devices()[0].id);
+	return run_rows(g->m, 0, all, rows, out, steps, g->m.prog.nthink, (cudaStream_t)stream);
+}
+
+// One host thread per GPU: copy its contiguous shard in, run, copy out. Output rows of a
+// shard land at the shard's own offset, so the gather keeps input order.
+extern "C" int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int per, float *out, int n, int *steps, int nt)
+{
+	clear_err();
+	if (!g || rows < 0 || (rows > 0 && (!all || !out))) return set_err(TG_CUDA_EINVAL, "tg_cuda_batch: NULL argument");
+	Prog &P = g->m.prog;
+	if (per != P.per) return set_err(TG_CUDA_EINVAL, "tg_cuda_batch: %d values per row, the model needs %d", per, P.per);
+	if (n != P.nout) return set_err(TG_CUDA_EINVAL, "tg_cuda_batch: %d outputs per row, the model has %d", n, P.nout);
+	if (P.nthink > 0 && (!steps || nt < P.nthink))
+		return set_err(TG_CUDA_EINVAL, "tg_cuda_batch: steps needs %d slots per row", P.nthink);
+	if (rows == 0) return TG_CUDA_OK;
+	size_t G = devices().size();
+	std::vector<int> rcs(G, 0);
+	std::vector<std::string> errs(G);
+	auto work = [&](size_t di) {
+		long lo = rows * (long)di / (long)G, hi = rows * (long)(di + 1) / (long)G, cnt = hi - lo;
+		if (cnt <= 0) return;
+		Device &dv = devices()[di];
+		cudaSetDevice(dv.id);
+		DevBuf din, dout, dst;
+		int rc;
+		auto done = [&](int r) {
+			rcs[di] = r;
+			if (r) errs[di] = tg_cuda_error();
+		};
+		if ((rc = din.alloc((size_t)cnt * per * sizeof(float), dv.id)) || (rc = dout.alloc((size_t)cnt * n * sizeof(float), dv.id)) ||
+		    (rc = dst.alloc((size_t)cnt * (nt > 0 ? nt : 1) * sizeof(int), dv.id)))
+			return done(rc);
+		if (fault("h2d")) return done(set_err(TG_CUDA_EFAULT, "injected copy failure (TG_CUDA_FAULT=h2d)"));
+		cudaError_t e = cudaMemcpyAsync(din.p, all + (size_t)lo * per, (size_t)cnt * per * sizeof(float), cudaMemcpyHostToDevice, dv.stream);
+		if (e != cudaSuccess) return done(set_err(TG_CUDA_ECUDA, "H2D: %s", cudaGetErrorString(e)));
+		if (nt > 0) cudaMemsetAsync(dst.p, 0, (size_t)cnt * nt * sizeof(int), dv.stream);
+		if ((rc = run_rows(g->m, di, din.as<float>(), cnt, dout.as<float>(), nt > 0 ? dst.as<int>() : nullptr, nt, dv.stream)))
+			return done(rc);
+		if (fault("gather")) return done(set_err(TG_CUDA_EFAULT, "injected gather failure (TG_CUDA_FAULT=gather)"));
+		e = cudaMemcpyAsync(out + (size_t)lo * n, dout.p, (size_t)cnt * n * sizeof(float), cudaMemcpyDeviceToHost, dv.stream);
+		if (e == cudaSuccess && nt > 0 && steps)
+			e = cudaMemcpyAsync(steps + (size_t)lo * nt, dst.p, (size_t)cnt * nt * sizeof(int), cudaMemcpyDeviceToHost, dv.stream);
+		if (e == cudaSuccess) e = cudaStreamSynchronize(dv.stream);
+		if (e != cudaSuccess) return done(set_err(TG_CUDA_ECUDA, "device %d: %s", dv.id, cudaGetErrorString(e)));
+		done(TG_CUDA_OK);
+	};
+	if (G == 1) work(0);
+	else {
+		std::vector<std::thread> th;
+		for (size_t di = 0; di < G; di++) th.emplace_back(work, di);
+		for (auto &t : th) t.join();
+	}
+	cudaSetDevice(devices()[0].id);
+	for (size_t di = 0; di < G; di++)
+		if (rcs[di]) return set_err(rcs[di], "%s", errs[di].c_str());
+	return TG_CUDA_OK;
+}
+
+extern "C" void tg_cuda_free(tg_cuda_model *g) { delete g; }

@@ -1,0 +1,245 @@
+"""Generate the golden fixtures in tests/golden/ from the reference itself.
+
+Run in a container that has the reference sources (it builds oracle/_ref with
+oracle/Makefile): `python tests/golden/make_golden.py`. Every fixture is an
+output of the reference's own code -- the `tgc` binary compiled from its
+sources, or its runtime/tg_rt.h kernels and src/quant.c quantizer behind
+oracle/ref_harness.c -- on seeded inputs. The tests compare the CPU oracle and
+the CUDA library against these files; nothing at test time reads the reference.
+
+Fixtures:
+  latent_reasoner.{f32,q8}.tgir    `tgc ir` / `tgc quantize --bits 8 --min-size 1` of examples/latent_reasoner.tg
+  lr_rows.csv                      2000 rows of f32[8], entries Bernoulli(0.5) (numpy default_rng(1))
+  lr_{f32,q8}_out.csv              `tgc batch ... -j 1` text output: 4 values and the think steps per row
+  ops.tgir, ops_expected.txt       tests/cases/ops.tg and the reference's own ops.expected
+  kernels.npz                      tg_matmul_qa/qb, tg_matmul, rmsnorm, softmax on seeded shapes
+  quant.npz                        quantize_param (RTN int8/int4 on both axes, GPTQ int4 with a Hessian)
+  nano/                            a Qwen3-structured program (examples/qwen3/import.py layout) at toy
+                                   sizes: weights, quantized TGIR (int8 RTN, int4 RTN, int4 GPTQ) and
+                                   `tgc batch` logits of 4 sequences
+"""
+from __future__ import annotations
+
+import gzip
+import math
+import os
+import shutil
+import subprocess
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+REF = os.environ.get("TG_REFERENCE", "/root/reference")
+sys.path.insert(0, ROOT)
+
+from oracle import tgo  # noqa: E402
+
+
+def sh(*args, **kw) -> str:
+    return subprocess.run([str(a) for a in args], check=True, capture_output=True, text=True, **kw).stdout
+
+
+def latent_reasoner(tgc: str) -> None:
+    src = os.path.join(REF, "examples", "latent_reasoner.tg")
+    with open(os.path.join(HERE, "latent_reasoner.f32.tgir"), "w") as f:
+        f.write(sh(tgc, "ir", src))
+    q8 = os.path.join(HERE, "latent_reasoner.q8.tgir")
+    sh(tgc, "quantize", src, "--bits", "8", "--min-size", "1", "-o", q8)
+    rows = np.random.default_rng(1).integers(0, 2, size=(2000, 8)).astype(np.float32)
+    rp = os.path.join(HERE, "lr_rows.csv")
+    np.savetxt(rp, rows, fmt="%g", delimiter=",")
+    for tag, model in (("f32", os.path.join(HERE, "latent_reasoner.f32.tgir")), ("q8", q8)):
+        sh(tgc, "batch", model, rp, "-j", "1", "-o", os.path.join(HERE, f"lr_{tag}_out.csv"))
+
+
+def ops(tgc: str) -> None:
+    with open(os.path.join(HERE, "ops.tgir"), "w") as f:
+        f.write(sh(tgc, "ir", os.path.join(REF, "tests", "cases", "ops.tg")))
+    shutil.copy(os.path.join(REF, "tests", "cases", "ops.expected"), os.path.join(HERE, "ops_expected.txt"))
+
+
+def kernels() -> None:
+    R = tgo.ref()
+    rng = np.random.default_rng(7)
+    out = {}
+    cases = [(0, 8, 5, 7, 1), (0, 4, 5, 7, 3), (0, 8, 33, 65, 2), (0, 4, 64, 96, 4), (0, 4, 17, 31, 1),
+             (1, 8, 3, 9, 11), (1, 4, 2, 13, 17), (1, 4, 5, 64, 40), (1, 8, 1, 128, 24)]
+    for idx, (axis, bits, m, k, n) in enumerate(cases):
+        lim = 127 if bits == 8 else 8
+        codes = rng.integers(-lim, lim if bits == 8 else 8, size=m * k if axis == 0 else k * n)
+        if bits == 4:
+            codes[0] = -8  # the int4 code TGIR cannot carry (src/ir.c:499-501)
+        from technograd_b200.tgir import pack_codes
+        q = np.ascontiguousarray(pack_codes(codes, bits))
+        s = (np.abs(rng.normal(0, 0.02, size=m if axis == 0 else n)) / 7).astype(np.float32)
+        act = rng.normal(0, 1, size=k * n if axis == 0 else m * k).astype(np.float32)
+        o = tgo.matmul_q(R, "ref_", axis, act, q, bits, s, m, k, n)
+        out[f"mq{idx}_meta"] = np.array([axis, bits, m, k, n])
+        out[f"mq{idx}_codes"] = codes.astype(np.int8)
+        out[f"mq{idx}_q"], out[f"mq{idx}_s"], out[f"mq{idx}_act"], out[f"mq{idx}_o"] = q, s, act, o
+    a = rng.normal(0, 1, size=(7, 13)).astype(np.float32)
+    b = rng.normal(0, 1, size=(13, 5)).astype(np.float32)
+    o = np.zeros((7, 5), np.float32)
+    R.ref_matmul(tgo.f32p(o), tgo.f32p(a), tgo.f32p(b), 7, 13, 5)
+    out.update(mm_a=a, mm_b=b, mm_o=o)
+    x = rng.normal(0, 3, size=(6, 37)).astype(np.float32)
+    rn = np.zeros_like(x)
+    sm = np.zeros_like(x)
+    R.ref_rmsnorm(tgo.f32p(rn), tgo.f32p(x), 6, 37)
+    R.ref_softmax(tgo.f32p(sm), tgo.f32p(x), 6, 37)
+    out.update(row_x=x, rms_o=rn, softmax_o=sm)
+    np.savez_compressed(os.path.join(HERE, "kernels.npz"), **out)
+
+
+def quant() -> None:
+    R = tgo.ref()
+    rng = np.random.default_rng(11)
+    out = {}
+    cases = [("r8a0", 8, 0, (24, 40), False), ("r8a1", 8, 1, (40, 24), False), ("r4a0", 4, 0, (17, 33), False),
+             ("r4a1", 4, 1, (33, 17), False), ("g4a1", 4, 1, (48, 20), True), ("g8a0", 8, 0, (12, 48), True),
+             ("zero", 4, 0, (4, 16), False)]
+    for name, bits, axis, shape, gptq in cases:
+        w = rng.normal(0, 0.02, size=shape).astype(np.float32)
+        if name == "zero":
+            w[1] = 0.0  # an all-zero channel takes the 1e-8 scale (src/quant.c:188)
+        H = None
+        if gptq:
+            K = shape[1 - axis]
+            x = rng.normal(0, 1, size=(64, K)).astype(np.float32)
+            H = np.zeros((K, K))
+            tgo.tgo().tgo_hessian_add(H.ctypes.data_as(tgo.DP), tgo.f32p(x), 64, K)
+            out[name + "_x"] = x
+        q, s = tgo.quantize(R, "ref_", w, axis, bits, H)
+        out[name + "_meta"] = np.array([bits, axis, *shape, int(gptq)])
+        out[name + "_w"], out[name + "_q"], out[name + "_s"] = w, q, s
+    np.savez_compressed(os.path.join(HERE, "quant.npz"), **out)
+
+
+# ---- a Qwen3-structured program at toy sizes ---------------------------------------------------
+NANO = dict(layers=2, hidden=32, nq=4, nkv=2, head_dim=8, ffn=48, vocab=96, theta=1e6, T=6)
+
+
+def nano_weights(cfg: dict, seed: int) -> dict:
+    rng = np.random.default_rng(seed)
+    D, L, NQ, NKV, HD, FF, V = (cfg[k] for k in ("hidden", "layers", "nq", "nkv", "head_dim", "ffn", "vocab"))
+    g = lambda *s: rng.normal(0, 0.02, size=s).astype(np.float32)  # noqa: E731
+    nw = lambda n: (1 + rng.normal(0, 0.1, size=n)).astype(np.float32)  # noqa: E731
+    w = {"E": rng.normal(0, 1.0, size=(V, D)).astype(np.float32), "LM": g(D, V), "lnf": nw(D)}
+    for l in range(L):
+        w[f"ln1_{l}"], w[f"ln2_{l}"], w[f"qn_{l}"], w[f"kn_{l}"] = nw(D), nw(D), nw(HD), nw(HD)
+        for h in range(NQ):
+            w[f"Wq_{l}_{h}"], w[f"Wo_{l}_{h}"] = g(D, HD), g(HD, D)
+        for j in range(NKV):
+            w[f"Wk_{l}_{j}"], w[f"Wv_{l}_{j}"] = g(D, HD), g(D, HD)
+        w[f"Wg_{l}"], w[f"Wu_{l}"], w[f"Wd_{l}"] = g(D, FF), g(D, FF), g(FF, D)
+    return w
+
+
+def emit_qwen3(cfg: dict, w: dict, outdir: str, T: int) -> str:
+    """The program examples/qwen3/import.py:51-131 emits, for random weights: per-head rank-2
+    matmuls, rotate-half RoPE through cos/sin tables and a Rot matrix, a -1e9 causal mask, the
+    LM head on every row and take(lastidx)."""
+    D, L, NQ, NKV, HD, FF, V = (cfg[k] for k in ("hidden", "layers", "nq", "nkv", "head_dim", "ffn", "vocab"))
+    os.makedirs(os.path.join(outdir, "w"), exist_ok=True)
+    tables = {}
+    inv = cfg["theta"] ** (-(np.arange(0, HD, 2) / HD))
+    ang = np.outer(np.arange(T), inv)
+    tables["cosT"] = np.concatenate([np.cos(ang), np.cos(ang)], axis=1)
+    tables["sinT"] = np.concatenate([np.sin(ang), np.sin(ang)], axis=1)
+    rot = np.zeros((HD, HD), np.float32)
+    for i in range(HD // 2):
+        rot[i + HD // 2, i] = -1.0
+        rot[i, i + HD // 2] = 1.0
+    tables["Rot"] = rot
+    tables["mask"] = np.where(np.arange(T)[None, :] <= np.arange(T)[:, None], 0.0, -1e9)
+    tables["lastidx"] = np.array([T - 1], np.float32)
+    for name, arr in list(w.items()) + list(tables.items()):
+        np.asarray(arr, dtype="<f4").tofile(os.path.join(outdir, "w", name + ".bin"))
+    lines = ["model qwen3", ""]
+
+    def par(name, *shape):
+        lines.append(f'param {name} : f32[{", ".join(map(str, shape))}] = file("w/{name}.bin")')
+
+    par("E", V, D), par("LM", D, V), par("lnf", D), par("cosT", T, HD), par("sinT", T, HD)
+    par("Rot", HD, HD), par("mask", T, T), par("lastidx", 1)
+    for l in range(L):
+        par(f"ln1_{l}", D), par(f"ln2_{l}", D), par(f"qn_{l}", HD), par(f"kn_{l}", HD)
+        for h in range(NQ):
+            par(f"Wq_{l}_{h}", D, HD), par(f"Wo_{l}_{h}", HD, D)
+        for j in range(NKV):
+            par(f"Wk_{l}_{j}", D, HD), par(f"Wv_{l}_{j}", D, HD)
+        par(f"Wg_{l}", D, FF), par(f"Wu_{l}", D, FF), par(f"Wd_{l}", FF, D)
+    lines += ["", f"def rotary(x: f32[{T}, {HD}]) -> f32[{T}, {HD}]:",
+              "    return x * cosT + (x @ Rot) * sinT", "",
+              f"def forward(ids: f32[{T}]) -> f32[{V}]:", "    h = take(E, ids)"]
+    grp = NQ // NKV
+    scale = 1.0 / math.sqrt(HD)
+    for l in range(L):
+        lines.append(f"    n = rmsnorm(h) * ln1_{l}")
+        for j in range(NKV):
+            lines.append(f"    k{j} = rotary(rmsnorm(n @ Wk_{l}_{j}) * kn_{l})")
+            lines.append(f"    v{j} = n @ Wv_{l}_{j}")
+        terms = []
+        for h in range(NQ):
+            j = h // grp
+            lines.append(f"    q{h} = rotary(rmsnorm(n @ Wq_{l}_{h}) * qn_{l})")
+            lines.append(f"    s{h} = softmax((q{h} @ transpose(k{j})) * {scale:.9g} + mask)")
+            lines.append(f"    o{h} = (s{h} @ v{j}) @ Wo_{l}_{h}")
+            terms.append(f"o{h}")
+        lines.append(f"    h = h + ({' + '.join(terms)})")
+        lines.append(f"    n = rmsnorm(h) * ln2_{l}")
+        lines.append(f"    h = h + (silu(n @ Wg_{l}) * (n @ Wu_{l})) @ Wd_{l}")
+    lines.append("    logits = (rmsnorm(h) * lnf) @ LM")
+    lines.append(f"    return reshape(take(logits, lastidx), {V})")
+    path = os.path.join(outdir, "qwen3.tg")
+    with open(path, "w") as f:
+        f.write("\n".join(lines) + "\n")
+    return path
+
+
+def nano(tgc: str) -> None:
+    cfg = NANO
+    T = cfg["T"]
+    out = os.path.join(HERE, "nano")
+    os.makedirs(out, exist_ok=True)
+    w = nano_weights(cfg, 4)
+    rng = np.random.default_rng(5)
+    ids = rng.integers(0, cfg["vocab"], size=(4, T)).astype(np.float32)
+    calib = rng.integers(0, cfg["vocab"], size=(16, T)).astype(np.float32)
+    with tempfile.TemporaryDirectory() as tmp:
+        prog = emit_qwen3(cfg, w, tmp, T)
+        np.savetxt(os.path.join(tmp, "ids.csv"), ids, fmt="%d", delimiter=",")
+        np.savetxt(os.path.join(tmp, "calib.csv"), calib, fmt="%d", delimiter=",")
+        minsz = str(cfg["head_dim"] ** 2 + 1)  # Rot (HD x HD) stays f32, every linear weight is quantized
+        variants = {"q8": ["--bits", "8"], "q4": ["--bits", "4"],
+                    "q4gptq": ["--bits", "4", "--method", "gptq", "--calib", os.path.join(tmp, "calib.csv")]}
+        for tag, flags in variants.items():
+            qp = os.path.join(tmp, f"{tag}.tgir")
+            sh(tgc, "quantize", prog, "--min-size", minsz, *flags, "-o", qp)
+            with open(qp, "rb") as f, open(os.path.join(out, f"{tag}.tgir.gz"), "wb") as raw:
+                with gzip.GzipFile(fileobj=raw, mode="wb", mtime=0) as g:
+                    g.write(f.read())
+            sh(tgc, "batch", qp, os.path.join(tmp, "ids.csv"), "-j", "1", "-o", os.path.join(out, f"{tag}_logits.csv"))
+        shutil.copy(os.path.join(tmp, "ids.csv"), os.path.join(out, "ids.csv"))
+        with open(os.path.join(out, "config.txt"), "w") as f:
+            f.write(" ".join(f"{k}={v}" for k, v in cfg.items()) + "\n")
+
+
+def main() -> None:
+    tgo.build()
+    tgc = tgo.REF_TGC
+    if not os.path.exists(tgc) or tgo.ref() is None:
+        sys.exit("oracle/_ref was not built: the reference sources are needed")
+    latent_reasoner(tgc)
+    ops(tgc)
+    kernels()
+    quant()
+    nano(tgc)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()
