@@ -1,0 +1,43 @@
+// gemm.cuh -- the tensor-core GEMM interface used inside the library.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+
+namespace tgc {
+
+enum { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
+
+// Operands: up to two A matrices [M, K] and two B matrices [N, K], bf16, K-major.
+struct GemmOperands {
+	const void *a[2] = { nullptr, nullptr };
+	const void *b[2] = { nullptr, nullptr };
+	long lda = 0, ldb = 0; // row strides in elements
+};
+
+struct GemmArgs {
+	int M, N, K;
+	int na, nb, npairs;
+	int pa[4], pb[4];        // pair q multiplies A[pa[q]] by B[pb[q]]
+	int epi;                 // EPI_*
+	int scale_mode;          // 0 none, 1 per row of D, 2 per column of D
+	const float *scale;      // per row / column; SwiGLU: gate scales (per channel)
+	const float *scale2;     // SwiGLU: up scales
+	float *out;              // f32 D (STORE: written; ADD: D += result)
+	__nv_bfloat16 *out_hi, *out_lo; // SwiGLU: bf16 hi/lo of silu(g) * u
+	long ldo;                // row stride of the output, elements
+	int *status;             // device status word (ST_*), may not be NULL
+};
+
+// Launch on stream. SwiGLU: B rows come in blocks of 256 (128 gate rows then the
+// 128 matching up rows), N = 2 * channels, output channels = N / 2.
+int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st);
+
+int split_to_bf16(const float *src, long rows, long cols, long lds, bool transpose, __nv_bfloat16 *hi, __nv_bfloat16 *lo,
+		  long ldd, cudaStream_t st);
+int codes_to_bf16(const signed char *q, int bits, long rows, long cols, bool transpose, __nv_bfloat16 *dst, long ldd,
+		  cudaStream_t st);
+int device_status_check(int *d_status, cudaStream_t st);
+
+} // namespace tgc

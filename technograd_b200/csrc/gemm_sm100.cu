@@ -1,14 +1,377 @@
-// gemm_sm100.cu -- tensor-core (tcgen05) dequant GEMM for large batches.
+// gemm_sm100.cu -- the tensor-core dequant GEMM: D[M,N] = sum over operand pairs
+// of A_i[M,K] B_j[N,K]^T, bf16 operands, f32 accumulation in TMEM (tcgen05).
+//
+// Why pairs: weight codes (int8 / int4) are exact in bf16, activations are not.
+// An f32 activation is split into hi = bf16(a) and lo = bf16(a - hi); summing
+// hi*C + lo*C reproduces the f32 product to ~2^-17 relative, which keeps the
+// reference's f32 dequant path (runtime/tg_rt.h:132-151) within 1e-3/1e-4.
+// Weights whose scale cannot stay in the epilogue (per-head o_proj scales) are
+// pre-scaled and split too, and use hi*hi + hi*lo + lo*hi.
+//
+// Kernel: 6 warps. Warp 0 lane 0 issues TMA tile loads (128-byte swizzle, K
+// blocks of 64) into a STAGES-deep shared-memory ring; warp 1 owns the TMEM
+// accumulator (BN f32 columns) and lane 0 issues tcgen05.mma (M=128, N=BN,
+// K=16 per instruction), committing each stage back to the producer; warps 2-5
+// drain TMEM with tcgen05.ld and run the epilogue (scale, residual add, SwiGLU
+// with a bf16 hi/lo split of the result). Every mbarrier wait is bounded and
+// reports into a device status word instead of hanging.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
 #include "common.cuh"
+#include "gemm.cuh"
 #include "kernels.cuh"
+#include "tc.cuh"
 
 namespace tgc {
+
+constexpr int BM = 128, BK = 64;
+constexpr int A_TILE = BM * BK * 2; // 16 KB
+
+struct TmaMaps {
+	CUtensorMap a[2], b[2];
+};
+
+__device__ __forceinline__ uint32_t bf16_bits(float x) { return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMaps maps, const GemmArgs p)
+{
+	extern __shared__ uint8_t smem_raw[];
+	uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+	constexpr int B_TILE = BN * BK * 2;
+	const int stage_bytes = p.na * A_TILE + p.nb * B_TILE;
+	uint64_t *full = (uint64_t *)(smem + STAGES * stage_bytes);
+	uint64_t *empty = full + STAGES;
+	uint64_t *accf = empty + STAGES;
+	uint32_t *tslot = (uint32_t *)(accf + 1);
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+	const int KB = (p.K + BK - 1) / BK;
+
+	if (threadIdx.x == 0) {
+		for (int s = 0; s < STAGES; s++) {
+			mbar_init(&full[s], 1);
+			mbar_init(&empty[s], 1);
+		}
+		mbar_init(accf, 1);
+		fence_barrier_init();
+		for (int i = 0; i < p.na; i++) tma_prefetch_desc(&maps.a[i]);
+		for (int i = 0; i < p.nb; i++) tma_prefetch_desc(&maps.b[i]);
+	}
+	if (warp == 1) tmem_alloc(tslot, BN);
+	__syncthreads();
+	tc_fence_after();
+	const uint32_t tmem = *tslot;
+
+	if (warp == 0 && lane == 0) { // ---- producer
+		for (int kb = 0; kb < KB; kb++) {
+			const int s = kb % STAGES;
+			const uint32_t ph = (kb / STAGES) & 1;
+			if (!mbar_wait(&empty[s], ph ^ 1, p.status, ST_TIMEOUT_EMPTY)) break;
+			uint8_t *st = smem + s * stage_bytes;
+			mbar_expect_tx(&full[s], stage_bytes);
+			for (int i = 0; i < p.na; i++) tma_load_2d(st + i * A_TILE, &maps.a[i], &full[s], kb * BK, m0);
+			for (int j = 0; j < p.nb; j++) tma_load_2d(st + p.na * A_TILE + j * B_TILE, &maps.b[j], &full[s], kb * BK, n0);
+		}
+	} else if (warp == 1 && lane == 0) { // ---- MMA issuer
+		constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+		int issued = 0;
+		for (int kb = 0; kb < KB; kb++) {
+			const int s = kb % STAGES;
+			const uint32_t ph = (kb / STAGES) & 1;
+			if (!mbar_wait(&full[s], ph, p.status, ST_TIMEOUT_FULL)) break;
+			tc_fence_after();
+			const uint32_t base = smem_u32(smem + s * stage_bytes);
+			for (int q = 0; q < p.npairs; q++) {
+				const uint32_t a = base + p.pa[q] * A_TILE, b = base + p.na * A_TILE + p.pb[q] * B_TILE;
+#pragma unroll
+				for (int kk = 0; kk < BK / 16; kk++) {
+					tc_mma_f16(tmem, sw128_kmajor_desc(a + kk * 32), sw128_kmajor_desc(b + kk * 32), idesc, issued);
+					issued = 1;
+				}
+			}
+			tc_commit(&empty[s]);
+		}
+		tc_commit(accf);
+	} else if (warp >= 2) { // ---- epilogue: TMEM lanes of quarter (warp % 4)
+		const int quarter = warp & 3;
+		const int row = m0 + quarter * 32 + lane;
+		const bool ok = mbar_wait(accf, 0, p.status, ST_TIMEOUT_ACC);
+		const bool live = ok && row < p.M;
+		tc_fence_after();
+		const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+		if (EPI == EPI_SWIGLU) {
+			// columns [0, BN/2) are gate channels, [BN/2, BN) the matching up channels
+			const int f0 = blockIdx.x * (BN / 2);
+			for (int c = 0; c < BN / 2; c += 16) {
+				float g[16], u[16];
+				__syncwarp();
+				tmem_ld16(trow + c, g);
+				tmem_ld16(trow + BN / 2 + c, u);
+				if (!live) continue;
+				uint32_t hi[8], lo[8];
+#pragma unroll
+				for (int i = 0; i < 16; i++) {
+					const int f = f0 + c + i;
+					float gs = g[i] * p.scale[f], us = u[i] * p.scale2[f];
+					float y = __fmul_rn(__fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs))), us); // silu(g) * u
+					uint32_t h = bf16_bits(y);
+					uint32_t l = bf16_bits(y - __uint_as_float(h << 16));
+					if (i & 1) {
+						hi[i >> 1] |= h << 16;
+						lo[i >> 1] |= l << 16;
+					} else {
+						hi[i >> 1] = h;
+						lo[i >> 1] = l;
+					}
+				}
+				const long off = (long)row * p.ldo + f0 + c;
+				uint4 *dh = (uint4 *)(p.out_hi + off), *dl = (uint4 *)(p.out_lo + off);
+				dh[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+				dh[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+				dl[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+				dl[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+			}
+		} else {
+			for (int c = 0; c < BN; c += 16) {
+				float v[16];
+				__syncwarp();
+				tmem_ld16(trow + c, v);
+				if (!live) continue;
+				const int n = n0 + c;
+				float *dst = p.out + (long)row * p.ldo + n;
+				const float rs = p.scale_mode == 1 ? p.scale[row] : 1.0f;
+#pragma unroll
+				for (int i = 0; i < 16; i++) {
+					float x = v[i];
+					if (p.scale_mode == 1) x = __fmul_rn(rs, x);
+					else if (p.scale_mode == 2 && n + i < p.N) x = __fmul_rn(p.scale[n + i], x);
+					v[i] = x;
+				}
+				if (n + 16 <= p.N && (p.ldo & 3) == 0) {
+#pragma unroll
+					for (int i = 0; i < 16; i += 4) {
+						float4 x = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+						if (EPI == EPI_ADD) {
+							float4 r = *(float4 *)(dst + i);
+							x.x = __fadd_rn(r.x, x.x), x.y = __fadd_rn(r.y, x.y), x.z = __fadd_rn(r.z, x.z), x.w = __fadd_rn(r.w, x.w);
+						}
+						*(float4 *)(dst + i) = x;
+					}
+				} else {
+					for (int i = 0; i < 16 && n + i < p.N; i++) dst[i] = EPI == EPI_ADD ? __fadd_rn(dst[i], v[i]) : v[i];
+				}
+			}
+		}
+		tc_fence_before();
+	}
+	__syncthreads();
+	if (warp == 1) {
+		tc_fence_after();
+		tmem_dealloc(tmem, BN);
+	}
+}
+
+// ---- host ----------------------------------------------------------------------------------
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int get_encode()
+{
+	static std::once_flag once;
+	static int rc = TG_CUDA_OK;
+	std::call_once(once, [] {
+		cudaDriverEntryPointQueryResult q;
+		void *fn = nullptr;
+		cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+		if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) rc = TG_CUDA_ECUDA;
+		else g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+	});
+	if (rc) return set_err(rc, "cuTensorMapEncodeTiled is not available from the driver");
+	return TG_CUDA_OK;
+}
+
+// bf16 [rows, K] K-major (row stride ld elements), box of 64 x box_rows, 128-byte swizzle.
+static int make_map(CUtensorMap *m, const void *base, long rows, long K, long ld, int box_rows)
+{
+	if (((uintptr_t)base & 15) || (ld * 2) % 16) return set_err(TG_CUDA_EINVAL, "TMA operand not 16-byte aligned (ld %ld)", ld);
+	cuuint64_t dims[2] = { (cuuint64_t)K, (cuuint64_t)rows };
+	cuuint64_t strides[1] = { (cuuint64_t)(ld * 2) };
+	cuuint32_t box[2] = { (cuuint32_t)BK, (cuuint32_t)box_rows };
+	cuuint32_t es[2] = { 1, 1 };
+	CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)base, dims, strides, box, es,
+			      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+			      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+	if (r != CUDA_SUCCESS) return set_err(TG_CUDA_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+	return TG_CUDA_OK;
+}
+
+template <int BN, int STAGES, int EPI>
+static int launch_bn(const TmaMaps &maps, const GemmArgs &p, cudaStream_t st)
+{
+	int stage = p.na * A_TILE + p.nb * BN * BK * 2;
+	size_t smem = (size_t)STAGES * stage + 1024 + 256;
+	static bool attr_set[64] = {};
+	int dev;
+	cudaGetDevice(&dev);
+	if (!attr_set[dev]) {
+		cudaFuncSetAttribute(gemm_tc<BN, STAGES, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+		attr_set[dev] = true;
+	}
+	dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM);
+	gemm_tc<BN, STAGES, EPI><<<grid, 192, smem, st>>>(maps, p);
+	TGC_LAUNCH_CHECK();
+	return TG_CUDA_OK;
+}
+
+int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
+{
+	int rc = get_encode();
+	if (rc) return rc;
+	if (p.M <= 0 || p.N <= 0 || p.K <= 0 || p.na < 1 || p.na > 2 || p.nb < 1 || p.nb > 2 || p.npairs < 1 || p.npairs > 4)
+		return set_err(TG_CUDA_EINVAL, "gemm: bad shape or operand count");
+	if (p.K % 8) return set_err(TG_CUDA_EINVAL, "gemm: K %d is not a multiple of 8", p.K);
+	const int BN = p.epi == EPI_SWIGLU || p.N >= 256 ? 256 : 128;
+	TmaMaps maps;
+	memset(&maps, 0, sizeof maps);
+	for (int i = 0; i < p.na; i++)
+		if ((rc = make_map(&maps.a[i], ops.a[i], p.M, p.K, ops.lda, BM))) return rc;
+	for (int j = 0; j < p.nb; j++)
+		if ((rc = make_map(&maps.b[j], ops.b[j], p.N, p.K, ops.ldb, BN))) return rc;
+	// as many ring stages (2..4) as fit in 220 KB of shared memory
+	const int stage = p.na * A_TILE + p.nb * BN * BK * 2;
+	const int stages = std::min(4, std::max(2, (220 * 1024) / stage));
+	if (stages * stage > 220 * 1024) return set_err(TG_CUDA_EINVAL, "gemm: %d operand tiles do not fit", p.na + p.nb);
+#define TGC_GEMM_DISPATCH(E)                                                                 \
+	if (BN == 256)                                                                      \
+		return stages >= 4 ? launch_bn<256, 4, E>(maps, p, st)                      \
+		       : stages == 3 ? launch_bn<256, 3, E>(maps, p, st) : launch_bn<256, 2, E>(maps, p, st); \
+	return stages >= 4 ? launch_bn<128, 4, E>(maps, p, st)                              \
+	       : stages == 3 ? launch_bn<128, 3, E>(maps, p, st) : launch_bn<128, 2, E>(maps, p, st);
+	if (p.epi == EPI_SWIGLU) {
+		TGC_GEMM_DISPATCH(EPI_SWIGLU)
+	}
+	if (p.epi == EPI_ADD) {
+		TGC_GEMM_DISPATCH(EPI_ADD)
+	}
+	TGC_GEMM_DISPATCH(EPI_STORE)
+#undef TGC_GEMM_DISPATCH
+}
+
+// ---- conversions feeding the GEMM ------------------------------------------------------------
+
+// f32 [rows, cols] (row stride lds) -> bf16 hi/lo, optionally transposed: dst[c, r] (K-major for B).
+__global__ void split_f32(const float *__restrict__ src, long rows, long cols, long lds, int transpose,
+			  __nv_bfloat16 *__restrict__ hi, __nv_bfloat16 *__restrict__ lo, long ldd)
+{
+	long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+	if (t >= rows * cols) return;
+	long r = t / cols, c = t % cols;
+	float x = src[r * lds + c];
+	__nv_bfloat16 h = __float2bfloat16_rn(x);
+	__nv_bfloat16 l = __float2bfloat16_rn(x - __bfloat162float(h));
+	long d = transpose ? c * ldd + r : r * ldd + c;
+	hi[d] = h;
+	if (lo) lo[d] = l;
+}
+
+// Codes of a [rows, cols] matrix in the reference packing -> bf16 (exact), optionally transposed.
+__global__ void codes_bf16(const signed char *__restrict__ q, int bits, long rows, long cols, int transpose,
+			   __nv_bfloat16 *__restrict__ dst, long ldd)
+{
+	long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+	if (t >= rows * cols) return;
+	long r = t / cols, c = t % cols;
+	float v = (float)qcode(q, bits, t);
+	dst[transpose ? c * ldd + r : r * ldd + c] = __float2bfloat16_rn(v);
+}
+
+int split_to_bf16(const float *src, long rows, long cols, long lds, bool transpose, __nv_bfloat16 *hi, __nv_bfloat16 *lo,
+		  long ldd, cudaStream_t st)
+{
+	long n = rows * cols;
+	split_f32<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, rows, cols, lds, transpose ? 1 : 0, hi, lo, ldd);
+	TGC_LAUNCH_CHECK();
+	return TG_CUDA_OK;
+}
+
+int codes_to_bf16(const signed char *q, int bits, long rows, long cols, bool transpose, __nv_bfloat16 *dst, long ldd,
+		  cudaStream_t st)
+{
+	long n = rows * cols;
+	codes_bf16<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(q, bits, rows, cols, transpose ? 1 : 0, dst, ldd);
+	TGC_LAUNCH_CHECK();
+	return TG_CUDA_OK;
+}
+
+// ---- tg_cuda_matmul_q, large batch -------------------------------------------------------------
+
+struct TcScratch {
+	DevBuf buf, status;
+};
+static TcScratch g_tc[64];
+
+int device_status_check(int *d_status, cudaStream_t st)
+{
+	int h = 0;
+	cudaError_t e = cudaMemcpyAsync(&h, d_status, sizeof h, cudaMemcpyDeviceToHost, st);
+	if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+	if (e != cudaSuccess) return set_err(TG_CUDA_ECUDA, "status read: %s", cudaGetErrorString(e));
+	if (h) return set_err(TG_CUDA_EDEVICE, "a tensor-core kernel gave up waiting (status %d)", h);
+	return TG_CUDA_OK;
+}
 
 int matmul_q_tc(int axis, float *o, const float *act, const signed char *q, int bits, const float *s, int m, int k, int n,
 		cudaStream_t st, bool *done)
 {
-	(void)axis; (void)o; (void)act; (void)q; (void)bits; (void)s; (void)m; (void)k; (void)n; (void)st;
 	*done = false;
+	// batch = columns of b (axis 0) or rows of a (axis 1); the GEMV covers batches up to 8
+	if (k % 8) return TG_CUDA_OK;
+	int dev;
+	cudaGetDevice(&dev);
+	TcScratch &S = g_tc[dev];
+	long wrows = axis == 0 ? m : n;   // weight channels
+	long brows = axis == 0 ? n : m;   // activation rows (batch)
+	size_t wbytes = (size_t)wrows * k * 2, abytes = (size_t)brows * k * 2;
+	int rc;
+	if ((rc = S.buf.ensure(wbytes + 2 * abytes + 256, dev)) || (rc = S.status.ensure(64, dev))) return rc;
+	__nv_bfloat16 *wq = (__nv_bfloat16 *)S.buf.p;
+	__nv_bfloat16 *ahi = (__nv_bfloat16 *)((uint8_t *)S.buf.p + ((wbytes + 127) & ~(size_t)127));
+	__nv_bfloat16 *alo = (__nv_bfloat16 *)((uint8_t *)ahi + ((abytes + 127) & ~(size_t)127));
+	cudaMemsetAsync(S.status.p, 0, sizeof(int), st);
+	GemmOperands ops;
+	GemmArgs p;
+	memset(&p, 0, sizeof p);
+	p.K = k;
+	p.na = 1;
+	p.nb = 2;
+	p.npairs = 2;
+	p.pa[0] = 0, p.pb[0] = 0, p.pa[1] = 0, p.pb[1] = 1;
+	p.epi = EPI_STORE;
+	p.out = o;
+	p.status = S.status.as<int>();
+	if (axis == 0) {
+		// o[m, n] = diag(s) Q[m, k] b[k, n]: A = codes [m, k], B = b^T [n, k] split
+		if ((rc = codes_to_bf16(q, bits, m, k, false, wq, k, st))) return rc;
+		if ((rc = split_to_bf16(act, k, n, n, true, ahi, alo, k, st))) return rc;
+		ops.a[0] = wq, ops.b[0] = ahi, ops.b[1] = alo;
+		p.M = m, p.N = n, p.ldo = n, p.scale = s, p.scale_mode = 1;
+	} else {
+		// o[m, n] = a[m, k] Q[k, n] diag(s): A = a split, B = codes^T [n, k]
+		if ((rc = codes_to_bf16(q, bits, k, n, true, wq, k, st))) return rc;
+		if ((rc = split_to_bf16(act, m, k, k, false, ahi, alo, k, st))) return rc;
+		ops.a[0] = ahi, ops.a[1] = alo, ops.b[0] = wq;
+		p.na = 2, p.nb = 1;
+		p.pa[0] = 0, p.pb[0] = 0, p.pa[1] = 1, p.pb[1] = 0;
+		p.M = m, p.N = n, p.ldo = n, p.scale = s, p.scale_mode = 2;
+	}
+	ops.lda = k, ops.ldb = k;
+	if ((rc = gemm(ops, p, st))) return rc;
+	if ((rc = device_status_check(p.status, st))) return rc;
+	*done = true;
 	return TG_CUDA_OK;
 }
 

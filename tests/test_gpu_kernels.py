@@ -58,6 +58,37 @@ def test_matmul_q_vs_oracle(cuda, axis, m, k, n, bits):
     np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
 
 
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("axis,m,k,n", [
+    (0, 128, 64, 128), (0, 200, 72, 130), (1, 130, 200, 136), (1, 9, 64, 128), (0, 4096, 4096, 256),
+    (1, 2048, 1024, 3072), (0, 1024, 4096, 4096),
+])
+def test_matmul_q_tensor_cores_vs_oracle(cuda, axis, m, k, n, bits):
+    """Batches above 8 take the tcgen05 GEMM; large shapes are checked on sampled outputs."""
+    rng = np.random.default_rng(4)
+    lim = 8 if bits == 4 else 127
+    codes = rng.integers(-lim, lim if bits == 8 else 8, size=m * k if axis == 0 else k * n)
+    q = tgir.pack_codes(codes, bits)
+    s = (np.abs(rng.normal(0, 0.02, size=m if axis == 0 else n)) / (7 if bits == 4 else 127)).astype(np.float32)
+    act = rng.normal(0, 1, size=k * n if axis == 0 else m * k).astype(np.float32)
+    got = gpu_matmul_q(cuda, axis, act, q, bits, s, m, k, n)
+    if m * n * k <= 1 << 26:
+        want = tgo.matmul_q(tgo.tgo(), "tgo_", axis, act, q, bits, s, m, k, n)
+        np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+        return
+    # sample: for axis 0 a few batch columns j (full GEMVs), for axis 1 a few rows i
+    pick = rng.choice(n if axis == 0 else m, size=6, replace=False)
+    for j in pick:
+        if axis == 0:
+            b = act.reshape(k, n)[:, j].copy()
+            want = tgo.matmul_q(tgo.tgo(), "tgo_", 0, b, q, bits, s, m, k, 1)[:, 0]
+            np.testing.assert_allclose(got[:, j], want, rtol=RTOL, atol=ATOL)
+        else:
+            a = act.reshape(m, k)[j].copy()
+            want = tgo.matmul_q(tgo.tgo(), "tgo_", 1, a, q, bits, s, 1, k, n)[0]
+            np.testing.assert_allclose(got[j], want, rtol=RTOL, atol=ATOL)
+
+
 def test_matmul_q_edge_cases(cuda):
     # code -8 everywhere, k = 1, and a row count that is not a multiple of anything
     for axis, bits, m, k, n in ((0, 4, 3, 1, 1), (1, 4, 1, 1, 2), (0, 4, 5, 64, 2), (1, 8, 2, 5, 3)):
