@@ -1,27 +1,839 @@
-// lm.cu -- decoder language models (the Qwen3 import) on the device.
+// lm.cu -- decoder language models of the Qwen3 import (examples/qwen3/import.py:90-132)
+// on the device: batched prefill and greedy decode with a per-sequence KV cache.
+//
+// The reference runs this program per sequence in the VM: per-head rank-2
+// tg_matmul_qb calls (x @ W, axis-1 int8/int4 codes with per-column scales),
+// rmsnorm then `* weight`, rotate-half RoPE through cos/sin tables and a
+// rotation matrix, softmax((q k^T) * scale + mask), (s v) @ Wo per head summed
+// into the residual, a SwiGLU MLP, and the LM head on every row followed by
+// take(lastidx). Here the same arithmetic runs for many sequences at once:
+//
+//   weights  converted once at load: codes -> exact bf16 in [out, in] K-major
+//            layout for the tcgen05 GEMM (q/k/v heads concatenated into one
+//            matrix; gate/up interleaved in 128-row blocks so one GEMM tile
+//            holds matching gate and up channels); o_proj pre-scaled by its
+//            per-head column scales and split into bf16 hi/lo.
+//   layer    rmsnorm*ln1 (split to bf16 hi/lo) -> QKV GEMM -> q/k rmsnorm*w +
+//            RoPE, k/v into the KV cache -> causal attention (prefill) or
+//            KV-cache attention (decode), output split hi/lo -> Wo GEMM added
+//            into the residual -> rmsnorm*ln2 -> gate/up GEMM with SwiGLU in
+//            its epilogue -> down GEMM added into the residual.
+//   head     rmsnorm*lnf of the last position only (take(lastidx) discards the
+//            other rows), LM-head GEMM, argmax for greedy decode.
+//
+// KV cache: f32, [layer][slot][kv head][position][head_dim]. Sequences run in
+// waves of at most max_seqs per device; the prefill of a wave runs in chunks
+// of at most PREFILL_ROWS tokens.
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <memory>
+#include <thread>
+#include <vector>
+
 #include "common.cuh"
+#include "gemm.cuh"
 #include "kernels.cuh"
+#include "tc.cuh"
+
+namespace tgc {
+
+constexpr long PREFILL_ROWS = 16384;
+
+__device__ __forceinline__ void split_bf16(float y, __nv_bfloat16 &h, __nv_bfloat16 &l)
+{
+	h = __float2bfloat16_rn(y);
+	l = __float2bfloat16_rn(y - __bfloat162float(h));
+}
+
+// ---- weight conversion ----------------------------------------------------------------------
+
+// Gate and up [D, FF] codes -> interleaved [2 FF, D]: block b = rows 256b.. holds gate
+// channels 128b..128b+127 then the same up channels.
+__global__ void k_codes_gu(const signed char *__restrict__ qg, const signed char *__restrict__ qu, int bits, int D, int FF,
+			   __nv_bfloat16 *__restrict__ dst)
+{
+	long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+	if (t >= 2L * D * FF) return;
+	int which = (int)(t / ((long)D * FF));
+	long e = t % ((long)D * FF); // element of the [D, FF] source
+	int p = (int)(e / FF), f = (int)(e % FF);
+	float v = (float)qcode(which ? qu : qg, bits, e);
+	long row = (long)(f / 128) * 256 + which * 128 + f % 128;
+	dst[row * D + p] = __float2bfloat16_rn(v);
+}
+
+// o_proj: stacked per-head codes [NQ*HD, D] with scales s[h*D + n] -> B[n][h*HD + p] =
+// code * s, split hi/lo (the dequantized value the program's param holds, src/ir.c:503-507).
+__global__ void k_wo_prescale(const signed char *__restrict__ q, const float *__restrict__ s, int bits, int KO, int HD,
+			      int D, __nv_bfloat16 *__restrict__ hi, __nv_bfloat16 *__restrict__ lo)
+{
+	long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+	if (t >= (long)KO * D) return;
+	int r = (int)(t / D), n = (int)(t % D), h = r / HD;
+	float v = __fmul_rn((float)qcode(q, bits, t), s[(long)h * D + n]);
+	__nv_bfloat16 a, b;
+	split_bf16(v, a, b);
+	hi[(long)n * KO + r] = a;
+	lo[(long)n * KO + r] = b;
+}
+
+// ---- per-token kernels ----------------------------------------------------------------------
+
+// h[r] = E[round(ids[r])] or zeros out of range (take, runtime/tg_rt.h:316-322). One warp per row.
+__global__ void k_embed(const float *__restrict__ ids, const int *__restrict__ tok, long M, const float *__restrict__ E,
+			int V, int D, float *__restrict__ h)
+{
+	long r = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+	int lane = threadIdx.x & 31;
+	if (r >= M) return;
+	int t;
+	if (tok) t = tok[r];
+	else {
+		float x = floorf(ids[r] + 0.5f);
+		t = x >= 0.0f && x < (float)V ? (int)x : -1;
+	}
+	t = t >= 0 && t < V ? t : -1;
+	const float4 *src = (const float4 *)(E + (long)(t < 0 ? 0 : t) * D);
+	float4 *dst = (float4 *)(h + r * D);
+	for (int i = lane; i < D / 4; i += 32) dst[i] = t >= 0 ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// y = rmsnorm(x) * w (runtime/tg_rt.h:165-175 then the broadcast mul), split to bf16 hi/lo.
+// One warp per output row; src row = rowmap ? rowmap(r) : r (the last position of each sequence).
+__global__ void k_rmsnorm_split(const float *__restrict__ x, long M, int D, const float *__restrict__ w, float eps,
+				int last_T, __nv_bfloat16 *__restrict__ hi, __nv_bfloat16 *__restrict__ lo)
+{
+	long r = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+	int lane = threadIdx.x & 31;
+	if (r >= M) return;
+	long src = last_T > 0 ? r * last_T + last_T - 1 : r;
+	const float *xr = x + src * D;
+	float ss = 0.0f;
+	for (int i = lane; i < D; i += 32) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+	for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+	float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+	for (int i = lane; i < D; i += 32) {
+		float y = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+		split_bf16(y, hi[r * D + i], lo[r * D + i]);
+	}
+}
+
+// Per (row, head) of the QKV projection [M, (NQ + 2 NKV) HD]: q and k heads get
+// rmsnorm * qn / kn then rotary(x) = x*cos + rotate_half(x)*sin (import.py:96-97);
+// q goes to q_out [seq][NQ][T][HD], k and v into the cache at position pos0 + t.
+// One warp per head, 4 dims per lane (HD = 128).
+__global__ void k_qk_rope(const float *__restrict__ qkv, long M, int T, int pos0, int NQ, int NKV, float eps,
+			  const float *__restrict__ qn, const float *__restrict__ kn, const float *__restrict__ cosT,
+			  const float *__restrict__ sinT, float *__restrict__ q_out, float *__restrict__ kc,
+			  float *__restrict__ vc, int slot0, int max_len)
+{
+	constexpr int HD = 128;
+	long gw = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+	int lane = threadIdx.x & 31;
+	const int H = NQ + 2 * NKV;
+	if (gw >= M * H) return;
+	long r = gw / H;
+	int hh = (int)(gw % H);
+	int s = (int)(r / T), t = (int)(r % T), pos = pos0 + t;
+	float4 x = ((const float4 *)(qkv + r * (long)H * HD + (long)hh * HD))[lane];
+	if (hh >= NQ + NKV) { // v head: straight into the cache
+		int kvh = hh - NQ - NKV;
+		((float4 *)(vc + (((long)(slot0 + s) * NKV + kvh) * max_len + pos) * HD))[lane] = x;
+		return;
+	}
+	const float *w = hh < NQ ? qn : kn;
+	float ss = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, x.w * x.w)));
+#pragma unroll
+	for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+	float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), eps)));
+	float v[4] = { x.x, x.y, x.z, x.w };
+#pragma unroll
+	for (int e = 0; e < 4; e++) v[e] = __fmul_rn(__fmul_rn(v[e], inv), w[lane * 4 + e]);
+	// rotate_half: dims i < 64 take -x[i + 64], dims i >= 64 take x[i - 64] (lane +- 16)
+	float o4[4];
+#pragma unroll
+	for (int e = 0; e < 4; e++) {
+		float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
+		float rot = lane < 16 ? -partner : partner;
+		int d = lane * 4 + e, f = d & (HD / 2 - 1);
+		float c = cosT[(long)pos * (HD / 2) + f], sn = sinT[(long)pos * (HD / 2) + f];
+		o4[e] = __fadd_rn(__fmul_rn(v[e], c), __fmul_rn(rot, sn));
+	}
+	float4 res = make_float4(o4[0], o4[1], o4[2], o4[3]);
+	if (hh < NQ) ((float4 *)(q_out + (((long)s * NQ + hh) * T + t) * HD))[lane] = res;
+	else ((float4 *)(kc + (((long)(slot0 + s) * NKV + (hh - NQ)) * max_len + pos) * HD))[lane] = res;
+}
+
+// ---- causal attention for the prefill, f32 on CUDA cores ------------------------------------
+// CTA = (64 queries, head, sequence); K/V tiles of 64 positions; online softmax.
+// Thread (ty, tx) of a 16 x 16 grid owns score rows ty + 16 r and columns tx + 16 c,
+// and output rows ty + 16 r, columns 4 tx.. and 64 + 4 tx...
+constexpr int AQ = 64, AK = 64, APAD = 132;
+
+__global__ void __launch_bounds__(256) k_attn_prefill(const float *__restrict__ q, const float *__restrict__ kc,
+						      const float *__restrict__ vc, int T, int NQ, int NKV, int slot0,
+						      int max_len, float scale, __nv_bfloat16 *__restrict__ ohi,
+						      __nv_bfloat16 *__restrict__ olo)
+{
+	constexpr int HD = 128;
+	extern __shared__ float sm[];
+	float *Qs = sm;                 // [64][132]
+	float *Ks = Qs + AQ * APAD;     // [64][132]
+	float *Vs = Ks + AK * APAD;     // [64][128]
+	float *Ps = Vs + AK * HD;       // [64][68]
+	const int qt = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+	const int kvh = h / (NQ / NKV);
+	const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+	const int q0 = qt * AQ;
+	const float *qb = q + (((long)s * NQ + h) * T) * HD;
+	const float *kb = kc + (((long)(slot0 + s) * NKV + kvh) * max_len) * HD;
+	const float *vb = vc + (((long)(slot0 + s) * NKV + kvh) * max_len) * HD;
+	for (int i = tid; i < AQ * HD / 4; i += 256) {
+		int r = i / (HD / 4), c = (i % (HD / 4)) * 4;
+		float4 v = q0 + r < T ? *(const float4 *)(qb + (long)(q0 + r) * HD + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+		*(float4 *)(Qs + r * APAD + c) = v;
+	}
+	float m[4], l[4], o[4][8];
+#pragma unroll
+	for (int r = 0; r < 4; r++) {
+		m[r] = -INFINITY;
+		l[r] = 0.0f;
+#pragma unroll
+		for (int c = 0; c < 8; c++) o[r][c] = 0.0f;
+	}
+	const int nkt = min((q0 + AQ + AK - 1) / AK, (T + AK - 1) / AK);
+	for (int kt = 0; kt < nkt; kt++) {
+		const int k0 = kt * AK;
+		__syncthreads();
+		for (int i = tid; i < AK * HD / 4; i += 256) {
+			int r = i / (HD / 4), c = (i % (HD / 4)) * 4;
+			bool in = k0 + r < T;
+			float4 kv = in ? *(const float4 *)(kb + (long)(k0 + r) * HD + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+			float4 vv = in ? *(const float4 *)(vb + (long)(k0 + r) * HD + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+			*(float4 *)(Ks + r * APAD + c) = kv;
+			*(float4 *)(Vs + r * HD + c) = vv;
+		}
+		__syncthreads();
+		float sc[4][4];
+#pragma unroll
+		for (int r = 0; r < 4; r++)
+#pragma unroll
+			for (int c = 0; c < 4; c++) sc[r][c] = 0.0f;
+#pragma unroll 4
+		for (int d = 0; d < HD; d += 4) {
+			float4 qa[4], ka[4];
+#pragma unroll
+			for (int r = 0; r < 4; r++) qa[r] = *(const float4 *)(Qs + (ty + 16 * r) * APAD + d);
+#pragma unroll
+			for (int c = 0; c < 4; c++) ka[c] = *(const float4 *)(Ks + (tx + 16 * c) * APAD + d);
+#pragma unroll
+			for (int r = 0; r < 4; r++)
+#pragma unroll
+				for (int c = 0; c < 4; c++) {
+					sc[r][c] = fmaf(qa[r].x, ka[c].x, sc[r][c]);
+					sc[r][c] = fmaf(qa[r].y, ka[c].y, sc[r][c]);
+					sc[r][c] = fmaf(qa[r].z, ka[c].z, sc[r][c]);
+					sc[r][c] = fmaf(qa[r].w, ka[c].w, sc[r][c]);
+				}
+		}
+		// scale, causal mask, online softmax over the 16 threads of this half-warp
+#pragma unroll
+		for (int r = 0; r < 4; r++) {
+			const int qi = q0 + ty + 16 * r;
+			float mx = -INFINITY;
+#pragma unroll
+			for (int c = 0; c < 4; c++) {
+				const int kj = k0 + tx + 16 * c;
+				float v = kj <= qi && kj < T ? __fmul_rn(sc[r][c], scale) : -INFINITY;
+				sc[r][c] = v;
+				mx = fmaxf(mx, v);
+			}
+#pragma unroll
+			for (int off = 8; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+			const float mnew = fmaxf(m[r], mx);
+			const float corr = mnew == -INFINITY ? 1.0f : expf(m[r] - mnew);
+			float sum = 0.0f;
+#pragma unroll
+			for (int c = 0; c < 4; c++) {
+				float p = sc[r][c] == -INFINITY ? 0.0f : expf(sc[r][c] - mnew);
+				Ps[(ty + 16 * r) * 68 + tx + 16 * c] = p;
+				sum += p;
+			}
+#pragma unroll
+			for (int off = 8; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+			l[r] = l[r] * corr + sum;
+			m[r] = mnew;
+#pragma unroll
+			for (int c = 0; c < 8; c++) o[r][c] *= corr;
+		}
+		__syncthreads();
+#pragma unroll 2
+		for (int j = 0; j < AK; j += 4) {
+			float4 pr[4];
+#pragma unroll
+			for (int r = 0; r < 4; r++) pr[r] = *(const float4 *)(Ps + (ty + 16 * r) * 68 + j);
+#pragma unroll
+			for (int jj = 0; jj < 4; jj++) {
+				float4 va = *(const float4 *)(Vs + (j + jj) * HD + 4 * tx);
+				float4 vb2 = *(const float4 *)(Vs + (j + jj) * HD + 64 + 4 * tx);
+#pragma unroll
+				for (int r = 0; r < 4; r++) {
+					float p = jj == 0 ? pr[r].x : jj == 1 ? pr[r].y : jj == 2 ? pr[r].z : pr[r].w;
+					o[r][0] = fmaf(p, va.x, o[r][0]);
+					o[r][1] = fmaf(p, va.y, o[r][1]);
+					o[r][2] = fmaf(p, va.z, o[r][2]);
+					o[r][3] = fmaf(p, va.w, o[r][3]);
+					o[r][4] = fmaf(p, vb2.x, o[r][4]);
+					o[r][5] = fmaf(p, vb2.y, o[r][5]);
+					o[r][6] = fmaf(p, vb2.z, o[r][6]);
+					o[r][7] = fmaf(p, vb2.w, o[r][7]);
+				}
+			}
+		}
+	}
+	// out[(s*T + t)][h*HD + c], split hi/lo for the o_proj GEMM
+#pragma unroll
+	for (int r = 0; r < 4; r++) {
+		const int t = q0 + ty + 16 * r;
+		if (t >= T) continue;
+		const float inv = 1.0f / l[r];
+		const long base = ((long)s * T + t) * (long)NQ * HD + (long)h * HD;
+#pragma unroll
+		for (int c = 0; c < 8; c++) {
+			int col = c < 4 ? 4 * tx + c : 64 + 4 * tx + (c - 4);
+			split_bf16(o[r][c] * inv, ohi[base + col], olo[base + col]);
+		}
+	}
+}
+
+// ---- decode attention over the KV cache -------------------------------------------------------
+// CTA = (kv head, sequence); the GRP query heads sharing that kv head are done together.
+// Scores: each warp takes every 8th position, a lane holds 4 dims; softmax in shared memory;
+// values: each warp accumulates its positions, warps are summed through shared memory.
+template <int GRP>
+__global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q, const float *__restrict__ kc,
+						     const float *__restrict__ vc, int len, int NQ, int NKV, int slot0,
+						     int max_len, float scale, __nv_bfloat16 *__restrict__ ohi,
+						     __nv_bfloat16 *__restrict__ olo)
+{
+	constexpr int HD = 128;
+	extern __shared__ float sm[];
+	float *sc = sm;                       // [GRP][len]
+	float *red = sc + GRP * ((len + 3) & ~3); // [8][GRP][HD]
+	__shared__ float wmax[8][GRP], wsum[8][GRP];
+	const int kvh = blockIdx.x, s = blockIdx.y;
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const float *kb = kc + (((long)(slot0 + s) * NKV + kvh) * max_len) * HD;
+	const float *vb = vc + (((long)(slot0 + s) * NKV + kvh) * max_len) * HD;
+	float4 qv[GRP];
+#pragma unroll
+	for (int g = 0; g < GRP; g++) qv[g] = ((const float4 *)(q + ((long)s * NQ + kvh * GRP + g) * HD))[lane];
+	float mx[GRP];
+#pragma unroll
+	for (int g = 0; g < GRP; g++) mx[g] = -INFINITY;
+	for (int p0 = warp * 4; p0 < len; p0 += 32) {
+		float4 kv[4];
+#pragma unroll
+		for (int u = 0; u < 4; u++) kv[u] = p0 + u < len ? ((const float4 *)(kb + (long)(p0 + u) * HD))[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+		for (int u = 0; u < 4; u++)
+#pragma unroll
+			for (int g = 0; g < GRP; g++) {
+				float d = fmaf(qv[g].x, kv[u].x, fmaf(qv[g].y, kv[u].y, fmaf(qv[g].z, kv[u].z, qv[g].w * kv[u].w)));
+#pragma unroll
+				for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+				if (p0 + u < len) {
+					d = __fmul_rn(d, scale);
+					if (lane == 0) sc[g * ((len + 3) & ~3) + p0 + u] = d;
+					mx[g] = fmaxf(mx[g], d);
+				}
+			}
+	}
+	if (lane == 0)
+#pragma unroll
+		for (int g = 0; g < GRP; g++) wmax[warp][g] = mx[g];
+	__syncthreads();
+	float gmax[GRP], gsum[GRP];
+#pragma unroll
+	for (int g = 0; g < GRP; g++) {
+		gmax[g] = wmax[0][g];
+		for (int w = 1; w < 8; w++) gmax[g] = fmaxf(gmax[g], wmax[w][g]);
+	}
+	const int stride = (len + 3) & ~3;
+	float part[GRP];
+#pragma unroll
+	for (int g = 0; g < GRP; g++) part[g] = 0.0f;
+	for (int p = threadIdx.x; p < len; p += 256)
+#pragma unroll
+		for (int g = 0; g < GRP; g++) {
+			float e = expf(sc[g * stride + p] - gmax[g]);
+			sc[g * stride + p] = e;
+			part[g] += e;
+		}
+#pragma unroll
+	for (int g = 0; g < GRP; g++) {
+#pragma unroll
+		for (int o = 16; o; o >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], o);
+		if (lane == 0) wsum[warp][g] = part[g];
+	}
+	__syncthreads();
+#pragma unroll
+	for (int g = 0; g < GRP; g++) {
+		gsum[g] = 0.0f;
+		for (int w = 0; w < 8; w++) gsum[g] += wsum[w][g];
+	}
+	float4 acc[GRP];
+#pragma unroll
+	for (int g = 0; g < GRP; g++) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+	for (int p0 = warp * 4; p0 < len; p0 += 32) {
+		float4 vv[4];
+#pragma unroll
+		for (int u = 0; u < 4; u++) vv[u] = p0 + u < len ? ((const float4 *)(vb + (long)(p0 + u) * HD))[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+		for (int u = 0; u < 4; u++) {
+			if (p0 + u >= len) break;
+#pragma unroll
+			for (int g = 0; g < GRP; g++) {
+				float e = sc[g * stride + p0 + u];
+				acc[g].x = fmaf(e, vv[u].x, acc[g].x);
+				acc[g].y = fmaf(e, vv[u].y, acc[g].y);
+				acc[g].z = fmaf(e, vv[u].z, acc[g].z);
+				acc[g].w = fmaf(e, vv[u].w, acc[g].w);
+			}
+		}
+	}
+#pragma unroll
+	for (int g = 0; g < GRP; g++) ((float4 *)(red + ((long)warp * GRP + g) * HD))[lane] = acc[g];
+	__syncthreads();
+	for (int i = threadIdx.x; i < GRP * HD; i += 256) {
+		int g = i / HD, d = i % HD;
+		float v = 0.0f;
+		for (int w = 0; w < 8; w++) v += red[((long)w * GRP + g) * HD + d];
+		v = v / gsum[g];
+		long o = (long)s * NQ * HD + (long)(kvh * GRP + g) * HD + d;
+		split_bf16(v, ohi[o], olo[o]);
+	}
+}
+
+// First index of the row maximum (greedy decode).
+__global__ void k_argmax(const float *__restrict__ logits, int V, int *__restrict__ tok, int *__restrict__ out, int ld_out,
+			 int col)
+{
+	const float *x = logits + (long)blockIdx.x * V;
+	float best = -INFINITY;
+	int bi = 0x7fffffff;
+	for (int i = threadIdx.x; i < V; i += blockDim.x) {
+		float v = x[i];
+		if (v > best || (v == best && i < bi)) best = v, bi = i;
+	}
+	__shared__ float sv[32];
+	__shared__ int si[32];
+#pragma unroll
+	for (int o = 16; o; o >>= 1) {
+		float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+		int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+		if (v2 > best || (v2 == best && i2 < bi)) best = v2, bi = i2;
+	}
+	int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	if (lane == 0) sv[w] = best, si[w] = bi;
+	__syncthreads();
+	if (threadIdx.x == 0) {
+		for (int i = 1; i < (int)(blockDim.x >> 5); i++)
+			if (sv[i] > best || (sv[i] == best && si[i] < bi)) best = sv[i], bi = si[i];
+		if (bi == 0x7fffffff) bi = 0; // all NaN
+		tok[blockIdx.x] = bi;
+		if (out) out[(long)blockIdx.x * ld_out + col] = bi;
+	}
+}
+
+// ---- the engine --------------------------------------------------------------------------------
+
+struct Layer {
+	DevBuf wqkv, sqkv, wo_hi, wo_lo, wgu, sg, su, wd, sd, ln1, ln2, qn, kn;
+};
+
+struct Engine {
+	int dev = 0;
+	cudaStream_t st = nullptr;
+	int L, D, NQ, NKV, HD, FF, V, bits, max_seqs, max_len;
+	float eps, scale;
+	DevBuf E, lnf, lmw, lms, cosT, sinT;
+	std::vector<std::unique_ptr<Layer>> layers;
+	DevBuf kc, vc;
+	// activations
+	long rows_cap = 0;
+	DevBuf h, xhi, xlo, qkv, q, ahi, alo, ghi, glo, logits, tok, ids, status, out_tok;
+	int HQKV() const { return (NQ + 2 * NKV) * HD; }
+};
+
+// Host -> device copy ordered on the engine's stream and complete on return. (A plain
+// cudaMemcpy from pageable memory may return before its DMA lands, and kernels on a
+// non-blocking stream are not ordered after it.)
+static int upload(DevBuf &b, const void *src, size_t bytes, int dev, cudaStream_t st)
+{
+	int rc = b.alloc(bytes, dev);
+	if (rc) return rc;
+	TGC_CUDA(cudaMemcpyAsync(b.p, src, bytes, cudaMemcpyHostToDevice, st));
+	TGC_CUDA(cudaStreamSynchronize(st));
+	return TG_CUDA_OK;
+}
+
+static size_t qbytes(long n, int bits) { return bits == 8 ? (size_t)n : (size_t)(n + 1) / 2; }
+
+static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seqs, int max_len)
+{
+	int rc;
+	g.dev = dev;
+	TGC_CUDA(cudaSetDevice(dev));
+	TGC_CUDA(cudaStreamCreateWithFlags(&g.st, cudaStreamNonBlocking));
+	g.L = d->layers, g.D = d->hidden, g.NQ = d->nq, g.NKV = d->nkv, g.HD = d->head_dim, g.FF = d->ffn, g.V = d->vocab;
+	g.bits = d->bits, g.eps = d->eps, g.scale = d->attn_scale, g.max_seqs = max_seqs, g.max_len = max_len;
+	const int D = g.D, HD = g.HD, NQ = g.NQ, NKV = g.NKV, FF = g.FF, V = g.V, bits = g.bits;
+	if ((rc = upload(g.E, d->embed, (size_t)V * D * 4, dev, g.st)) || (rc = upload(g.lnf, d->final_norm, (size_t)D * 4, dev, g.st)))
+		return rc;
+	// RoPE tables in double, stored f32 (import.py:76-78): [pos][HD/2]
+	{
+		std::vector<float> c((size_t)max_len * HD / 2), s((size_t)max_len * HD / 2);
+		for (int t = 0; t < max_len; t++)
+			for (int i = 0; i < HD / 2; i++) {
+				double inv = pow(d->rope_theta, -((double)(2 * i) / HD)), ang = (double)t * inv;
+				c[(size_t)t * HD / 2 + i] = (float)cos(ang);
+				s[(size_t)t * HD / 2 + i] = (float)sin(ang);
+			}
+		if ((rc = upload(g.cosT, c.data(), c.size() * 4, dev, g.st)) || (rc = upload(g.sinT, s.data(), s.size() * 4, dev, g.st))) return rc;
+	}
+	DevBuf tmpq, tmpq2, tmps;
+	auto codes_T = [&](const tg_cuda_qmat &m, long rows, long cols, __nv_bfloat16 *dst, long ldd) -> int {
+		// [rows=in, cols=out] codes -> dst[out][in]
+		int r;
+		if ((r = upload(tmpq, m.q, qbytes(rows * cols, bits), dev, g.st))) return r;
+		if ((r = codes_to_bf16(tmpq.as<signed char>(), bits, rows, cols, true, dst, ldd, g.st))) return r;
+		TGC_CUDA(cudaStreamSynchronize(g.st));
+		return TG_CUDA_OK;
+	};
+	// LM head [D, V] -> [V][D]
+	if ((rc = g.lmw.alloc((size_t)V * D * 2, dev)) || (rc = codes_T(d->lm_head, D, V, g.lmw.as<__nv_bfloat16>(), D)) ||
+	    (rc = upload(g.lms, d->lm_head.s, (size_t)V * 4, dev, g.st)))
+		return rc;
+	for (int l = 0; l < g.L; l++) {
+		g.layers.emplace_back(new Layer);
+		Layer &Y = *g.layers.back();
+		const int HQKV = g.HQKV();
+		if ((rc = Y.wqkv.alloc((size_t)HQKV * D * 2, dev))) return rc;
+		__nv_bfloat16 *w = Y.wqkv.as<__nv_bfloat16>();
+		if ((rc = codes_T(d->wq[l], D, NQ * HD, w, D)) || (rc = codes_T(d->wk[l], D, NKV * HD, w + (size_t)NQ * HD * D, D)) ||
+		    (rc = codes_T(d->wv[l], D, NKV * HD, w + (size_t)(NQ + NKV) * HD * D, D)))
+			return rc;
+		{
+			std::vector<float> s(HQKV);
+			memcpy(s.data(), d->wq[l].s, (size_t)NQ * HD * 4);
+			memcpy(s.data() + NQ * HD, d->wk[l].s, (size_t)NKV * HD * 4);
+			memcpy(s.data() + (NQ + NKV) * HD, d->wv[l].s, (size_t)NKV * HD * 4);
+			if ((rc = upload(Y.sqkv, s.data(), s.size() * 4, dev, g.st))) return rc;
+		}
+		// o_proj: pre-scaled hi/lo [D][NQ*HD]
+		const long KO = (long)NQ * HD;
+		if ((rc = Y.wo_hi.alloc((size_t)D * KO * 2, dev)) || (rc = Y.wo_lo.alloc((size_t)D * KO * 2, dev)) ||
+		    (rc = upload(tmpq, d->wo[l].q, qbytes(KO * D, bits), dev, g.st)) || (rc = upload(tmps, d->wo[l].s, (size_t)NQ * D * 4, dev, g.st)))
+			return rc;
+		k_wo_prescale<<<(unsigned)((KO * D + 255) / 256), 256, 0, g.st>>>(tmpq.as<signed char>(), tmps.as<float>(), bits, (int)KO,
+										      HD, D, Y.wo_hi.as<__nv_bfloat16>(), Y.wo_lo.as<__nv_bfloat16>());
+		TGC_LAUNCH_CHECK();
+		TGC_CUDA(cudaStreamSynchronize(g.st));
+		// gate/up interleaved [2FF][D]
+		if ((rc = Y.wgu.alloc((size_t)2 * FF * D * 2, dev)) || (rc = upload(tmpq, d->wg[l].q, qbytes((long)D * FF, bits), dev, g.st)) ||
+		    (rc = upload(tmpq2, d->wu[l].q, qbytes((long)D * FF, bits), dev, g.st)))
+			return rc;
+		k_codes_gu<<<(unsigned)((2L * D * FF + 255) / 256), 256, 0, g.st>>>(tmpq.as<signed char>(), tmpq2.as<signed char>(), bits, D,
+										      FF, Y.wgu.as<__nv_bfloat16>());
+		TGC_LAUNCH_CHECK();
+		TGC_CUDA(cudaStreamSynchronize(g.st));
+		if ((rc = upload(Y.sg, d->wg[l].s, (size_t)FF * 4, dev, g.st)) || (rc = upload(Y.su, d->wu[l].s, (size_t)FF * 4, dev, g.st))) return rc;
+		// down [FF, D] -> [D][FF]
+		if ((rc = Y.wd.alloc((size_t)D * FF * 2, dev)) || (rc = codes_T(d->wd[l], FF, D, Y.wd.as<__nv_bfloat16>(), FF)) ||
+		    (rc = upload(Y.sd, d->wd[l].s, (size_t)D * 4, dev, g.st)))
+			return rc;
+		if ((rc = upload(Y.ln1, d->ln1[l], (size_t)D * 4, dev, g.st)) || (rc = upload(Y.ln2, d->ln2[l], (size_t)D * 4, dev, g.st)) ||
+		    (rc = upload(Y.qn, d->qn[l], (size_t)HD * 4, dev, g.st)) || (rc = upload(Y.kn, d->kn[l], (size_t)HD * 4, dev, g.st)))
+			return rc;
+	}
+	size_t kv = (size_t)g.L * max_seqs * NKV * (size_t)max_len * HD * 4;
+	if ((rc = g.kc.alloc(kv, dev)) || (rc = g.vc.alloc(kv, dev))) return rc;
+	long R = std::max<long>(PREFILL_ROWS, max_seqs);
+	g.rows_cap = R;
+	if ((rc = g.h.alloc((size_t)R * D * 4, dev)) || (rc = g.xhi.alloc((size_t)R * D * 2, dev)) ||
+	    (rc = g.xlo.alloc((size_t)R * D * 2, dev)) || (rc = g.qkv.alloc((size_t)R * g.HQKV() * 4, dev)) ||
+	    (rc = g.q.alloc((size_t)R * NQ * HD * 4, dev)) || (rc = g.ahi.alloc((size_t)R * NQ * HD * 2, dev)) ||
+	    (rc = g.alo.alloc((size_t)R * NQ * HD * 2, dev)) || (rc = g.ghi.alloc((size_t)R * FF * 2, dev)) ||
+	    (rc = g.glo.alloc((size_t)R * FF * 2, dev)) || (rc = g.logits.alloc((size_t)max_seqs * V * 4, dev)) ||
+	    (rc = g.tok.alloc((size_t)max_seqs * 4, dev)) || (rc = g.ids.alloc((size_t)R * 4, dev)) ||
+	    (rc = g.status.alloc(64, dev)))
+		return rc;
+	TGC_CUDA(cudaMemsetAsync(g.status.p, 0, 64, g.st));
+	TGC_CUDA(cudaStreamSynchronize(g.st));
+	return TG_CUDA_OK;
+}
+
+static GemmArgs gemm_args(int M, int N, int K, int epi)
+{
+	GemmArgs p;
+	memset(&p, 0, sizeof p);
+	p.M = M, p.N = N, p.K = K, p.epi = epi;
+	p.na = 2, p.nb = 1, p.npairs = 2;
+	p.pa[0] = 0, p.pb[0] = 0, p.pa[1] = 1, p.pb[1] = 0;
+	return p;
+}
+
+// One pass of every layer over M rows: T tokens per sequence of the chunk (decode: T = 1 at
+// position pos0), sequences in KV slots slot0.., attention over len positions (decode).
+static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode)
+{
+	int rc;
+	const int D = g.D, HD = g.HD, NQ = g.NQ, NKV = g.NKV, FF = g.FF;
+	const long S = M / T;
+	int *status = g.status.as<int>();
+	const unsigned warps_grid = (unsigned)((M * 32 + 255) / 256);
+	for (int l = 0; l < g.L; l++) {
+		Layer &Y = *g.layers[l];
+		float *kc = g.kc.as<float>() + (size_t)l * g.max_seqs * NKV * (size_t)g.max_len * HD;
+		float *vc = g.vc.as<float>() + (size_t)l * g.max_seqs * NKV * (size_t)g.max_len * HD;
+		k_rmsnorm_split<<<warps_grid, 256, 0, g.st>>>(g.h.as<float>(), M, D, Y.ln1.as<float>(), g.eps, 0,
+							     g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>());
+		GemmOperands op;
+		op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = Y.wqkv.p, op.lda = D, op.ldb = D;
+		GemmArgs p = gemm_args((int)M, g.HQKV(), D, EPI_STORE);
+		p.scale = Y.sqkv.as<float>(), p.scale_mode = 2, p.out = g.qkv.as<float>(), p.ldo = g.HQKV(), p.status = status;
+		if ((rc = gemm(op, p, g.st))) return rc;
+		long heads = M * (NQ + 2 * NKV);
+		k_qk_rope<<<(unsigned)((heads * 32 + 255) / 256), 256, 0, g.st>>>(
+			g.qkv.as<float>(), M, T, pos0, NQ, NKV, g.eps, Y.qn.as<float>(), Y.kn.as<float>(), g.cosT.as<float>(),
+			g.sinT.as<float>(), g.q.as<float>(), kc, vc, slot0, g.max_len);
+		if (!decode) {
+			size_t smem = (size_t)(AQ * APAD + AK * APAD + AK * HD + AQ * 68) * 4;
+			static bool attr[64] = {};
+			if (!attr[g.dev]) {
+				cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+				attr[g.dev] = true;
+			}
+			dim3 grid((T + AQ - 1) / AQ, NQ, (unsigned)S);
+			k_attn_prefill<<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, T, NQ, NKV, slot0, g.max_len, g.scale,
+								  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>());
+		} else {
+			int len = pos0 + 1;
+			size_t smem = (size_t)((NQ / NKV) * ((len + 3) & ~3) + 8 * (NQ / NKV) * HD) * 4;
+			static bool attr[64] = {};
+			if (!attr[g.dev]) {
+				cudaFuncSetAttribute(k_attn_decode<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+				cudaFuncSetAttribute(k_attn_decode<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+				attr[g.dev] = true;
+			}
+			dim3 grid(NKV, (unsigned)S);
+			if (NQ / NKV == 2)
+				k_attn_decode<2><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, len, NQ, NKV, slot0, g.max_len, g.scale,
+									  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>());
+			else
+				k_attn_decode<1><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, len, NQ, NKV, slot0, g.max_len, g.scale,
+									  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>());
+		}
+		TGC_LAUNCH_CHECK();
+		// o_proj with the residual: h += attn @ Wo (hi*hi + hi*lo + lo*hi)
+		op = GemmOperands();
+		op.a[0] = g.ahi.p, op.a[1] = g.alo.p, op.b[0] = Y.wo_hi.p, op.b[1] = Y.wo_lo.p, op.lda = (long)NQ * HD, op.ldb = (long)NQ * HD;
+		p = gemm_args((int)M, D, NQ * HD, EPI_ADD);
+		p.nb = 2, p.npairs = 3;
+		p.pa[0] = 0, p.pb[0] = 0, p.pa[1] = 0, p.pb[1] = 1, p.pa[2] = 1, p.pb[2] = 0;
+		p.out = g.h.as<float>(), p.ldo = D, p.status = status;
+		if ((rc = gemm(op, p, g.st))) return rc;
+		k_rmsnorm_split<<<warps_grid, 256, 0, g.st>>>(g.h.as<float>(), M, D, Y.ln2.as<float>(), g.eps, 0,
+							     g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>());
+		op = GemmOperands();
+		op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = Y.wgu.p, op.lda = D, op.ldb = D;
+		p = gemm_args((int)M, 2 * FF, D, EPI_SWIGLU);
+		p.scale = Y.sg.as<float>(), p.scale2 = Y.su.as<float>(), p.out_hi = g.ghi.as<__nv_bfloat16>(),
+		p.out_lo = g.glo.as<__nv_bfloat16>(), p.ldo = FF, p.status = status;
+		if ((rc = gemm(op, p, g.st))) return rc;
+		op = GemmOperands();
+		op.a[0] = g.ghi.p, op.a[1] = g.glo.p, op.b[0] = Y.wd.p, op.lda = FF, op.ldb = FF;
+		p = gemm_args((int)M, D, FF, EPI_ADD);
+		p.scale = Y.sd.as<float>(), p.scale_mode = 2, p.out = g.h.as<float>(), p.ldo = D, p.status = status;
+		if ((rc = gemm(op, p, g.st))) return rc;
+	}
+	return TG_CUDA_OK;
+}
+
+// Final norm of the last position of each of S sequences (T tokens each), LM head -> logits.
+static int head(Engine &g, long S, int T)
+{
+	int rc;
+	k_rmsnorm_split<<<(unsigned)((S * 32 + 255) / 256), 256, 0, g.st>>>(g.h.as<float>(), S, g.D, g.lnf.as<float>(), g.eps, T,
+									    g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>());
+	TGC_LAUNCH_CHECK();
+	GemmOperands op;
+	op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = g.lmw.p, op.lda = g.D, op.ldb = g.D;
+	GemmArgs p = gemm_args((int)S, g.V, g.D, EPI_STORE);
+	p.scale = g.lms.as<float>(), p.scale_mode = 2, p.out = g.logits.as<float>(), p.ldo = g.V, p.status = g.status.as<int>();
+	if ((rc = gemm(op, p, g.st))) return rc;
+	return TG_CUDA_OK;
+}
+
+// Prefill S sequences (ids on the host, T each) into KV slots slot0..; logits of the last positions.
+static int prefill(Engine &g, const float *ids_host, long S, int T, int slot0, float *logits_host, int *tokens_host,
+		   int ld_tok)
+{
+	int rc;
+	const long chunk = std::max<long>(1, std::min<long>(S, g.rows_cap / T));
+	for (long s0 = 0; s0 < S; s0 += chunk) {
+		long n = std::min(chunk, S - s0), M = n * T;
+		if (fault("h2d")) return set_err(TG_CUDA_EFAULT, "injected copy failure (TG_CUDA_FAULT=h2d)");
+		TGC_CUDA(cudaMemcpyAsync(g.ids.p, ids_host + s0 * T, (size_t)M * 4, cudaMemcpyHostToDevice, g.st));
+		k_embed<<<(unsigned)((M * 32 + 255) / 256), 256, 0, g.st>>>(g.ids.as<float>(), nullptr, M, g.E.as<float>(), g.V, g.D,
+									     g.h.as<float>());
+		TGC_LAUNCH_CHECK();
+		if ((rc = run_layers(g, M, T, 0, slot0 + (int)s0, false))) return rc;
+		if ((rc = head(g, n, T))) return rc;
+		if (logits_host)
+			TGC_CUDA(cudaMemcpyAsync(logits_host + s0 * g.V, g.logits.p, (size_t)n * g.V * 4, cudaMemcpyDeviceToHost, g.st));
+		if (tokens_host) {
+			k_argmax<<<(unsigned)n, 256, 0, g.st>>>(g.logits.as<float>(), g.V, g.tok.as<int>() + s0, nullptr, 0, 0);
+			TGC_LAUNCH_CHECK();
+		}
+	}
+	(void)tokens_host;
+	(void)ld_tok;
+	return TG_CUDA_OK;
+}
+
+static int generate_wave(Engine &g, const float *ids_host, long S, int T, int nnew, int *tokens_host)
+{
+	int rc;
+	if ((rc = prefill(g, ids_host, S, T, 0, nullptr, tokens_host, nnew))) return rc;
+	if ((rc = g.out_tok.ensure((size_t)S * nnew * 4, g.dev))) return rc;
+	// tokens[:, 0] = the prefill's argmax
+	cudaMemcpy2DAsync(g.out_tok.p, (size_t)nnew * 4, g.tok.p, 4, 4, (size_t)S, cudaMemcpyDeviceToDevice, g.st);
+	for (int step = 1; step < nnew; step++) {
+		const int pos = T + step - 1; // position of the token being fed
+		k_embed<<<(unsigned)((S * 32 + 255) / 256), 256, 0, g.st>>>(nullptr, g.tok.as<int>(), S, g.E.as<float>(), g.V, g.D,
+									     g.h.as<float>());
+		TGC_LAUNCH_CHECK();
+		if ((rc = run_layers(g, S, 1, pos, 0, true))) return rc;
+		if ((rc = head(g, S, 1))) return rc;
+		k_argmax<<<(unsigned)S, 256, 0, g.st>>>(g.logits.as<float>(), g.V, g.tok.as<int>(), g.out_tok.as<int>(), nnew, step);
+		TGC_LAUNCH_CHECK();
+	}
+	if (fault("gather")) return set_err(TG_CUDA_EFAULT, "injected gather failure (TG_CUDA_FAULT=gather)");
+	TGC_CUDA(cudaMemcpyAsync(tokens_host, g.out_tok.p, (size_t)S * nnew * 4, cudaMemcpyDeviceToHost, g.st));
+	return TG_CUDA_OK;
+}
+
+} // namespace tgc
 
 using namespace tgc;
 
 struct tg_cuda_lm {
-	int unused;
+	std::vector<std::unique_ptr<Engine>> eng;
 };
+
+static int check_desc(const tg_cuda_lm_desc *d)
+{
+	if (!d) return set_err(TG_CUDA_EINVAL, "NULL descriptor");
+	if (d->head_dim != 128) return set_err(TG_CUDA_EUNSUPPORTED, "head_dim %d: the device kernels are built for 128", d->head_dim);
+	if (d->nkv <= 0 || d->nq % d->nkv || (d->nq / d->nkv != 1 && d->nq / d->nkv != 2))
+		return set_err(TG_CUDA_EUNSUPPORTED, "grouped-query ratio nq/nkv must be 1 or 2");
+	if (d->bits != 8 && d->bits != 4) return set_err(TG_CUDA_EINVAL, "bits must be 8 or 4");
+	if (d->hidden % 64 || d->ffn % 128 || d->hidden < 64)
+		return set_err(TG_CUDA_EUNSUPPORTED, "hidden must be a multiple of 64 and ffn of 128");
+	if (!d->embed || !d->final_norm || !d->lm_head.q || !d->ln1 || !d->wq || !d->wo || !d->wd)
+		return set_err(TG_CUDA_EINVAL, "descriptor has NULL weights");
+	return TG_CUDA_OK;
+}
 
 extern "C" int tg_cuda_lm_load(const tg_cuda_lm_desc *d, int max_seqs, int max_len, tg_cuda_lm **out)
 {
-	(void)d; (void)max_seqs; (void)max_len;
-	if (out) *out = nullptr;
-	return set_err(TG_CUDA_EUNSUPPORTED, "tg_cuda_lm_load: not built yet");
+	clear_err();
+	if (!out) return set_err(TG_CUDA_EINVAL, "tg_cuda_lm_load: NULL out");
+	*out = nullptr;
+	if (!inited()) return set_err(TG_CUDA_ENODEV, "tg_cuda_lm_load: call tg_cuda_init first");
+	int rc = check_desc(d);
+	if (rc) return rc;
+	if (max_seqs <= 0 || max_len <= 0) return set_err(TG_CUDA_EINVAL, "max_seqs and max_len must be positive");
+	tg_cuda_lm *g = new tg_cuda_lm;
+	for (auto &dv : devices()) {
+		g->eng.emplace_back(new Engine);
+		if ((rc = load_engine(*g->eng.back(), d, dv.id, max_seqs, max_len))) {
+			tg_cuda_lm_free(g);
+			return rc;
+		}
+	}
+	cudaSetDevice(devices()[0].id);
+	*out = g;
+	return TG_CUDA_OK;
 }
+
+// Shard nseq sequences over the engines (one host thread each), in waves of max_seqs.
+template <class F>
+static int shard(tg_cuda_lm *g, long nseq, F &&fn)
+{
+	size_t G = g->eng.size();
+	std::vector<int> rcs(G, 0);
+	std::vector<std::string> errs(G);
+	auto work = [&](size_t di) {
+		Engine &e = *g->eng[di];
+		cudaSetDevice(e.dev);
+		long lo = nseq * (long)di / (long)G, hi = nseq * (long)(di + 1) / (long)G;
+		int rc = TG_CUDA_OK;
+		for (long w0 = lo; w0 < hi && !rc; w0 += e.max_seqs) rc = fn(e, w0, std::min<long>(e.max_seqs, hi - w0));
+		if (!rc) {
+			cudaError_t ce = cudaStreamSynchronize(e.st);
+			if (ce != cudaSuccess) rc = set_err(TG_CUDA_ECUDA, "device %d: %s", e.dev, cudaGetErrorString(ce));
+		}
+		if (!rc) rc = device_status_check(e.status.as<int>(), e.st);
+		rcs[di] = rc;
+		if (rc) errs[di] = tg_cuda_error();
+	};
+	if (G == 1) work(0);
+	else {
+		std::vector<std::thread> th;
+		for (size_t di = 0; di < G; di++) th.emplace_back(work, di);
+		for (auto &t : th) t.join();
+	}
+	cudaSetDevice(g->eng[0]->dev);
+	for (size_t di = 0; di < G; di++)
+		if (rcs[di]) return set_err(rcs[di], "%s", errs[di].c_str());
+	return TG_CUDA_OK;
+}
+
 extern "C" int tg_cuda_lm_forward(tg_cuda_lm *g, const float *ids, long nseq, int T, float *logits)
 {
-	(void)g; (void)ids; (void)nseq; (void)T; (void)logits;
-	return set_err(TG_CUDA_EUNSUPPORTED, "tg_cuda_lm_forward: not built yet");
+	clear_err();
+	if (!g || !ids || !logits || nseq < 0 || T <= 0) return set_err(TG_CUDA_EINVAL, "tg_cuda_lm_forward: bad arguments");
+	if (T > g->eng[0]->max_len) return set_err(TG_CUDA_EINVAL, "T %d exceeds max_len %d", T, g->eng[0]->max_len);
+	const int V = g->eng[0]->V;
+	return shard(g, nseq, [&](Engine &e, long w0, long n) {
+		return prefill(e, ids + w0 * T, n, T, 0, logits + w0 * V, nullptr, 0);
+	});
 }
+
 extern "C" int tg_cuda_lm_generate(tg_cuda_lm *g, const float *ids, long nseq, int T, int nnew, int *tokens)
 {
-	(void)g; (void)ids; (void)nseq; (void)T; (void)nnew; (void)tokens;
-	return set_err(TG_CUDA_EUNSUPPORTED, "tg_cuda_lm_generate: not built yet");
+	clear_err();
+	if (!g || !ids || !tokens || nseq < 0 || T <= 0 || nnew <= 0) return set_err(TG_CUDA_EINVAL, "tg_cuda_lm_generate: bad arguments");
+	if (T + nnew - 1 > g->eng[0]->max_len)
+		return set_err(TG_CUDA_EINVAL, "T + nnew - 1 = %d exceeds max_len %d", T + nnew - 1, g->eng[0]->max_len);
+	return shard(g, nseq, [&](Engine &e, long w0, long n) { return generate_wave(e, ids + w0 * T, n, T, nnew, tokens + w0 * nnew); });
 }
-extern "C" void tg_cuda_lm_free(tg_cuda_lm *g) { delete g; }
+
+extern "C" void tg_cuda_lm_free(tg_cuda_lm *g)
+{
+	if (!g) return;
+	for (auto &e : g->eng) {
+		cudaSetDevice(e->dev);
+		if (e->st) {
+			cudaStreamSynchronize(e->st);
+			cudaStreamDestroy(e->st);
+		}
+	}
+	delete g;
+}

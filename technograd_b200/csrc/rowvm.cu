@@ -869,6 +869,9 @@ extern "C" int tg_cuda_load(const tg_cuda_program *p, tg_cuda_model **out)
 		TGC_CUDA(cudaMemcpy(D.blob.p, P.blob.data(), P.blob.size() * sizeof(float), cudaMemcpyHostToDevice));
 		TGC_CUDA(cudaMemcpy(D.inloc.p, P.in_off.data(), P.in_off.size() * sizeof(int), cudaMemcpyHostToDevice));
 		TGC_CUDA(cudaMemcpy(D.inlen.p, P.in_len.data(), P.in_len.size() * sizeof(int), cudaMemcpyHostToDevice));
+		// copies from pageable memory may still be in flight on return; later kernels run on
+		// non-blocking streams, so wait for them here
+		TGC_CUDA(cudaDeviceSynchronize());
 		TGC_CUDA(cudaFuncSetAttribute(vm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
 	}
 	cudaSetDevice(devices()[0].id);

@@ -111,3 +111,28 @@ def test_live_reference_kernels():
             qa, sa = tgo.quantize(tgo.tgo(), "tgo_", w, axis, bits, h)
             qb, sb = tgo.quantize(R, "ref_", w, axis, bits, h)
             assert np.array_equal(qa, qb) and np.array_equal(sa, sb)
+
+
+def _nano_cfg(golden):
+    kv = dict(x.split("=") for x in open(os.path.join(golden, "nano", "config.txt")).read().split())
+    return {k: (float(v) if k == "theta" else int(v)) for k, v in kv.items()}
+
+
+@pytest.mark.parametrize("tag", ["q8", "q4", "q4gptq"])
+def test_lm_oracle_matches_tgc_on_the_qwen3_program(golden, tag):
+    """tgo_lm_forward restates the program examples/qwen3/import.py emits; the reference
+    ran that program (quantized by `tgc quantize`) through `tgc batch`."""
+    import ctypes as C
+
+    from technograd_b200 import lm
+    cfg = _nano_cfg(golden)
+    model = lm.Model.from_tgir(os.path.join(golden, "nano", f"{tag}.tgir.gz"), cfg)
+    d, keep = model.desc()
+    ids = np.loadtxt(os.path.join(golden, "nano", "ids.csv"), delimiter=",", dtype=np.float32)
+    want = np.loadtxt(os.path.join(golden, "nano", f"{tag}_logits.csv"), delimiter=",", dtype=np.float64).astype(np.float32)
+    L = tgo.tgo()
+    for r in range(ids.shape[0]):
+        out = np.zeros(cfg["vocab"], np.float32)
+        L.tgo_lm_forward(C.addressof(d), tgo.f32p(np.ascontiguousarray(ids[r])), ids.shape[1], tgo.f32p(out))
+        np.testing.assert_allclose(out, want[r], rtol=1e-5, atol=1e-6)
+        assert out.argmax() == want[r].argmax()
