@@ -1,18 +1,24 @@
 """Benchmark of the batch backend (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload lr|gemv] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|lr] [--impl ours|reference]
 
-Workloads (synthetic seeded inputs of the stated shapes):
-  lr    config 1: latent_reasoner int8 (RTN, --min-size 1), 1,048,576 rows of f32[8]
-        with Bernoulli(0.5) entries (seed 1) per GPU; unit rows/s.
-  gemv  config 2: int4 dequant GEMV, W [4096, 4096] codes uniform in [-8, 7],
-        x f32 [4096] ~ N(0,1) (seed 2); unit GB/s of algorithmic bytes.
+Workloads (seeded synthetic inputs of the stated shapes):
+  decode  config 5, the headline: Qwen3-0.6B architecture (28 layers, hidden 1024,
+          16/8 heads x 128, SwiGLU 3072, vocab 151936), random init N(0, 0.02),
+          int4 GPTQ per output column against 256 seeded N(0,1) calibration rows
+          per input width (the 3072-wide down projection RTN, as src/quant.c:346
+          does), greedy decode: 2048 sequences of 1024 uniform-random ids, each
+          continued by 257 argmax tokens (the prefill's plus 256 decode steps over
+          the KV cache). Sequences shard over ranks (2048/N each) and run in waves of
+          at most 256 per GPU; one step = one wave. Unit: generated tokens/s.
+  lr      config 1: latent_reasoner int8 RTN (--min-size 1), 1,048,576 rows of f32[8]
+          with Bernoulli(0.5) entries (seed 1) per GPU; unit rows/s.
 
-A step is one pass of the hot path over the whole per-GPU input. value is the
-whole-job throughput with inputs resident in HBM (CUDA events on the launching
-stream, max over ranks); e2e is the same metric through the C ABI with host
-buffers, the copies inside the timed region. Under torchrun each rank runs the
-same per-GPU workload (weak scaling, no collective on the data path).
+value: the device time of each step (CUDA events on the stream the library
+launches on, first to last launch), summed over steps, max over ranks. e2e: the
+same steps timed around the synchronous C-ABI call with host buffers (ids in,
+tokens out). Under torchrun every rank runs its own shard (weak scaling: the
+per-GPU work of a step is fixed), no collective on the data path.
 """
 from __future__ import annotations
 
@@ -25,6 +31,7 @@ import statistics
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 
 import numpy as np
@@ -34,13 +41,13 @@ sys.path.insert(0, ROOT)
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # 74.4: 148 SMs x 128 FP32 lanes x FMA x 1965 MHz
+TOTAL_SEQS, PROMPT, NEW, WAVE = 2048, 1024, 257, 256
 
 
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
-        d = json.load(open(p))
-        return d, "measured"
+        return json.load(open(p)), "measured"
     return PEAKS_FALLBACK, "fallback"
 
 
@@ -64,29 +71,35 @@ class Clocks:
         self.p.terminate()
         self.p.wait()
         self.f.seek(0)
-        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        rows = [[x.strip() for x in r.split(",")] for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
         os.unlink(self.f.name)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [v for v in (num(r[1]) for r in rows) if v is not None]
+        mx = [v for v in (num(r[2]) for r in rows) if v is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(rows)}
 
 
-def dist_setup(n_gpus: int):
+def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         import datetime
 
-        import torch.distributed as dist
         import torch
+        import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     return world, rank, local
 
 
@@ -106,11 +119,113 @@ def barrier(world: int) -> None:
         dist.barrier()
 
 
-def flush_l2(buf) -> None:
-    buf.add_(1.0)  # 256 MB write: larger than the 126 MB L2
+# ---- config 5: int4 GPTQ Qwen3-0.6B-shape greedy decode ----------------------------------------
+
+def decode_ids() -> np.ndarray:
+    return np.random.default_rng(5).integers(0, 151936, size=(TOTAL_SEQS, PROMPT)).astype(np.float32)
 
 
-# ---- config 1: latent_reasoner ----------------------------------------------------------------
+def bench_decode(args, world, rank, local):
+    import torch
+
+    from technograd_b200 import _lib, lm
+    _lib.init(0, [local])
+    torch.cuda.set_device(local)
+    cfg = lm.QWEN3_0_6B
+    t0 = time.perf_counter()
+    built = lm.DeviceBuilt(cfg, bits=4, method="gptq", seed=5)
+    t_build = time.perf_counter() - t0
+    shard = TOTAL_SEQS // world
+    wave = min(WAVE, shard)
+    ids = decode_ids()[rank * shard:(rank + 1) * shard]
+    nwaves = (shard + wave - 1) // wave
+    eng = lm.Engine(built, max_seqs=wave, max_len=PROMPT + NEW - 1, devices=[local])
+
+    def step(i):
+        w = i % nwaves
+        return eng.generate(ids[w * wave:(w + 1) * wave], NEW)
+
+    for i in range(args.warmup):
+        step(i)
+    eng.profile(True)
+    barrier(world)
+    clk = Clocks(local)
+    dev_ms, wall, stats = [], [], []
+    for i in range(args.steps):
+        t = time.perf_counter()
+        tok = step(args.warmup + i)
+        wall.append(time.perf_counter() - t)
+        s = eng.stats()
+        stats.append(s)
+        dev_ms.append(s["device_ms"])
+    barrier(world)
+    clocks = clk.stop()
+    t_dev = max_over_ranks(sum(dev_ms) / 1e3, world)
+    t_wall = max_over_ranks(sum(wall), world)
+    tokens_step = wave * NEW
+    value = world * tokens_step * args.steps / t_dev
+    pk, src = peaks()
+    dec_bytes = sum(s["attn_decode_bytes"] for s in stats)
+    dec_ms = sum(s["attn_decode_ms"] for s in stats)
+    dec_launches = sum(s["attn_decode_launches"] for s in stats)
+    achieved = dec_bytes / (dec_ms / 1e3) / 1e9
+    gemm_tf = sum(s["gemm_flops"] for s in stats) / (sum(s["gemm_ms"] for s in stats) / 1e3) / 1e12
+    pre_tf = sum(s["attn_prefill_flops"] for s in stats) / (sum(s["attn_prefill_ms"] for s in stats) / 1e3) / 1e12
+    tot_ms = sum(dev_ms)
+    line = {
+        "metric": "int4 Qwen3-0.6B-shape greedy decode tokens/s (config 5)", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
+        "data": "synthetic: random-init weights N(0,0.02), uniform-random prompt ids (seed 5)",
+        "config": {"workload": "config5 int4 GPTQ Qwen3-0.6B-shape: 2048 seqs x 1024-token prompts + 256 decode steps",
+                   "seqs_per_step_per_gpu": wave, "prompt": PROMPT, "new_tokens_per_seq": NEW,
+                   "steps_for_full_job": (TOTAL_SEQS // world + wave - 1) // wave,
+                   "kv_cache": "f32, per GPU 75 GB at 256 seqs x 1280 positions",
+                   "l2": "inputs larger than L2 (KV cache of 75 GB streamed every decode step)",
+                   "share_of_step": {"attn_decode": dec_ms / tot_ms, "gemm": sum(s["gemm_ms"] for s in stats) / tot_ms,
+                                     "attn_prefill": sum(s["attn_prefill_ms"] for s in stats) / tot_ms},
+                   "gemm_tflops": gemm_tf, "attn_prefill_tflops_f32": pre_tf, "build_s": t_build},
+        "roofline": {"kernel": "k_attn_decode (KV-cache attention)", "bound": "hbm", "achieved": achieved,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "peak_source": src,
+                     "traffic": None, "bytes_per_launch": dec_bytes / max(dec_launches, 1),
+                     "ms_per_launch": dec_ms / max(dec_launches, 1)},
+        "e2e": {"value": world * tokens_step * args.steps / t_wall, "unit": "tokens/s",
+                "h2d_bytes_per_step": wave * PROMPT * 4, "d2h_bytes_per_step": wave * NEW * 4},
+        "gpu_launches": int(sum(s["launches"] for s in stats)), "clocks": clocks,
+    }
+    return line, built, tok
+
+
+def cpu_baseline_decode(built, seconds_budget: float = 30.0):
+    """The oracle port of the reference VM (tgo_lm_forward: the same arithmetic as `tgc batch`
+    over the Qwen3 program, pinned bit-exact to the reference in tests/test_oracle.py) on the
+    host cores: one teacher-forced next token per sequence. The reference has no KV cache, so
+    each new token costs a full forward of the prefix; the sample uses a 16-token prefix."""
+    from oracle import tgo
+    d, keep = built.desc()
+    L = tgo.tgo()
+    threads = os.cpu_count() or 1
+    T = 16
+    ids = np.random.default_rng(5).integers(0, 151936, size=(threads, T)).astype(np.float32)
+    out = np.zeros((threads, 151936), np.float32)
+
+    def work(r):
+        L.tgo_lm_forward(C.addressof(d), tgo.f32p(np.ascontiguousarray(ids[r])), T, out[r].ctypes.data_as(tgo.FP))
+
+    t0 = time.perf_counter()
+    th = [threading.Thread(target=work, args=(r,)) for r in range(threads)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    dt = time.perf_counter() - t0
+    return {"value": threads / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{threads} sequences x 1 teacher-forced token at a {T}-token prefix (full Qwen3-0.6B shape, "
+                      f"int4 GPTQ codes), one thread per sequence, {dt:.1f} s; at the config's 1024-1280-token "
+                      f"prefixes each token costs ~64-80x more"}
+
+
+# ---- config 1: latent_reasoner -----------------------------------------------------------------
 LR_ROWS = 1 << 20
 
 
@@ -128,8 +243,7 @@ def bench_lr(args, world, rank, local):
 
     from technograd_b200 import _lib, tgir
     from technograd_b200.batch import Batch
-    model = os.path.join(ROOT, "tests", "golden", "latent_reasoner.q8.tgir")
-    m = tgir.load(model)
+    m = tgir.load(os.path.join(ROOT, "tests", "golden", "latent_reasoner.q8.tgir"))
     rows = lr_inputs(LR_ROWS)
     _lib.init(0, [local])
     b = Batch(m)
@@ -150,9 +264,8 @@ def bench_lr(args, world, rank, local):
     barrier(world)
     clk = Clocks(local)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    torch.cuda.synchronize()
     for i in range(args.steps):
-        flush_l2(flush)
+        flush.add_(1.0)  # 256 MB write between steps: larger than the 126 MB L2
         ev[i][0].record(stream)
         step()
         ev[i][1].record(stream)
@@ -162,10 +275,7 @@ def bench_lr(args, world, rank, local):
     ms = [a.elapsed_time(z) for a, z in ev]
     t = max_over_ranks(sum(ms) / 1e3, world)
     steps_np = d_steps.cpu().numpy()
-    value = world * LR_ROWS * args.steps / t
-    flops = lr_flops(steps_np)
-    achieved = flops / (t / args.steps) / 1e12
-    # e2e: host buffers through tg_cuda_batch (H2D + kernel + D2H per step)
+    achieved = lr_flops(steps_np) / (t / args.steps) / 1e12
     out_h = np.empty((LR_ROWS, 4), np.float32)
     st_h = np.empty((LR_ROWS, 1), np.int32)
     for _ in range(2):
@@ -175,23 +285,24 @@ def bench_lr(args, world, rank, local):
     for _ in range(args.steps):
         _lib.check(L.tg_cuda_batch(b.handle, rows.ctypes.data, LR_ROWS, 8, out_h.ctypes.data, 4, st_h.ctypes.data, 1))
     te = max_over_ranks(time.perf_counter() - t0, world)
-    e2e = {"value": world * LR_ROWS * args.steps / te, "unit": "rows/s", "h2d_bytes_per_step": rows.nbytes,
-           "d2h_bytes_per_step": out_h.nbytes + st_h.nbytes}
     line = {
-        "metric": "latent_reasoner int8 batch rows/s (config 1)", "value": value, "unit": "rows/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sum(ms) / len(ms),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "metric": "latent_reasoner int8 batch rows/s (config 1)", "value": world * LR_ROWS * args.steps / t,
+        "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sum(ms) / len(ms), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
         "config": {"workload": "config1 latent_reasoner int8 RTN --min-size 1", "rows_per_gpu": LR_ROWS,
                    "think_steps_mean": float(steps_np.mean()), "l2": "flushed between steps (256 MB write)"},
-        "roofline": {"bound": "fp32", "achieved": achieved, "peak": FP32_NOMINAL_TFLOPS, "unit": "TFLOP/s",
-                     "frac": achieved / FP32_NOMINAL_TFLOPS, "traffic": None,
+        "roofline": {"kernel": "vm_kernel", "bound": "fp32", "achieved": achieved, "peak": FP32_NOMINAL_TFLOPS,
+                     "unit": "TFLOP/s", "frac": achieved / FP32_NOMINAL_TFLOPS, "traffic": None,
                      "peak_source": "nominal FP32 SIMT (148 SMs x 128 lanes x FMA x 1965 MHz); not in MEASURED_PEAKS"},
-        "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
+        "e2e": {"value": world * LR_ROWS * args.steps / te, "unit": "rows/s", "h2d_bytes_per_step": rows.nbytes,
+                "d2h_bytes_per_step": out_h.nbytes + st_h.nbytes},
+        "gpu_launches": args.steps, "clocks": clocks,
     }
-    return line, m, rows
+    return line, rows
 
 
-def cpu_baseline_lr(rows: np.ndarray, sample: int = LR_ROWS):
+def cpu_baseline_lr(rows: np.ndarray):
     """The reference's own `tgc batch -j auto` (oracle/_ref/tgc, compiled from its sources) on the host cores."""
     from oracle import tgo
     tgc = tgo.REF_TGC
@@ -200,7 +311,7 @@ def cpu_baseline_lr(rows: np.ndarray, sample: int = LR_ROWS):
     model = os.path.join(ROOT, "tests", "golden", "latent_reasoner.q8.tgir")
     with tempfile.TemporaryDirectory() as d:
         inp = os.path.join(d, "rows.bin")
-        rows[:sample].astype("<f4").tofile(inp)
+        rows.astype("<f4").tofile(inp)
         r = subprocess.run([tgc, "batch", model, inp, "-j", "auto", "-v", "-o", os.path.join(d, "out.bin")],
                            capture_output=True, text=True, check=True)
     mt = re.search(r"\[batch\] (\d+) row\(s\) in ([0-9.]+) ms .* on (\d+) thread", r.stderr)
@@ -209,56 +320,67 @@ def cpu_baseline_lr(rows: np.ndarray, sample: int = LR_ROWS):
             "sample": f"{n} rows of config 1, `tgc batch -j auto` binary I/O, [batch] event time"}
 
 
-def reference_arm(args, world, rank):
+# ---- the reference arm --------------------------------------------------------------------------
+
+def reference_arm(args, world, rank, local):
     if rank != 0:
         return None
-    rows = lr_inputs(LR_ROWS)
-    vals = []
-    base = None
-    for _ in range(args.warmup):
-        cpu_baseline_lr(rows)
-    for _ in range(args.steps):
-        base = cpu_baseline_lr(rows)
-        if base is None:
-            break
-        vals.append(base["value"])
-    if base is None:
-        return {"impl": "reference", "unavailable": "oracle/_ref/tgc was not built (needs the reference sources)"}
+    if args.workload == "lr":
+        rows = lr_inputs(LR_ROWS)
+        for _ in range(args.warmup):
+            cpu_baseline_lr(rows)
+        vals, base = [], None
+        for _ in range(args.steps):
+            base = cpu_baseline_lr(rows)
+            if base is None:
+                return {"impl": "reference", "unavailable": "oracle/_ref/tgc was not built (needs the reference sources)"}
+            vals.append(base["value"])
+        metric, unit, cfgw = "latent_reasoner int8 batch rows/s (config 1)", "rows/s", "config1 latent_reasoner int8 RTN --min-size 1"
+    else:
+        # the model is generated on the GPU (same seeds as our arm), then the CPU port runs
+        from technograd_b200 import _lib, lm
+        _lib.init(0, [local])
+        built = lm.DeviceBuilt(lm.QWEN3_0_6B, bits=4, method="gptq", seed=5)
+        vals, base = [], None
+        for _ in range(args.steps):
+            base = cpu_baseline_decode(built)
+            vals.append(base["value"])
+        metric, unit = "int4 Qwen3-0.6B-shape greedy decode tokens/s (config 5)", "tokens/s"
+        cfgw = "config5 int4 GPTQ Qwen3-0.6B-shape: 2048 seqs x 1024-token prompts + 256 decode steps"
     v = statistics.median(vals)
     base["value"] = v
-    return {"impl": "reference", "metric": "latent_reasoner int8 batch rows/s (config 1)", "value": v,
-            "unit": "rows/s", "n_gpus": 0, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config1 latent_reasoner int8 RTN --min-size 1", "rows_per_gpu": LR_ROWS},
-            "cpu_baseline": base, "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    return {"impl": "reference", "metric": metric, "value": v, "unit": unit, "n_gpus": 0, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": cfgw}, "cpu_baseline": base,
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="lr")
-    ap.add_argument("--impl", default="ours")
+    ap.add_argument("--workload", default="decode", choices=["decode", "lr"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    world, rank, local = dist_setup(args.gpus)
+    world, rank, local = dist_setup()
     if args.impl == "reference":
-        line = reference_arm(args, world, rank)
-        if rank == 0 and line:
-            print(json.dumps(line), flush=True)
-        if world > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
-        return
-    line, m, rows = bench_lr(args, world, rank, local)
-    if rank == 0:
-        if world == 1 and not args.no_cpu_baseline:
+        line = reference_arm(args, world, rank, local)
+    elif args.workload == "lr":
+        line, rows = bench_lr(args, world, rank, local)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_lr(rows)
+    else:
+        line, built, _ = bench_decode(args, world, rank, local)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_decode(built)
+    if rank == 0 and line:
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
+        barrier(world)
         dist.destroy_process_group()
 
 

@@ -64,6 +64,20 @@ int tg_cuda_matmul_q(int axis, float *o, const float *act, const signed char *q,
  * f32 scale per channel. */
 int tg_cuda_quantize_rtn(const float *w, int rows, int cols, int axis, int bits, signed char *q, float *s, void *stream);
 
+/* GPTQ, bit-exact with quant.c (src/quant.c:92-316, the GPTQ branch of
+ * quantize_param). prepare: the Hessian of nrows calibration rows of K inputs
+ * (HOST memory), dampened 1%, and the upper Cholesky factor of its inverse,
+ * kept on the current device. quantize: like tg_cuda_quantize_rtn (device
+ * pointers) with K = the non-channel extent; a Hessian that is not positive
+ * definite keeps the Hessian-weighted scale search without error feedback, as
+ * the reference does. The reference only calibrates inputs of at most 2048
+ * (src/quant.c:346); wider layers are the caller's RTN. */
+typedef struct tg_cuda_gptq tg_cuda_gptq;
+int tg_cuda_gptq_prepare(const float *calib, int nrows, int K, tg_cuda_gptq **out);
+int tg_cuda_quantize_gptq(tg_cuda_gptq *g, const float *w, int rows, int cols, int axis, int bits, signed char *q, float *s,
+			  void *stream);
+void tg_cuda_gptq_free(tg_cuda_gptq *g);
+
 /* ---- programs ------------------------------------------------------------- */
 /* A planned TGIR program, flattened. The host builds it from its Module
  * (src/tg.h:112-200); the numbering of ops is the reference's enum Op. */
@@ -172,6 +186,26 @@ int tg_cuda_lm_forward(tg_cuda_lm *g, const float *ids, long nseq, int T, float 
  * each step feeding the previous token back through a per-sequence KV cache. */
 int tg_cuda_lm_generate(tg_cuda_lm *g, const float *ids, long nseq, int T, int nnew, int *tokens);
 void tg_cuda_lm_free(tg_cuda_lm *g);
+
+/* Measurements of the last tg_cuda_lm_forward / _generate call (no reference
+ * counterpart: the reference's --profile times VM instructions, src/vm.c:100-193).
+ * Times are CUDA-event device times on the engine streams; with several devices,
+ * device_ms is the maximum and the rest are sums. Per-kernel-class times are
+ * collected only after tg_cuda_lm_profile(g, 1). */
+typedef struct {
+	double device_ms;          /* first to last launch of the call */
+	long launches;             /* kernels the call launched */
+	double attn_decode_ms;     /* KV-cache attention launches */
+	double attn_decode_bytes;  /* their algorithmic bytes: K and V rows read, q read, output written */
+	long attn_decode_launches;
+	double attn_prefill_ms;    /* causal attention of the prefill */
+	double attn_prefill_flops; /* 4 * head_dim per (query, key) pair kept by the causal mask */
+	double gemm_ms;            /* tensor-core GEMMs */
+	double gemm_flops;         /* 2 M N K per GEMM (the useful work, not the bf16 hi/lo passes) */
+	long gemm_launches;
+} tg_cuda_lm_stats;
+int tg_cuda_lm_profile(tg_cuda_lm *g, int enable);
+int tg_cuda_lm_get_stats(const tg_cuda_lm *g, tg_cuda_lm_stats *out);
 
 #ifdef __cplusplus
 }

@@ -23,8 +23,9 @@ PARAM, INPUT, TMP, STATE = 0, 1, 2, 3
 
 # Every entry point include/tg_cuda.h declares.
 SYMBOLS = ["tg_cuda_error", "tg_cuda_init", "tg_cuda_ngpus", "tg_cuda_shutdown", "tg_cuda_matmul_q",
-           "tg_cuda_quantize_rtn", "tg_cuda_load", "tg_cuda_batch", "tg_cuda_batch_device", "tg_cuda_free",
-           "tg_cuda_lm_load", "tg_cuda_lm_forward", "tg_cuda_lm_generate", "tg_cuda_lm_free"]
+           "tg_cuda_quantize_rtn", "tg_cuda_gptq_prepare", "tg_cuda_quantize_gptq", "tg_cuda_gptq_free", "tg_cuda_load", "tg_cuda_batch", "tg_cuda_batch_device", "tg_cuda_free",
+           "tg_cuda_lm_load", "tg_cuda_lm_forward", "tg_cuda_lm_generate", "tg_cuda_lm_free", "tg_cuda_lm_profile",
+           "tg_cuda_lm_get_stats"]
 
 
 class TgCudaError(RuntimeError):
@@ -75,6 +76,13 @@ class LmDesc(C.Structure):
                 ("wq", QP), ("wk", QP), ("wv", QP), ("wo", QP), ("wg", QP), ("wu", QP), ("wd", QP)]
 
 
+class LmStats(C.Structure):
+    _fields_ = [("device_ms", C.c_double), ("launches", C.c_long), ("attn_decode_ms", C.c_double),
+                ("attn_decode_bytes", C.c_double), ("attn_decode_launches", C.c_long), ("attn_prefill_ms", C.c_double),
+                ("attn_prefill_flops", C.c_double), ("gemm_ms", C.c_double), ("gemm_flops", C.c_double),
+                ("gemm_launches", C.c_long)]
+
+
 _lib = None
 
 
@@ -93,6 +101,9 @@ def lib() -> C.CDLL:
             "tg_cuda_shutdown": ([], None),
             "tg_cuda_matmul_q": ([i, vp, vp, vp, i, vp, i, i, i, vp], i),
             "tg_cuda_quantize_rtn": ([vp, i, i, i, i, vp, vp, vp], i),
+            "tg_cuda_gptq_prepare": ([vp, i, i, C.POINTER(vp)], i),
+            "tg_cuda_quantize_gptq": ([vp, vp, i, i, i, i, vp, vp, vp], i),
+            "tg_cuda_gptq_free": ([vp], None),
             "tg_cuda_load": ([C.POINTER(Program), C.POINTER(vp)], i),
             "tg_cuda_batch": ([vp, vp, l, i, vp, i, vp, i], i),
             "tg_cuda_batch_device": ([vp, vp, l, vp, vp, vp], i),
@@ -101,6 +112,8 @@ def lib() -> C.CDLL:
             "tg_cuda_lm_forward": ([vp, vp, l, i, vp], i),
             "tg_cuda_lm_generate": ([vp, vp, l, i, i, vp], i),
             "tg_cuda_lm_free": ([vp], None),
+            "tg_cuda_lm_profile": ([vp, i], i),
+            "tg_cuda_lm_get_stats": ([vp, C.POINTER(LmStats)], i),
         }
         for name, (args, res) in sigs.items():
             f = getattr(L, name)

@@ -467,7 +467,83 @@ struct Engine {
 	long rows_cap = 0;
 	DevBuf h, xhi, xlo, qkv, q, ahi, alo, ghi, glo, logits, tok, ids, status, out_tok;
 	int HQKV() const { return (NQ + 2 * NKV) * HD; }
+	// measurements of the current call (tg_cuda_lm_stats)
+	bool prof = false;
+	long launches = 0;
+	cudaEvent_t ev_start = nullptr, ev_end = nullptr;
+	struct Mark {
+		cudaEvent_t a = nullptr, b = nullptr;
+		int cls = 0;
+		double work = 0;
+	};
+	std::vector<Mark> marks;
+	size_t nmarks = 0;
+	tg_cuda_lm_stats last;
 };
+
+enum { MK_DECODE = 1, MK_PREFILL = 2, MK_GEMM = 3 };
+
+// A pair of events around one launch of class cls (only while profiling).
+static int mark_begin(Engine &g, int cls, double work)
+{
+	g.launches++;
+	if (!g.prof) return -1;
+	if (g.nmarks == g.marks.size()) {
+		Engine::Mark m;
+		cudaEventCreate(&m.a);
+		cudaEventCreate(&m.b);
+		g.marks.push_back(m);
+	}
+	Engine::Mark &m = g.marks[g.nmarks];
+	m.cls = cls;
+	m.work = work;
+	cudaEventRecord(m.a, g.st);
+	return (int)g.nmarks++;
+}
+
+static void mark_end(Engine &g, int i)
+{
+	if (i >= 0) cudaEventRecord(g.marks[i].b, g.st);
+}
+
+static int gemm_m(Engine &g, const GemmOperands &op, const GemmArgs &p)
+{
+	int mk = mark_begin(g, MK_GEMM, 2.0 * p.M * p.N * p.K);
+	int rc = gemm(op, p, g.st);
+	mark_end(g, mk);
+	return rc;
+}
+
+static void call_begin(Engine &g)
+{
+	if (!g.ev_start) {
+		cudaEventCreate(&g.ev_start);
+		cudaEventCreate(&g.ev_end);
+	}
+	g.launches = 0;
+	g.nmarks = 0;
+	cudaEventRecord(g.ev_start, g.st);
+}
+
+// After the stream is synchronized: the call's statistics.
+static void call_end(Engine &g)
+{
+	tg_cuda_lm_stats &t = g.last;
+	memset(&t, 0, sizeof t);
+	float ms = 0;
+	cudaEventElapsedTime(&ms, g.ev_start, g.ev_end);
+	t.device_ms = ms;
+	t.launches = g.launches;
+	for (size_t i = 0; i < g.nmarks; i++) {
+		float e = 0;
+		cudaEventElapsedTime(&e, g.marks[i].a, g.marks[i].b);
+		switch (g.marks[i].cls) {
+		case MK_DECODE: t.attn_decode_ms += e, t.attn_decode_bytes += g.marks[i].work, t.attn_decode_launches++; break;
+		case MK_PREFILL: t.attn_prefill_ms += e, t.attn_prefill_flops += g.marks[i].work; break;
+		case MK_GEMM: t.gemm_ms += e, t.gemm_flops += g.marks[i].work, t.gemm_launches++; break;
+		}
+	}
+}
 
 // Host -> device copy ordered on the engine's stream and complete on return. (A plain
 // cudaMemcpy from pageable memory may return before its DMA lands, and kernels on a
@@ -600,13 +676,14 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 		Layer &Y = *g.layers[l];
 		float *kc = g.kc.as<float>() + (size_t)l * g.max_seqs * NKV * (size_t)g.max_len * HD;
 		float *vc = g.vc.as<float>() + (size_t)l * g.max_seqs * NKV * (size_t)g.max_len * HD;
+		g.launches += 3; // two norms and the q/k rope of this layer
 		k_rmsnorm_split<<<warps_grid, 256, 0, g.st>>>(g.h.as<float>(), M, D, Y.ln1.as<float>(), g.eps, 0,
 							     g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>());
 		GemmOperands op;
 		op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = Y.wqkv.p, op.lda = D, op.ldb = D;
 		GemmArgs p = gemm_args((int)M, g.HQKV(), D, EPI_STORE);
 		p.scale = Y.sqkv.as<float>(), p.scale_mode = 2, p.out = g.qkv.as<float>(), p.ldo = g.HQKV(), p.status = status;
-		if ((rc = gemm(op, p, g.st))) return rc;
+		if ((rc = gemm_m(g, op, p))) return rc;
 		long heads = M * (NQ + 2 * NKV);
 		k_qk_rope<<<(unsigned)((heads * 32 + 255) / 256), 256, 0, g.st>>>(
 			g.qkv.as<float>(), M, T, pos0, NQ, NKV, g.eps, Y.qn.as<float>(), Y.kn.as<float>(), g.cosT.as<float>(),
@@ -619,8 +696,10 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 				attr[g.dev] = true;
 			}
 			dim3 grid((T + AQ - 1) / AQ, NQ, (unsigned)S);
+			int mk = mark_begin(g, MK_PREFILL, 4.0 * HD * (double)T * (T + 1) / 2 * NQ * S);
 			k_attn_prefill<<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, T, NQ, NKV, slot0, g.max_len, g.scale,
 								  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>());
+			mark_end(g, mk);
 		} else {
 			int len = pos0 + 1;
 			size_t smem = (size_t)((NQ / NKV) * ((len + 3) & ~3) + 8 * (NQ / NKV) * HD) * 4;
@@ -631,12 +710,15 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 				attr[g.dev] = true;
 			}
 			dim3 grid(NKV, (unsigned)S);
+			double bytes = (double)S * NKV * len * HD * 4 * 2 + (double)S * NQ * HD * 4 + (double)S * NQ * HD * 4;
+			int mk = mark_begin(g, MK_DECODE, bytes);
 			if (NQ / NKV == 2)
 				k_attn_decode<2><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, len, NQ, NKV, slot0, g.max_len, g.scale,
 									  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>());
 			else
 				k_attn_decode<1><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, len, NQ, NKV, slot0, g.max_len, g.scale,
 									  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>());
+			mark_end(g, mk);
 		}
 		TGC_LAUNCH_CHECK();
 		// o_proj with the residual: h += attn @ Wo (hi*hi + hi*lo + lo*hi)
@@ -646,7 +728,7 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 		p.nb = 2, p.npairs = 3;
 		p.pa[0] = 0, p.pb[0] = 0, p.pa[1] = 0, p.pb[1] = 1, p.pa[2] = 1, p.pb[2] = 0;
 		p.out = g.h.as<float>(), p.ldo = D, p.status = status;
-		if ((rc = gemm(op, p, g.st))) return rc;
+		if ((rc = gemm_m(g, op, p))) return rc;
 		k_rmsnorm_split<<<warps_grid, 256, 0, g.st>>>(g.h.as<float>(), M, D, Y.ln2.as<float>(), g.eps, 0,
 							     g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>());
 		op = GemmOperands();
@@ -654,12 +736,12 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 		p = gemm_args((int)M, 2 * FF, D, EPI_SWIGLU);
 		p.scale = Y.sg.as<float>(), p.scale2 = Y.su.as<float>(), p.out_hi = g.ghi.as<__nv_bfloat16>(),
 		p.out_lo = g.glo.as<__nv_bfloat16>(), p.ldo = FF, p.status = status;
-		if ((rc = gemm(op, p, g.st))) return rc;
+		if ((rc = gemm_m(g, op, p))) return rc;
 		op = GemmOperands();
 		op.a[0] = g.ghi.p, op.a[1] = g.glo.p, op.b[0] = Y.wd.p, op.lda = FF, op.ldb = FF;
 		p = gemm_args((int)M, D, FF, EPI_ADD);
 		p.scale = Y.sd.as<float>(), p.scale_mode = 2, p.out = g.h.as<float>(), p.ldo = D, p.status = status;
-		if ((rc = gemm(op, p, g.st))) return rc;
+		if ((rc = gemm_m(g, op, p))) return rc;
 	}
 	return TG_CUDA_OK;
 }
@@ -668,6 +750,7 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 static int head(Engine &g, long S, int T)
 {
 	int rc;
+	g.launches++;
 	k_rmsnorm_split<<<(unsigned)((S * 32 + 255) / 256), 256, 0, g.st>>>(g.h.as<float>(), S, g.D, g.lnf.as<float>(), g.eps, T,
 									    g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>());
 	TGC_LAUNCH_CHECK();
@@ -675,7 +758,7 @@ static int head(Engine &g, long S, int T)
 	op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = g.lmw.p, op.lda = g.D, op.ldb = g.D;
 	GemmArgs p = gemm_args((int)S, g.V, g.D, EPI_STORE);
 	p.scale = g.lms.as<float>(), p.scale_mode = 2, p.out = g.logits.as<float>(), p.ldo = g.V, p.status = g.status.as<int>();
-	if ((rc = gemm(op, p, g.st))) return rc;
+	if ((rc = gemm_m(g, op, p))) return rc;
 	return TG_CUDA_OK;
 }
 
@@ -689,6 +772,7 @@ static int prefill(Engine &g, const float *ids_host, long S, int T, int slot0, f
 		long n = std::min(chunk, S - s0), M = n * T;
 		if (fault("h2d")) return set_err(TG_CUDA_EFAULT, "injected copy failure (TG_CUDA_FAULT=h2d)");
 		TGC_CUDA(cudaMemcpyAsync(g.ids.p, ids_host + s0 * T, (size_t)M * 4, cudaMemcpyHostToDevice, g.st));
+		g.launches++;
 		k_embed<<<(unsigned)((M * 32 + 255) / 256), 256, 0, g.st>>>(g.ids.as<float>(), nullptr, M, g.E.as<float>(), g.V, g.D,
 									     g.h.as<float>());
 		TGC_LAUNCH_CHECK();
@@ -697,6 +781,7 @@ static int prefill(Engine &g, const float *ids_host, long S, int T, int slot0, f
 		if (logits_host)
 			TGC_CUDA(cudaMemcpyAsync(logits_host + s0 * g.V, g.logits.p, (size_t)n * g.V * 4, cudaMemcpyDeviceToHost, g.st));
 		if (tokens_host) {
+			g.launches++;
 			k_argmax<<<(unsigned)n, 256, 0, g.st>>>(g.logits.as<float>(), g.V, g.tok.as<int>() + s0, nullptr, 0, 0);
 			TGC_LAUNCH_CHECK();
 		}
@@ -715,6 +800,7 @@ static int generate_wave(Engine &g, const float *ids_host, long S, int T, int nn
 	cudaMemcpy2DAsync(g.out_tok.p, (size_t)nnew * 4, g.tok.p, 4, 4, (size_t)S, cudaMemcpyDeviceToDevice, g.st);
 	for (int step = 1; step < nnew; step++) {
 		const int pos = T + step - 1; // position of the token being fed
+		g.launches += 2; // embed and argmax
 		k_embed<<<(unsigned)((S * 32 + 255) / 256), 256, 0, g.st>>>(nullptr, g.tok.as<int>(), S, g.E.as<float>(), g.V, g.D,
 									     g.h.as<float>());
 		TGC_LAUNCH_CHECK();
@@ -784,11 +870,14 @@ static int shard(tg_cuda_lm *g, long nseq, F &&fn)
 		cudaSetDevice(e.dev);
 		long lo = nseq * (long)di / (long)G, hi = nseq * (long)(di + 1) / (long)G;
 		int rc = TG_CUDA_OK;
+		call_begin(e);
 		for (long w0 = lo; w0 < hi && !rc; w0 += e.max_seqs) rc = fn(e, w0, std::min<long>(e.max_seqs, hi - w0));
+		cudaEventRecord(e.ev_end, e.st);
 		if (!rc) {
 			cudaError_t ce = cudaStreamSynchronize(e.st);
 			if (ce != cudaSuccess) rc = set_err(TG_CUDA_ECUDA, "device %d: %s", e.dev, cudaGetErrorString(ce));
 		}
+		if (!rc) call_end(e);
 		if (!rc) rc = device_status_check(e.status.as<int>(), e.st);
 		rcs[di] = rc;
 		if (rc) errs[di] = tg_cuda_error();
@@ -825,6 +914,31 @@ extern "C" int tg_cuda_lm_generate(tg_cuda_lm *g, const float *ids, long nseq, i
 	return shard(g, nseq, [&](Engine &e, long w0, long n) { return generate_wave(e, ids + w0 * T, n, T, nnew, tokens + w0 * nnew); });
 }
 
+extern "C" int tg_cuda_lm_profile(tg_cuda_lm *g, int enable)
+{
+	clear_err();
+	if (!g) return set_err(TG_CUDA_EINVAL, "tg_cuda_lm_profile: NULL model");
+	for (auto &e : g->eng) e->prof = enable != 0;
+	return TG_CUDA_OK;
+}
+
+extern "C" int tg_cuda_lm_get_stats(const tg_cuda_lm *g, tg_cuda_lm_stats *out)
+{
+	clear_err();
+	if (!g || !out) return set_err(TG_CUDA_EINVAL, "tg_cuda_lm_get_stats: NULL argument");
+	memset(out, 0, sizeof *out);
+	for (auto &e : g->eng) {
+		const tg_cuda_lm_stats &t = e->last;
+		out->device_ms = std::max(out->device_ms, t.device_ms);
+		out->launches += t.launches;
+		out->attn_decode_ms += t.attn_decode_ms, out->attn_decode_bytes += t.attn_decode_bytes;
+		out->attn_decode_launches += t.attn_decode_launches;
+		out->attn_prefill_ms += t.attn_prefill_ms, out->attn_prefill_flops += t.attn_prefill_flops;
+		out->gemm_ms += t.gemm_ms, out->gemm_flops += t.gemm_flops, out->gemm_launches += t.gemm_launches;
+	}
+	return TG_CUDA_OK;
+}
+
 extern "C" void tg_cuda_lm_free(tg_cuda_lm *g)
 {
 	if (!g) return;
@@ -833,6 +947,14 @@ extern "C" void tg_cuda_lm_free(tg_cuda_lm *g)
 		if (e->st) {
 			cudaStreamSynchronize(e->st);
 			cudaStreamDestroy(e->st);
+		}
+		for (auto &m : e->marks) {
+			cudaEventDestroy(m.a);
+			cudaEventDestroy(m.b);
+		}
+		if (e->ev_start) {
+			cudaEventDestroy(e->ev_start);
+			cudaEventDestroy(e->ev_end);
 		}
 	}
 	delete g;

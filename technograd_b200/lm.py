@@ -159,7 +159,7 @@ def quantize_rtn_device(w: dict, cfg: dict, bits: int) -> Model:
 class Engine:
     """A model loaded on the selected GPUs."""
 
-    def __init__(self, model: Model, max_seqs: int, max_len: int, gpus: int = 0, devices=None):
+    def __init__(self, model, max_seqs: int, max_len: int, gpus: int = 0, devices=None):
         _lib.init(gpus, devices)
         self.model = model
         d, keep = model.desc()
@@ -187,3 +187,131 @@ class Engine:
         tok = np.empty((S, nnew), np.int32)
         _lib.check(_lib.lib().tg_cuda_lm_generate(self.handle, ids.ctypes.data, S, T, nnew, tok.ctypes.data))
         return tok
+
+    def profile(self, on: bool) -> None:
+        _lib.check(_lib.lib().tg_cuda_lm_profile(self.handle, 1 if on else 0))
+
+    def stats(self) -> dict:
+        st = _lib.LmStats()
+        _lib.check(_lib.lib().tg_cuda_lm_get_stats(self.handle, C.byref(st)))
+        return {f: getattr(st, f) for f, _ in st._fields_}
+
+
+class Gptq:
+    """tg_cuda_gptq_prepare over seeded calibration rows (HOST memory)."""
+
+    def __init__(self, calib: np.ndarray):
+        calib = np.ascontiguousarray(calib, np.float32)
+        h = C.c_void_p()
+        _lib.check(_lib.lib().tg_cuda_gptq_prepare(calib.ctypes.data, calib.shape[0], calib.shape[1], C.byref(h)))
+        self.h, self.K = h, calib.shape[1]
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            _lib.lib().tg_cuda_gptq_free(self.h)
+            self.h = None
+
+
+def quantize_device(w, bits: int, gptq: "Gptq | None", out_q=None, out_s=None):
+    """Quantize a device f32 [in, out] matrix per output column (axis 1); GPTQ when a
+    calibration of the right width is given and in <= 2048 (src/quant.c:346), else RTN."""
+    import torch
+    rows, cols = w.shape
+    n = rows * cols
+    q = out_q if out_q is not None else torch.empty(n if bits == 8 else (n + 1) // 2, dtype=torch.int8, device=w.device)
+    s = out_s if out_s is not None else torch.empty(cols, dtype=torch.float32, device=w.device)
+    L = _lib.lib()
+    if gptq is not None and gptq.K == rows and rows <= 2048:
+        _lib.check(L.tg_cuda_quantize_gptq(gptq.h, w.data_ptr(), rows, cols, 1, bits, q.data_ptr(), s.data_ptr(), None))
+    else:
+        _lib.check(L.tg_cuda_quantize_rtn(w.data_ptr(), rows, cols, 1, bits, q.data_ptr(), s.data_ptr(), None))
+    return q, s
+
+
+class DeviceBuilt:
+    """A Qwen3-shaped model generated and quantized on the device, kept as the C
+    descriptor's concatenated per-layer matrices (host copies for tg_cuda_lm_load).
+
+    Random init: linear weights and the embedding ~ N(0, 0.02), norm weights 1.
+    Calibration: 256 seeded N(0,1) rows per input width; every param of that width
+    shares them. Per-head params are column blocks of one matrix (q/k/v) or row
+    blocks quantized one head at a time (o_proj, whose scales are per head)."""
+
+    def __init__(self, cfg: dict, bits: int = 4, method: str = "gptq", seed: int = 5, ncal: int = 256):
+        import torch
+        self.cfg, self.bits = dict(cfg), bits
+        L, D, NQ, NKV, HD, FF, V = (cfg[k] for k in ("layers", "hidden", "nq", "nkv", "head_dim", "ffn", "vocab"))
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(seed)
+
+        def randn(*shape):
+            return torch.randn(*shape, generator=gen, device="cuda", dtype=torch.float32) * 0.02
+
+        cal = {}
+        if method == "gptq":
+            rng = np.random.default_rng(seed)
+            cal = {K: Gptq(rng.standard_normal((ncal, K)).astype(np.float32)) for K in sorted({D, HD})}
+
+        def quant(w):
+            q, s = quantize_device(w, bits, cal.get(w.shape[0]))
+            return q.cpu().numpy(), s.cpu().numpy()
+
+        self.E = randn(V, D).cpu().numpy()
+        self.lnf = np.ones(D, np.float32)
+        self.lm = quant(randn(D, V))
+        self.layers = []
+        for _ in range(L):
+            lay = {"ln1": np.ones(D, np.float32), "ln2": np.ones(D, np.float32), "qn": np.ones(HD, np.float32),
+                   "kn": np.ones(HD, np.float32)}
+            lay["wq"], lay["wk"], lay["wv"] = quant(randn(D, NQ * HD)), quant(randn(D, NKV * HD)), quant(randn(D, NKV * HD))
+            wo = randn(NQ * HD, D)
+            per = HD * D if bits == 8 else HD * D // 2
+            qo = torch.empty(NQ * per, dtype=torch.int8, device="cuda")
+            so = torch.empty(NQ * D, dtype=torch.float32, device="cuda")
+            for h in range(NQ):
+                quantize_device(wo[h * HD:(h + 1) * HD].contiguous(), bits, cal.get(HD), qo[h * per:(h + 1) * per],
+                                so[h * D:(h + 1) * D])
+            lay["wo"] = (qo.cpu().numpy(), so.cpu().numpy())
+            lay["wg"], lay["wu"], lay["wd"] = quant(randn(D, FF)), quant(randn(D, FF)), quant(randn(FF, D))
+            self.layers.append(lay)
+        torch.cuda.synchronize()
+        del cal
+
+    def desc(self):
+        c = self.cfg
+        keep = []
+
+        def f32p(a):
+            a = np.ascontiguousarray(a, np.float32)
+            keep.append(a)
+            return a.ctypes.data_as(_lib.FP)
+
+        def qmat(qs):
+            q, s = (np.ascontiguousarray(qs[0], np.int8), np.ascontiguousarray(qs[1], np.float32))
+            keep.extend([q, s])
+            m = _lib.QMat()
+            m.q, m.s = q.ctypes.data_as(C.POINTER(C.c_byte)), s.ctypes.data_as(_lib.FP)
+            return m
+
+        L = c["layers"]
+        d = _lib.LmDesc()
+        d.layers, d.hidden, d.nq, d.nkv, d.head_dim, d.ffn, d.vocab = (c[k] for k in (
+            "layers", "hidden", "nq", "nkv", "head_dim", "ffn", "vocab"))
+        d.bits, d.eps = self.bits, 1e-6
+        d.attn_scale = float(np.float32(float(f"{1.0 / math.sqrt(c['head_dim']):.9g}")))
+        d.rope_theta = float(c["theta"])
+        d.embed, d.final_norm, d.lm_head = f32p(self.E), f32p(self.lnf), qmat(self.lm)
+        arrs = {k: (_lib.FP * L)() for k in ("ln1", "ln2", "qn", "kn")}
+        mats = {k: (_lib.QMat * L)() for k in ("wq", "wk", "wv", "wo", "wg", "wu", "wd")}
+        for l, lay in enumerate(self.layers):
+            for k in arrs:
+                arrs[k][l] = f32p(lay[k])
+            for k in mats:
+                mats[k][l] = qmat(lay[k])
+        for k, v in arrs.items():
+            setattr(d, k, C.cast(v, _lib.FPP))
+        for k, v in mats.items():
+            setattr(d, k, C.cast(v, _lib.QP))
+        keep.extend(list(arrs.values()) + list(mats.values()))
+        return d, keep
+

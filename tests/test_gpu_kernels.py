@@ -124,3 +124,30 @@ def test_quantize_rtn_bit_exact(cuda, bits, axis, shape):
     torch.cuda.synchronize()
     assert np.array_equal(dq.cpu().numpy(), q_want)
     assert np.array_equal(ds.cpu().numpy().view(np.uint32), s_want.view(np.uint32))
+
+
+@pytest.mark.parametrize("bits,axis,shape,ncal", [(4, 1, (256, 96), 64), (8, 0, (40, 128), 256), (4, 0, (33, 64), 20),
+                                                  (4, 1, (1024, 384), 256)])
+def test_quantize_gptq_bit_exact(cuda, bits, axis, shape, ncal):
+    """Device GPTQ against the oracle restatement of src/quant.c (itself pinned to the
+    reference's quantize_param in test_oracle.py). ncal < K makes H rank-deficient:
+    the 1% dampening keeps it positive definite, as in the reference."""
+    rng = np.random.default_rng(17)
+    w = rng.normal(0, 0.02, size=shape).astype(np.float32)
+    K = shape[1 - axis]
+    x = rng.normal(0, 1, size=(ncal, K)).astype(np.float32)
+    x[:, 3] = 0.0  # an input never active: its weights are zeroed (src/quant.c:274-277)
+    H = np.zeros((K, K))
+    tgo.tgo().tgo_hessian_add(H.ctypes.data_as(tgo.DP), tgo.f32p(x), ncal, K)
+    q_want, s_want = tgo.quantize(tgo.tgo(), "tgo_", w, axis, bits, H)
+    h = C.c_void_p()
+    assert cuda.tg_cuda_gptq_prepare(x.ctypes.data, ncal, K, C.byref(h)) == 0, cuda.tg_cuda_error()
+    dw = dev(w)
+    dq = torch.zeros(q_want.size, dtype=torch.int8, device="cuda")
+    ds = torch.zeros(s_want.size, dtype=torch.float32, device="cuda")
+    rc = cuda.tg_cuda_quantize_gptq(h, dw.data_ptr(), shape[0], shape[1], axis, bits, dq.data_ptr(), ds.data_ptr(), None)
+    assert rc == 0, cuda.tg_cuda_error()
+    torch.cuda.synchronize()
+    cuda.tg_cuda_gptq_free(h)
+    assert np.array_equal(ds.cpu().numpy().view(np.uint32), s_want.view(np.uint32))
+    assert np.array_equal(dq.cpu().numpy(), q_want)
