@@ -58,6 +58,19 @@ void tg_cuda_shutdown(void);
 int tg_cuda_matmul_q(int axis, float *o, const float *act, const signed char *q, int bits, const float *s, int m,
 		     int k, int n, void *stream);
 
+/* The x @ W case of tg_cuda_matmul_q (axis 1) for a batch m <= 8, without any
+ * allocation. No counterpart in the reference: it exists for callers that must
+ * not allocate device memory while they run (the reference's par_for workers
+ * may not allocate at all, src/par.c:11-12; hosts with a fixed memory budget).
+ * Its split-K partial sums use a 4 MiB static device array that every GPU
+ * loading the library keeps until exit, so m * n may be at most 1,048,576; n a
+ * multiple of 8 (int4) or 4 (int8), q 4-byte aligned. The first call on a
+ * device looks the array's address up (make it before any stream capture).
+ * Calls overlapping on one device share the array and race. Device pointers,
+ * asynchronous on stream; larger shapes are rejected with TG_CUDA_EINVAL. */
+int tg_cuda_matmul_qb_noalloc(float *o, const float *act, const signed char *q, int bits, const float *s, int m, int k,
+			      int n, void *stream);
+
 /* Per-channel RTN quantization on the device, bit-exact with quant.c: w is the
  * f32 matrix [rows, cols] (device), axis 0 = one scale per row, 1 = per column;
  * q receives (bits 8) rows*cols bytes or (bits 4) (rows*cols+1)/2 bytes, s one

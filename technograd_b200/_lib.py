@@ -23,6 +23,7 @@ PARAM, INPUT, TMP, STATE = 0, 1, 2, 3
 
 # Every entry point include/tg_cuda.h declares.
 SYMBOLS = ["tg_cuda_error", "tg_cuda_init", "tg_cuda_ngpus", "tg_cuda_shutdown", "tg_cuda_matmul_q",
+           "tg_cuda_matmul_qb_noalloc",
            "tg_cuda_quantize_rtn", "tg_cuda_gptq_prepare", "tg_cuda_quantize_gptq", "tg_cuda_gptq_free", "tg_cuda_load", "tg_cuda_batch", "tg_cuda_batch_device", "tg_cuda_free",
            "tg_cuda_lm_load", "tg_cuda_lm_forward", "tg_cuda_lm_generate", "tg_cuda_lm_free", "tg_cuda_lm_profile",
            "tg_cuda_lm_get_stats"]
@@ -100,6 +101,7 @@ def lib() -> C.CDLL:
             "tg_cuda_ngpus": ([], i),
             "tg_cuda_shutdown": ([], None),
             "tg_cuda_matmul_q": ([i, vp, vp, vp, i, vp, i, i, i, vp], i),
+            "tg_cuda_matmul_qb_noalloc": ([vp, vp, vp, i, vp, i, i, i, vp], i),
             "tg_cuda_quantize_rtn": ([vp, i, i, i, i, vp, vp, vp], i),
             "tg_cuda_gptq_prepare": ([vp, i, i, C.POINTER(vp)], i),
             "tg_cuda_quantize_gptq": ([vp, vp, i, i, i, i, vp, vp, vp], i),
