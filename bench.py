@@ -121,8 +121,8 @@ def barrier(world: int) -> None:
 
 # ---- config 5: int4 GPTQ Qwen3-0.6B-shape greedy decode ----------------------------------------
 
-def decode_ids() -> np.ndarray:
-    return np.random.default_rng(5).integers(0, 151936, size=(TOTAL_SEQS, PROMPT)).astype(np.float32)
+def decode_ids(total: int, prompt: int) -> np.ndarray:
+    return np.random.default_rng(5).integers(0, 151936, size=(total, prompt)).astype(np.float32)
 
 
 def bench_decode(args, world, rank, local):
@@ -131,19 +131,20 @@ def bench_decode(args, world, rank, local):
     from technograd_b200 import _lib, lm
     _lib.init(0, [local])
     torch.cuda.set_device(local)
-    cfg = lm.QWEN3_0_6B
+    cfg = dict(lm.QWEN3_0_6B, layers=args.layers or lm.QWEN3_0_6B["layers"])
+    total, prompt, new = args.seqs or TOTAL_SEQS, args.prompt or PROMPT, args.new or NEW
     t0 = time.perf_counter()
     built = lm.DeviceBuilt(cfg, bits=4, method="gptq", seed=5)
     t_build = time.perf_counter() - t0
-    shard = TOTAL_SEQS // world
+    shard = total // world
     wave = min(WAVE, shard)
-    ids = decode_ids()[rank * shard:(rank + 1) * shard]
+    ids = decode_ids(total, prompt)[rank * shard:(rank + 1) * shard]
     nwaves = (shard + wave - 1) // wave
-    eng = lm.Engine(built, max_seqs=wave, max_len=PROMPT + NEW - 1, devices=[local])
+    eng = lm.Engine(built, max_seqs=wave, max_len=prompt + new - 1, devices=[local])
 
     def step(i):
         w = i % nwaves
-        return eng.generate(ids[w * wave:(w + 1) * wave], NEW)
+        return eng.generate(ids[w * wave:(w + 1) * wave], new)
 
     for i in range(args.warmup):
         step(i)
@@ -162,7 +163,7 @@ def bench_decode(args, world, rank, local):
     clocks = clk.stop()
     t_dev = max_over_ranks(sum(dev_ms) / 1e3, world)
     t_wall = max_over_ranks(sum(wall), world)
-    tokens_step = wave * NEW
+    tokens_step = wave * new
     value = world * tokens_step * args.steps / t_dev
     pk, src = peaks()
     dec_bytes = sum(s["attn_decode_bytes"] for s in stats)
@@ -177,9 +178,11 @@ def bench_decode(args, world, rank, local):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
         "data": "synthetic: random-init weights N(0,0.02), uniform-random prompt ids (seed 5)",
-        "config": {"workload": "config5 int4 GPTQ Qwen3-0.6B-shape: 2048 seqs x 1024-token prompts + 256 decode steps",
-                   "seqs_per_step_per_gpu": wave, "prompt": PROMPT, "new_tokens_per_seq": NEW,
-                   "steps_for_full_job": (TOTAL_SEQS // world + wave - 1) // wave,
+        "config": {"workload": "config5 int4 GPTQ Qwen3-0.6B-shape: 2048 seqs x 1024-token prompts + 256 decode steps"
+                   if (total, prompt, new, cfg["layers"]) == (TOTAL_SEQS, PROMPT, NEW, 28) else
+                   f"REDUCED config5 shape (profiling): {total} seqs x {prompt} + {new - 1} steps, {cfg['layers']} layers",
+                   "seqs_per_step_per_gpu": wave, "prompt": prompt, "new_tokens_per_seq": new,
+                   "steps_for_full_job": (total // world + wave - 1) // wave,
                    "kv_cache": "f32, per GPU 75 GB at 256 seqs x 1280 positions",
                    "l2": "inputs larger than L2 (KV cache of 75 GB streamed every decode step)",
                    "share_of_step": {"attn_decode": dec_ms / tot_ms, "gemm": sum(s["gemm_ms"] for s in stats) / tot_ms,
@@ -190,7 +193,7 @@ def bench_decode(args, world, rank, local):
                      "traffic": None, "bytes_per_launch": dec_bytes / max(dec_launches, 1),
                      "ms_per_launch": dec_ms / max(dec_launches, 1)},
         "e2e": {"value": world * tokens_step * args.steps / t_wall, "unit": "tokens/s",
-                "h2d_bytes_per_step": wave * PROMPT * 4, "d2h_bytes_per_step": wave * NEW * 4},
+                "h2d_bytes_per_step": wave * prompt * 4, "d2h_bytes_per_step": wave * new * 4},
         "gpu_launches": int(sum(s["launches"] for s in stats)), "clocks": clocks,
     }
     return line, built, tok
@@ -363,6 +366,11 @@ def main():
     ap.add_argument("--workload", default="decode", choices=["decode", "lr"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # shape overrides for small profiling captures; the line's config says when they were used
+    ap.add_argument("--seqs", type=int, default=0)
+    ap.add_argument("--prompt", type=int, default=0)
+    ap.add_argument("--new", type=int, default=0)
+    ap.add_argument("--layers", type=int, default=0)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()

@@ -28,6 +28,7 @@ struct GemmArgs {
 	__nv_bfloat16 *out_hi, *out_lo; // SwiGLU: bf16 hi/lo of silu(g) * u
 	long ldo;                // row stride of the output, elements
 	int *status;             // device status word (ST_*), may not be NULL
+	int tma_out;             // set by gemm(): the output is written through a TMA map
 };
 
 // Launch on stream. SwiGLU: B rows come in blocks of 256 (128 gate rows then the

@@ -32,6 +32,7 @@ constexpr int A_TILE = BM * BK * 2; // 16 KB
 
 struct TmaMaps {
 	CUtensorMap a[2], b[2];
+	CUtensorMap o[2]; // the output (SwiGLU: the bf16 hi and lo outputs), when p.tma_out
 };
 
 __device__ __forceinline__ uint32_t bf16_bits(float x) { return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x)); }
@@ -47,6 +48,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 	uint64_t *empty = full + STAGES;
 	uint64_t *accf = empty + STAGES;
 	uint32_t *tslot = (uint32_t *)(accf + 1);
+	float *ssc = (float *)(accf + 2); // BN floats: the tile's scales (SwiGLU: gate then up)
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
 	const int KB = (p.K + BK - 1) / BK;
@@ -98,25 +100,42 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 		tc_commit(accf);
 	} else if (warp >= 2) { // ---- epilogue: TMEM lanes of quarter (warp % 4)
 		const int quarter = warp & 3;
-		const int row = m0 + quarter * 32 + lane;
+		const int r = quarter * 32 + lane; // tile row = TMEM lane
+		const int row = m0 + r;
+		const int et = threadIdx.x - 64;   // 0..127 over the epilogue warps
+		// scales of this tile into shared memory while the main loop runs
+		if (EPI == EPI_SWIGLU) {
+			const int f0 = blockIdx.x * (BN / 2);
+			for (int j = et; j < BN / 2; j += 128) {
+				ssc[j] = p.scale[f0 + j];
+				ssc[BN / 2 + j] = p.scale2[f0 + j];
+			}
+		} else if (p.scale_mode == 2) {
+			for (int j = et; j < BN; j += 128) ssc[j] = n0 + j < p.N ? p.scale[n0 + j] : 0.0f;
+		} else if (p.scale_mode == 1) {
+			ssc[et] = m0 + et < p.M ? p.scale[m0 + et] : 0.0f;
+		}
+		epilogue_sync();
 		const bool ok = mbar_wait(accf, 0, p.status, ST_TIMEOUT_ACC);
 		const bool live = ok && row < p.M;
 		tc_fence_after();
 		const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
 		if (EPI == EPI_SWIGLU) {
-			// columns [0, BN/2) are gate channels, [BN/2, BN) the matching up channels
+			// columns [0, BN/2) are gate channels, [BN/2, BN) the matching up channels. The
+			// results (bf16 hi, lo) are staged in the idle ring as 128-byte-swizzled chunks
+			// of 64 channels, then written by TMA stores.
 			const int f0 = blockIdx.x * (BN / 2);
-			for (int c = 0; c < BN / 2; c += 16) {
-				float g[16], u[16];
+			for (int c = 0; c < BN / 2; c += 32) {
+				float g[32], u[32];
 				__syncwarp();
-				tmem_ld16(trow + c, g);
-				tmem_ld16(trow + BN / 2 + c, u);
-				if (!live) continue;
-				uint32_t hi[8], lo[8];
+				tmem_ld16(trow + c, *(float(*)[16])g);
+				tmem_ld16(trow + c + 16, *(float(*)[16])(g + 16));
+				tmem_ld16(trow + BN / 2 + c, *(float(*)[16])u);
+				tmem_ld16(trow + BN / 2 + c + 16, *(float(*)[16])(u + 16));
+				uint32_t hi[16], lo[16];
 #pragma unroll
-				for (int i = 0; i < 16; i++) {
-					const int f = f0 + c + i;
-					float gs = g[i] * p.scale[f], us = u[i] * p.scale2[f];
+				for (int i = 0; i < 32; i++) {
+					float gs = g[i] * ssc[c + i], us = u[i] * ssc[BN / 2 + c + i];
 					float y = __fmul_rn(__fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs))), us); // silu(g) * u
 					uint32_t h = bf16_bits(y);
 					uint32_t l = bf16_bits(y - __uint_as_float(h << 16));
@@ -128,14 +147,69 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 						lo[i >> 1] = l;
 					}
 				}
-				const long off = (long)row * p.ldo + f0 + c;
-				uint4 *dh = (uint4 *)(p.out_hi + off), *dl = (uint4 *)(p.out_lo + off);
-				dh[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-				dh[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-				dl[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-				dl[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+				if (p.tma_out) {
+					const int chunk = c / 64, unit0 = (c % 64) / 8; // 32 channels = 64 bytes = 4 units
+					uint8_t *rh = smem + chunk * 16384 + r * 128, *rl = smem + (2 + chunk) * 16384 + r * 128;
+#pragma unroll
+					for (int q = 0; q < 4; q++) {
+						const int pu = ((unit0 + q) ^ (r & 7)) * 16;
+						*(uint4 *)(rh + pu) = make_uint4(hi[4 * q], hi[4 * q + 1], hi[4 * q + 2], hi[4 * q + 3]);
+						*(uint4 *)(rl + pu) = make_uint4(lo[4 * q], lo[4 * q + 1], lo[4 * q + 2], lo[4 * q + 3]);
+					}
+				} else if (live) {
+					const long off = (long)row * p.ldo + f0 + c;
+					uint4 *dh = (uint4 *)(p.out_hi + off), *dl = (uint4 *)(p.out_lo + off);
+#pragma unroll
+					for (int q = 0; q < 4; q++) {
+						dh[q] = make_uint4(hi[4 * q], hi[4 * q + 1], hi[4 * q + 2], hi[4 * q + 3]);
+						dl[q] = make_uint4(lo[4 * q], lo[4 * q + 1], lo[4 * q + 2], lo[4 * q + 3]);
+					}
+				}
+			}
+			if (p.tma_out) {
+				fence_async_smem();
+				epilogue_sync();
+				if (et == 0 && ok) {
+					for (int h = 0; h < BN / 128; h++) {
+						tma_store_2d(&maps.o[0], smem + h * 16384, f0 + 64 * h, m0);
+						tma_store_2d(&maps.o[1], smem + (2 + h) * 16384, f0 + 64 * h, m0);
+					}
+					tma_store_commit();
+					tma_store_wait_read();
+				}
+			}
+		} else if (p.tma_out) {
+			// f32 result in 128-byte-swizzled chunks of 32 columns, written (or added into the
+			// output, EPI_ADD) by TMA; rows past M and columns past N are clipped by the map
+			for (int c = 0; c < BN; c += 32) {
+				float v[32];
+				__syncwarp();
+				tmem_ld16(trow + c, *(float(*)[16])v);
+				tmem_ld16(trow + c + 16, *(float(*)[16])(v + 16));
+				const float rs = p.scale_mode == 1 ? ssc[r] : 1.0f;
+#pragma unroll
+				for (int i = 0; i < 32; i++) {
+					if (p.scale_mode == 1) v[i] = __fmul_rn(rs, v[i]);
+					else if (p.scale_mode == 2) v[i] = __fmul_rn(ssc[c + i], v[i]);
+				}
+				uint8_t *rp = smem + (c / 32) * 16384 + r * 128;
+#pragma unroll
+				for (int q = 0; q < 8; q++)
+					*(float4 *)(rp + ((q ^ (r & 7)) * 16)) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+			}
+			fence_async_smem();
+			epilogue_sync();
+			if (et == 0 && ok) {
+				for (int c = 0; c < BN; c += 32) {
+					if (n0 + c >= p.N) break;
+					if (EPI == EPI_ADD) tma_reduce_add_2d(&maps.o[0], smem + (c / 32) * 16384, n0 + c, m0);
+					else tma_store_2d(&maps.o[0], smem + (c / 32) * 16384, n0 + c, m0);
+				}
+				tma_store_commit();
+				tma_store_wait_read();
 			}
 		} else {
+			// direct stores, for outputs TMA cannot address (row pitch not a multiple of 16 bytes)
 			for (int c = 0; c < BN; c += 16) {
 				float v[16];
 				__syncwarp();
@@ -143,27 +217,15 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 				if (!live) continue;
 				const int n = n0 + c;
 				float *dst = p.out + (long)row * p.ldo + n;
-				const float rs = p.scale_mode == 1 ? p.scale[row] : 1.0f;
+				const float rs = p.scale_mode == 1 ? ssc[r] : 1.0f;
 #pragma unroll
 				for (int i = 0; i < 16; i++) {
 					float x = v[i];
 					if (p.scale_mode == 1) x = __fmul_rn(rs, x);
-					else if (p.scale_mode == 2 && n + i < p.N) x = __fmul_rn(p.scale[n + i], x);
+					else if (p.scale_mode == 2 && n + i < p.N) x = __fmul_rn(ssc[c + i], x);
 					v[i] = x;
 				}
-				if (n + 16 <= p.N && (p.ldo & 3) == 0) {
-#pragma unroll
-					for (int i = 0; i < 16; i += 4) {
-						float4 x = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-						if (EPI == EPI_ADD) {
-							float4 r = *(float4 *)(dst + i);
-							x.x = __fadd_rn(r.x, x.x), x.y = __fadd_rn(r.y, x.y), x.z = __fadd_rn(r.z, x.z), x.w = __fadd_rn(r.w, x.w);
-						}
-						*(float4 *)(dst + i) = x;
-					}
-				} else {
-					for (int i = 0; i < 16 && n + i < p.N; i++) dst[i] = EPI == EPI_ADD ? __fadd_rn(dst[i], v[i]) : v[i];
-				}
+				for (int i = 0; i < 16 && n + i < p.N; i++) dst[i] = EPI == EPI_ADD ? __fadd_rn(dst[i], v[i]) : v[i];
 			}
 		}
 		tc_fence_before();
@@ -209,11 +271,25 @@ static int make_map(CUtensorMap *m, const void *base, long rows, long K, long ld
 	return TG_CUDA_OK;
 }
 
+// f32 or bf16 [rows, cols] output (row pitch ld elements), box of box_x x 128 rows, 128-byte swizzle.
+static int make_out_map(CUtensorMap *m, CUtensorMapDataType dt, int esize, const void *base, long rows, long cols, long ld,
+			int box_x)
+{
+	cuuint64_t dims[2] = { (cuuint64_t)cols, (cuuint64_t)rows };
+	cuuint64_t strides[1] = { (cuuint64_t)(ld * esize) };
+	cuuint32_t box[2] = { (cuuint32_t)box_x, 128u };
+	cuuint32_t es[2] = { 1, 1 };
+	CUresult r = g_encode(m, dt, 2, (void *)base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+			      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+	if (r != CUDA_SUCCESS) return set_err(TG_CUDA_ECUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+	return TG_CUDA_OK;
+}
+
 template <int BN, int STAGES, int EPI>
 static int launch_bn(const TmaMaps &maps, const GemmArgs &p, cudaStream_t st)
 {
 	int stage = p.na * A_TILE + p.nb * BN * BK * 2;
-	size_t smem = (size_t)STAGES * stage + 1024 + 256;
+	size_t smem = (size_t)STAGES * stage + 1024 + 256 + BN * 4; // ring, alignment, barriers, scales
 	static bool attr_set[64] = {};
 	int dev;
 	cudaGetDevice(&dev);
@@ -244,6 +320,21 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 	// as many ring stages (2..4) as fit in 220 KB of shared memory
 	const int stage = p.na * A_TILE + p.nb * BN * BK * 2;
 	const int stages = std::min(4, std::max(2, (220 * 1024) / stage));
+	// the output goes through TMA when its pitch and base allow; the tile is staged in the
+	// ring once the main loop has drained it (128 rows x BN f32, or 4 bf16 chunks of 16 KB)
+	p.tma_out = 0;
+	if (p.epi == EPI_SWIGLU) {
+		if ((p.ldo * 2) % 16 == 0 && !((uintptr_t)p.out_hi & 15) && !((uintptr_t)p.out_lo & 15) && (p.N / 2) % 64 == 0 &&
+		    stages * stage >= 4 * 16384) {
+			if ((rc = make_out_map(&maps.o[0], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.out_hi, p.M, p.N / 2, p.ldo, 64)) ||
+			    (rc = make_out_map(&maps.o[1], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.out_lo, p.M, p.N / 2, p.ldo, 64)))
+				return rc;
+			p.tma_out = 1;
+		}
+	} else if ((p.ldo * 4) % 16 == 0 && !((uintptr_t)p.out & 15) && stages * stage >= 128 * BN * 4) {
+		if ((rc = make_out_map(&maps.o[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.out, p.M, p.N, p.ldo, 32))) return rc;
+		p.tma_out = 1;
+	}
 	if (stages * stage > 220 * 1024) return set_err(TG_CUDA_EINVAL, "gemm: %d operand tiles do not fit", p.na + p.nb);
 #define TGC_GEMM_DISPATCH(E)                                                                 \
 	if (BN == 256)                                                                      \

@@ -125,10 +125,10 @@ __global__ void k_rmsnorm_split(const float *__restrict__ x, long M, int D, cons
 // rmsnorm * qn / kn then rotary(x) = x*cos + rotate_half(x)*sin (import.py:96-97);
 // q goes to q_out [seq][NQ][T][HD], k and v into the cache at position pos0 + t.
 // One warp per head, 4 dims per lane (HD = 128).
-__global__ void k_qk_rope(const float *__restrict__ qkv, long M, int T, int pos0, int NQ, int NKV, float eps,
-			  const float *__restrict__ qn, const float *__restrict__ kn, const float *__restrict__ cosT,
-			  const float *__restrict__ sinT, float *__restrict__ q_out, float *__restrict__ kc,
-			  float *__restrict__ vc, int slot0, int max_len)
+__global__ void k_qk_rope(const float *__restrict__ qkv, long M, int T, int pos0, const int *__restrict__ dpos, int NQ,
+			  int NKV, float eps, const float *__restrict__ qn, const float *__restrict__ kn,
+			  const float *__restrict__ cosT, const float *__restrict__ sinT, float *__restrict__ q_out,
+			  float *__restrict__ kc, float *__restrict__ vc, int slot0, int max_len)
 {
 	constexpr int HD = 128;
 	long gw = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -137,6 +137,7 @@ __global__ void k_qk_rope(const float *__restrict__ qkv, long M, int T, int pos0
 	if (gw >= M * H) return;
 	long r = gw / H;
 	int hh = (int)(gw % H);
+	if (dpos) pos0 = *dpos; // decode: the position lives on the device (one graph serves every step)
 	int s = (int)(r / T), t = (int)(r % T), pos = pos0 + t;
 	float4 x = ((const float4 *)(qkv + r * (long)H * HD + (long)hh * HD))[lane];
 	if (hh >= NQ + NKV) { // v head: straight into the cache
@@ -315,14 +316,15 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const float *__restrict__ 
 // values: each warp accumulates its positions, warps are summed through shared memory.
 template <int GRP>
 __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q, const float *__restrict__ kc,
-						     const float *__restrict__ vc, int len, int NQ, int NKV, int slot0,
-						     int max_len, float scale, __nv_bfloat16 *__restrict__ ohi,
+						     const float *__restrict__ vc, int len, const int *__restrict__ dpos, int NQ,
+						     int NKV, int slot0, int max_len, float scale, __nv_bfloat16 *__restrict__ ohi,
 						     __nv_bfloat16 *__restrict__ olo)
 {
 	constexpr int HD = 128;
 	extern __shared__ float sm[];
-	float *sc = sm;                       // [GRP][len]
-	float *red = sc + GRP * ((len + 3) & ~3); // [8][GRP][HD]
+	if (dpos) len = *dpos + 1; // keys 0..pos, the new token's own included
+	float *sc = sm;                               // [GRP][max_len rounded up]
+	float *red = sc + GRP * ((max_len + 3) & ~3); // [8][GRP][HD]
 	__shared__ float wmax[8][GRP], wsum[8][GRP];
 	const int kvh = blockIdx.x, s = blockIdx.y;
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -347,7 +349,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 				for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
 				if (p0 + u < len) {
 					d = __fmul_rn(d, scale);
-					if (lane == 0) sc[g * ((len + 3) & ~3) + p0 + u] = d;
+					if (lane == 0) sc[g * ((max_len + 3) & ~3) + p0 + u] = d;
 					mx[g] = fmaxf(mx[g], d);
 				}
 			}
@@ -362,7 +364,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 		gmax[g] = wmax[0][g];
 		for (int w = 1; w < 8; w++) gmax[g] = fmaxf(gmax[g], wmax[w][g]);
 	}
-	const int stride = (len + 3) & ~3;
+	const int stride = (max_len + 3) & ~3;
 	float part[GRP];
 #pragma unroll
 	for (int g = 0; g < GRP; g++) part[g] = 0.0f;
@@ -420,8 +422,9 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 
 // First index of the row maximum (greedy decode).
 __global__ void k_argmax(const float *__restrict__ logits, int V, int *__restrict__ tok, int *__restrict__ out, int ld_out,
-			 int col)
+			 int col, const int *__restrict__ dpos, int T)
 {
+	if (dpos) col = *dpos - T + 1; // decode: the token fed at position pos yields output column pos - T + 1
 	const float *x = logits + (long)blockIdx.x * V;
 	float best = -INFINITY;
 	int bi = 0x7fffffff;
@@ -474,36 +477,65 @@ struct Engine {
 	struct Mark {
 		cudaEvent_t a = nullptr, b = nullptr;
 		int cls = 0;
-		double work = 0;
+		double work = 0, work_len = 0; // decode attention: bytes = work + work_len * keys
 	};
-	std::vector<Mark> marks;
-	size_t nmarks = 0;
-	tg_cuda_lm_stats last;
+	std::vector<Mark> marks, gmarks; // launched directly / recorded inside the decode graph
+	size_t nmarks = 0, ngmarks = 0;
+	bool capturing = false;
+	tg_cuda_lm_stats acc, last;
+	const char *ev_fail = nullptr; // first event call that failed in this call (reported by the API)
+	// one decode step (every layer, head, argmax, position bump) as a CUDA graph
+	DevBuf dpos; // the position of the token being fed, read by the decode kernels
+	int pos_host = 0;
+	cudaGraphExec_t gexec = nullptr;
+	long g_S = -1, g_kernels = 0;
+	int g_T = -1, g_nnew = -1;
+	bool g_prof = false;
 };
 
 enum { MK_DECODE = 1, MK_PREFILL = 2, MK_GEMM = 3 };
 
-// A pair of events around one launch of class cls (only while profiling).
-static int mark_begin(Engine &g, int cls, double work)
+static void ev_check(Engine &g, cudaError_t e, const char *what)
+{
+	if (e != cudaSuccess && !g.ev_fail) {
+		g.ev_fail = what;
+		set_err(TG_CUDA_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+	}
+	if (e != cudaSuccess) cudaGetLastError(); // reported here; do not leave it for the next launch check
+}
+
+// Inside a capture a plain cudaEventRecord only orders work; the External flag makes it an
+// event-record node that records (with a timestamp) at every replay.
+static cudaError_t record(Engine &g, cudaEvent_t ev)
+{
+	return g.capturing ? cudaEventRecordWithFlags(ev, g.st, cudaEventRecordExternal) : cudaEventRecord(ev, g.st);
+}
+
+// A pair of events around one launch of class cls (only while profiling). Inside a graph
+// capture the events become event-record nodes of the graph, read after each replay.
+static int mark_begin(Engine &g, int cls, double work, double work_len = 0)
 {
 	g.launches++;
 	if (!g.prof) return -1;
-	if (g.nmarks == g.marks.size()) {
+	std::vector<Engine::Mark> &v = g.capturing ? g.gmarks : g.marks;
+	size_t &n = g.capturing ? g.ngmarks : g.nmarks;
+	if (n == v.size()) {
 		Engine::Mark m;
-		cudaEventCreate(&m.a);
-		cudaEventCreate(&m.b);
-		g.marks.push_back(m);
+		ev_check(g, cudaEventCreate(&m.a), "cudaEventCreate");
+		ev_check(g, cudaEventCreate(&m.b), "cudaEventCreate");
+		v.push_back(m);
 	}
-	Engine::Mark &m = g.marks[g.nmarks];
+	Engine::Mark &m = v[n];
 	m.cls = cls;
 	m.work = work;
-	cudaEventRecord(m.a, g.st);
-	return (int)g.nmarks++;
+	m.work_len = work_len;
+	ev_check(g, record(g, m.a), "cudaEventRecord(mark begin)");
+	return (int)n++;
 }
 
 static void mark_end(Engine &g, int i)
 {
-	if (i >= 0) cudaEventRecord(g.marks[i].b, g.st);
+	if (i >= 0) ev_check(g, record(g, (g.capturing ? g.gmarks : g.marks)[i].b), "cudaEventRecord(mark end)");
 }
 
 static int gemm_m(Engine &g, const GemmOperands &op, const GemmArgs &p)
@@ -514,35 +546,51 @@ static int gemm_m(Engine &g, const GemmOperands &op, const GemmArgs &p)
 	return rc;
 }
 
+static void add_marks(Engine &g, tg_cuda_lm_stats &t, const std::vector<Engine::Mark> &v, size_t n, double keys)
+{
+	for (size_t i = 0; i < n; i++) {
+		float e = 0;
+		ev_check(g, cudaEventElapsedTime(&e, v[i].a, v[i].b), "cudaEventElapsedTime(mark)");
+		switch (v[i].cls) {
+		case MK_DECODE:
+			t.attn_decode_ms += e, t.attn_decode_bytes += v[i].work + v[i].work_len * keys, t.attn_decode_launches++;
+			break;
+		case MK_PREFILL: t.attn_prefill_ms += e, t.attn_prefill_flops += v[i].work; break;
+		case MK_GEMM: t.gemm_ms += e, t.gemm_flops += v[i].work, t.gemm_launches++; break;
+		}
+	}
+}
+
 static void call_begin(Engine &g)
 {
+	g.ev_fail = nullptr;
 	if (!g.ev_start) {
-		cudaEventCreate(&g.ev_start);
-		cudaEventCreate(&g.ev_end);
+		ev_check(g, cudaEventCreate(&g.ev_start), "cudaEventCreate(start)");
+		ev_check(g, cudaEventCreate(&g.ev_end), "cudaEventCreate(end)");
 	}
 	g.launches = 0;
 	g.nmarks = 0;
-	cudaEventRecord(g.ev_start, g.st);
+	memset(&g.acc, 0, sizeof g.acc);
+	ev_check(g, cudaEventRecord(g.ev_start, g.st), "cudaEventRecord(start)");
 }
 
 // After the stream is synchronized: the call's statistics.
 static void call_end(Engine &g)
 {
-	tg_cuda_lm_stats &t = g.last;
-	memset(&t, 0, sizeof t);
+	tg_cuda_lm_stats &t = g.acc;
 	float ms = 0;
-	cudaEventElapsedTime(&ms, g.ev_start, g.ev_end);
+	ev_check(g, cudaEventElapsedTime(&ms, g.ev_start, g.ev_end), "cudaEventElapsedTime(call)");
 	t.device_ms = ms;
 	t.launches = g.launches;
-	for (size_t i = 0; i < g.nmarks; i++) {
-		float e = 0;
-		cudaEventElapsedTime(&e, g.marks[i].a, g.marks[i].b);
-		switch (g.marks[i].cls) {
-		case MK_DECODE: t.attn_decode_ms += e, t.attn_decode_bytes += g.marks[i].work, t.attn_decode_launches++; break;
-		case MK_PREFILL: t.attn_prefill_ms += e, t.attn_prefill_flops += g.marks[i].work; break;
-		case MK_GEMM: t.gemm_ms += e, t.gemm_flops += g.marks[i].work, t.gemm_launches++; break;
-		}
-	}
+	add_marks(g, t, g.marks, g.nmarks, 0);
+	g.last = t;
+}
+
+static size_t prefill_smem() { return (size_t)(AQ * APAD + AK * APAD + AK * 128 + AQ * 68) * 4; }
+static size_t decode_smem(const Engine &g)
+{
+	const int grp = g.NQ / g.NKV;
+	return (size_t)(grp * ((g.max_len + 3) & ~3) + 8 * grp * g.HD) * 4;
 }
 
 // Host -> device copy ordered on the engine's stream and complete on return. (A plain
@@ -648,6 +696,12 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 	    (rc = g.tok.alloc((size_t)max_seqs * 4, dev)) || (rc = g.ids.alloc((size_t)R * 4, dev)) ||
 	    (rc = g.status.alloc(64, dev)))
 		return rc;
+	if ((rc = g.dpos.alloc(16, dev))) return rc;
+	// kernel attributes are set here, never inside a graph capture
+	if (decode_smem(g) > 220 * 1024) return set_err(TG_CUDA_EINVAL, "max_len %d: decode scores exceed shared memory", max_len);
+	TGC_CUDA(cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prefill_smem()));
+	TGC_CUDA(cudaFuncSetAttribute(k_attn_decode<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_smem(g)));
+	TGC_CUDA(cudaFuncSetAttribute(k_attn_decode<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_smem(g)));
 	TGC_CUDA(cudaMemsetAsync(g.status.p, 0, 64, g.st));
 	TGC_CUDA(cudaStreamSynchronize(g.st));
 	return TG_CUDA_OK;
@@ -686,38 +740,28 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 		if ((rc = gemm_m(g, op, p))) return rc;
 		long heads = M * (NQ + 2 * NKV);
 		k_qk_rope<<<(unsigned)((heads * 32 + 255) / 256), 256, 0, g.st>>>(
-			g.qkv.as<float>(), M, T, pos0, NQ, NKV, g.eps, Y.qn.as<float>(), Y.kn.as<float>(), g.cosT.as<float>(),
-			g.sinT.as<float>(), g.q.as<float>(), kc, vc, slot0, g.max_len);
+			g.qkv.as<float>(), M, T, pos0, decode ? g.dpos.as<int>() : nullptr, NQ, NKV, g.eps, Y.qn.as<float>(),
+			Y.kn.as<float>(), g.cosT.as<float>(), g.sinT.as<float>(), g.q.as<float>(), kc, vc, slot0, g.max_len);
 		if (!decode) {
-			size_t smem = (size_t)(AQ * APAD + AK * APAD + AK * HD + AQ * 68) * 4;
-			static bool attr[64] = {};
-			if (!attr[g.dev]) {
-				cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-				attr[g.dev] = true;
-			}
+			size_t smem = prefill_smem();
 			dim3 grid((T + AQ - 1) / AQ, NQ, (unsigned)S);
 			int mk = mark_begin(g, MK_PREFILL, 4.0 * HD * (double)T * (T + 1) / 2 * NQ * S);
 			k_attn_prefill<<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, T, NQ, NKV, slot0, g.max_len, g.scale,
 								  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>());
 			mark_end(g, mk);
 		} else {
-			int len = pos0 + 1;
-			size_t smem = (size_t)((NQ / NKV) * ((len + 3) & ~3) + 8 * (NQ / NKV) * HD) * 4;
-			static bool attr[64] = {};
-			if (!attr[g.dev]) {
-				cudaFuncSetAttribute(k_attn_decode<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-				cudaFuncSetAttribute(k_attn_decode<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-				attr[g.dev] = true;
-			}
+			// the key count (position + 1) is read on the device; bytes = per-key part * len + the rest
+			size_t smem = decode_smem(g);
 			dim3 grid(NKV, (unsigned)S);
-			double bytes = (double)S * NKV * len * HD * 4 * 2 + (double)S * NQ * HD * 4 + (double)S * NQ * HD * 4;
-			int mk = mark_begin(g, MK_DECODE, bytes);
+			int mk = mark_begin(g, MK_DECODE, (double)S * NQ * HD * 4 * 2, (double)S * NKV * HD * 4 * 2);
 			if (NQ / NKV == 2)
-				k_attn_decode<2><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, len, NQ, NKV, slot0, g.max_len, g.scale,
-									  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>());
+				k_attn_decode<2><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, 0, g.dpos.as<int>(), NQ, NKV, slot0,
+									  g.max_len, g.scale, g.ahi.as<__nv_bfloat16>(),
+									  g.alo.as<__nv_bfloat16>());
 			else
-				k_attn_decode<1><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, len, NQ, NKV, slot0, g.max_len, g.scale,
-									  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>());
+				k_attn_decode<1><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, 0, g.dpos.as<int>(), NQ, NKV, slot0,
+									  g.max_len, g.scale, g.ahi.as<__nv_bfloat16>(),
+									  g.alo.as<__nv_bfloat16>());
 			mark_end(g, mk);
 		}
 		TGC_LAUNCH_CHECK();
@@ -782,12 +826,65 @@ static int prefill(Engine &g, const float *ids_host, long S, int T, int slot0, f
 			TGC_CUDA(cudaMemcpyAsync(logits_host + s0 * g.V, g.logits.p, (size_t)n * g.V * 4, cudaMemcpyDeviceToHost, g.st));
 		if (tokens_host) {
 			g.launches++;
-			k_argmax<<<(unsigned)n, 256, 0, g.st>>>(g.logits.as<float>(), g.V, g.tok.as<int>() + s0, nullptr, 0, 0);
+			k_argmax<<<(unsigned)n, 256, 0, g.st>>>(g.logits.as<float>(), g.V, g.tok.as<int>() + s0, nullptr, 0, 0, nullptr,
+								 0);
 			TGC_LAUNCH_CHECK();
 		}
 	}
 	(void)tokens_host;
 	(void)ld_tok;
+	return TG_CUDA_OK;
+}
+
+// One decode step for S sequences whose fed token sits at position *dpos: embed the last
+// tokens, every layer against the KV cache, the LM head, argmax into column *dpos - T + 1
+// of out_tok, then *dpos += 1. Launch arguments do not depend on the step.
+__global__ void k_bump(int *pos) { pos[0] += 1; }
+
+static int decode_step(Engine &g, long S, int T, int nnew)
+{
+	int rc;
+	g.launches++;
+	k_embed<<<(unsigned)((S * 32 + 255) / 256), 256, 0, g.st>>>(nullptr, g.tok.as<int>(), S, g.E.as<float>(), g.V, g.D,
+								     g.h.as<float>());
+	if ((rc = run_layers(g, S, 1, 0, 0, true))) return rc;
+	if ((rc = head(g, S, 1))) return rc;
+	g.launches += 2;
+	k_argmax<<<(unsigned)S, 256, 0, g.st>>>(g.logits.as<float>(), g.V, g.tok.as<int>(), g.out_tok.as<int>(), nnew, 0,
+						 g.dpos.as<int>(), T);
+	k_bump<<<1, 1, 0, g.st>>>(g.dpos.as<int>());
+	TGC_LAUNCH_CHECK();
+	return TG_CUDA_OK;
+}
+
+// The decode step captured as a CUDA graph (re-captured when S, T, nnew or profiling change):
+// about 9 launches per layer replay without host work per step.
+static int decode_graph(Engine &g, long S, int T, int nnew)
+{
+	if (g.gexec && g.g_S == S && g.g_T == T && g.g_nnew == nnew && g.g_prof == g.prof) return TG_CUDA_OK;
+	if (g.gexec) {
+		cudaGraphExecDestroy(g.gexec);
+		g.gexec = nullptr;
+	}
+	g.ngmarks = 0;
+	const long before = g.launches;
+	cudaGraph_t graph = nullptr;
+	TGC_CUDA(cudaStreamBeginCapture(g.st, cudaStreamCaptureModeThreadLocal));
+	g.capturing = true;
+	int rc = decode_step(g, S, T, nnew);
+	g.capturing = false;
+	cudaError_t e = cudaStreamEndCapture(g.st, &graph);
+	g.g_kernels = g.launches - before;
+	g.launches = before;
+	if (rc) {
+		if (graph) cudaGraphDestroy(graph);
+		return rc;
+	}
+	if (e != cudaSuccess) return set_err(TG_CUDA_ECUDA, "decode graph capture: %s", cudaGetErrorString(e));
+	e = cudaGraphInstantiate(&g.gexec, graph, 0);
+	cudaGraphDestroy(graph);
+	if (e != cudaSuccess) return set_err(TG_CUDA_ECUDA, "decode graph instantiate: %s", cudaGetErrorString(e));
+	g.g_S = S, g.g_T = T, g.g_nnew = nnew, g.g_prof = g.prof;
 	return TG_CUDA_OK;
 }
 
@@ -797,17 +894,20 @@ static int generate_wave(Engine &g, const float *ids_host, long S, int T, int nn
 	if ((rc = prefill(g, ids_host, S, T, 0, nullptr, tokens_host, nnew))) return rc;
 	if ((rc = g.out_tok.ensure((size_t)S * nnew * 4, g.dev))) return rc;
 	// tokens[:, 0] = the prefill's argmax
-	cudaMemcpy2DAsync(g.out_tok.p, (size_t)nnew * 4, g.tok.p, 4, 4, (size_t)S, cudaMemcpyDeviceToDevice, g.st);
-	for (int step = 1; step < nnew; step++) {
-		const int pos = T + step - 1; // position of the token being fed
-		g.launches += 2; // embed and argmax
-		k_embed<<<(unsigned)((S * 32 + 255) / 256), 256, 0, g.st>>>(nullptr, g.tok.as<int>(), S, g.E.as<float>(), g.V, g.D,
-									     g.h.as<float>());
-		TGC_LAUNCH_CHECK();
-		if ((rc = run_layers(g, S, 1, pos, 0, true))) return rc;
-		if ((rc = head(g, S, 1))) return rc;
-		k_argmax<<<(unsigned)S, 256, 0, g.st>>>(g.logits.as<float>(), g.V, g.tok.as<int>(), g.out_tok.as<int>(), nnew, step);
-		TGC_LAUNCH_CHECK();
+	TGC_CUDA(cudaMemcpy2DAsync(g.out_tok.p, (size_t)nnew * 4, g.tok.p, 4, 4, (size_t)S, cudaMemcpyDeviceToDevice, g.st));
+	if (nnew > 1) {
+		// the first decode step feeds the token at position T; the graph bumps it each step
+		g.pos_host = T;
+		TGC_CUDA(cudaMemcpyAsync(g.dpos.p, &g.pos_host, sizeof(int), cudaMemcpyHostToDevice, g.st));
+		if ((rc = decode_graph(g, S, T, nnew))) return rc;
+		for (int step = 1; step < nnew; step++) {
+			TGC_CUDA(cudaGraphLaunch(g.gexec, g.st));
+			g.launches += g.g_kernels;
+			if (g.prof) { // read this replay's event pairs before the next replay re-records them
+				TGC_CUDA(cudaStreamSynchronize(g.st));
+				add_marks(g, g.acc, g.gmarks, g.ngmarks, (double)(T + step));
+			}
+		}
 	}
 	if (fault("gather")) return set_err(TG_CUDA_EFAULT, "injected gather failure (TG_CUDA_FAULT=gather)");
 	TGC_CUDA(cudaMemcpyAsync(tokens_host, g.out_tok.p, (size_t)S * nnew * 4, cudaMemcpyDeviceToHost, g.st));
@@ -872,12 +972,17 @@ static int shard(tg_cuda_lm *g, long nseq, F &&fn)
 		int rc = TG_CUDA_OK;
 		call_begin(e);
 		for (long w0 = lo; w0 < hi && !rc; w0 += e.max_seqs) rc = fn(e, w0, std::min<long>(e.max_seqs, hi - w0));
-		cudaEventRecord(e.ev_end, e.st);
+		ev_check(e, cudaEventRecord(e.ev_end, e.st), "cudaEventRecord(end)");
 		if (!rc) {
 			cudaError_t ce = cudaStreamSynchronize(e.st);
 			if (ce != cudaSuccess) rc = set_err(TG_CUDA_ECUDA, "device %d: %s", e.dev, cudaGetErrorString(ce));
 		}
 		if (!rc) call_end(e);
+		if (!rc && e.ev_fail) rc = TG_CUDA_ECUDA; // the text was set by ev_check
+		if (!rc) {
+			cudaError_t le = cudaGetLastError(); // nothing may be left pending from this call
+			if (le != cudaSuccess) rc = set_err(TG_CUDA_ECUDA, "pending error after the call: %s", cudaGetErrorString(le));
+		}
 		if (!rc) rc = device_status_check(e.status.as<int>(), e.st);
 		rcs[di] = rc;
 		if (rc) errs[di] = tg_cuda_error();
@@ -947,6 +1052,11 @@ extern "C" void tg_cuda_lm_free(tg_cuda_lm *g)
 		if (e->st) {
 			cudaStreamSynchronize(e->st);
 			cudaStreamDestroy(e->st);
+		}
+		if (e->gexec) cudaGraphExecDestroy(e->gexec);
+		for (auto &m : e->gmarks) {
+			cudaEventDestroy(m.a);
+			cudaEventDestroy(m.b);
 		}
 		for (auto &m : e->marks) {
 			cudaEventDestroy(m.a);

@@ -11,15 +11,11 @@ namespace tgc {
 // Device status word values (set by a kernel that gave up waiting).
 enum : int { ST_OK = 0, ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_ACC = 3 };
 
-// A wait gives up (and reports ST_TIMEOUT_*) after this much global time.
-constexpr uint64_t WAIT_NS = 2000000000ull; // 2 s
-
-__device__ __forceinline__ uint64_t global_ns()
-{
-	uint64_t t;
-	asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-	return t;
-}
+// A wait gives up (and reports ST_TIMEOUT_*) after this many SM clock cycles: about
+// 2 s at the B200's 1.965 GHz maximum, longer at lower clocks. The per-SM cycle
+// counter is cheap to read, unlike the global timer, so the check costs nothing on
+// the waits of the main loop.
+constexpr long long WAIT_CYCLES = 4000000000ll;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -55,10 +51,10 @@ __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity)
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status, int code)
 {
 	if (mbar_try(bar, parity)) return true;
-	const uint64_t t0 = global_ns();
+	const long long t0 = clock64();
 	for (uint32_t i = 1;; i++) {
 		if (mbar_try(bar, parity)) return true;
-		if ((i & 255) == 0 && global_ns() - t0 > WAIT_NS) break;
+		if ((i & 63) == 0 && clock64() - t0 > WAIT_CYCLES) break;
 	}
 	if (status) atomicExch(status, code);
 	return false;
@@ -75,6 +71,29 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
 		::"r"(smem_u32(dst)), "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
 		: "memory");
 }
+
+// 2D TMA tile store / reduce-add from shared memory (bulk-group completion; no multicast).
+// The x coordinate must be 16-byte aligned and neither coordinate negative.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y)
+{
+	asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+		     ::"l"((uint64_t)map), "r"(smem_u32(src)), "r"(x), "r"(y)
+		     : "memory");
+}
+
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *src, int x, int y)
+{
+	asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
+		     ::"l"((uint64_t)map), "r"(smem_u32(src)), "r"(x), "r"(y)
+		     : "memory");
+}
+
+__device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the committed bulk stores have finished reading shared memory.
+__device__ __forceinline__ void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
+// Barrier among the 128 threads of the four epilogue warps (barrier 0 is __syncthreads).
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map)
 {
