@@ -7,7 +7,7 @@
 
 namespace tgc {
 
-enum { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
+enum { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3 };
 
 // Operands: up to two A matrices [M, K] and two B matrices [N, K], bf16, K-major.
 struct GemmOperands {
@@ -29,6 +29,10 @@ struct GemmArgs {
 	long ldo;                // row stride of the output, elements
 	int *status;             // device status word (ST_*), may not be NULL
 	int tma_out;             // set by gemm(): the output is written through a TMA map
+	float *partial;          // optional scratch for split-K (small batches); NULL: never split
+	long partial_floats;     // its size in floats
+	int kb_per_split;        // set by gemm() for the split launch: K blocks per split
+	long mpad;               // set by gemm(): rows per split block of the partial buffer
 };
 
 // Launch on stream. SwiGLU: B rows come in blocks of 256 (128 gate rows then the

@@ -51,7 +51,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 	float *ssc = (float *)(accf + 2); // BN floats: the tile's scales (SwiGLU: gate then up)
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
-	const int KB = (p.K + BK - 1) / BK;
+	// split-K (EPI_PARTIAL): this CTA takes K blocks [kb0, kb0 + KB) and stores its raw sums
+	const int KBall = (p.K + BK - 1) / BK;
+	const int kb0 = p.kb_per_split ? blockIdx.z * p.kb_per_split : 0;
+	const int KB = p.kb_per_split ? min(p.kb_per_split, KBall - kb0) : KBall;
 
 	if (threadIdx.x == 0) {
 		for (int s = 0; s < STAGES; s++) {
@@ -75,8 +78,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 			if (!mbar_wait(&empty[s], ph ^ 1, p.status, ST_TIMEOUT_EMPTY)) break;
 			uint8_t *st = smem + s * stage_bytes;
 			mbar_expect_tx(&full[s], stage_bytes);
-			for (int i = 0; i < p.na; i++) tma_load_2d(st + i * A_TILE, &maps.a[i], &full[s], kb * BK, m0);
-			for (int j = 0; j < p.nb; j++) tma_load_2d(st + p.na * A_TILE + j * B_TILE, &maps.b[j], &full[s], kb * BK, n0);
+			for (int i = 0; i < p.na; i++) tma_load_2d(st + i * A_TILE, &maps.a[i], &full[s], (kb0 + kb) * BK, m0);
+			for (int j = 0; j < p.nb; j++) tma_load_2d(st + p.na * A_TILE + j * B_TILE, &maps.b[j], &full[s], (kb0 + kb) * BK, n0);
 		}
 	} else if (warp == 1 && lane == 0) { // ---- MMA issuer
 		constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
@@ -200,10 +203,12 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 			fence_async_smem();
 			epilogue_sync();
 			if (et == 0 && ok) {
+				// EPI_PARTIAL: the split's own padded row block of the partial-sum buffer
+				const int y0 = EPI == EPI_PARTIAL ? (int)(blockIdx.z * p.mpad) + m0 : m0;
 				for (int c = 0; c < BN; c += 32) {
 					if (n0 + c >= p.N) break;
-					if (EPI == EPI_ADD) tma_reduce_add_2d(&maps.o[0], smem + (c / 32) * 16384, n0 + c, m0);
-					else tma_store_2d(&maps.o[0], smem + (c / 32) * 16384, n0 + c, m0);
+					if (EPI == EPI_ADD) tma_reduce_add_2d(&maps.o[0], smem + (c / 32) * 16384, n0 + c, y0);
+					else tma_store_2d(&maps.o[0], smem + (c / 32) * 16384, n0 + c, y0);
 				}
 				tma_store_commit();
 				tma_store_wait_read();
@@ -297,10 +302,49 @@ static int launch_bn(const TmaMaps &maps, const GemmArgs &p, cudaStream_t st)
 		cudaFuncSetAttribute(gemm_tc<BN, STAGES, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
 		attr_set[dev] = true;
 	}
-	dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM);
+	dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, p.kb_per_split ? (unsigned)(((p.K + BK - 1) / BK + p.kb_per_split - 1) / p.kb_per_split) : 1u);
 	gemm_tc<BN, STAGES, EPI><<<grid, 192, smem, st>>>(maps, p);
 	TGC_LAUNCH_CHECK();
 	return TG_CUDA_OK;
+}
+
+static int launch_split(int BN, int stages, const TmaMaps &maps, const GemmArgs &q, dim3, cudaStream_t st)
+{
+	if (BN == 256)
+		return stages >= 4 ? launch_bn<256, 4, EPI_PARTIAL>(maps, q, st)
+		       : stages == 3 ? launch_bn<256, 3, EPI_PARTIAL>(maps, q, st) : launch_bn<256, 2, EPI_PARTIAL>(maps, q, st);
+	return stages >= 4 ? launch_bn<128, 4, EPI_PARTIAL>(maps, q, st)
+	       : stages == 3 ? launch_bn<128, 3, EPI_PARTIAL>(maps, q, st) : launch_bn<128, 2, EPI_PARTIAL>(maps, q, st);
+}
+
+// Fixed-order sum of the split-K partials, then the epilogue the split GEMM skipped.
+template <int EPI>
+__global__ void k_split_reduce(const float *__restrict__ part, int splits, long mpad, int M, int N, GemmArgs p)
+{
+	long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+	const int outc = EPI == EPI_SWIGLU ? N / 2 : N;
+	if (t >= (long)M * outc) return;
+	const int m = (int)(t / outc), n = (int)(t % outc);
+	if (EPI == EPI_SWIGLU) {
+		const int gc = (n / 128) * 256 + n % 128, uc = gc + 128;
+		float g = 0.0f, u = 0.0f;
+		for (int z = 0; z < splits; z++) {
+			g += part[((long)z * mpad + m) * N + gc];
+			u += part[((long)z * mpad + m) * N + uc];
+		}
+		float gs = g * p.scale[n], us = u * p.scale2[n];
+		float y = __fmul_rn(__fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs))), us);
+		__nv_bfloat16 h = __float2bfloat16_rn(y);
+		p.out_hi[(long)m * p.ldo + n] = h;
+		p.out_lo[(long)m * p.ldo + n] = __float2bfloat16_rn(y - __bfloat162float(h));
+		return;
+	}
+	float v = 0.0f;
+	for (int z = 0; z < splits; z++) v += part[((long)z * mpad + m) * N + n];
+	if (p.scale_mode == 2) v = __fmul_rn(p.scale[n], v);
+	else if (p.scale_mode == 1) v = __fmul_rn(p.scale[m], v);
+	float *o = p.out + (long)m * p.ldo + n;
+	*o = EPI == EPI_ADD ? __fadd_rn(*o, v) : v;
 }
 
 int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
@@ -320,6 +364,41 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 	// as many ring stages (2..4) as fit in 220 KB of shared memory
 	const int stage = p.na * A_TILE + p.nb * BN * BK * 2;
 	const int stages = std::min(4, std::max(2, (220 * 1024) / stage));
+	// Split K when the tiles would leave most SMs idle (small-batch decode): each split stores raw
+	// f32 sums into the caller's partial buffer, then k_split_reduce adds them in a fixed order.
+	int sms = 148, dev = 0;
+	cudaGetDevice(&dev);
+	cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+	const long tiles = (long)((p.N + BN - 1) / BN) * ((p.M + BM - 1) / BM);
+	const int KBall = (p.K + BK - 1) / BK;
+	int splits = 1;
+	if (p.partial && tiles * 2 <= sms && KBall >= 8 && p.N % 4 == 0) {
+		splits = (int)std::min<long>((sms + tiles - 1) / tiles, KBall / 4);
+		const long mpad = (long)(p.M + BM - 1) / BM * BM;
+		while (splits > 1 && (long)splits * mpad * p.N > p.partial_floats) splits--;
+	}
+	if (splits > 1) {
+		const int kper = (KBall + splits - 1) / splits;
+		splits = (KBall + kper - 1) / kper;
+		GemmArgs q = p;
+		q.kb_per_split = kper;
+		q.mpad = (long)(p.M + BM - 1) / BM * BM;
+		q.epi = EPI_PARTIAL;
+		q.scale_mode = 0;
+		if (stages * stage < 128 * BN * 4) return set_err(TG_CUDA_EINVAL, "gemm: split tile does not fit the ring");
+		if ((rc = make_out_map(&maps.o[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.partial, q.mpad * splits, p.N, p.N, 32)))
+			return rc;
+		q.tma_out = 1;
+		dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, splits);
+		if ((rc = launch_split(BN, stages, maps, q, grid, st))) return rc;
+		const long outs = (long)p.M * (p.epi == EPI_SWIGLU ? p.N / 2 : p.N);
+		const unsigned blocks = (unsigned)((outs + 255) / 256);
+		if (p.epi == EPI_SWIGLU) k_split_reduce<EPI_SWIGLU><<<blocks, 256, 0, st>>>(p.partial, splits, q.mpad, p.M, p.N, p);
+		else if (p.epi == EPI_ADD) k_split_reduce<EPI_ADD><<<blocks, 256, 0, st>>>(p.partial, splits, q.mpad, p.M, p.N, p);
+		else k_split_reduce<EPI_STORE><<<blocks, 256, 0, st>>>(p.partial, splits, q.mpad, p.M, p.N, p);
+		TGC_LAUNCH_CHECK();
+		return TG_CUDA_OK;
+	}
 	// the output goes through TMA when its pitch and base allow; the tile is staged in the
 	// ring once the main loop has drained it (128 rows x BN f32, or 4 bf16 chunks of 16 KB)
 	p.tma_out = 0;

@@ -468,7 +468,7 @@ struct Engine {
 	DevBuf kc, vc;
 	// activations
 	long rows_cap = 0;
-	DevBuf h, xhi, xlo, qkv, q, ahi, alo, ghi, glo, logits, tok, ids, status, out_tok;
+	DevBuf h, xhi, xlo, qkv, q, ahi, alo, ghi, glo, logits, tok, ids, status, out_tok, part;
 	int HQKV() const { return (NQ + 2 * NKV) * HD; }
 	// measurements of the current call (tg_cuda_lm_stats)
 	bool prof = false;
@@ -538,8 +538,11 @@ static void mark_end(Engine &g, int i)
 	if (i >= 0) ev_check(g, record(g, (g.capturing ? g.gmarks : g.marks)[i].b), "cudaEventRecord(mark end)");
 }
 
-static int gemm_m(Engine &g, const GemmOperands &op, const GemmArgs &p)
+static int gemm_m(Engine &g, const GemmOperands &op, const GemmArgs &p0)
 {
+	GemmArgs p = p0;
+	p.partial = g.part.as<float>(); // split-K scratch for the small-batch decode GEMMs
+	p.partial_floats = (long)(g.part.bytes / sizeof(float));
 	int mk = mark_begin(g, MK_GEMM, 2.0 * p.M * p.N * p.K);
 	int rc = gemm(op, p, g.st);
 	mark_end(g, mk);
@@ -697,6 +700,10 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 	    (rc = g.status.alloc(64, dev)))
 		return rc;
 	if ((rc = g.dpos.alloc(16, dev))) return rc;
+	{ // split-K partial sums of the decode GEMMs: up to 16 splits of a 128-row-padded batch
+		long mpad = ((long)max_seqs + 127) / 128 * 128, nmax = std::max<long>(g.HQKV(), std::max<long>(2L * FF, D));
+		if ((rc = g.part.alloc((size_t)16 * mpad * nmax * sizeof(float), dev))) return rc;
+	}
 	// kernel attributes are set here, never inside a graph capture
 	if (decode_smem(g) > 220 * 1024) return set_err(TG_CUDA_EINVAL, "max_len %d: decode scores exceed shared memory", max_len);
 	TGC_CUDA(cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prefill_smem()));
