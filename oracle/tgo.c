@@ -472,6 +472,8 @@ static int oone(OVM *vm, const tg_cuda_ins *in)
 			if (in->halt >= 0) {
 				float pr = *optr(vm, in->halt);
 				survive *= 1.0f - (pr < 0.0f ? 0.0f : pr > 1.0f ? 1.0f : pr);
+				if (vm->margin && fabsf((1.0f - survive) - in->hthr) < vm->margin[in->tid])
+					vm->margin[in->tid] = fabsf((1.0f - survive) - in->hthr);
 				if (1.0f - survive > in->hthr) break;
 			}
 		}

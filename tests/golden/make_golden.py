@@ -228,6 +228,42 @@ def nano(tgc: str) -> None:
             f.write(" ".join(f"{k}={v}" for k, v in cfg.items()) + "\n")
 
 
+# The reference's control-flow test programs: scan carries and stacked outputs, think
+# loops (`until` and learned halting), gradients through loops (lowered into the IR by
+# the compiler), and rope + windowed attention. name -> (source, rows, value range)
+PROGRAMS = {
+    "scan": ("tests/scan/scan.tg", 300, 2.0),
+    "halt": ("tests/think/halt.tg", 400, 3.0),
+    "nested_grad": ("tests/scan/nested_grad.tg", 300, 1.0),
+    "window": ("tests/attn/window.tg", 200, 1.5),
+}
+# the inputs tests/run.sh:45 runs these programs on, prepended to the random rows
+RUN_SH_ROWS = {
+    "scan": [[1, 2, 3, 4, 5, 6, 7, 8, 1, 0.5, -1, 2]],
+    "halt": [[1, 1], [0, 0]],
+    "nested_grad": [[0.1, 0.2, 0.3, -0.4, 0.5, 0.1, -0.2, 0.3]],
+}
+
+
+def programs(tgc: str) -> None:
+    out = os.path.join(HERE, "programs")
+    os.makedirs(out, exist_ok=True)
+    for name, (src, n, span) in PROGRAMS.items():
+        ir = os.path.join(out, f"{name}.tgir")
+        with open(ir, "w") as f:
+            f.write(sh(tgc, "ir", os.path.join(REF, src)))
+        from technograd_b200 import tgir
+        per = tgir.load(ir).per
+        rng = np.random.default_rng(sum(map(ord, name)))
+        rows = rng.uniform(-span, span, size=(n, per)).astype(np.float32)
+        rows = np.round(rows, 3)  # text rows that read back exactly as the same f32
+        if name in RUN_SH_ROWS:
+            rows = np.concatenate([np.array(RUN_SH_ROWS[name], np.float32), rows])
+        rp = os.path.join(out, f"{name}_rows.csv")
+        np.savetxt(rp, rows, fmt="%.9g", delimiter=",")
+        sh(tgc, "batch", ir, rp, "-j", "1", "-o", os.path.join(out, f"{name}_out.csv"))
+
+
 def main() -> None:
     tgo.build()
     tgc = tgo.REF_TGC
@@ -238,6 +274,7 @@ def main() -> None:
     kernels()
     quant()
     nano(tgc)
+    programs(tgc)
     print("golden fixtures written to", HERE)
 
 

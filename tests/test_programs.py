@@ -1,0 +1,54 @@
+"""The reference's control-flow test programs (tests/scan/scan.tg, tests/think/halt.tg,
+tests/scan/nested_grad.tg, tests/attn/window.tg) on the oracle VM and on the device
+row executor, against `tgc batch` output of the reference (tests/golden/programs).
+
+The oracle follows the reference's arithmetic order with the same libm, so it must
+agree bit for bit. The device path: values within 1e-4 + 1e-3 |ref|; think steps
+equal except rows whose halting quantity came within 1e-6 of its threshold."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import tgo
+from technograd_b200 import tgir
+from technograd_b200.batch import Batch, load_samples
+
+RTOL, ATOL = 1e-3, 1e-4
+NAMES = ["scan", "halt", "nested_grad", "window"]
+
+
+def fixture(golden, name):
+    d = os.path.join(golden, "programs")
+    m = tgir.load(os.path.join(d, f"{name}.tgir"))
+    rows = load_samples(os.path.join(d, f"{name}_rows.csv"), m.per)
+    ref = np.loadtxt(os.path.join(d, f"{name}_out.csv"), delimiter=",", dtype=np.float64, ndmin=2)
+    return m, rows, ref[:, :m.nout].astype(np.float32), ref[:, m.nout:].astype(np.int32)
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_oracle_vm_matches_tgc_batch(golden, name):
+    m, rows, want, want_steps = fixture(golden, name)
+    out, steps = tgo.program_run(tgir.CProgram(m), rows)
+    assert steps.shape == want_steps.shape
+    assert np.array_equal(steps, want_steps)
+    assert np.array_equal(out.view(np.uint32), want.view(np.uint32))
+
+
+def test_halt_step_counts(golden):
+    """tests/run.sh:374: `tgc run tests/think/halt.tg 1,1` stops after 5 steps, 0,0 after 19."""
+    m, rows, _, want_steps = fixture(golden, "halt")
+    _, steps = tgo.program_run(tgir.CProgram(m), rows[:2])
+    assert steps[:, 0].tolist() == [5, 19] == want_steps[:2, 0].tolist()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", NAMES)
+def test_device_executor_matches_tgc_batch(cuda, golden, name):
+    m, rows, want, want_steps = fixture(golden, name)
+    out, steps = Batch(m).run(rows)
+    np.testing.assert_allclose(out, want, rtol=RTOL, atol=ATOL)
+    bad = steps != want_steps
+    if bad.any():
+        _, _, margin = tgo.program_run(tgir.CProgram(m), rows, margins=True)
+        assert (margin[bad] < 1e-6).all(), f"{int(bad.any(axis=1).sum())} rows differ in think steps away from the threshold"
