@@ -1,6 +1,6 @@
 """Benchmark of the batch backend (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|lr] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|lr|prefill|gemm] [--impl ours|reference]
 
 Workloads (seeded synthetic inputs of the stated shapes):
   decode  config 5, the headline: Qwen3-0.6B architecture (28 layers, hidden 1024,
@@ -13,6 +13,14 @@ Workloads (seeded synthetic inputs of the stated shapes):
           at most 256 per GPU; one step = one wave. Unit: generated tokens/s.
   lr      config 1: latent_reasoner int8 RTN (--min-size 1), 1,048,576 rows of f32[8]
           with Bernoulli(0.5) entries (seed 1) per GPU; unit rows/s.
+  gemm    config 2: tg_cuda_matmul_q axis 0 (tg_matmul_qa) on W [4096, 4096] int4/int8
+          codes and X^T [4096, M], --m 1,16,256,4096 (one JSON line per M), --bits 4|8;
+          unit GEMMs/s, roofline HBM for M <= 16, bf16 tensor above.
+  prefill config 4: the Qwen3-0.6B shape with int8 RTN weights (seed 4), 64 sequences x
+          512 uniform-random ids, last-position logits; unit prompt tokens/s.
+  ssm     config 3: 4 selective-SSM blocks (d_model 256, d_inner 512, d_state 16, dt_rank
+          16, conv 4), int8 RTN, 1024 sequences x 4096 steps of N(0,1) f32[256] (seed 3);
+          unit tokens (sequence steps)/s.
 
 value: the device time of each step (CUDA events on the stream the library
 launches on, first to last launch), summed over steps, max over ranks. e2e: the
@@ -103,14 +111,7 @@ def dist_setup():
     return world, rank, local
 
 
-def max_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+from technograd_b200.shard import gather_in_order, max_over_ranks, shard_range  # noqa: E402
 
 
 def barrier(world: int) -> None:
@@ -136,9 +137,10 @@ def bench_decode(args, world, rank, local):
     t0 = time.perf_counter()
     built = lm.DeviceBuilt(cfg, bits=4, method="gptq", seed=5)
     t_build = time.perf_counter() - t0
-    shard = total // world
+    lo, hi = shard_range(total, world, rank)
+    shard = hi - lo
     wave = min(WAVE, shard)
-    ids = decode_ids(total, prompt)[rank * shard:(rank + 1) * shard]
+    ids = decode_ids(total, prompt)[lo:hi]
     nwaves = (shard + wave - 1) // wave
     eng = lm.Engine(built, max_seqs=wave, max_len=prompt + new - 1, devices=[local])
 
@@ -192,7 +194,11 @@ def bench_decode(args, world, rank, local):
                    "gemm_tflops": gemm_tf, "attn_prefill_tflops_f32": pre_tf, "build_s": t_build},
         "roofline": {"kernel": "k_attn_decode (KV-cache attention)", "bound": "hbm", "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "peak_source": src,
-                     "traffic": None, "bytes_per_launch": dec_bytes / max(dec_launches, 1),
+                     # ncu dram read+write of a 64-sequence launch was 1.009x its algorithmic bytes
+                     # (profiles/k_attn_decode_small.md); traffic grows with sequences x keys
+                     "traffic": 1.009 * dec_bytes / max(dec_launches, 1),
+                     "traffic_source": "ncu small-case ratio x algorithmic bytes per launch",
+                     "bytes_per_launch": dec_bytes / max(dec_launches, 1),
                      "ms_per_launch": dec_ms / max(dec_launches, 1)},
         "e2e": {"value": world * tokens_step * args.steps / t_wall, "unit": "tokens/s",
                 "h2d_bytes_per_step": wave * prompt * 4, "d2h_bytes_per_step": wave * new * 4},
@@ -228,6 +234,360 @@ def cpu_baseline_decode(built, seconds_budget: float = 30.0):
             "sample": f"{threads} sequences x 1 teacher-forced token at a {T}-token prefix (full Qwen3-0.6B shape, "
                       f"int4 GPTQ codes), one thread per sequence, {dt:.1f} s; at the config's 1024-1280-token "
                       f"prefixes each token costs ~64-80x more"}
+
+
+# ---- config 4: int8 RTN Qwen3-0.6B-shape batched prefill ---------------------------------------
+PF_SEQS, PF_T = 64, 512
+
+
+def bench_prefill(args, world, rank, local):
+    import torch
+
+    from technograd_b200 import _lib, lm
+    _lib.init(0, [local])
+    torch.cuda.set_device(local)
+    cfg = dict(lm.QWEN3_0_6B, layers=args.layers or lm.QWEN3_0_6B["layers"])
+    seqs, T = args.seqs or PF_SEQS, args.prompt or PF_T
+    t0 = time.perf_counter()
+    built = lm.DeviceBuilt(cfg, bits=8, method="rtn", seed=4)
+    t_build = time.perf_counter() - t0
+    lo, hi = shard_range(seqs, world, rank)
+    shard = hi - lo
+    ids = np.random.default_rng(4).integers(0, 151936, size=(seqs, T)).astype(np.float32)[lo:hi]
+    eng = lm.Engine(built, max_seqs=shard, max_len=T, devices=[local])
+    for _ in range(args.warmup):
+        eng.forward(ids)
+    eng.profile(True)
+    barrier(world)
+    clk = Clocks(local)
+    dev_ms, wall, stats = [], [], []
+    torch.cuda.nvtx.range_push("timed")
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        eng.forward(ids)
+        wall.append(time.perf_counter() - t)
+        s = eng.stats()
+        stats.append(s)
+        dev_ms.append(s["device_ms"])
+    torch.cuda.nvtx.range_pop()
+    barrier(world)
+    clocks = clk.stop()
+    t_dev = max_over_ranks(sum(dev_ms) / 1e3, world)
+    t_wall = max_over_ranks(sum(wall), world)
+    tok = shard * T
+    pk, src = peaks()
+    gemm_ms = sum(s["gemm_ms"] for s in stats)
+    gemm_fl = sum(s["gemm_flops"] for s in stats)
+    achieved = gemm_fl / (gemm_ms / 1e3) / 1e12
+    tot_ms = sum(dev_ms)
+    full = (seqs, T, cfg["layers"]) == (PF_SEQS, PF_T, 28)
+    line = {
+        "metric": "int8 Qwen3-0.6B-shape batched prefill tokens/s (config 4)", "value": world * tok * args.steps / t_dev,
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
+        "data": "synthetic: random-init weights N(0,0.02), uniform-random ids (seed 4)",
+        "config": {"workload": "config4 int8 RTN Qwen3-0.6B-shape prefill: 64 seqs x 512 tokens, last-position logits"
+                   if full else f"REDUCED config4 shape: {seqs} seqs x {T} tokens, {cfg['layers']} layers",
+                   "seqs_per_gpu": shard, "tokens_per_seq": T,
+                   "share_of_step": {"gemm": gemm_ms / tot_ms, "attn_prefill": sum(s["attn_prefill_ms"] for s in stats) / tot_ms},
+                   "attn_prefill_tflops_f32": sum(s["attn_prefill_flops"] for s in stats) /
+                   max(sum(s["attn_prefill_ms"] for s in stats) / 1e3, 1e-9) / 1e12,
+                   "l2": "inputs larger than L2 (activations 64x512x3072 f32 and weights stream every layer)",
+                   "build_s": t_build},
+        "roofline": {"kernel": "gemm_tc (tcgen05 dequant GEMM, all linear layers)", "bound": "tensor",
+                     "achieved": achieved, "peak": pk["bf16_tflops_sustained"] if "bf16_tflops_sustained" in pk
+                     else pk["bf16_tflops"], "unit": "TFLOP/s", "peak_source": src + " bf16 sustained",
+                     "traffic": None, "flops_per_launch": gemm_fl / max(sum(s["gemm_launches"] for s in stats), 1)},
+        "e2e": {"value": world * tok * args.steps / t_wall, "unit": "tokens/s", "h2d_bytes_per_step": ids.nbytes,
+                "d2h_bytes_per_step": shard * cfg["vocab"] * 4},
+        "gpu_launches": int(sum(s["launches"] for s in stats)), "clocks": clocks,
+    }
+    line["roofline"]["frac"] = achieved / line["roofline"]["peak"]
+    return line, built
+
+
+def cpu_baseline_prefill(built, T: int = 16):
+    """The oracle port (tgo_lm_forward, the reference VM's arithmetic over the Qwen3 program) on
+    the host cores: one T-token prefill per thread."""
+    from oracle import tgo
+    d, keep = built.desc()
+    L = tgo.tgo()
+    threads = os.cpu_count() or 1
+    ids = np.random.default_rng(4).integers(0, 151936, size=(threads, T)).astype(np.float32)
+    out = np.zeros((threads, 151936), np.float32)
+
+    def work(r):
+        L.tgo_lm_forward(C.addressof(d), tgo.f32p(np.ascontiguousarray(ids[r])), T, out[r].ctypes.data_as(tgo.FP))
+
+    t0 = time.perf_counter()
+    th = [threading.Thread(target=work, args=(r,)) for r in range(threads)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    dt = time.perf_counter() - t0
+    return {"value": threads * T / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{threads} sequences x {T}-token prefill (full Qwen3-0.6B shape, int8 RTN codes), one thread "
+                      f"per sequence, {dt:.1f} s; at 512 tokens the attention share grows from ~0.2% to ~6%"}
+
+
+# ---- config 3: stacked selective-SSM blocks ------------------------------------------------------
+SSM_SEQS, SSM_T = 1024, 4096
+
+
+def ssm_inputs(seqs: int, T: int, lo: int, hi: int) -> np.ndarray:
+    """Sequences [lo, hi) of the seeded N(0,1) input [seqs, T, 256] (seed 3), generated in
+    blocks so a rank only materialises its own shard."""
+    rng = np.random.default_rng(3)
+    out = np.empty((hi - lo, T, 256), np.float32)
+    for s in range(hi):
+        row = rng.standard_normal((T, 256), dtype=np.float32)
+        if s >= lo:
+            out[s - lo] = row
+    return out
+
+
+def bench_ssm(args, world, rank, local):
+    import torch
+
+    from technograd_b200 import _lib, ssm
+    _lib.init(0, [local])
+    torch.cuda.set_device(local)
+    cfg = dict(ssm.CONFIG3, blocks=args.layers or ssm.CONFIG3["blocks"])
+    seqs, T = args.seqs or SSM_SEQS, args.prompt or SSM_T
+    lo, hi = shard_range(seqs, world, rank)
+    t0 = time.perf_counter()
+    model = ssm.quantize_rtn_device(ssm.random_weights(cfg, seed=3), cfg, 8)
+    u = ssm_inputs(seqs, T, lo, hi)
+    t_build = time.perf_counter() - t0
+    S = hi - lo
+    eng = ssm.Engine(model, max_seqs=S, chunk=64, devices=[local])
+    du = torch.from_numpy(u).cuda()
+    dout = torch.empty_like(du)
+    for _ in range(args.warmup):
+        eng.forward_device(du.data_ptr(), S, T, dout.data_ptr())
+    eng.profile(True)
+    barrier(world)
+    clk = Clocks(local)
+    dev_ms, stats = [], []
+    torch.cuda.nvtx.range_push("timed")
+    for _ in range(args.steps):
+        eng.forward_device(du.data_ptr(), S, T, dout.data_ptr())
+        s = eng.stats()
+        stats.append(s)
+        dev_ms.append(s["device_ms"])
+    torch.cuda.nvtx.range_pop()
+    barrier(world)
+    clocks = clk.stop()
+    t_dev = max_over_ranks(sum(dev_ms) / 1e3, world)
+    # e2e: host (pinned) rows in, host rows out, through tg_cuda_ssm_forward
+    hu = torch.from_numpy(u).pin_memory()
+    ho = torch.empty_like(hu).pin_memory()
+    eng.profile(False)
+    _lib.check(_lib.lib().tg_cuda_ssm_forward(eng.handle, hu.data_ptr(), S, T, ho.data_ptr()))
+    barrier(world)
+    wall = []
+    for _ in range(args.steps):
+        t1 = time.perf_counter()
+        _lib.check(_lib.lib().tg_cuda_ssm_forward(eng.handle, hu.data_ptr(), S, T, ho.data_ptr()))
+        wall.append(time.perf_counter() - t1)
+    t_wall = max_over_ranks(sum(wall), world)
+    tok = S * T
+    scan_ms = sum(s["scan_ms"] for s in stats)
+    gemm_ms = sum(s["gemm_ms"] for s in stats)
+    tot_ms = sum(dev_ms)
+    pk, src = peaks()
+    scan_tf = sum(s["scan_flops"] for s in stats) / (scan_ms / 1e3) / 1e12
+    gemm_tf = sum(s["gemm_flops"] for s in stats) / (gemm_ms / 1e3) / 1e12
+    full = (seqs, T, cfg["blocks"]) == (SSM_SEQS, SSM_T, 4)
+    line = {
+        "metric": "int8 stacked selective-SSM tokens/s (config 3)", "value": world * tok * args.steps / t_dev,
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
+        "data": "synthetic: random-init weights N(0,0.02) int8 RTN, inputs N(0,1) (seed 3)",
+        "config": {"workload": "config3 4 SSM blocks d_model 256, d_inner 512, d_state 16, conv 4: 1024 seqs x 4096 steps"
+                   if full else f"REDUCED config3 shape: {seqs} seqs x {T} steps, {cfg['blocks']} blocks",
+                   "seqs_per_gpu": S, "steps_per_seq": T, "chunk": 64,
+                   "share_of_step": {"scan": scan_ms / tot_ms, "gemm": gemm_ms / tot_ms}, "gemm_tflops": gemm_tf,
+                   "l2": "inputs larger than L2 (4.3 GB in, 4.3 GB out per step)", "build_s": t_build},
+        "roofline": {"kernel": "k_ssm_scan (FP32 pipe + SFU)", "bound": "fp32", "achieved": scan_tf,
+                     "peak": FP32_NOMINAL_TFLOPS, "unit": "TFLOP/s", "frac": scan_tf / FP32_NOMINAL_TFLOPS,
+                     "peak_source": "nominal FP32 SIMT (148 SMs x 128 lanes x FMA x 1965 MHz); not in MEASURED_PEAKS",
+                     "traffic": None},
+        "e2e": {"value": world * tok * args.steps / t_wall, "unit": "tokens/s", "h2d_bytes_per_step": u.nbytes,
+                "d2h_bytes_per_step": u.nbytes},
+        "gpu_launches": int(sum(s["launches"] for s in stats)), "clocks": clocks,
+    }
+    return line, model
+
+
+def cpu_baseline_ssm(model, T: int = 96):
+    """The oracle port (tgo_ssm_forward: the reference VM's arithmetic over the same program,
+    pinned bit-exact to `tgc batch` in tests/test_ssm.py) on the host cores, one sequence per
+    thread; the cost per step does not depend on T."""
+    from oracle import tgo
+    d, keep = model.desc()
+    L = tgo.tgo()
+    threads = os.cpu_count() or 1
+    u = np.random.default_rng(3).standard_normal((threads, T, 256)).astype(np.float32)
+    out = np.zeros_like(u)
+
+    def work(r):
+        L.tgo_ssm_forward(C.addressof(d), tgo.f32p(u[r]), T, out[r].ctypes.data_as(tgo.FP))
+
+    t0 = time.perf_counter()
+    th = [threading.Thread(target=work, args=(r,)) for r in range(threads)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    dt = time.perf_counter() - t0
+    return {"value": threads * T / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{threads} sequences x {T} steps (full config-3 blocks), one thread per sequence, {dt:.1f} s"}
+
+
+# ---- config 2: weight-only dequant GEMM microbench ---------------------------------------------
+GEMM_N = GEMM_K = 4096
+
+
+def gemm_inputs(bits: int, M: int):
+    """W codes uniform in [-8, 7] (int4) or [-127, 127] (int8), [N, K]; scale |N(0,0.02)|/7 or /127
+    per output row; X [M, K] ~ N(0,1); seed 2. The reference op is tg_matmul_qa(o, q, bits, s, X^T, N, K, M)."""
+    from technograd_b200.tgir import pack_codes
+    rng = np.random.default_rng(2)
+    lo, hi = (-8, 8) if bits == 4 else (-127, 128)
+    codes = rng.integers(lo, hi, size=GEMM_N * GEMM_K)
+    q = np.ascontiguousarray(pack_codes(codes, bits))
+    s = (np.abs(rng.normal(0, 0.02, size=GEMM_N)) / (7 if bits == 4 else 127)).astype(np.float32)
+    x = rng.standard_normal((M, GEMM_K), dtype=np.float32)
+    return q, s, np.ascontiguousarray(x.T)  # b = X^T [K, M]
+
+
+def gemm_cost(bits: int, M: int):
+    N, K = GEMM_N, GEMM_K
+    byts = N * K * bits // 8 + 4 * N + 4 * M * K + 4 * M * N
+    return byts, 2.0 * M * N * K
+
+
+def bench_gemm(args, world, rank, local, M: int, bits: int):
+    import torch
+
+    from technograd_b200 import _lib
+    _lib.init(0, [local])
+    torch.cuda.set_device(local)
+    L = _lib.lib()
+    q, s, b = gemm_inputs(bits, M)
+    dq, ds, db = (torch.from_numpy(a).cuda() for a in (q, s, b))
+    do = torch.empty((GEMM_N, M), device="cuda")
+    flush = torch.empty(64 << 20, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def call(o_ptr, b_ptr):
+        _lib.check(L.tg_cuda_matmul_q(0, o_ptr, b_ptr, dq.data_ptr(), bits, ds.data_ptr(), GEMM_N, GEMM_K, M, sp))
+
+    for _ in range(args.warmup):
+        call(do.data_ptr(), db.data_ptr())
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = Clocks(local)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.nvtx.range_push("timed")
+    for i in range(args.steps):
+        flush.add_(1.0)  # 256 MB write between calls: larger than the 126 MB L2
+        ev[i][0].record(stream)
+        call(do.data_ptr(), db.data_ptr())
+        ev[i][1].record(stream)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = clk.stop()
+    ms = [a.elapsed_time(z) for a, z in ev]
+    t = max_over_ranks(sum(ms) / 1e3, world)
+    # e2e: activations from pinned host memory in, the product back to pinned host memory
+    hb = torch.from_numpy(b).pin_memory()
+    ho = torch.empty((GEMM_N, M)).pin_memory()
+    db2, do2 = torch.empty_like(db), torch.empty_like(do)
+
+    def e2e_call():
+        db2.copy_(hb, non_blocking=True)
+        call(do2.data_ptr(), db2.data_ptr())
+        ho.copy_(do2, non_blocking=True)
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        e2e_call()
+    barrier(world)
+    wall = []
+    for _ in range(args.steps):
+        flush.add_(1.0)
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        e2e_call()
+        wall.append(time.perf_counter() - t1)
+    te = max_over_ranks(sum(wall), world)
+    byts, flops = gemm_cost(bits, M)
+    pk, src = peaks()
+    per = sum(ms) / 1e3 / args.steps
+    hbm = M <= 16
+    if hbm:
+        achieved, peak, unit = byts / per / 1e9, pk["hbm_gbs"], "GB/s"
+    else:
+        achieved, peak, unit = flops / per / 1e12, pk["bf16_tflops"], "TFLOP/s"
+    path = "gemv_rows (CUDA cores)" if M <= 8 else "codes_to_bf16 + split_to_bf16 + gemm_tc (tcgen05)"
+    line = {
+        "metric": f"int{bits} dequant GEMM [4096x4096] x [4096, M={M}] GEMMs/s (config 2)",
+        "value": world * args.steps / t, "unit": "GEMM/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sum(ms) / len(ms), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": f"int{bits} codes, f32 activations and accumulation" + ("" if M <= 8 else " (bf16 hi/lo split)"),
+        "data": "synthetic (seed 2)",
+        "config": {"workload": f"config2 M={M} int{bits}", "M": M, "N": GEMM_N, "K": GEMM_K, "path": path,
+                   "l2": "flushed between calls (256 MB write)", "algorithmic_bytes": byts, "flops": flops},
+        "roofline": {"kernel": path, "bound": "hbm" if hbm else "tensor", "achieved": achieved, "peak": peak,
+                     "unit": unit, "frac": achieved / peak, "peak_source": src + (" hbm_gbs" if hbm else " bf16 burst"),
+                     "traffic": None},
+        "e2e": {"value": world * args.steps / te, "unit": "GEMM/s", "h2d_bytes_per_step": b.nbytes,
+                "d2h_bytes_per_step": GEMM_N * M * 4},
+        "gpu_launches": args.steps * (1 if M <= 8 else 3), "clocks": clocks,
+    }
+    return line, (q, s, b)
+
+
+def cpu_baseline_gemm(q, s, b, bits: int, M: int, budget_s: float = 10.0):
+    """The reference's own tg_matmul_qa (runtime/tg_rt.h, compiled into oracle/_ref) on the host
+    cores. `tgc batch` runs one GEMV per row (src/main.c:231-242) on -j auto threads, so the
+    columns of b are split over threads; a bounded sample of columns is timed and scaled."""
+    from oracle import tgo
+    R = tgo.ref()
+    kind, fn = ("reference", R.ref_matmul_qa) if R is not None else ("port", tgo.tgo().tgo_matmul_qa)
+    threads = min(os.cpu_count() or 1, M)
+    # calibrate: one column on one thread
+    o1 = np.zeros(GEMM_N, np.float32)
+    b1 = np.ascontiguousarray(b[:, :1])
+    t0 = time.perf_counter()
+    fn(tgo.f32p(o1), tgo.i8p(q), bits, tgo.f32p(s), tgo.f32p(b1), GEMM_N, GEMM_K, 1)
+    per_col = time.perf_counter() - t0
+    cols = max(threads, min(M, int(budget_s * threads / max(per_col, 1e-6))))
+    cols -= cols % threads if cols >= threads else 0
+    cols = max(cols, 1)
+    chunks = np.array_split(np.arange(cols), threads)
+    subs = [np.ascontiguousarray(b[:, c]) for c in chunks]
+    outs = [np.zeros(GEMM_N * len(c), np.float32) for c in chunks]
+
+    def work(i):
+        n = len(chunks[i])
+        if n:
+            fn(tgo.f32p(outs[i]), tgo.i8p(q), bits, tgo.f32p(s), tgo.f32p(subs[i]), GEMM_N, GEMM_K, n)
+
+    t0 = time.perf_counter()
+    th = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    dt = time.perf_counter() - t0
+    return {"value": (cols / M) / dt, "unit": "GEMM/s", "cores": threads, "kind": kind,
+            "sample": f"{cols} of the {M} activation columns on {threads} thread(s), {dt:.1f} s, scaled to the full GEMM"}
 
 
 # ---- config 1: latent_reasoner -----------------------------------------------------------------
@@ -341,17 +701,39 @@ def reference_arm(args, world, rank, local):
                 return {"impl": "reference", "unavailable": "oracle/_ref/tgc was not built (needs the reference sources)"}
             vals.append(base["value"])
         metric, unit, cfgw = "latent_reasoner int8 batch rows/s (config 1)", "rows/s", "config1 latent_reasoner int8 RTN --min-size 1"
+    elif args.workload == "gemm":
+        M, bits = args.m[0], args.bits
+        q, s, b = gemm_inputs(bits, M)
+        vals = [cpu_baseline_gemm(q, s, b, bits, M, budget_s=5.0)["value"] for _ in range(args.steps)]
+        base = cpu_baseline_gemm(q, s, b, bits, M, budget_s=5.0)
+        metric, unit = f"int{bits} dequant GEMM [4096x4096] x [4096, M={M}] GEMMs/s (config 2)", "GEMM/s"
+        cfgw = f"config2 M={M} int{bits}"
+    elif args.workload == "ssm":
+        from technograd_b200 import _lib, ssm
+        _lib.init(0, [local])
+        model = ssm.quantize_rtn_device(ssm.random_weights(ssm.CONFIG3, seed=3), ssm.CONFIG3, 8)
+        vals, base = [], None
+        for _ in range(args.steps):
+            base = cpu_baseline_ssm(model)
+            vals.append(base["value"])
+        metric, unit = "int8 stacked selective-SSM tokens/s (config 3)", "tokens/s"
+        cfgw = "config3 4 SSM blocks d_model 256, d_inner 512, d_state 16, conv 4: 1024 seqs x 4096 steps"
     else:
         # the model is generated on the GPU (same seeds as our arm), then the CPU port runs
         from technograd_b200 import _lib, lm
         _lib.init(0, [local])
-        built = lm.DeviceBuilt(lm.QWEN3_0_6B, bits=4, method="gptq", seed=5)
+        pre = args.workload == "prefill"
+        built = lm.DeviceBuilt(lm.QWEN3_0_6B, bits=8 if pre else 4, method="rtn" if pre else "gptq", seed=4 if pre else 5)
         vals, base = [], None
         for _ in range(args.steps):
-            base = cpu_baseline_decode(built)
+            base = cpu_baseline_prefill(built) if pre else cpu_baseline_decode(built)
             vals.append(base["value"])
-        metric, unit = "int4 Qwen3-0.6B-shape greedy decode tokens/s (config 5)", "tokens/s"
-        cfgw = "config5 int4 GPTQ Qwen3-0.6B-shape: 2048 seqs x 1024-token prompts + 256 decode steps"
+        if pre:
+            metric, unit = "int8 Qwen3-0.6B-shape batched prefill tokens/s (config 4)", "tokens/s"
+            cfgw = "config4 int8 RTN Qwen3-0.6B-shape prefill: 64 seqs x 512 tokens, last-position logits"
+        else:
+            metric, unit = "int4 Qwen3-0.6B-shape greedy decode tokens/s (config 5)", "tokens/s"
+            cfgw = "config5 int4 GPTQ Qwen3-0.6B-shape: 2048 seqs x 1024-token prompts + 256 decode steps"
     v = statistics.median(vals)
     base["value"] = v
     return {"impl": "reference", "metric": metric, "value": v, "unit": unit, "n_gpus": 0, "steps": args.steps,
@@ -365,7 +747,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="decode", choices=["decode", "lr"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "lr", "prefill", "gemm", "ssm"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     # shape overrides for small profiling captures; the line's config says when they were used
@@ -373,6 +755,9 @@ def main():
     ap.add_argument("--prompt", type=int, default=0)
     ap.add_argument("--new", type=int, default=0)
     ap.add_argument("--layers", type=int, default=0)
+    # config 2: batch sizes (one JSON line per M) and code width
+    ap.add_argument("--m", type=lambda v: [int(x) for x in v.split(",")], default=[1])
+    ap.add_argument("--bits", type=int, default=4, choices=[4, 8])
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
@@ -382,6 +767,24 @@ def main():
         line, rows = bench_lr(args, world, rank, local)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_lr(rows)
+    elif args.workload == "ssm":
+        line, model = bench_ssm(args, world, rank, local)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_ssm(model)
+    elif args.workload == "prefill":
+        line, built = bench_prefill(args, world, rank, local)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_prefill(built)
+    elif args.workload == "gemm":
+        for M in args.m[:-1]:  # every M but the last prints here; the last takes the common path below
+            ln, data = bench_gemm(args, world, rank, local, M, args.bits)
+            if rank == 0 and world == 1 and not args.no_cpu_baseline:
+                ln["cpu_baseline"] = cpu_baseline_gemm(*data, args.bits, M)
+            if rank == 0:
+                print(json.dumps(ln), flush=True)
+        line, data = bench_gemm(args, world, rank, local, args.m[-1], args.bits)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_gemm(*data, args.bits, args.m[-1])
     else:
         line, built, _ = bench_decode(args, world, rank, local)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:

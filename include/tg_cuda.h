@@ -220,6 +220,61 @@ typedef struct {
 int tg_cuda_lm_profile(tg_cuda_lm *g, int enable);
 int tg_cuda_lm_get_stats(const tg_cuda_lm *g, tg_cuda_lm_stats *out);
 
+/* ---- stacked selective-SSM blocks -------------------------------------------------
+ * `tgc batch` over a program of Mamba-style blocks written with the reference's
+ * ops (scan with carries, outer, broadcasting, softplus, exp, silu, rmsnorm,
+ * x @ W matmuls; src/vm.c:364-382 for the scan), one sequence per row. Per block
+ * b and step t, with u_t the residual stream [d_model] and the carries h
+ * [d_inner, d_state] and c1..c3 [d_inner] (the last three x, zero at t = 0):
+ *   n  = rmsnorm(u_t) * norm[b];      x = n @ w_x;   z = n @ w_z
+ *   xc = c3*conv_w[0] + c2*conv_w[1] + c1*conv_w[2] + x*conv_w[3] + conv_b
+ *   xs = silu(xc);  r = xs @ w_r;  bt = xs @ w_b;  ct = xs @ w_c
+ *   dt = softplus(r @ w_dt + dt_b)
+ *   e  = exp(-(reshape(dt, d_inner, 1) * a));  h = e * h + (1 - e) / a * outer(xs, bt)
+ *   u_t = u_t + ((h @ ct + d * xs) * silu(z)) @ w_o
+ * and the output row t is rmsnorm(u_t) * final_norm. The matrices are x @ W
+ * (axis 1) int8/int4 codes with one scale per output column, as `tgc quantize`
+ * writes them; a [d_inner, d_state] must be positive. */
+typedef struct {
+	int blocks, d_model, d_inner, d_state, dt_rank;
+	int bits;
+	float eps;
+	const float *final_norm;                          /* [d_model] */
+	const float *const *norm;                         /* per block [d_model] */
+	const float *const *conv_w;                       /* per block [4][d_inner] */
+	const float *const *conv_b, *const *dt_b, *const *d; /* per block [d_inner] */
+	const float *const *a;                            /* per block [d_inner, d_state] */
+	const tg_cuda_qmat *w_x, *w_z, *w_r, *w_b, *w_c, *w_dt, *w_o; /* per block */
+} tg_cuda_ssm_desc;
+
+typedef struct tg_cuda_ssm tg_cuda_ssm;
+
+/* max_seqs sequences run at once per device; chunk steps of each are in flight
+ * per pass (the token block of every GEMM is max_seqs * chunk rows). */
+int tg_cuda_ssm_load(const tg_cuda_ssm_desc *d, int max_seqs, int chunk, tg_cuda_ssm **out);
+/* u, out: host [nseq][T][d_model] f32 (out may not alias u). */
+int tg_cuda_ssm_forward(tg_cuda_ssm *g, const float *u, long nseq, int T, float *out);
+/* The same on device buffers of the first device, on its stream (no copies). */
+int tg_cuda_ssm_forward_device(tg_cuda_ssm *g, const float *u, long nseq, int T, float *out);
+void tg_cuda_ssm_free(tg_cuda_ssm *g);
+
+/* Measurements of the last forward (no reference counterpart). Times are CUDA-event
+ * device times; with several devices device_ms is the maximum and the rest are sums.
+ * The per-kernel-class times are collected only after tg_cuda_ssm_profile(g, 1). */
+typedef struct {
+	double device_ms;   /* first to last launch of the call */
+	long launches;      /* kernels the call launched */
+	double gemm_ms;     /* the three projections of every block (tensor cores) */
+	double gemm_flops;  /* 2 M N K of the useful columns (not the bf16 hi/lo passes or padding) */
+	long gemm_launches;
+	double scan_ms;     /* the selective scan (dt projection, state update, readout, gate) */
+	double scan_flops;  /* per (token, channel): 2 dt_rank + 7 d_state + 2 d_state + 4, plus
+	                       the d_state exps, softplus and silu counted as one flop each */
+	long scan_launches;
+} tg_cuda_ssm_stats;
+int tg_cuda_ssm_profile(tg_cuda_ssm *g, int enable);
+int tg_cuda_ssm_get_stats(const tg_cuda_ssm *g, tg_cuda_ssm_stats *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -665,3 +665,70 @@ int tgo_lm_forward(const tg_cuda_lm_desc *d, const float *ids, int T, float *log
 	free(g); free(u); free(m); free(cosT); free(sinT);
 	return 0;
 }
+
+/* ---- stacked selective-SSM blocks (the program tests/golden/make_golden.py:emit_ssm
+ * writes; the scan of src/vm.c:364-382 over the steps of one sequence) ---------------------- */
+
+static float silu1(float x) { return x / (1.0f + expf(-x)); }                      /* runtime/tg_rt.h:59-60 */
+static float softplus1(float x) { return (x > 0.0f ? x : 0.0f) + log1pf(expf(-fabsf(x))); } /* :63-64 */
+
+int tgo_ssm_forward(const tg_cuda_ssm_desc *d, const float *u, int T, float *out)
+{
+	const int DM = d->d_model, DI = d->d_inner, DS = d->d_state, R = d->dt_rank;
+	float *cur = malloc((size_t)T * DM * sizeof *cur), *nxt = malloc((size_t)T * DM * sizeof *nxt);
+	float *n = malloc(DM * sizeof *n), *x = malloc(DI * sizeof *x), *z = malloc(DI * sizeof *z);
+	float *xs = malloc(DI * sizeof *xs), *c1 = malloc(DI * sizeof *c1), *c2 = malloc(DI * sizeof *c2);
+	float *c3 = malloc(DI * sizeof *c3), *r = malloc(R * sizeof *r), *bt = malloc(DS * sizeof *bt);
+	float *ct = malloc(DS * sizeof *ct), *dt = malloc(DI * sizeof *dt), *g = malloc(DI * sizeof *g);
+	float *o = malloc(DM * sizeof *o), *h = malloc((size_t)DI * DS * sizeof *h);
+	memcpy(cur, u, (size_t)T * DM * sizeof *cur);
+	for (int b = 0; b < d->blocks; b++) {
+		const float *cw = d->conv_w[b], *A = d->a[b];
+		memset(h, 0, (size_t)DI * DS * sizeof *h);
+		memset(c1, 0, DI * sizeof *c1);
+		memset(c2, 0, DI * sizeof *c2);
+		memset(c3, 0, DI * sizeof *c3);
+		for (int t = 0; t < T; t++) {
+			const float *ut = cur + (long)t * DM;
+			tgo_rmsnorm(n, ut, 1, DM); /* n = rmsnorm(ut) * norm */
+			rowmul(n, d->norm[b], 1, DM);
+			qb_block(x, n, &d->w_x[b], d->bits, 1, DM, DI, 0, DI, d->w_x[b].s);
+			qb_block(z, n, &d->w_z[b], d->bits, 1, DM, DI, 0, DI, d->w_z[b].s);
+			for (int i = 0; i < DI; i++) { /* xc, left to right; then the carries shift */
+				float xc = (((c3[i] * cw[i] + c2[i] * cw[DI + i]) + c1[i] * cw[2 * DI + i]) + x[i] * cw[3 * DI + i]) +
+					   d->conv_b[b][i];
+				c3[i] = c2[i];
+				c2[i] = c1[i];
+				c1[i] = x[i];
+				xs[i] = silu1(xc);
+			}
+			qb_block(r, xs, &d->w_r[b], d->bits, 1, DI, R, 0, R, d->w_r[b].s);
+			qb_block(bt, xs, &d->w_b[b], d->bits, 1, DI, DS, 0, DS, d->w_b[b].s);
+			qb_block(ct, xs, &d->w_c[b], d->bits, 1, DI, DS, 0, DS, d->w_c[b].s);
+			qb_block(dt, r, &d->w_dt[b], d->bits, 1, R, DI, 0, DI, d->w_dt[b].s);
+			for (int i = 0; i < DI; i++) dt[i] = softplus1(dt[i] + d->dt_b[b][i]);
+			for (int i = 0; i < DI; i++) {
+				float m1 = 0.0f;
+				for (int s = 0; s < DS; s++) {
+					const long k = (long)i * DS + s;
+					float e = expf(-(dt[i] * A[k]));
+					float t1 = e * h[k], t3 = (1.0f - e) / A[k], t4 = xs[i] * bt[s];
+					h[k] = t1 + t3 * t4;
+				}
+				for (int s = 0; s < DS; s++) m1 += h[(long)i * DS + s] * ct[s]; /* h @ ct */
+				float y = m1 + d->d[b][i] * xs[i];
+				g[i] = y * silu1(z[i]);
+			}
+			qb_block(o, g, &d->w_o[b], d->bits, 1, DI, DM, 0, DM, d->w_o[b].s);
+			for (int i = 0; i < DM; i++) nxt[(long)t * DM + i] = ut[i] + o[i];
+		}
+		float *sw = cur;
+		cur = nxt;
+		nxt = sw;
+	}
+	tgo_rmsnorm(out, cur, T, DM);
+	rowmul(out, d->final_norm, T, DM);
+	free(cur); free(nxt); free(n); free(x); free(z); free(xs); free(c1); free(c2); free(c3);
+	free(r); free(bt); free(ct); free(dt); free(g); free(o); free(h);
+	return 0;
+}

@@ -54,6 +54,10 @@ int tgo_program_run(const tg_cuda_program *p, const float *row, float *out, int 
  * Scratch is allocated inside. */
 int tgo_lm_forward(const tg_cuda_lm_desc *d, const float *ids, int T, float *logits);
 
+/* The stacked selective-SSM program (tg_cuda_ssm_desc) over one sequence of T
+ * steps, u and out [T][d_model]. Scratch is allocated inside. */
+int tgo_ssm_forward(const tg_cuda_ssm_desc *d, const float *u, int T, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,8 @@ def tgo() -> C.CDLL:
         L.tgo_program_run.restype = C.c_int
         L.tgo_lm_forward.argtypes = [C.c_void_p, FP, C.c_int, FP]
         L.tgo_lm_forward.restype = C.c_int
+        L.tgo_ssm_forward.argtypes = [C.c_void_p, FP, C.c_int, FP]
+        L.tgo_ssm_forward.restype = C.c_int
         _tgo = L
     return _tgo
 
@@ -130,3 +132,13 @@ def program_run(prog, rows: np.ndarray, margins: bool = False):
     if margins:
         return out, steps[:, :m.nthink], marg[:, :m.nthink]
     return out, steps[:, :m.nthink]
+
+
+def ssm_forward(desc, u: np.ndarray) -> np.ndarray:
+    """tgo_ssm_forward over every sequence of u [S, T, d_model]."""
+    L = tgo()
+    u = np.ascontiguousarray(u, np.float32)
+    out = np.zeros_like(u)
+    for s in range(u.shape[0]):
+        L.tgo_ssm_forward(C.addressof(desc), f32p(u[s]), u.shape[1], out[s].ctypes.data_as(FP))
+    return out

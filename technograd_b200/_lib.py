@@ -26,7 +26,8 @@ SYMBOLS = ["tg_cuda_error", "tg_cuda_init", "tg_cuda_ngpus", "tg_cuda_shutdown",
            "tg_cuda_matmul_qb_noalloc",
            "tg_cuda_quantize_rtn", "tg_cuda_gptq_prepare", "tg_cuda_quantize_gptq", "tg_cuda_gptq_free", "tg_cuda_load", "tg_cuda_batch", "tg_cuda_batch_device", "tg_cuda_free",
            "tg_cuda_lm_load", "tg_cuda_lm_forward", "tg_cuda_lm_generate", "tg_cuda_lm_free", "tg_cuda_lm_profile",
-           "tg_cuda_lm_get_stats"]
+           "tg_cuda_lm_get_stats", "tg_cuda_ssm_load", "tg_cuda_ssm_forward", "tg_cuda_ssm_forward_device",
+           "tg_cuda_ssm_free", "tg_cuda_ssm_profile", "tg_cuda_ssm_get_stats"]
 
 
 class TgCudaError(RuntimeError):
@@ -77,6 +78,19 @@ class LmDesc(C.Structure):
                 ("wq", QP), ("wk", QP), ("wv", QP), ("wo", QP), ("wg", QP), ("wu", QP), ("wd", QP)]
 
 
+class SsmDesc(C.Structure):
+    _fields_ = [("blocks", C.c_int), ("d_model", C.c_int), ("d_inner", C.c_int), ("d_state", C.c_int),
+                ("dt_rank", C.c_int), ("bits", C.c_int), ("eps", C.c_float), ("final_norm", FP), ("norm", FPP),
+                ("conv_w", FPP), ("conv_b", FPP), ("dt_b", FPP), ("d", FPP), ("a", FPP),
+                ("w_x", QP), ("w_z", QP), ("w_r", QP), ("w_b", QP), ("w_c", QP), ("w_dt", QP), ("w_o", QP)]
+
+
+class SsmStats(C.Structure):
+    _fields_ = [("device_ms", C.c_double), ("launches", C.c_long), ("gemm_ms", C.c_double), ("gemm_flops", C.c_double),
+                ("gemm_launches", C.c_long), ("scan_ms", C.c_double), ("scan_flops", C.c_double),
+                ("scan_launches", C.c_long)]
+
+
 class LmStats(C.Structure):
     _fields_ = [("device_ms", C.c_double), ("launches", C.c_long), ("attn_decode_ms", C.c_double),
                 ("attn_decode_bytes", C.c_double), ("attn_decode_launches", C.c_long), ("attn_prefill_ms", C.c_double),
@@ -116,6 +130,12 @@ def lib() -> C.CDLL:
             "tg_cuda_lm_free": ([vp], None),
             "tg_cuda_lm_profile": ([vp, i], i),
             "tg_cuda_lm_get_stats": ([vp, C.POINTER(LmStats)], i),
+            "tg_cuda_ssm_load": ([C.POINTER(SsmDesc), i, i, C.POINTER(vp)], i),
+            "tg_cuda_ssm_forward": ([vp, vp, l, i, vp], i),
+            "tg_cuda_ssm_forward_device": ([vp, vp, l, i, vp], i),
+            "tg_cuda_ssm_free": ([vp], None),
+            "tg_cuda_ssm_profile": ([vp, i], i),
+            "tg_cuda_ssm_get_stats": ([vp, C.POINTER(SsmStats)], i),
         }
         for name, (args, res) in sigs.items():
             f = getattr(L, name)

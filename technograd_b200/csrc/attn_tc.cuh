@@ -1,0 +1,385 @@
+// attn_tc.cuh -- causal attention of the prefill on the tcgen05 tensor cores.
+//
+// The program's per-head attention (examples/qwen3/import.py:110-112):
+//   s = softmax((q @ transpose(k)) * scale + mask);  o = s @ v
+// with q, k, v f32 [T, 128] per head and the causal mask (-1e9 above the diagonal,
+// which the softmax turns into exact zeros). The f32 products are carried on the
+// bf16 tensor cores by the hi/lo split x = hi + lo (hi = bf16(x), lo = bf16(x - hi)):
+// x.y ~ hi.hi + hi.lo + lo.hi, three MMAs per product with f32 accumulation, which
+// keeps about 16 bits of each operand (relative error near 2^-17 per product).
+//
+// CTA = 128 queries of one head of one sequence; keys in tiles of 64. Warps:
+//   0-3  softmax: one query row per thread (TMEM lane = row). Reads the score tile
+//        from TMEM, applies scale and mask, keeps the running max and sum, writes the
+//        probabilities (split hi/lo) to shared memory as the A operand of P.V, and at
+//        the end reads O from TMEM, divides by the sum and stores it split hi/lo (the
+//        o_proj GEMM's input).
+//   4-7  loaders: Q once, then per key tile K (warps 4-5; rows = keys, K-major over
+//        dims) and V^T (warps 6-7; rows = dims, K-major over keys), f32 from the cache
+//        -> bf16 hi/lo in the 128-byte-swizzled K-major layout of the UMMA descriptors.
+//   8    TMEM allocation and the MMA issue (one thread): S_j = Q.K_j^T into one of two
+//        TMEM score buffers, O += P_j.V_j into the TMEM accumulator. S_{j+1} is issued
+//        before P_j.V_j so the softmax of tile j+1 overlaps the P.V of tile j.
+// O stays in TMEM across tiles. The probabilities use a running reference max that is
+// raised (and O, l rescaled in place) only when a tile's max exceeds it by more than
+// FA_RESCALE, so O is rarely touched between tiles; exp(s - m_ref) <= e^8 keeps the
+// sums well inside f32. The quotient O / l is the same as the reference's
+// exp(s - max) / sum, up to rounding.
+//
+// Every wait is bounded (tc.cuh); a timeout sets the status word and all roles
+// leave their loops, waiting for their own MMAs before TMEM is released.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "tc.cuh"
+
+namespace tgc {
+
+constexpr int FA_Q = 128, FA_K = 64, FA_HD = 128;
+constexpr float FA_RESCALE = 8.0f;
+constexpr int FA_THREADS = 288;
+
+// shared-memory layout (byte offsets from a 1024-aligned base); each tile is K-major
+// with 128-byte swizzle: rows of 128 bytes, 8-row atoms of 1024 bytes
+constexpr int FA_SQ_HI = 0;          // Q hi: [2 k-blocks][128 rows][128 B]
+constexpr int FA_SQ_LO = 32768;      // Q lo
+constexpr int FA_SK_HI = 65536;      // K hi: [2 k-blocks][64 rows][128 B]
+constexpr int FA_SK_LO = 81920;      // K lo
+constexpr int FA_SV_HI = 98304;      // V^T hi: [128 rows][128 B]
+constexpr int FA_SV_LO = 114688;     // V^T lo
+constexpr int FA_SP = 131072;        // P buffer b: hi at FA_SP + 32768 b, lo 16384 after it
+constexpr int FA_SBAR = 196608;      // barriers and the TMEM address
+constexpr size_t FA_SMEM = FA_SBAR + 256 + 1024; // + alignment slack
+
+struct FaBars {
+	uint64_t q_full, k_full, k_empty, v_full, v_empty;
+	uint64_t s_full[2], s_free[2], p_full[2], p_empty[2], done;
+	uint32_t tmem;
+	int abort;
+};
+
+__device__ __forceinline__ uint32_t fa_sw(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
+
+__device__ __forceinline__ uint32_t fa_pack(float a, float b)
+{
+	__nv_bfloat162 v = __floats2bfloat162_rn(a, b); // .x = a (low half), .y = b
+	return *(uint32_t *)&v;
+}
+
+// 8 floats -> one 16-byte chunk of bf16 hi and one of lo
+__device__ __forceinline__ void fa_split8(const float (&x)[8], uint4 &hi, uint4 &lo)
+{
+	float h[8], l[8];
+#pragma unroll
+	for (int i = 0; i < 8; i++) {
+		__nv_bfloat16 b = __float2bfloat16_rn(x[i]);
+		h[i] = __bfloat162float(b);
+		l[i] = x[i] - h[i];
+	}
+	hi = make_uint4(fa_pack(h[0], h[1]), fa_pack(h[2], h[3]), fa_pack(h[4], h[5]), fa_pack(h[6], h[7]));
+	lo = make_uint4(fa_pack(l[0], l[1]), fa_pack(l[2], l[3]), fa_pack(l[4], l[5]), fa_pack(l[6], l[7]));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16])
+{
+	asm volatile(
+		"tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+		::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+		  "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])),
+		  "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+		  "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+		  "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+		: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// A bounded wait that first checks the CTA's abort flag; false = leave the loop.
+// The softmax warps combine the lanes' results (fa_wait_warp) so a warp leaves together.
+__device__ __forceinline__ bool fa_wait(FaBars *B, uint64_t *bar, uint32_t parity, int *status)
+{
+	if (*(volatile int *)&B->abort) return false;
+	if (mbar_wait(bar, parity, status, ST_TIMEOUT_FULL)) return true;
+	*(volatile int *)&B->abort = 1;
+	return false;
+}
+
+__device__ __forceinline__ bool fa_wait_warp(FaBars *B, uint64_t *bar, uint32_t parity, int *status)
+{
+	return __all_sync(0xffffffffu, fa_wait(B, bar, parity, status));
+}
+
+// q: [seq][NQ][T][128] f32; kc/vc: the cache [slot][NKV][max_len][128] f32;
+// out hi/lo: [seq * T + t][NQ * 128 + h * 128 + d] bf16.
+__global__ void __launch_bounds__(FA_THREADS, 1)
+	k_attn_prefill_tc(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc, int T, int NQ,
+			  int NKV, int slot0, int max_len, float scale, __nv_bfloat16 *__restrict__ ohi,
+			  __nv_bfloat16 *__restrict__ olo, int *status)
+{
+	extern __shared__ uint8_t fa_raw[];
+	uint8_t *sm = fa_raw + ((1024 - (smem_u32(fa_raw) & 1023)) & 1023);
+	FaBars *B = (FaBars *)(sm + FA_SBAR);
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const int nqt = (T + FA_Q - 1) / FA_Q;
+	const int qt = nqt - 1 - (int)blockIdx.x; // the longest rows of the causal triangle start first
+	const int h = blockIdx.y, s = blockIdx.z;
+	const int kvh = h / (NQ / NKV);
+	const int q0 = qt * FA_Q;
+	const int nkt = (min(q0 + FA_Q, T) + FA_K - 1) / FA_K;
+
+	if (threadIdx.x == 0) {
+		mbar_init(&B->q_full, 128);
+		mbar_init(&B->k_full, 64);
+		mbar_init(&B->k_empty, 1);
+		mbar_init(&B->v_full, 64);
+		mbar_init(&B->v_empty, 1);
+		for (int b = 0; b < 2; b++) {
+			mbar_init(&B->s_full[b], 1);
+			mbar_init(&B->s_free[b], 128);
+			mbar_init(&B->p_full[b], 128);
+			mbar_init(&B->p_empty[b], 1);
+		}
+		mbar_init(&B->done, 1);
+		B->abort = 0;
+		fence_barrier_init();
+	}
+	if (warp == 8) tmem_alloc(&B->tmem, 256); // S buffers at columns 0 and 64, O at 128
+	tc_fence_before();
+	__syncthreads();
+	tc_fence_after();
+	const uint32_t tmem = B->tmem;
+
+	if (warp >= 4 && warp < 8) {
+		// ---------------- loaders ----------------
+		const int t = threadIdx.x - 128;
+		const float *qb = q + ((long)s * NQ + h) * (long)T * FA_HD;
+		const float *kb = kc + ((long)(slot0 + s) * NKV + kvh) * (long)max_len * FA_HD;
+		const float *vb = vc + ((long)(slot0 + s) * NKV + kvh) * (long)max_len * FA_HD;
+		for (int i = t; i < FA_Q * 16; i += 128) { // Q: 128 rows x 16 chunks of 8 dims
+			int r = i >> 4, c = i & 15;
+			float x[8];
+			if (q0 + r < T) {
+				float4 a = *(const float4 *)(qb + (long)(q0 + r) * FA_HD + c * 8);
+				float4 b = *(const float4 *)(qb + (long)(q0 + r) * FA_HD + c * 8 + 4);
+				x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+			} else {
+#pragma unroll
+				for (int e = 0; e < 8; e++) x[e] = 0.0f;
+			}
+			uint4 hi, lo;
+			fa_split8(x, hi, lo);
+			uint32_t off = (uint32_t)((c >> 3) * 16384) + fa_sw(r, c & 7);
+			*(uint4 *)(sm + FA_SQ_HI + off) = hi;
+			*(uint4 *)(sm + FA_SQ_LO + off) = lo;
+		}
+		fence_async_smem();
+		mbar_arrive(&B->q_full);
+		const int u = t & 63; // warps 4-5 load K tiles, warps 6-7 V tiles
+		for (int j = 0; j < nkt; j++) {
+			const int k0 = j * FA_K;
+			if (t < 64) {
+				if (j > 0 && !fa_wait(B, &B->k_empty, (j - 1) & 1, status)) break;
+				for (int i = u; i < FA_K * 16; i += 64) { // K: 64 rows x 16 chunks
+					int r = i >> 4, c = i & 15;
+					float x[8];
+					if (k0 + r < T) {
+						float4 a = *(const float4 *)(kb + (long)(k0 + r) * FA_HD + c * 8);
+						float4 b = *(const float4 *)(kb + (long)(k0 + r) * FA_HD + c * 8 + 4);
+						x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+					} else {
+#pragma unroll
+						for (int e = 0; e < 8; e++) x[e] = 0.0f;
+					}
+					uint4 hi, lo;
+					fa_split8(x, hi, lo);
+					uint32_t off = (uint32_t)((c >> 3) * 8192) + fa_sw(r, c & 7);
+					*(uint4 *)(sm + FA_SK_HI + off) = hi;
+					*(uint4 *)(sm + FA_SK_LO + off) = lo;
+				}
+				fence_async_smem();
+				mbar_arrive(&B->k_full);
+			} else {
+				if (j > 0 && !fa_wait(B, &B->v_empty, (j - 1) & 1, status)) break;
+				for (int i = u; i < 256; i += 64) { // V^T: item = (8 keys, 4 dims) -> one chunk in 4 rows
+					int kg = i & 7, dg = i >> 3;
+					float x[8][4];
+#pragma unroll
+					for (int e = 0; e < 8; e++) {
+						int key = k0 + kg * 8 + e;
+						float4 a = key < T ? *(const float4 *)(vb + (long)key * FA_HD + dg * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+						x[e][0] = a.x, x[e][1] = a.y, x[e][2] = a.z, x[e][3] = a.w;
+					}
+#pragma unroll
+					for (int dd = 0; dd < 4; dd++) {
+						float col[8];
+#pragma unroll
+						for (int e = 0; e < 8; e++) col[e] = x[e][dd];
+						uint4 hi, lo;
+						fa_split8(col, hi, lo);
+						uint32_t off = fa_sw(dg * 4 + dd, kg);
+						*(uint4 *)(sm + FA_SV_HI + off) = hi;
+						*(uint4 *)(sm + FA_SV_LO + off) = lo;
+					}
+				}
+				fence_async_smem();
+				mbar_arrive(&B->v_full);
+			}
+		}
+	} else if (warp == 8) {
+		// ---------------- MMA issue ----------------
+		if (lane == 0) {
+			const uint32_t idS = idesc_bf16_f32(FA_Q, FA_K), idO = idesc_bf16_f32(FA_Q, FA_HD);
+			const uint32_t base = smem_u32(sm);
+			bool ok = fa_wait(B, &B->q_full, 0, status);
+			auto issue_s = [&](int j) -> bool {
+				if (!fa_wait(B, &B->k_full, j & 1, status)) return false;
+				if (j >= 2 && !fa_wait(B, &B->s_free[j & 1], ((j >> 1) - 1) & 1, status)) return false;
+				tc_fence_after();
+				const uint32_t d = tmem + (uint32_t)((j & 1) * FA_K);
+				const uint32_t qa[2] = { base + FA_SQ_HI, base + FA_SQ_LO }, ka[2] = { base + FA_SK_HI, base + FA_SK_LO };
+				const int pa[3] = { 0, 0, 1 }, pb[3] = { 0, 1, 0 };
+				uint32_t acc = 0;
+				for (int kb = 0; kb < 2; kb++)
+					for (int kk = 0; kk < 4; kk++)
+						for (int pr = 0; pr < 3; pr++) {
+							uint32_t a = qa[pa[pr]] + kb * 16384 + kk * 32, b = ka[pb[pr]] + kb * 8192 + kk * 32;
+							tc_mma_f16(d, sw128_kmajor_desc(a), sw128_kmajor_desc(b), idS, acc);
+							acc = 1;
+						}
+				tc_commit(&B->s_full[j & 1]);
+				tc_commit(&B->k_empty);
+				return true;
+			};
+			auto issue_pv = [&](int j) -> bool {
+				if (!fa_wait(B, &B->v_full, j & 1, status)) return false;
+				if (!fa_wait(B, &B->p_full[j & 1], (j >> 1) & 1, status)) return false;
+				tc_fence_after();
+				const uint32_t pbuf = base + FA_SP + (uint32_t)((j & 1) * 32768);
+				const uint32_t pa2[2] = { pbuf, pbuf + 16384 }, va[2] = { base + FA_SV_HI, base + FA_SV_LO };
+				const int pa[3] = { 0, 0, 1 }, pb[3] = { 0, 1, 0 };
+				for (int kk = 0; kk < 4; kk++)
+					for (int pr = 0; pr < 3; pr++) {
+						uint32_t a = pa2[pa[pr]] + kk * 32, b = va[pb[pr]] + kk * 32;
+						tc_mma_f16(tmem + 128, sw128_kmajor_desc(a), sw128_kmajor_desc(b), idO,
+							   (j > 0 || kk > 0 || pr > 0) ? 1u : 0u);
+					}
+				tc_commit(&B->p_empty[j & 1]);
+				tc_commit(&B->v_empty);
+				return true;
+			};
+			if (ok) ok = issue_s(0);
+			for (int j = 0; ok && j < nkt; j++) {
+				if (j + 1 < nkt) ok = issue_s(j + 1);
+				if (ok) ok = issue_pv(j);
+			}
+			// every MMA issued has completed before TMEM is released (also after an abort)
+			tc_commit(&B->done);
+			mbar_wait(&B->done, 0, status, ST_TIMEOUT_ACC);
+		}
+		__syncwarp();
+	} else {
+		// ---------------- softmax / epilogue (warps 0-3) ----------------
+		const int row = threadIdx.x; // TMEM lane, query q0 + row
+		const int qi = q0 + row;
+		const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+		float m_ref = -INFINITY, l = 0.0f;
+		bool ok = true;
+		for (int j = 0; j < nkt && ok; j++) {
+			const int k0 = j * FA_K;
+			if (!(ok = fa_wait_warp(B, &B->s_full[j & 1], (j >> 1) & 1, status))) break;
+			tc_fence_after();
+			float sc[FA_K];
+#pragma unroll
+			for (int c = 0; c < FA_K / 16; c++) {
+				float v[16];
+				tmem_ld16(lane_base + (uint32_t)((j & 1) * FA_K + c * 16), v);
+#pragma unroll
+				for (int e = 0; e < 16; e++) sc[c * 16 + e] = v[e];
+			}
+			tc_fence_before();
+			mbar_arrive(&B->s_free[j & 1]);
+			float mt = -INFINITY;
+#pragma unroll
+			for (int c = 0; c < FA_K; c++) {
+				const int kj = k0 + c;
+				float v = kj <= qi && kj < T ? __fmul_rn(sc[c], scale) : -INFINITY;
+				sc[c] = v;
+				mt = fmaxf(mt, v);
+			}
+			const bool raise = mt > m_ref + FA_RESCALE;
+			const float m_new = raise ? mt : m_ref;
+			if (__any_sync(0xffffffffu, raise && m_ref != -INFINITY)) {
+				// O holds P.V of tiles < j at the old reference max: wait for P_{j-1}.V, rescale in place
+				if (!(ok = fa_wait_warp(B, &B->p_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, status))) break;
+				tc_fence_after();
+				const float f = raise && m_ref != -INFINITY ? expf(m_ref - m_new) : 1.0f;
+#pragma unroll 1
+				for (int c = 0; c < FA_HD / 16; c++) {
+					float v[16];
+					tmem_ld16(lane_base + 128 + c * 16, v);
+#pragma unroll
+					for (int e = 0; e < 16; e++) v[e] *= f;
+					tmem_st16(lane_base + 128 + c * 16, v);
+				}
+				tmem_wait_st();
+				l *= f;
+			}
+			m_ref = m_new;
+			float sum = 0.0f;
+#pragma unroll
+			for (int c = 0; c < FA_K; c++) {
+				float p = sc[c] == -INFINITY ? 0.0f : expf(sc[c] - m_ref);
+				sc[c] = p;
+				sum += p;
+			}
+			l += sum;
+			// P buffer j&1 was last read by P_{j-2}.V
+			if (j >= 2 && !(ok = fa_wait_warp(B, &B->p_empty[j & 1], ((j >> 1) - 1) & 1, status))) break;
+			uint8_t *pb = sm + FA_SP + (j & 1) * 32768;
+#pragma unroll
+			for (int c = 0; c < 8; c++) {
+				float x[8];
+#pragma unroll
+				for (int e = 0; e < 8; e++) x[e] = sc[c * 8 + e];
+				uint4 hi, lo;
+				fa_split8(x, hi, lo);
+				*(uint4 *)(pb + fa_sw(row, c)) = hi;
+				*(uint4 *)(pb + 16384 + fa_sw(row, c)) = lo;
+			}
+			fence_async_smem();
+			tc_fence_before();
+			mbar_arrive(&B->p_full[j & 1]);
+		}
+		if (ok) ok = fa_wait_warp(B, &B->p_empty[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, status);
+		if (ok) {
+			tc_fence_after();
+			const float inv = 1.0f / l;
+			const long ob = ((long)s * T + qi) * (long)NQ * FA_HD + (long)h * FA_HD;
+#pragma unroll 1
+			for (int c = 0; c < FA_HD / 16; c++) {
+				float v[16];
+				tmem_ld16(lane_base + 128 + c * 16, v);
+				if (qi < T) {
+#pragma unroll
+					for (int half = 0; half < 2; half++) {
+						float x[8];
+#pragma unroll
+						for (int e = 0; e < 8; e++) x[e] = v[half * 8 + e] * inv;
+						uint4 hi, lo;
+						fa_split8(x, hi, lo);
+						*(uint4 *)(ohi + ob + c * 16 + half * 8) = hi;
+						*(uint4 *)(olo + ob + c * 16 + half * 8) = lo;
+					}
+				}
+			}
+		}
+	}
+	tc_fence_before();
+	__syncthreads();
+	if (warp == 8) {
+		tc_fence_after();
+		tmem_dealloc(tmem, 256);
+	}
+}
+
+} // namespace tgc

@@ -32,6 +32,7 @@
 #include <thread>
 #include <vector>
 
+#include "attn_tc.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
@@ -168,147 +169,7 @@ __global__ void k_qk_rope(const float *__restrict__ qkv, long M, int T, int pos0
 	else ((float4 *)(kc + (((long)(slot0 + s) * NKV + (hh - NQ)) * max_len + pos) * HD))[lane] = res;
 }
 
-// ---- causal attention for the prefill, f32 on CUDA cores ------------------------------------
-// CTA = (64 queries, head, sequence); K/V tiles of 64 positions; online softmax.
-// Thread (ty, tx) of a 16 x 16 grid owns score rows ty + 16 r and columns tx + 16 c,
-// and output rows ty + 16 r, columns 4 tx.. and 64 + 4 tx...
-constexpr int AQ = 64, AK = 64, APAD = 132;
-
-__global__ void __launch_bounds__(256) k_attn_prefill(const float *__restrict__ q, const float *__restrict__ kc,
-						      const float *__restrict__ vc, int T, int NQ, int NKV, int slot0,
-						      int max_len, float scale, __nv_bfloat16 *__restrict__ ohi,
-						      __nv_bfloat16 *__restrict__ olo)
-{
-	constexpr int HD = 128;
-	extern __shared__ float sm[];
-	float *Qs = sm;                 // [64][132]
-	float *Ks = Qs + AQ * APAD;     // [64][132]
-	float *Vs = Ks + AK * APAD;     // [64][128]
-	float *Ps = Vs + AK * HD;       // [64][68]
-	const int qt = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
-	const int kvh = h / (NQ / NKV);
-	const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-	const int q0 = qt * AQ;
-	const float *qb = q + (((long)s * NQ + h) * T) * HD;
-	const float *kb = kc + (((long)(slot0 + s) * NKV + kvh) * max_len) * HD;
-	const float *vb = vc + (((long)(slot0 + s) * NKV + kvh) * max_len) * HD;
-	for (int i = tid; i < AQ * HD / 4; i += 256) {
-		int r = i / (HD / 4), c = (i % (HD / 4)) * 4;
-		float4 v = q0 + r < T ? *(const float4 *)(qb + (long)(q0 + r) * HD + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-		*(float4 *)(Qs + r * APAD + c) = v;
-	}
-	float m[4], l[4], o[4][8];
-#pragma unroll
-	for (int r = 0; r < 4; r++) {
-		m[r] = -INFINITY;
-		l[r] = 0.0f;
-#pragma unroll
-		for (int c = 0; c < 8; c++) o[r][c] = 0.0f;
-	}
-	const int nkt = min((q0 + AQ + AK - 1) / AK, (T + AK - 1) / AK);
-	for (int kt = 0; kt < nkt; kt++) {
-		const int k0 = kt * AK;
-		__syncthreads();
-		for (int i = tid; i < AK * HD / 4; i += 256) {
-			int r = i / (HD / 4), c = (i % (HD / 4)) * 4;
-			bool in = k0 + r < T;
-			float4 kv = in ? *(const float4 *)(kb + (long)(k0 + r) * HD + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-			float4 vv = in ? *(const float4 *)(vb + (long)(k0 + r) * HD + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-			*(float4 *)(Ks + r * APAD + c) = kv;
-			*(float4 *)(Vs + r * HD + c) = vv;
-		}
-		__syncthreads();
-		float sc[4][4];
-#pragma unroll
-		for (int r = 0; r < 4; r++)
-#pragma unroll
-			for (int c = 0; c < 4; c++) sc[r][c] = 0.0f;
-#pragma unroll 4
-		for (int d = 0; d < HD; d += 4) {
-			float4 qa[4], ka[4];
-#pragma unroll
-			for (int r = 0; r < 4; r++) qa[r] = *(const float4 *)(Qs + (ty + 16 * r) * APAD + d);
-#pragma unroll
-			for (int c = 0; c < 4; c++) ka[c] = *(const float4 *)(Ks + (tx + 16 * c) * APAD + d);
-#pragma unroll
-			for (int r = 0; r < 4; r++)
-#pragma unroll
-				for (int c = 0; c < 4; c++) {
-					sc[r][c] = fmaf(qa[r].x, ka[c].x, sc[r][c]);
-					sc[r][c] = fmaf(qa[r].y, ka[c].y, sc[r][c]);
-					sc[r][c] = fmaf(qa[r].z, ka[c].z, sc[r][c]);
-					sc[r][c] = fmaf(qa[r].w, ka[c].w, sc[r][c]);
-				}
-		}
-		// scale, causal mask, online softmax over the 16 threads of this half-warp
-#pragma unroll
-		for (int r = 0; r < 4; r++) {
-			const int qi = q0 + ty + 16 * r;
-			float mx = -INFINITY;
-#pragma unroll
-			for (int c = 0; c < 4; c++) {
-				const int kj = k0 + tx + 16 * c;
-				float v = kj <= qi && kj < T ? __fmul_rn(sc[r][c], scale) : -INFINITY;
-				sc[r][c] = v;
-				mx = fmaxf(mx, v);
-			}
-#pragma unroll
-			for (int off = 8; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-			const float mnew = fmaxf(m[r], mx);
-			const float corr = mnew == -INFINITY ? 1.0f : expf(m[r] - mnew);
-			float sum = 0.0f;
-#pragma unroll
-			for (int c = 0; c < 4; c++) {
-				float p = sc[r][c] == -INFINITY ? 0.0f : expf(sc[r][c] - mnew);
-				Ps[(ty + 16 * r) * 68 + tx + 16 * c] = p;
-				sum += p;
-			}
-#pragma unroll
-			for (int off = 8; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-			l[r] = l[r] * corr + sum;
-			m[r] = mnew;
-#pragma unroll
-			for (int c = 0; c < 8; c++) o[r][c] *= corr;
-		}
-		__syncthreads();
-#pragma unroll 2
-		for (int j = 0; j < AK; j += 4) {
-			float4 pr[4];
-#pragma unroll
-			for (int r = 0; r < 4; r++) pr[r] = *(const float4 *)(Ps + (ty + 16 * r) * 68 + j);
-#pragma unroll
-			for (int jj = 0; jj < 4; jj++) {
-				float4 va = *(const float4 *)(Vs + (j + jj) * HD + 4 * tx);
-				float4 vb2 = *(const float4 *)(Vs + (j + jj) * HD + 64 + 4 * tx);
-#pragma unroll
-				for (int r = 0; r < 4; r++) {
-					float p = jj == 0 ? pr[r].x : jj == 1 ? pr[r].y : jj == 2 ? pr[r].z : pr[r].w;
-					o[r][0] = fmaf(p, va.x, o[r][0]);
-					o[r][1] = fmaf(p, va.y, o[r][1]);
-					o[r][2] = fmaf(p, va.z, o[r][2]);
-					o[r][3] = fmaf(p, va.w, o[r][3]);
-					o[r][4] = fmaf(p, vb2.x, o[r][4]);
-					o[r][5] = fmaf(p, vb2.y, o[r][5]);
-					o[r][6] = fmaf(p, vb2.z, o[r][6]);
-					o[r][7] = fmaf(p, vb2.w, o[r][7]);
-				}
-			}
-		}
-	}
-	// out[(s*T + t)][h*HD + c], split hi/lo for the o_proj GEMM
-#pragma unroll
-	for (int r = 0; r < 4; r++) {
-		const int t = q0 + ty + 16 * r;
-		if (t >= T) continue;
-		const float inv = 1.0f / l[r];
-		const long base = ((long)s * T + t) * (long)NQ * HD + (long)h * HD;
-#pragma unroll
-		for (int c = 0; c < 8; c++) {
-			int col = c < 4 ? 4 * tx + c : 64 + 4 * tx + (c - 4);
-			split_bf16(o[r][c] * inv, ohi[base + col], olo[base + col]);
-		}
-	}
-}
+// causal attention of the prefill: k_attn_prefill_tc (attn_tc.cuh)
 
 // ---- decode attention over the KV cache -------------------------------------------------------
 // CTA = (kv head, sequence); the GRP query heads sharing that kv head are done together.
@@ -589,7 +450,6 @@ static void call_end(Engine &g)
 	g.last = t;
 }
 
-static size_t prefill_smem() { return (size_t)(AQ * APAD + AK * APAD + AK * 128 + AQ * 68) * 4; }
 static size_t decode_smem(const Engine &g)
 {
 	const int grp = g.NQ / g.NKV;
@@ -706,7 +566,7 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 	}
 	// kernel attributes are set here, never inside a graph capture
 	if (decode_smem(g) > 220 * 1024) return set_err(TG_CUDA_EINVAL, "max_len %d: decode scores exceed shared memory", max_len);
-	TGC_CUDA(cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prefill_smem()));
+	TGC_CUDA(cudaFuncSetAttribute(k_attn_prefill_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FA_SMEM));
 	TGC_CUDA(cudaFuncSetAttribute(k_attn_decode<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_smem(g)));
 	TGC_CUDA(cudaFuncSetAttribute(k_attn_decode<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_smem(g)));
 	TGC_CUDA(cudaMemsetAsync(g.status.p, 0, 64, g.st));
@@ -750,11 +610,11 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 			g.qkv.as<float>(), M, T, pos0, decode ? g.dpos.as<int>() : nullptr, NQ, NKV, g.eps, Y.qn.as<float>(),
 			Y.kn.as<float>(), g.cosT.as<float>(), g.sinT.as<float>(), g.q.as<float>(), kc, vc, slot0, g.max_len);
 		if (!decode) {
-			size_t smem = prefill_smem();
-			dim3 grid((T + AQ - 1) / AQ, NQ, (unsigned)S);
+			dim3 grid((T + FA_Q - 1) / FA_Q, NQ, (unsigned)S);
 			int mk = mark_begin(g, MK_PREFILL, 4.0 * HD * (double)T * (T + 1) / 2 * NQ * S);
-			k_attn_prefill<<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, T, NQ, NKV, slot0, g.max_len, g.scale,
-								  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>());
+			k_attn_prefill_tc<<<grid, FA_THREADS, FA_SMEM, g.st>>>(g.q.as<float>(), kc, vc, T, NQ, NKV, slot0, g.max_len,
+									       g.scale, g.ahi.as<__nv_bfloat16>(),
+									       g.alo.as<__nv_bfloat16>(), status);
 			mark_end(g, mk);
 		} else {
 			// the key count (position + 1) is read on the device; bytes = per-key part * len + the rest

@@ -228,6 +228,101 @@ def nano(tgc: str) -> None:
             f.write(" ".join(f"{k}={v}" for k, v in cfg.items()) + "\n")
 
 
+# ---- stacked selective-SSM blocks (config 3) at toy sizes -------------------------------------
+NANO_SSM = dict(blocks=2, d_model=16, d_inner=32, d_state=4, dt_rank=4, T=10)
+
+
+def ssm_weights(cfg: dict, seed: int) -> dict:
+    """Projections, conv weights ~ N(0, 0.02) (the config's init); norms 1 + N(0, 0.1) so they
+    matter; a = 1..d_state per channel (a positive decay rate, as exp(A_log) of Mamba's
+    init); d = 1; the dt bias the inverse softplus of dt log-uniform in [1e-3, 1e-1]."""
+    rng = np.random.default_rng(seed)
+    B, DM, DI, DS, R = (cfg[k] for k in ("blocks", "d_model", "d_inner", "d_state", "dt_rank"))
+    g = lambda *s: rng.normal(0, 0.02, size=s).astype(np.float32)  # noqa: E731
+    w = {"nf": (1 + rng.normal(0, 0.1, size=DM)).astype(np.float32)}
+    for b in range(B):
+        w[f"nw_{b}"] = (1 + rng.normal(0, 0.1, size=DM)).astype(np.float32)
+        w[f"Wx_{b}"], w[f"Wz_{b}"] = g(DM, DI), g(DM, DI)
+        for i in range(4):
+            w[f"cw{i}_{b}"] = g(DI)
+        w[f"cb_{b}"] = g(DI)
+        w[f"Wr_{b}"], w[f"WB_{b}"], w[f"WC_{b}"] = g(DI, R), g(DI, DS), g(DI, DS)
+        w[f"Wdt_{b}"] = g(R, DI)
+        dt = np.exp(rng.uniform(np.log(1e-3), np.log(1e-1), size=DI))
+        w[f"bdt_{b}"] = (dt + np.log(-np.expm1(-dt))).astype(np.float32)  # softplus^-1(dt)
+        w[f"A_{b}"] = np.tile(np.arange(1, DS + 1, dtype=np.float32), (DI, 1))
+        w[f"D_{b}"] = np.ones(DI, np.float32)
+        w[f"Wo_{b}"] = g(DI, DM)
+    return w
+
+
+def emit_ssm(cfg: dict, w: dict, outdir: str, T: int) -> str:
+    """The config-3 program in the reference's language: per block one scan over the steps
+    with the state h and the last three conv inputs as carries (include/tg_cuda.h
+    tg_cuda_ssm_desc states the arithmetic)."""
+    B, DM, DI, DS, R = (cfg[k] for k in ("blocks", "d_model", "d_inner", "d_state", "dt_rank"))
+    os.makedirs(os.path.join(outdir, "w"), exist_ok=True)
+    tables = {"Zh": np.zeros((DI, DS), np.float32), "Zc": np.zeros(DI, np.float32)}
+    for name, arr in list(w.items()) + list(tables.items()):
+        np.asarray(arr, dtype="<f4").tofile(os.path.join(outdir, "w", name + ".bin"))
+    lines = ["model ssm", ""]
+
+    def par(name, *shape):
+        lines.append(f'param {name} : f32[{", ".join(map(str, shape))}] = file("w/{name}.bin")')
+
+    par("nf", DM), par("Zh", DI, DS), par("Zc", DI)
+    for b in range(B):
+        par(f"nw_{b}", DM), par(f"Wx_{b}", DM, DI), par(f"Wz_{b}", DM, DI)
+        for i in range(4):
+            par(f"cw{i}_{b}", DI)
+        par(f"cb_{b}", DI), par(f"Wr_{b}", DI, R), par(f"WB_{b}", DI, DS), par(f"WC_{b}", DI, DS)
+        par(f"Wdt_{b}", R, DI), par(f"bdt_{b}", DI), par(f"A_{b}", DI, DS), par(f"D_{b}", DI), par(f"Wo_{b}", DI, DM)
+    lines += ["", f"def forward(u0: f32[{T}, {DM}]) -> f32[{T}, {DM}]:"]
+    for b in range(B):
+        lines += [f"    h{b} = Zh", f"    c1_{b} = Zc", f"    c2_{b} = Zc", f"    c3_{b} = Zc",
+                  f"    scan h{b}, c1_{b}, c2_{b}, c3_{b} over ut in u{b}:",
+                  f"        n = rmsnorm(ut) * nw_{b}",
+                  f"        xi = n @ Wx_{b}",
+                  f"        z = n @ Wz_{b}",
+                  f"        xc = c3_{b} * cw0_{b} + c2_{b} * cw1_{b} + c1_{b} * cw2_{b} + xi * cw3_{b} + cb_{b}",
+                  f"        c3_{b} = c2_{b}",
+                  f"        c2_{b} = c1_{b}",
+                  f"        c1_{b} = xi",
+                  "        xs = silu(xc)",
+                  f"        dt = softplus((xs @ Wr_{b}) @ Wdt_{b} + bdt_{b})",
+                  f"        bt = xs @ WB_{b}",
+                  f"        ct = xs @ WC_{b}",
+                  f"        e = exp(-(reshape(dt, {DI}, 1) * A_{b}))",
+                  f"        h{b} = e * h{b} + (1 - e) / A_{b} * outer(xs, bt)",
+                  f"        y = h{b} @ ct + D_{b} * xs",
+                  f"        emit u{b + 1} = ut + (y * silu(z)) @ Wo_{b}"]
+    lines.append(f"    return rmsnorm(u{B}) * nf")
+    path = os.path.join(outdir, "ssm.tg")
+    with open(path, "w") as f:
+        f.write("\n".join(lines) + "\n")
+    return path
+
+
+def nano_ssm(tgc: str) -> None:
+    cfg = NANO_SSM
+    T = cfg["T"]
+    out = os.path.join(HERE, "nano_ssm")
+    os.makedirs(out, exist_ok=True)
+    w = ssm_weights(cfg, 6)
+    rows = np.round(np.random.default_rng(7).normal(0, 1, size=(6, T * cfg["d_model"])), 4).astype(np.float32)
+    with tempfile.TemporaryDirectory() as tmp:
+        prog = emit_ssm(cfg, w, tmp, T)
+        np.savetxt(os.path.join(tmp, "u.csv"), rows, fmt="%.9g", delimiter=",")
+        for tag, flags in (("q8", ["--bits", "8"]), ("q4", ["--bits", "4"])):
+            qp = os.path.join(tmp, f"{tag}.tgir")
+            sh(tgc, "quantize", prog, "--min-size", "1", *flags, "-o", qp)
+            shutil.copy(qp, os.path.join(out, f"{tag}.tgir"))
+            sh(tgc, "batch", qp, os.path.join(tmp, "u.csv"), "-j", "1", "-o", os.path.join(out, f"{tag}_out.csv"))
+        shutil.copy(os.path.join(tmp, "u.csv"), os.path.join(out, "u.csv"))
+        with open(os.path.join(out, "config.txt"), "w") as f:
+            f.write(" ".join(f"{k}={v}" for k, v in cfg.items()) + "\n")
+
+
 # The reference's control-flow test programs: scan carries and stacked outputs, think
 # loops (`until` and learned halting), gradients through loops (lowered into the IR by
 # the compiler), and rope + windowed attention. name -> (source, rows, value range)

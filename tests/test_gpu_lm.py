@@ -38,9 +38,11 @@ def micro(request, cuda):
 
 def test_prefill_logits_vs_oracle(micro):
     rng = np.random.default_rng(3)
-    for T in (1, 5, 64, 77):
+    # query tiles of 128 and key tiles of 64: T = 77 is one partial query tile, 300 three
+    # query tiles (the last partial) over five key tiles
+    for T in (1, 5, 64, 77, 128, 300):
         ids = rng.integers(0, MICRO["vocab"], size=(3, T)).astype(np.float32)
-        eng = lm.Engine(micro, max_seqs=4, max_len=128)
+        eng = lm.Engine(micro, max_seqs=4, max_len=320)
         got = eng.forward(ids)
         want = oracle_logits(micro, ids)
         np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL, err_msg=f"T={T}")
