@@ -54,7 +54,9 @@ void tg_cuda_shutdown(void);
  * e in byte e/2, low nibble first, sign-extended (runtime/tg_rt.h:124-129).
  * All pointers are DEVICE pointers on the current device; the call is
  * asynchronous on `stream` (NULL = the legacy default stream). Scratch for the
- * tensor-core path (m*k or k*n large) is cached per device by the library. */
+ * tensor-core path (m*k or k*n large) is cached per device by the library. A
+ * tensor-core kernel that gave up waiting (TG_CUDA_EDEVICE) is reported by a
+ * later call on the same device, like CUDA's own asynchronous errors. */
 int tg_cuda_matmul_q(int axis, float *o, const float *act, const signed char *q, int bits, const float *s, int m,
 		     int k, int n, void *stream);
 

@@ -35,8 +35,8 @@ struct GemmArgs {
 	long mpad;               // set by gemm(): rows per split block of the partial buffer
 };
 
-// Launch on stream. SwiGLU: B rows come in blocks of 256 (128 gate rows then the
-// 128 matching up rows), N = 2 * channels, output channels = N / 2.
+// Launch on stream. SwiGLU: B rows come in blocks of 64 (32 gate rows then the
+// 32 matching up rows), N = 2 * channels, output channels = N / 2.
 int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st);
 
 int split_to_bf16(const float *src, long rows, long cols, long lds, bool transpose, __nv_bfloat16 *hi, __nv_bfloat16 *lo,

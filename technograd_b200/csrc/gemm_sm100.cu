@@ -124,17 +124,17 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 		tc_fence_after();
 		const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
 		if (EPI == EPI_SWIGLU) {
-			// columns [0, BN/2) are gate channels, [BN/2, BN) the matching up channels. The
-			// results (bf16 hi, lo) are staged in the idle ring as 128-byte-swizzled chunks
-			// of 64 channels, then written by TMA stores.
+			// columns come in blocks of 64: 32 gate channels, then the matching 32 up channels.
+			// The results (bf16 hi, lo) are staged in the idle ring as 128-byte-swizzled
+			// chunks of 64 channels, then written by TMA stores (direct stores when BN = 64).
 			const int f0 = blockIdx.x * (BN / 2);
 			for (int c = 0; c < BN / 2; c += 32) {
 				float g[32], u[32];
 				__syncwarp();
-				tmem_ld16(trow + c, *(float(*)[16])g);
-				tmem_ld16(trow + c + 16, *(float(*)[16])(g + 16));
-				tmem_ld16(trow + BN / 2 + c, *(float(*)[16])u);
-				tmem_ld16(trow + BN / 2 + c + 16, *(float(*)[16])(u + 16));
+				tmem_ld16(trow + 2 * c, *(float(*)[16])g);
+				tmem_ld16(trow + 2 * c + 16, *(float(*)[16])(g + 16));
+				tmem_ld16(trow + 2 * c + 32, *(float(*)[16])u);
+				tmem_ld16(trow + 2 * c + 48, *(float(*)[16])(u + 16));
 				uint32_t hi[16], lo[16];
 #pragma unroll
 				for (int i = 0; i < 32; i++) {
@@ -310,6 +310,7 @@ static int launch_bn(const TmaMaps &maps, const GemmArgs &p, cudaStream_t st)
 
 static int launch_split(int BN, int stages, const TmaMaps &maps, const GemmArgs &q, dim3, cudaStream_t st)
 {
+	if (BN == 64) return launch_bn<64, 4, EPI_PARTIAL>(maps, q, st);
 	if (BN == 256)
 		return stages >= 4 ? launch_bn<256, 4, EPI_PARTIAL>(maps, q, st)
 		       : stages == 3 ? launch_bn<256, 3, EPI_PARTIAL>(maps, q, st) : launch_bn<256, 2, EPI_PARTIAL>(maps, q, st);
@@ -326,7 +327,7 @@ __global__ void k_split_reduce(const float *__restrict__ part, int splits, long 
 	if (t >= (long)M * outc) return;
 	const int m = (int)(t / outc), n = (int)(t % outc);
 	if (EPI == EPI_SWIGLU) {
-		const int gc = (n / 128) * 256 + n % 128, uc = gc + 128;
+		const int gc = (n / 32) * 64 + n % 32, uc = gc + 32;
 		float g = 0.0f, u = 0.0f;
 		for (int z = 0; z < splits; z++) {
 			g += part[((long)z * mpad + m) * N + gc];
@@ -354,7 +355,14 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 	if (p.M <= 0 || p.N <= 0 || p.K <= 0 || p.na < 1 || p.na > 2 || p.nb < 1 || p.nb > 2 || p.npairs < 1 || p.npairs > 4)
 		return set_err(TG_CUDA_EINVAL, "gemm: bad shape or operand count");
 	if (p.K % 8) return set_err(TG_CUDA_EINVAL, "gemm: K %d is not a multiple of 8", p.K);
-	const int BN = p.epi == EPI_SWIGLU || p.N >= 256 ? 256 : 128;
+	int sms = 148, dev = 0;
+	cudaGetDevice(&dev);
+	cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+	// Small batches (decode): tiles of 64 columns when the wide tiles would leave most SMs idle;
+	// each CTA then streams a narrower slab of the weights and no K split may be needed.
+	const long mtiles = (p.M + BM - 1) / BM;
+	int BN = p.epi == EPI_SWIGLU || p.N >= 256 ? 256 : 128;
+	if (((p.N + BN - 1) / BN) * mtiles * 2 <= sms && p.N % 64 == 0 && mtiles <= 4) BN = 64;
 	TmaMaps maps;
 	memset(&maps, 0, sizeof maps);
 	for (int i = 0; i < p.na; i++)
@@ -366,9 +374,6 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 	const int stages = std::min(4, std::max(2, (220 * 1024) / stage));
 	// Split K when the tiles would leave most SMs idle (small-batch decode): each split stores raw
 	// f32 sums into the caller's partial buffer, then k_split_reduce adds them in a fixed order.
-	int sms = 148, dev = 0;
-	cudaGetDevice(&dev);
-	cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
 	const long tiles = (long)((p.N + BN - 1) / BN) * ((p.M + BM - 1) / BM);
 	const int KBall = (p.K + BK - 1) / BK;
 	int splits = 1;
@@ -403,8 +408,8 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 	// ring once the main loop has drained it (128 rows x BN f32, or 4 bf16 chunks of 16 KB)
 	p.tma_out = 0;
 	if (p.epi == EPI_SWIGLU) {
-		if ((p.ldo * 2) % 16 == 0 && !((uintptr_t)p.out_hi & 15) && !((uintptr_t)p.out_lo & 15) && (p.N / 2) % 64 == 0 &&
-		    stages * stage >= 4 * 16384) {
+		if (BN >= 128 && (p.ldo * 2) % 16 == 0 && !((uintptr_t)p.out_hi & 15) && !((uintptr_t)p.out_lo & 15) &&
+		    (p.N / 2) % 64 == 0 && stages * stage >= 4 * 16384) {
 			if ((rc = make_out_map(&maps.o[0], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.out_hi, p.M, p.N / 2, p.ldo, 64)) ||
 			    (rc = make_out_map(&maps.o[1], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.out_lo, p.M, p.N / 2, p.ldo, 64)))
 				return rc;
@@ -416,6 +421,7 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 	}
 	if (stages * stage > 220 * 1024) return set_err(TG_CUDA_EINVAL, "gemm: %d operand tiles do not fit", p.na + p.nb);
 #define TGC_GEMM_DISPATCH(E)                                                                 \
+	if (BN == 64) return launch_bn<64, 4, E>(maps, p, st); /* 40-48 KB stages: always 4 */ \
 	if (BN == 256)                                                                      \
 		return stages >= 4 ? launch_bn<256, 4, E>(maps, p, st)                      \
 		       : stages == 3 ? launch_bn<256, 3, E>(maps, p, st) : launch_bn<256, 2, E>(maps, p, st); \
@@ -459,10 +465,38 @@ __global__ void codes_bf16(const signed char *__restrict__ q, int bits, long row
 	dst[transpose ? c * ldd + r : r * ldd + c] = __float2bfloat16_rn(v);
 }
 
+// The transposed split through 32 x 32 shared-memory tiles: reads along src rows and
+// writes along dst rows are both coalesced.
+__global__ void split_f32_t(const float *__restrict__ src, long rows, long cols, long lds, __nv_bfloat16 *__restrict__ hi,
+			    __nv_bfloat16 *__restrict__ lo, long ldd)
+{
+	__shared__ float tile[32][33];
+	const long r0 = (long)blockIdx.y * 32, c0 = (long)blockIdx.x * 32;
+	for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+		long r = r0 + i, c = c0 + threadIdx.x;
+		tile[i][threadIdx.x] = r < rows && c < cols ? src[r * lds + c] : 0.0f;
+	}
+	__syncthreads();
+	for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+		long c = c0 + i, r = r0 + threadIdx.x; // dst[c, r] = src[r, c]
+		if (c >= cols || r >= rows) continue;
+		float x = tile[threadIdx.x][i];
+		__nv_bfloat16 h = __float2bfloat16_rn(x);
+		hi[c * ldd + r] = h;
+		if (lo) lo[c * ldd + r] = __float2bfloat16_rn(x - __bfloat162float(h));
+	}
+}
+
 int split_to_bf16(const float *src, long rows, long cols, long lds, bool transpose, __nv_bfloat16 *hi, __nv_bfloat16 *lo,
 		  long ldd, cudaStream_t st)
 {
 	long n = rows * cols;
+	if (transpose && (rows + 31) / 32 <= 65535) {
+		dim3 grid((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32));
+		split_f32_t<<<grid, dim3(32, 8), 0, st>>>(src, rows, cols, lds, hi, lo, ldd);
+		TGC_LAUNCH_CHECK();
+		return TG_CUDA_OK;
+	}
 	split_f32<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, rows, cols, lds, transpose ? 1 : 0, hi, lo, ldd);
 	TGC_LAUNCH_CHECK();
 	return TG_CUDA_OK;
@@ -479,8 +513,11 @@ int codes_to_bf16(const signed char *q, int bits, long rows, long cols, bool tra
 
 // ---- tg_cuda_matmul_q, large batch -------------------------------------------------------------
 
+// The drop-in call stays asynchronous: the GEMM's device status word is copied into a
+// pinned host word after each call, and a later call on the device reports it.
 struct TcScratch {
 	DevBuf buf, status;
+	int *h_status = nullptr; // pinned
 };
 static TcScratch g_tc[64];
 
@@ -507,6 +544,15 @@ int matmul_q_tc(int axis, float *o, const float *act, const signed char *q, int 
 	long brows = axis == 0 ? n : m;   // activation rows (batch)
 	size_t wbytes = (size_t)wrows * k * 2, abytes = (size_t)brows * k * 2;
 	int rc;
+	if (!S.h_status) {
+		TGC_CUDA(cudaHostAlloc((void **)&S.h_status, sizeof(int), cudaHostAllocDefault));
+		*S.h_status = 0;
+	}
+	if (int prev = *(volatile int *)S.h_status) { // an earlier call's kernel gave up waiting
+		*S.h_status = 0;
+		return set_err(TG_CUDA_EDEVICE, "a tensor-core kernel of an earlier call on this device gave up waiting (status %d)",
+			       prev);
+	}
 	if ((rc = S.buf.ensure(wbytes + 2 * abytes + 256, dev)) || (rc = S.status.ensure(64, dev))) return rc;
 	__nv_bfloat16 *wq = (__nv_bfloat16 *)S.buf.p;
 	__nv_bfloat16 *ahi = (__nv_bfloat16 *)((uint8_t *)S.buf.p + ((wbytes + 127) & ~(size_t)127));
@@ -540,7 +586,7 @@ int matmul_q_tc(int axis, float *o, const float *act, const signed char *q, int 
 	}
 	ops.lda = k, ops.ldb = k;
 	if ((rc = gemm(ops, p, st))) return rc;
-	if ((rc = device_status_check(p.status, st))) return rc;
+	TGC_CUDA(cudaMemcpyAsync(S.h_status, p.status, sizeof(int), cudaMemcpyDeviceToHost, st));
 	*done = true;
 	return TG_CUDA_OK;
 }

@@ -10,7 +10,7 @@
 //
 //   weights  converted once at load: codes -> exact bf16 in [out, in] K-major
 //            layout for the tcgen05 GEMM (q/k/v heads concatenated into one
-//            matrix; gate/up interleaved in 128-row blocks so one GEMM tile
+//            matrix; gate/up interleaved in 32-row blocks so every GEMM tile
 //            holds matching gate and up channels); o_proj pre-scaled by its
 //            per-head column scales and split into bf16 hi/lo.
 //   layer    rmsnorm*ln1 (split to bf16 hi/lo) -> QKV GEMM -> q/k rmsnorm*w +
@@ -50,8 +50,9 @@ __device__ __forceinline__ void split_bf16(float y, __nv_bfloat16 &h, __nv_bfloa
 
 // ---- weight conversion ----------------------------------------------------------------------
 
-// Gate and up [D, FF] codes -> interleaved [2 FF, D]: block b = rows 256b.. holds gate
-// channels 128b..128b+127 then the same up channels.
+// Gate and up [D, FF] codes -> interleaved [2 FF, D]: block b = rows 64b.. holds gate
+// channels 32b..32b+31 then the same up channels, so every GEMM tile of 64 or more
+// columns holds matching gate and up channels.
 __global__ void k_codes_gu(const signed char *__restrict__ qg, const signed char *__restrict__ qu, int bits, int D, int FF,
 			   __nv_bfloat16 *__restrict__ dst)
 {
@@ -61,7 +62,7 @@ __global__ void k_codes_gu(const signed char *__restrict__ qg, const signed char
 	long e = t % ((long)D * FF); // element of the [D, FF] source
 	int p = (int)(e / FF), f = (int)(e % FF);
 	float v = (float)qcode(which ? qu : qg, bits, e);
-	long row = (long)(f / 128) * 256 + which * 128 + f % 128;
+	long row = (long)(f / 32) * 64 + which * 32 + f % 32;
 	dst[row * D + p] = __float2bfloat16_rn(v);
 }
 
@@ -289,9 +290,36 @@ __global__ void k_argmax(const float *__restrict__ logits, int V, int *__restric
 	const float *x = logits + (long)blockIdx.x * V;
 	float best = -INFINITY;
 	int bi = 0x7fffffff;
-	for (int i = threadIdx.x; i < V; i += blockDim.x) {
-		float v = x[i];
-		if (v > best || (v == best && i < bi)) best = v, bi = i;
+	if ((V & 3) == 0) { // 16-byte loads, several in flight per thread; each thread scans its indices in order
+		const float4 *x4 = (const float4 *)x;
+		const int n4 = V >> 2;
+		int j = threadIdx.x;
+		for (; j + 3 * (int)blockDim.x < n4; j += 4 * blockDim.x) {
+			float4 v[4];
+#pragma unroll
+			for (int u = 0; u < 4; u++) v[u] = x4[j + u * blockDim.x];
+#pragma unroll
+			for (int u = 0; u < 4; u++) {
+				const int i = 4 * (j + u * blockDim.x);
+				if (v[u].x > best || (v[u].x == best && i < bi)) best = v[u].x, bi = i;
+				if (v[u].y > best || (v[u].y == best && i + 1 < bi)) best = v[u].y, bi = i + 1;
+				if (v[u].z > best || (v[u].z == best && i + 2 < bi)) best = v[u].z, bi = i + 2;
+				if (v[u].w > best || (v[u].w == best && i + 3 < bi)) best = v[u].w, bi = i + 3;
+			}
+		}
+		for (; j < n4; j += blockDim.x) {
+			const float4 v = x4[j];
+			const int i = 4 * j;
+			if (v.x > best || (v.x == best && i < bi)) best = v.x, bi = i;
+			if (v.y > best || (v.y == best && i + 1 < bi)) best = v.y, bi = i + 1;
+			if (v.z > best || (v.z == best && i + 2 < bi)) best = v.z, bi = i + 2;
+			if (v.w > best || (v.w == best && i + 3 < bi)) best = v.w, bi = i + 3;
+		}
+	} else {
+		for (int i = threadIdx.x; i < V; i += blockDim.x) {
+			float v = x[i];
+			if (v > best || (v == best && i < bi)) best = v, bi = i;
+		}
 	}
 	__shared__ float sv[32];
 	__shared__ int si[32];
@@ -693,7 +721,7 @@ static int prefill(Engine &g, const float *ids_host, long S, int T, int slot0, f
 			TGC_CUDA(cudaMemcpyAsync(logits_host + s0 * g.V, g.logits.p, (size_t)n * g.V * 4, cudaMemcpyDeviceToHost, g.st));
 		if (tokens_host) {
 			g.launches++;
-			k_argmax<<<(unsigned)n, 256, 0, g.st>>>(g.logits.as<float>(), g.V, g.tok.as<int>() + s0, nullptr, 0, 0, nullptr,
+			k_argmax<<<(unsigned)n, 1024, 0, g.st>>>(g.logits.as<float>(), g.V, g.tok.as<int>() + s0, nullptr, 0, 0, nullptr,
 								 0);
 			TGC_LAUNCH_CHECK();
 		}
@@ -717,7 +745,7 @@ static int decode_step(Engine &g, long S, int T, int nnew)
 	if ((rc = run_layers(g, S, 1, 0, 0, true))) return rc;
 	if ((rc = head(g, S, 1))) return rc;
 	g.launches += 2;
-	k_argmax<<<(unsigned)S, 256, 0, g.st>>>(g.logits.as<float>(), g.V, g.tok.as<int>(), g.out_tok.as<int>(), nnew, 0,
+	k_argmax<<<(unsigned)S, 1024, 0, g.st>>>(g.logits.as<float>(), g.V, g.tok.as<int>(), g.out_tok.as<int>(), nnew, 0,
 						 g.dpos.as<int>(), T);
 	k_bump<<<1, 1, 0, g.st>>>(g.dpos.as<int>());
 	TGC_LAUNCH_CHECK();
