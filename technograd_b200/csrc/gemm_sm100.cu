@@ -36,6 +36,10 @@ struct TmaMaps {
 };
 
 __device__ __forceinline__ uint32_t bf16_bits(float x) { return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+// two bf16 in one word, a in the low half (the lower K index)
+__device__ __forceinline__ uint32_t bf16x2(float a, float b) { return bf16_bits(a) | (bf16_bits(b) << 16); }
+// row rr of a 128-byte-swizzled K-major tile: rows of 128 bytes, 8-row atoms of 1024 bytes
+__device__ __forceinline__ uint8_t *smem_row(uint8_t *tile, int rr) { return tile + rr * 128; }
 
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMaps maps, const GemmArgs p)
@@ -58,7 +62,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 
 	if (threadIdx.x == 0) {
 		for (int s = 0; s < STAGES; s++) {
-			mbar_init(&full[s], 1);
+			mbar_init(&full[s], p.cside ? 1 + 128 : 1); // + the 128 converting threads
 			mbar_init(&empty[s], 1);
 		}
 		mbar_init(accf, 1);
@@ -77,9 +81,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 			const uint32_t ph = (kb / STAGES) & 1;
 			if (!mbar_wait(&empty[s], ph ^ 1, p.status, ST_TIMEOUT_EMPTY)) break;
 			uint8_t *st = smem + s * stage_bytes;
-			mbar_expect_tx(&full[s], stage_bytes);
-			for (int i = 0; i < p.na; i++) tma_load_2d(st + i * A_TILE, &maps.a[i], &full[s], (kb0 + kb) * BK, m0);
-			for (int j = 0; j < p.nb; j++) tma_load_2d(st + p.na * A_TILE + j * B_TILE, &maps.b[j], &full[s], (kb0 + kb) * BK, n0);
+			mbar_expect_tx(&full[s], stage_bytes - (p.cside == 1 ? A_TILE : p.cside == 2 ? B_TILE : 0));
+			for (int i = p.cside == 1 ? 1 : 0; i < p.na; i++) tma_load_2d(st + i * A_TILE, &maps.a[i], &full[s], (kb0 + kb) * BK, m0);
+			for (int j = p.cside == 2 ? 1 : 0; j < p.nb; j++)
+				tma_load_2d(st + p.na * A_TILE + j * B_TILE, &maps.b[j], &full[s], (kb0 + kb) * BK, n0);
 		}
 	} else if (warp == 1 && lane == 0) { // ---- MMA issuer
 		constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
@@ -117,6 +122,65 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 			for (int j = et; j < BN; j += 128) ssc[j] = n0 + j < p.N ? p.scale[n0 + j] : 0.0f;
 		} else if (p.scale_mode == 1) {
 			ssc[et] = m0 + et < p.M ? p.scale[m0 + et] : 0.0f;
+		}
+		if (p.cside) {
+			// Build the code operand of every K block in its ring slot while the producer's TMA
+			// brings the others: integer codes (exact in bf16) in the 128-byte-swizzled K-major
+			// layout; rows past the matrix are zero, like TMA's out-of-bounds fill. Each thread
+			// owns `per` 16-byte code chunks of a block; those of block kb + 1 are loaded while
+			// block kb is written, so up to 8 loads per thread are in flight.
+			const int R = p.cside == 1 ? BM : BN;
+			const int row0 = p.cside == 1 ? m0 : n0, valid = p.cside == 1 ? p.M : p.N;
+			const int cpr = p.cbits == 8 ? 4 : 2;       // 16-byte code chunks per row of a K block
+			const int kbytes = p.cbits == 8 ? BK : BK / 2;
+			const int per = R * cpr / 128;              // 1, 2, 4 or 8
+			uint4 buf[8];
+			auto load = [&](int kb) {
+				const signed char *src = p.codes + (long)(kb0 + kb) * kbytes;
+#pragma unroll
+				for (int i = 0; i < 8; i++)
+					if (i < per) {
+						const int it = et + i * 128, rr = it / cpr, c = it % cpr, grow = row0 + rr;
+						buf[i] = grow < valid ? __ldg((const uint4 *)(src + (long)grow * p.cld + c * 16)) : make_uint4(0u, 0u, 0u, 0u);
+					}
+			};
+			if (KB > 0) load(0);
+			for (int kb = 0; kb < KB; kb++) {
+				const int s = kb % STAGES;
+				const uint32_t ph = (kb / STAGES) & 1;
+				if (!mbar_wait(&empty[s], ph ^ 1, p.status, ST_TIMEOUT_EMPTY)) break;
+				uint8_t *slot = smem + s * stage_bytes + (p.cside == 1 ? 0 : p.na * A_TILE);
+#pragma unroll
+				for (int i = 0; i < 8; i++) {
+					if (i >= per) break;
+					const int it = et + i * 128, rr = it / cpr, c = it % cpr, sw = rr & 7;
+					const uint32_t w[4] = { buf[i].x, buf[i].y, buf[i].z, buf[i].w };
+					uint8_t *dst = smem_row(slot, rr);
+					if (p.cbits == 8) { // 16 codes -> swizzle units 2c, 2c + 1
+						uint32_t h[8];
+#pragma unroll
+						for (int j = 0; j < 4; j++) {
+							h[2 * j] = bf16x2((float)(int8_t)(w[j] & 0xff), (float)(int8_t)((w[j] >> 8) & 0xff));
+							h[2 * j + 1] = bf16x2((float)(int8_t)((w[j] >> 16) & 0xff), (float)(int8_t)(w[j] >> 24));
+						}
+						*(uint4 *)(dst + (((2 * c) ^ sw) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+						*(uint4 *)(dst + (((2 * c + 1) ^ sw) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+					} else { // 32 codes -> units 4c .. 4c + 3, one 32-bit word (8 codes) each
+#pragma unroll
+						for (int j = 0; j < 4; j++) {
+							uint32_t h[4];
+#pragma unroll
+							for (int e = 0; e < 4; e++)
+								h[e] = bf16x2((float)((int32_t)(w[j] << (28 - 8 * e)) >> 28),
+									      (float)((int32_t)(w[j] << (24 - 8 * e)) >> 28));
+							*(uint4 *)(dst + (((4 * c + j) ^ sw) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+						}
+					}
+				}
+				fence_async_smem();
+				mbar_arrive(&full[s]);
+				if (kb + 1 < KB) load(kb + 1);
+			}
 		}
 		epilogue_sync();
 		const bool ok = mbar_wait(accf, 0, p.status, ST_TIMEOUT_ACC);
@@ -355,6 +419,9 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 	if (p.M <= 0 || p.N <= 0 || p.K <= 0 || p.na < 1 || p.na > 2 || p.nb < 1 || p.nb > 2 || p.npairs < 1 || p.npairs > 4)
 		return set_err(TG_CUDA_EINVAL, "gemm: bad shape or operand count");
 	if (p.K % 8) return set_err(TG_CUDA_EINVAL, "gemm: K %d is not a multiple of 8", p.K);
+	if (p.cside && (p.cside > 2 || !p.codes || (p.cbits != 8 && p.cbits != 4) || p.K % BK || p.cld % 16 ||
+			((uintptr_t)p.codes & 15) || (p.cside == 1 && p.pa[0] != 0 && p.na < 1)))
+		return set_err(TG_CUDA_EINVAL, "gemm: in-kernel dequant needs K %% 64 == 0 and 16-byte aligned code rows");
 	int sms = 148, dev = 0;
 	cudaGetDevice(&dev);
 	cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -366,9 +433,9 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 	TmaMaps maps;
 	memset(&maps, 0, sizeof maps);
 	for (int i = 0; i < p.na; i++)
-		if ((rc = make_map(&maps.a[i], ops.a[i], p.M, p.K, ops.lda, BM))) return rc;
+		if (!(i == 0 && p.cside == 1) && (rc = make_map(&maps.a[i], ops.a[i], p.M, p.K, ops.lda, BM))) return rc;
 	for (int j = 0; j < p.nb; j++)
-		if ((rc = make_map(&maps.b[j], ops.b[j], p.N, p.K, ops.ldb, BN))) return rc;
+		if (!(j == 0 && p.cside == 2) && (rc = make_map(&maps.b[j], ops.b[j], p.N, p.K, ops.ldb, BN))) return rc;
 	// as many ring stages (2..4) as fit in 220 KB of shared memory
 	const int stage = p.na * A_TILE + p.nb * BN * BK * 2;
 	const int stages = std::min(4, std::max(2, (220 * 1024) / stage));
@@ -516,7 +583,7 @@ int codes_to_bf16(const signed char *q, int bits, long rows, long cols, bool tra
 // The drop-in call stays asynchronous: the GEMM's device status word is copied into a
 // pinned host word after each call, and a later call on the device reports it.
 struct TcScratch {
-	DevBuf buf, status;
+	DevBuf buf, status, part; // part: split-K partial sums of small-batch calls (64 MB)
 	int *h_status = nullptr; // pinned
 };
 static TcScratch g_tc[64];
@@ -569,9 +636,17 @@ int matmul_q_tc(int axis, float *o, const float *act, const signed char *q, int 
 	p.epi = EPI_STORE;
 	p.out = o;
 	p.status = S.status.as<int>();
+	// small batches leave most SMs idle with one tile per weight slab: let gemm() split K
+	if ((rc = S.part.ensure((size_t)64 << 20, dev))) return rc;
+	p.partial = S.part.as<float>(), p.partial_floats = (long)((64 << 20) / sizeof(float));
 	if (axis == 0) {
-		// o[m, n] = diag(s) Q[m, k] b[k, n]: A = codes [m, k], B = b^T [n, k] split
-		if ((rc = codes_to_bf16(q, bits, m, k, false, wq, k, st))) return rc;
+		// o[m, n] = diag(s) Q[m, k] b[k, n]: A = codes [m, k], B = b^T [n, k] split. The codes
+		// rows are K-major already: the kernel expands them itself when the K blocks are whole.
+		if (k % 64 == 0 && !((uintptr_t)q & 15)) {
+			p.codes = q, p.cbits = bits, p.cside = 1, p.cld = (long)k * bits / 8;
+		} else if ((rc = codes_to_bf16(q, bits, m, k, false, wq, k, st))) {
+			return rc;
+		}
 		if ((rc = split_to_bf16(act, k, n, n, true, ahi, alo, k, st))) return rc;
 		ops.a[0] = wq, ops.b[0] = ahi, ops.b[1] = alo;
 		p.M = m, p.N = n, p.ldo = n, p.scale = s, p.scale_mode = 1;

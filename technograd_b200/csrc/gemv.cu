@@ -3,9 +3,8 @@
 // where the op streams codes from HBM once and is bandwidth-bound.
 //
 //   gemv_rows : axis 0, o[i,j] = s[i] sum_p code(i*k+p) b[p*n+j], n <= 8.
-//               One warp owns 4 channel rows; each lane streams 16-byte code
-//               chunks of those rows and keeps the matching activations in
-//               registers, so one activation load feeds 4 rows.
+//               A lane owns a channel row and a warp one K slice of 32 rows;
+//               the activations of the slice are shared by the 32 lanes.
 //   gemv_cols : axis 1, o[i,j] = s[j] sum_p a[i*k+p] code(p*n+j), m <= 8.
 //               A code row p is contiguous over channels j: each lane streams
 //               4 bytes (8 int4 / 4 int8 channels) of row p; the K axis is split
@@ -20,74 +19,73 @@
 namespace tgc {
 
 // ---- axis 0 --------------------------------------------------------------------------
+// Lane = channel row: a warp takes 32 rows and one K slice, so every lane needs the same
+// activations (broadcast reads of b, staged once per CTA in shared memory when it fits)
+// and loads 16-byte code chunks of its own row, U at a time. The KS warps of a CTA take
+// the KS slices of the same 32 rows; their partial sums are added in a fixed order.
+// Codes become floats without an int-to-float conversion: 2^23 + the unsigned code read as
+// an f32, minus 2^23 + the code offset, is exact.
 
-constexpr int GR_ROWS = 4;    // channel rows per warp
-constexpr int GR_WARPS = 8;   // warps per CTA
+constexpr int GR_U = 4; // 16-byte chunks in flight per lane
 
-template <int BITS, int NB>
-__global__ void __launch_bounds__(GR_WARPS * 32) gemv_rows(float *__restrict__ o, const signed char *__restrict__ q,
-							     const float *__restrict__ s, const float *__restrict__ b,
-							     int m, int k)
+template <int BITS, int NB, int KS, bool SMB>
+__global__ void __launch_bounds__(32 * KS) gemv_rows(float *__restrict__ o, const signed char *__restrict__ q,
+						     const float *__restrict__ s, const float *__restrict__ b, int m, int k)
 {
-	constexpr int CPC = BITS == 8 ? 16 : 32;  // codes per 16-byte chunk
-	const int lane = threadIdx.x & 31;
-	const int warp = blockIdx.x * GR_WARPS + (threadIdx.x >> 5);
-	const int nwarps = gridDim.x * GR_WARPS;
-	const long row_bytes = BITS == 8 ? (long)k : (long)k / 2;
-	const int nchunks = k / CPC;
-	for (int r0 = warp * GR_ROWS; r0 < m; r0 += nwarps * GR_ROWS) {
-		float acc[GR_ROWS][NB];
+	constexpr int CPC = BITS == 8 ? 16 : 32; // codes per 16-byte chunk
+	constexpr int PER = BITS == 8 ? 4 : 8;   // codes per 32-bit word
+	__shared__ float part[KS][32][NB];
+	extern __shared__ float4 sb4[];          // SMB: b [k][NB]
+	const int lane = threadIdx.x & 31, ks = threadIdx.x >> 5;
+	const int row = blockIdx.x * 32 + lane;
+	const long row_bytes = (long)k * BITS / 8;
+	const int nchunks = k / CPC, cper = (nchunks + KS - 1) / KS;
+	const int c0 = ks * cper, c1 = min(nchunks, c0 + cper);
+	const signed char *qr = q + (long)min(row, m - 1) * row_bytes;
+	if (SMB) {
+		for (int i = threadIdx.x; i < k * NB / 4; i += blockDim.x) sb4[i] = ((const float4 *)b)[i];
+		__syncthreads();
+	}
+	float acc[NB];
 #pragma unroll
-		for (int r = 0; r < GR_ROWS; r++)
+	for (int j = 0; j < NB; j++) acc[j] = 0.0f;
+	for (int cb = c0; cb < c1; cb += GR_U) {
+		uint4 w[GR_U];
 #pragma unroll
-			for (int j = 0; j < NB; j++) acc[r][j] = 0.0f;
-		for (int c = lane; c < nchunks; c += 32) {
-			uint4 w[GR_ROWS];
+		for (int u = 0; u < GR_U; u++) w[u] = cb + u < c1 ? __ldg((const uint4 *)(qr + (long)(cb + u) * 16)) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-			for (int r = 0; r < GR_ROWS; r++) {
-				int row = r0 + r < m ? r0 + r : m - 1;
-				w[r] = __ldg((const uint4 *)(q + (long)row * row_bytes + (long)c * 16));
-			}
-			const float *bp = b + (long)c * CPC * NB;
+		for (int u = 0; u < GR_U; u++) {
+			if (cb + u >= c1) break;
+			const float4 *bp = SMB ? sb4 + (long)(cb + u) * CPC * NB / 4 : (const float4 *)(b + (long)(cb + u) * CPC * NB);
 #pragma unroll
 			for (int word = 0; word < 4; word++) {
-				constexpr int PER = BITS == 8 ? 4 : 8; // codes per 32-bit word
-				float bv[PER][NB];
+				const uint32_t x = word == 0 ? w[u].x : word == 1 ? w[u].y : word == 2 ? w[u].z : w[u].w;
+				float bv[PER * NB];
 #pragma unroll
-				for (int e = 0; e < PER; e++)
+				for (int i = 0; i < PER * NB / 4; i++) {
+					const float4 t = bp[word * PER * NB / 4 + i];
+					bv[4 * i] = t.x, bv[4 * i + 1] = t.y, bv[4 * i + 2] = t.z, bv[4 * i + 3] = t.w;
+				}
 #pragma unroll
-					for (int j = 0; j < NB; j++) bv[e][j] = __ldg(bp + (word * PER + e) * NB + j);
+				for (int e = 0; e < PER; e++) {
+					const float cf = BITS == 8 ? __int_as_float(0x4B000000 | (((x >> (8 * e)) & 0xFF) ^ 0x80)) - 8388736.0f
+								   : __int_as_float(0x4B000000 | (((x >> (4 * e)) & 0xF) ^ 0x8)) - 8388616.0f;
 #pragma unroll
-				for (int r = 0; r < GR_ROWS; r++) {
-					uint32_t x = word == 0 ? w[r].x : word == 1 ? w[r].y : word == 2 ? w[r].z : w[r].w;
-#pragma unroll
-					for (int e = 0; e < PER; e++) {
-						float cf = BITS == 8 ? (float)(int)(int8_t)(x >> (8 * e))
-								     : (float)((int32_t)(x << (28 - 4 * e)) >> 28);
-#pragma unroll
-						for (int j = 0; j < NB; j++) acc[r][j] = fmaf(cf, bv[e][j], acc[r][j]);
-					}
+					for (int j = 0; j < NB; j++) acc[j] = fmaf(cf, bv[e * NB + j], acc[j]);
 				}
 			}
 		}
-#pragma unroll
-		for (int r = 0; r < GR_ROWS; r++)
-#pragma unroll
-			for (int j = 0; j < NB; j++) {
-				float v = acc[r][j];
-#pragma unroll
-				for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-				acc[r][j] = v;
-			}
-		if (lane == 0)
-#pragma unroll
-			for (int r = 0; r < GR_ROWS; r++)
-				if (r0 + r < m) {
-					float sc = s[r0 + r];
-#pragma unroll
-					for (int j = 0; j < NB; j++) o[(long)(r0 + r) * NB + j] = sc * acc[r][j];
-				}
 	}
+#pragma unroll
+	for (int j = 0; j < NB; j++) part[ks][lane][j] = acc[j];
+	__syncthreads();
+	if (ks == 0 && row < m)
+#pragma unroll
+		for (int j = 0; j < NB; j++) {
+			float v = part[0][lane][j];
+			for (int i = 1; i < KS; i++) v += part[i][lane][j];
+			o[(long)row * NB + j] = s[row] * v;
+		}
 }
 
 // axis 1: gemv_cols and reduce_splits live in gemv_cols.cuh
@@ -138,17 +136,40 @@ static int sm_count()
 	return n;
 }
 
-template <int BITS>
-static void launch_rows(int nb, float *o, const signed char *q, const float *s, const float *b, int m, int k,
-			cudaStream_t st)
+template <int BITS, int NB>
+static int launch_rows_nb(float *o, const signed char *q, const float *s, const float *b, int m, int k, cudaStream_t st)
 {
-	int rows_per_cta = GR_WARPS * GR_ROWS;
-	int grid = (m + rows_per_cta - 1) / rows_per_cta;
+	constexpr int KS = NB == 1 ? 32 : 16;
+	const unsigned grid = (unsigned)((m + 31) / 32);
+	const size_t smem = (size_t)k * NB * 4;
+	if (smem <= 96 * 1024) {
+		static bool attr[64] = {};
+		int dev = 0;
+		cudaGetDevice(&dev);
+		if (!attr[dev]) {
+			cudaFuncSetAttribute(gemv_rows<BITS, NB, KS, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+			attr[dev] = true;
+		}
+		gemv_rows<BITS, NB, KS, true><<<grid, 32 * KS, smem, st>>>(o, q, s, b, m, k);
+	} else {
+		gemv_rows<BITS, NB, KS, false><<<grid, 32 * KS, 0, st>>>(o, q, s, b, m, k);
+	}
+	TGC_LAUNCH_CHECK();
+	return TG_CUDA_OK;
+}
+
+template <int BITS>
+static int launch_rows(int nb, float *o, const signed char *q, const float *s, const float *b, int m, int k, cudaStream_t st)
+{
 	switch (nb) {
-#define NB_CASE(N) \
-	case N: gemv_rows<BITS, N><<<grid, GR_WARPS * 32, 0, st>>>(o, q, s, b, m, k); break;
-		NB_CASE(1) NB_CASE(2) NB_CASE(3) NB_CASE(4) NB_CASE(5) NB_CASE(6) NB_CASE(7) NB_CASE(8)
-#undef NB_CASE
+	case 1: return launch_rows_nb<BITS, 1>(o, q, s, b, m, k, st);
+	case 2: return launch_rows_nb<BITS, 2>(o, q, s, b, m, k, st);
+	case 3: return launch_rows_nb<BITS, 3>(o, q, s, b, m, k, st);
+	case 4: return launch_rows_nb<BITS, 4>(o, q, s, b, m, k, st);
+	case 5: return launch_rows_nb<BITS, 5>(o, q, s, b, m, k, st);
+	case 6: return launch_rows_nb<BITS, 6>(o, q, s, b, m, k, st);
+	case 7: return launch_rows_nb<BITS, 7>(o, q, s, b, m, k, st);
+	default: return launch_rows_nb<BITS, 8>(o, q, s, b, m, k, st);
 	}
 }
 
@@ -190,10 +211,10 @@ int matmul_q_gemv(int axis, float *o, const float *act, const signed char *q, in
 		  int n, cudaStream_t st, bool *done)
 {
 	*done = false;
-	bool aligned16 = ((uintptr_t)q & 15) == 0;
+	bool aligned16 = ((uintptr_t)q & 15) == 0 && ((uintptr_t)act & 15) == 0;
 	if (axis == 0 && n <= 8 && aligned16 && k % (bits == 8 ? 16 : 32) == 0) {
-		if (bits == 8) launch_rows<8>(n, o, q, s, act, m, k, st);
-		else launch_rows<4>(n, o, q, s, act, m, k, st);
+		int rc = bits == 8 ? launch_rows<8>(n, o, q, s, act, m, k, st) : launch_rows<4>(n, o, q, s, act, m, k, st);
+		if (rc) return rc;
 		*done = true;
 	} else if (axis == 1 && m <= 8 && ((uintptr_t)q & 3) == 0 && n % (bits == 8 ? 4 : 8) == 0) {
 		int rc = bits == 8 ? launch_cols<8>(o, act, q, s, m, k, n, st) : launch_cols<4>(o, act, q, s, m, k, n, st);
