@@ -39,6 +39,7 @@ namespace tgc {
 constexpr int FA_Q = 128, FA_K = 64, FA_HD = 128;
 constexpr float FA_RESCALE = 8.0f;
 constexpr int FA_THREADS = 288;
+constexpr int FA_LB = 4; // items whose global loads a loader issues before converting them
 
 // shared-memory layout (byte offsets from a 1024-aligned base); each tile is K-major
 // with 128-byte swizzle: rows of 128 bytes, 8-row atoms of 1024 bytes
@@ -155,22 +156,28 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 		const float *qb = q + ((long)s * NQ + h) * (long)T * FA_HD;
 		const float *kb = kc + ((long)(slot0 + s) * NKV + kvh) * (long)max_len * FA_HD;
 		const float *vb = vc + ((long)(slot0 + s) * NKV + kvh) * (long)max_len * FA_HD;
-		for (int i = t; i < FA_Q * 16; i += 128) { // Q: 128 rows x 16 chunks of 8 dims
-			int r = i >> 4, c = i & 15;
-			float x[8];
-			if (q0 + r < T) {
-				float4 a = *(const float4 *)(qb + (long)(q0 + r) * FA_HD + c * 8);
-				float4 b = *(const float4 *)(qb + (long)(q0 + r) * FA_HD + c * 8 + 4);
-				x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
-			} else {
+		// The loaders issue FA_LB items' global loads before converting any of them: the
+		// latency of a load round is paid once per batch, not once per item.
+		for (int i0 = t; i0 < FA_Q * 16; i0 += 128 * FA_LB) { // Q: 128 rows x 16 chunks of 8 dims
+			float4 a[FA_LB], b[FA_LB];
 #pragma unroll
-				for (int e = 0; e < 8; e++) x[e] = 0.0f;
+			for (int u = 0; u < FA_LB; u++) {
+				const int i = i0 + u * 128, r = i >> 4, c = i & 15;
+				const bool in = i < FA_Q * 16 && q0 + r < T;
+				a[u] = in ? *(const float4 *)(qb + (long)(q0 + r) * FA_HD + c * 8) : make_float4(0.f, 0.f, 0.f, 0.f);
+				b[u] = in ? *(const float4 *)(qb + (long)(q0 + r) * FA_HD + c * 8 + 4) : make_float4(0.f, 0.f, 0.f, 0.f);
 			}
-			uint4 hi, lo;
-			fa_split8(x, hi, lo);
-			uint32_t off = (uint32_t)((c >> 3) * 16384) + fa_sw(r, c & 7);
-			*(uint4 *)(sm + FA_SQ_HI + off) = hi;
-			*(uint4 *)(sm + FA_SQ_LO + off) = lo;
+#pragma unroll
+			for (int u = 0; u < FA_LB; u++) {
+				const int i = i0 + u * 128, r = i >> 4, c = i & 15;
+				if (i >= FA_Q * 16) break;
+				const float x[8] = { a[u].x, a[u].y, a[u].z, a[u].w, b[u].x, b[u].y, b[u].z, b[u].w };
+				uint4 hi, lo;
+				fa_split8(x, hi, lo);
+				uint32_t off = (uint32_t)((c >> 3) * 16384) + fa_sw(r, c & 7);
+				*(uint4 *)(sm + FA_SQ_HI + off) = hi;
+				*(uint4 *)(sm + FA_SQ_LO + off) = lo;
+			}
 		}
 		fence_async_smem();
 		mbar_arrive(&B->q_full);
@@ -179,46 +186,56 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 			const int k0 = j * FA_K;
 			if (t < 64) {
 				if (j > 0 && !fa_wait(B, &B->k_empty, (j - 1) & 1, status)) break;
-				for (int i = u; i < FA_K * 16; i += 64) { // K: 64 rows x 16 chunks
-					int r = i >> 4, c = i & 15;
-					float x[8];
-					if (k0 + r < T) {
-						float4 a = *(const float4 *)(kb + (long)(k0 + r) * FA_HD + c * 8);
-						float4 b = *(const float4 *)(kb + (long)(k0 + r) * FA_HD + c * 8 + 4);
-						x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
-					} else {
+				for (int i0 = u; i0 < FA_K * 16; i0 += 64 * FA_LB) { // K: 64 rows x 16 chunks
+					float4 a[FA_LB], b[FA_LB];
 #pragma unroll
-						for (int e = 0; e < 8; e++) x[e] = 0.0f;
+					for (int v = 0; v < FA_LB; v++) {
+						const int i = i0 + v * 64, r = i >> 4, c = i & 15;
+						const bool in = i < FA_K * 16 && k0 + r < T;
+						a[v] = in ? *(const float4 *)(kb + (long)(k0 + r) * FA_HD + c * 8) : make_float4(0.f, 0.f, 0.f, 0.f);
+						b[v] = in ? *(const float4 *)(kb + (long)(k0 + r) * FA_HD + c * 8 + 4) : make_float4(0.f, 0.f, 0.f, 0.f);
 					}
-					uint4 hi, lo;
-					fa_split8(x, hi, lo);
-					uint32_t off = (uint32_t)((c >> 3) * 8192) + fa_sw(r, c & 7);
-					*(uint4 *)(sm + FA_SK_HI + off) = hi;
-					*(uint4 *)(sm + FA_SK_LO + off) = lo;
+#pragma unroll
+					for (int v = 0; v < FA_LB; v++) {
+						const int i = i0 + v * 64, r = i >> 4, c = i & 15;
+						if (i >= FA_K * 16) break;
+						const float x[8] = { a[v].x, a[v].y, a[v].z, a[v].w, b[v].x, b[v].y, b[v].z, b[v].w };
+						uint4 hi, lo;
+						fa_split8(x, hi, lo);
+						uint32_t off = (uint32_t)((c >> 3) * 8192) + fa_sw(r, c & 7);
+						*(uint4 *)(sm + FA_SK_HI + off) = hi;
+						*(uint4 *)(sm + FA_SK_LO + off) = lo;
+					}
 				}
 				fence_async_smem();
 				mbar_arrive(&B->k_full);
 			} else {
 				if (j > 0 && !fa_wait(B, &B->v_empty, (j - 1) & 1, status)) break;
-				for (int i = u; i < 256; i += 64) { // V^T: item = (8 keys, 4 dims) -> one chunk in 4 rows
-					int kg = i & 7, dg = i >> 3;
-					float x[8][4];
+				for (int i0 = u; i0 < 256; i0 += 128) { // V^T: item = (8 keys, 4 dims) -> one chunk in 4 rows
+					float4 x[2][8];                   // two items' loads in flight at once
 #pragma unroll
-					for (int e = 0; e < 8; e++) {
-						int key = k0 + kg * 8 + e;
-						float4 a = key < T ? *(const float4 *)(vb + (long)key * FA_HD + dg * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-						x[e][0] = a.x, x[e][1] = a.y, x[e][2] = a.z, x[e][3] = a.w;
+					for (int v = 0; v < 2; v++) {
+						const int i = i0 + v * 64, kg = i & 7, dg = i >> 3;
+#pragma unroll
+						for (int e = 0; e < 8; e++) {
+							const int key = k0 + kg * 8 + e;
+							x[v][e] = key < T ? *(const float4 *)(vb + (long)key * FA_HD + dg * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+						}
 					}
 #pragma unroll
-					for (int dd = 0; dd < 4; dd++) {
-						float col[8];
+					for (int v = 0; v < 2; v++) {
+						const int i = i0 + v * 64, kg = i & 7, dg = i >> 3;
 #pragma unroll
-						for (int e = 0; e < 8; e++) col[e] = x[e][dd];
-						uint4 hi, lo;
-						fa_split8(col, hi, lo);
-						uint32_t off = fa_sw(dg * 4 + dd, kg);
-						*(uint4 *)(sm + FA_SV_HI + off) = hi;
-						*(uint4 *)(sm + FA_SV_LO + off) = lo;
+						for (int dd = 0; dd < 4; dd++) {
+							float col[8];
+#pragma unroll
+							for (int e = 0; e < 8; e++) col[e] = dd == 0 ? x[v][e].x : dd == 1 ? x[v][e].y : dd == 2 ? x[v][e].z : x[v][e].w;
+							uint4 hi, lo;
+							fa_split8(col, hi, lo);
+							uint32_t off = fa_sw(dg * 4 + dd, kg);
+							*(uint4 *)(sm + FA_SV_HI + off) = hi;
+							*(uint4 *)(sm + FA_SV_LO + off) = lo;
+						}
 					}
 				}
 				fence_async_smem();
