@@ -206,7 +206,8 @@ def bench_decode(args, world, rank, local):
                    f"REDUCED config5 shape (profiling): {total} seqs x {prompt} + {new - 1} steps, {cfg['layers']} layers",
                    "seqs_per_step_per_gpu": wave, "prompt": prompt, "new_tokens_per_seq": new,
                    "steps_for_full_job": (total // world + wave - 1) // wave,
-                   "kv_cache": "f32, per GPU 75 GB at 256 seqs x 1280 positions",
+                   "kv_cache": "24-bit elements (bf16 + remainder byte, within 2^-16 of f32), 56 GB per GPU at "
+                               "256 seqs x 1280 positions",
                    "l2": "inputs larger than L2 (KV cache of 75 GB streamed every decode step)",
                    "share_of_step": {"attn_decode": dec_ms / tot_ms, "gemm": sum(s["gemm_ms"] for s in stats) / tot_ms,
                                      "attn_prefill": sum(s["attn_prefill_ms"] for s in stats) / tot_ms},

@@ -15,8 +15,9 @@
 //        the end reads O from TMEM, divides by the sum and stores it split hi/lo (the
 //        o_proj GEMM's input).
 //   4-7  loaders: Q once, then per key tile K (warps 4-5; rows = keys, K-major over
-//        dims) and V^T (warps 6-7; rows = dims, K-major over keys), f32 from the cache
-//        -> bf16 hi/lo in the 128-byte-swizzled K-major layout of the UMMA descriptors.
+//        dims) and V^T (warps 6-7; rows = dims, K-major over keys): the cache's bf16
+//        part and the bf16 of its remainder (kv.cuh) as hi/lo, in the 128-byte-swizzled
+//        K-major layout of the UMMA descriptors.
 //   8    TMEM allocation and the MMA issue (one thread): S_j = Q.K_j^T into one of two
 //        TMEM score buffers, O += P_j.V_j into the TMEM accumulator. S_{j+1} is issued
 //        before P_j.V_j so the softmax of tile j+1 overlaps the P.V of tile j.
@@ -39,7 +40,7 @@ namespace tgc {
 constexpr int FA_Q = 128, FA_K = 64, FA_HD = 128;
 constexpr float FA_RESCALE = 8.0f;
 constexpr int FA_THREADS = 288;
-constexpr int FA_LB = 4; // items whose global loads a loader issues before converting them
+constexpr int FA_LB = 8; // items whose global loads a loader issues before converting them
 
 // shared-memory layout (byte offsets from a 1024-aligned base); each tile is K-major
 // with 128-byte swizzle: rows of 128 bytes, 8-row atoms of 1024 bytes
@@ -110,10 +111,11 @@ __device__ __forceinline__ bool fa_wait_warp(FaBars *B, uint64_t *bar, uint32_t 
 	return __all_sync(0xffffffffu, fa_wait(B, bar, parity, status));
 }
 
-// q: [seq][NQ][T][128] f32; kc/vc: the cache [slot][NKV][max_len][128] f32;
+// q: [seq][NQ][T][128] f32; kc/vc: the cache [slot][NKV][max_len][128] in the 24-bit
+// format of kv.cuh, whose bf16 part is the hi operand and whose remainder is the lo one;
 // out hi/lo: [seq * T + t][NQ * 128 + h * 128 + d] bf16.
 __global__ void __launch_bounds__(FA_THREADS, 1)
-	k_attn_prefill_tc(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc, int T, int NQ,
+	k_attn_prefill_tc(const float *__restrict__ q, KvPlaneC kc, KvPlaneC vc, int T, int NQ,
 			  int NKV, int slot0, int max_len, float scale, __nv_bfloat16 *__restrict__ ohi,
 			  __nv_bfloat16 *__restrict__ olo, int *status)
 {
@@ -154,8 +156,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 		// ---------------- loaders ----------------
 		const int t = threadIdx.x - 128;
 		const float *qb = q + ((long)s * NQ + h) * (long)T * FA_HD;
-		const float *kb = kc + ((long)(slot0 + s) * NKV + kvh) * (long)max_len * FA_HD;
-		const float *vb = vc + ((long)(slot0 + s) * NKV + kvh) * (long)max_len * FA_HD;
+		const long cb = ((long)(slot0 + s) * NKV + kvh) * (long)max_len * FA_HD;
+		const __nv_bfloat16 *kh = kc.h + cb, *vh = vc.h + cb;
+		const signed char *kq = kc.q + cb, *vq = vc.q + cb;
 		// The loaders issue FA_LB items' global loads before converting any of them: the
 		// latency of a load round is paid once per batch, not once per item.
 		for (int i0 = t; i0 < FA_Q * 16; i0 += 128 * FA_LB) { // Q: 128 rows x 16 chunks of 8 dims
@@ -186,25 +189,32 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 			const int k0 = j * FA_K;
 			if (t < 64) {
 				if (j > 0 && !fa_wait(B, &B->k_empty, (j - 1) & 1, status)) break;
-				for (int i0 = u; i0 < FA_K * 16; i0 += 64 * FA_LB) { // K: 64 rows x 16 chunks
-					float4 a[FA_LB], b[FA_LB];
+				for (int i0 = u; i0 < FA_K * 16; i0 += 64 * FA_LB) { // K: 64 rows x 16 chunks of 8 dims
+					uint4 hv[FA_LB];
+					uint2 qv[FA_LB];
 #pragma unroll
 					for (int v = 0; v < FA_LB; v++) {
 						const int i = i0 + v * 64, r = i >> 4, c = i & 15;
 						const bool in = i < FA_K * 16 && k0 + r < T;
-						a[v] = in ? *(const float4 *)(kb + (long)(k0 + r) * FA_HD + c * 8) : make_float4(0.f, 0.f, 0.f, 0.f);
-						b[v] = in ? *(const float4 *)(kb + (long)(k0 + r) * FA_HD + c * 8 + 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+						const long e = (long)(k0 + r) * FA_HD + c * 8;
+						hv[v] = in ? *(const uint4 *)(kh + e) : make_uint4(0u, 0u, 0u, 0u);
+						qv[v] = in ? *(const uint2 *)(kq + e) : make_uint2(0u, 0u);
 					}
 #pragma unroll
 					for (int v = 0; v < FA_LB; v++) {
 						const int i = i0 + v * 64, r = i >> 4, c = i & 15;
 						if (i >= FA_K * 16) break;
-						const float x[8] = { a[v].x, a[v].y, a[v].z, a[v].w, b[v].x, b[v].y, b[v].z, b[v].w };
-						uint4 hi, lo;
-						fa_split8(x, hi, lo);
+						const uint32_t hw[4] = { hv[v].x, hv[v].y, hv[v].z, hv[v].w }, qw[2] = { qv[v].x, qv[v].y };
+						uint32_t lw[4];
+#pragma unroll
+						for (int w = 0; w < 4; w++) {
+							const uint32_t qq = qw[w >> 1] >> (16 * (w & 1)); // the two bytes of this word's elements
+							lw[w] = kv_lo_bits(hw[w] & 0xFFFF, (int)(int8_t)(qq & 0xFF)) |
+								(kv_lo_bits(hw[w] >> 16, (int)(int8_t)((qq >> 8) & 0xFF)) << 16);
+						}
 						uint32_t off = (uint32_t)((c >> 3) * 8192) + fa_sw(r, c & 7);
-						*(uint4 *)(sm + FA_SK_HI + off) = hi;
-						*(uint4 *)(sm + FA_SK_LO + off) = lo;
+						*(uint4 *)(sm + FA_SK_HI + off) = hv[v];
+						*(uint4 *)(sm + FA_SK_LO + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
 					}
 				}
 				fence_async_smem();
@@ -212,14 +222,17 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 			} else {
 				if (j > 0 && !fa_wait(B, &B->v_empty, (j - 1) & 1, status)) break;
 				for (int i0 = u; i0 < 256; i0 += 128) { // V^T: item = (8 keys, 4 dims) -> one chunk in 4 rows
-					float4 x[2][8];                   // two items' loads in flight at once
+					uint2 hv[2][8];                   // two items' loads in flight at once
+					uint32_t qv[2][8];
 #pragma unroll
 					for (int v = 0; v < 2; v++) {
 						const int i = i0 + v * 64, kg = i & 7, dg = i >> 3;
 #pragma unroll
 						for (int e = 0; e < 8; e++) {
 							const int key = k0 + kg * 8 + e;
-							x[v][e] = key < T ? *(const float4 *)(vb + (long)key * FA_HD + dg * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+							const long o = (long)key * FA_HD + dg * 4;
+							hv[v][e] = key < T ? *(const uint2 *)(vh + o) : make_uint2(0u, 0u);
+							qv[v][e] = key < T ? *(const uint32_t *)(vq + o) : 0u;
 						}
 					}
 #pragma unroll
@@ -227,11 +240,15 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 						const int i = i0 + v * 64, kg = i & 7, dg = i >> 3;
 #pragma unroll
 						for (int dd = 0; dd < 4; dd++) {
-							float col[8];
+							uint32_t hb[8], lb[8]; // dim dg*4+dd of the 8 keys
 #pragma unroll
-							for (int e = 0; e < 8; e++) col[e] = dd == 0 ? x[v][e].x : dd == 1 ? x[v][e].y : dd == 2 ? x[v][e].z : x[v][e].w;
-							uint4 hi, lo;
-							fa_split8(col, hi, lo);
+							for (int e = 0; e < 8; e++) {
+								const uint32_t hw = dd < 2 ? hv[v][e].x : hv[v][e].y;
+								hb[e] = (dd & 1) ? hw >> 16 : hw & 0xFFFF;
+								lb[e] = kv_lo_bits(hb[e], (int)(int8_t)((qv[v][e] >> (8 * dd)) & 0xFF));
+							}
+							const uint4 hi = make_uint4(hb[0] | (hb[1] << 16), hb[2] | (hb[3] << 16), hb[4] | (hb[5] << 16), hb[6] | (hb[7] << 16));
+							const uint4 lo = make_uint4(lb[0] | (lb[1] << 16), lb[2] | (lb[3] << 16), lb[4] | (lb[5] << 16), lb[6] | (lb[7] << 16));
 							uint32_t off = fa_sw(dg * 4 + dd, kg);
 							*(uint4 *)(sm + FA_SV_HI + off) = hi;
 							*(uint4 *)(sm + FA_SV_LO + off) = lo;

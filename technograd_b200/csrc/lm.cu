@@ -21,7 +21,8 @@
 //   head     rmsnorm*lnf of the last position only (take(lastidx) discards the
 //            other rows), LM-head GEMM, argmax for greedy decode.
 //
-// KV cache: f32, [layer][slot][kv head][position][head_dim]. Sequences run in
+// KV cache: [layer][slot][kv head][position][head_dim], each f32 key/value kept in 3
+// bytes (its bf16 rounding and a byte of remainder, kv.cuh). Sequences run in
 // waves of at most max_seqs per device; the prefill of a wave runs in chunks
 // of at most PREFILL_ROWS tokens.
 #include <math.h>
@@ -32,6 +33,7 @@
 #include <thread>
 #include <vector>
 
+#include "kv.cuh"
 #include "attn_tc.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
@@ -125,12 +127,12 @@ __global__ void k_rmsnorm_split(const float *__restrict__ x, long M, int D, cons
 
 // Per (row, head) of the QKV projection [M, (NQ + 2 NKV) HD]: q and k heads get
 // rmsnorm * qn / kn then rotary(x) = x*cos + rotate_half(x)*sin (import.py:96-97);
-// q goes to q_out [seq][NQ][T][HD], k and v into the cache at position pos0 + t.
-// One warp per head, 4 dims per lane (HD = 128).
+// q goes to q_out [seq][NQ][T][HD], k and v into the cache (24-bit elements, kv.cuh) at
+// position pos0 + t. One warp per head, 4 dims per lane (HD = 128).
 __global__ void k_qk_rope(const float *__restrict__ qkv, long M, int T, int pos0, const int *__restrict__ dpos, int NQ,
 			  int NKV, float eps, const float *__restrict__ qn, const float *__restrict__ kn,
 			  const float *__restrict__ cosT, const float *__restrict__ sinT, float *__restrict__ q_out,
-			  float *__restrict__ kc, float *__restrict__ vc, int slot0, int max_len)
+			  KvPlane kc, KvPlane vc, int slot0, int max_len)
 {
 	constexpr int HD = 128;
 	long gw = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -144,7 +146,12 @@ __global__ void k_qk_rope(const float *__restrict__ qkv, long M, int T, int pos0
 	float4 x = ((const float4 *)(qkv + r * (long)H * HD + (long)hh * HD))[lane];
 	if (hh >= NQ + NKV) { // v head: straight into the cache
 		int kvh = hh - NQ - NKV;
-		((float4 *)(vc + (((long)(slot0 + s) * NKV + kvh) * max_len + pos) * HD))[lane] = x;
+		const long e = (((long)(slot0 + s) * NKV + kvh) * max_len + pos) * HD + 4 * lane;
+		uint2 h;
+		uint32_t q;
+		kv_encode4(x, h, q);
+		*(uint2 *)(vc.h + e) = h;
+		*(uint32_t *)(vc.q + e) = q;
 		return;
 	}
 	const float *w = hh < NQ ? qn : kn;
@@ -166,8 +173,16 @@ __global__ void k_qk_rope(const float *__restrict__ qkv, long M, int T, int pos0
 		o4[e] = __fadd_rn(__fmul_rn(v[e], c), __fmul_rn(rot, sn));
 	}
 	float4 res = make_float4(o4[0], o4[1], o4[2], o4[3]);
-	if (hh < NQ) ((float4 *)(q_out + (((long)s * NQ + hh) * T + t) * HD))[lane] = res;
-	else ((float4 *)(kc + (((long)(slot0 + s) * NKV + (hh - NQ)) * max_len + pos) * HD))[lane] = res;
+	if (hh < NQ) {
+		((float4 *)(q_out + (((long)s * NQ + hh) * T + t) * HD))[lane] = res;
+	} else {
+		const long e = (((long)(slot0 + s) * NKV + (hh - NQ)) * max_len + pos) * HD + 4 * lane;
+		uint2 h;
+		uint32_t q;
+		kv_encode4(res, h, q);
+		*(uint2 *)(kc.h + e) = h;
+		*(uint32_t *)(kc.q + e) = q;
+	}
 }
 
 // causal attention of the prefill: k_attn_prefill_tc (attn_tc.cuh)
@@ -177,12 +192,14 @@ __global__ void k_qk_rope(const float *__restrict__ qkv, long M, int T, int pos0
 // Scores: each warp takes every 8th position, a lane holds 4 dims; softmax in shared memory;
 // values: each warp accumulates its positions, warps are summed through shared memory.
 template <int GRP>
-__global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q, const float *__restrict__ kc,
-						     const float *__restrict__ vc, int len, const int *__restrict__ dpos, int NQ,
+__global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q, KvPlaneC kc, KvPlaneC vc, int len,
+						     const int *__restrict__ dpos, int NQ,
 						     int NKV, int slot0, int max_len, float scale, __nv_bfloat16 *__restrict__ ohi,
 						     __nv_bfloat16 *__restrict__ olo)
 {
 	constexpr int HD = 128;
+	constexpr int DU = 8; // positions a warp loads per step (8 x 384 bytes in flight)
+	static_assert(DU == 8, "the score butterfly reduces exactly 8 positions");
 	extern __shared__ float sm[];
 	if (dpos) len = *dpos + 1; // keys 0..pos, the new token's own included
 	float *sc = sm;                               // [GRP][max_len rounded up]
@@ -190,32 +207,63 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 	__shared__ float wmax[8][GRP], wsum[8][GRP];
 	const int kvh = blockIdx.x, s = blockIdx.y;
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	const float *kb = kc + (((long)(slot0 + s) * NKV + kvh) * max_len) * HD;
-	const float *vb = vc + (((long)(slot0 + s) * NKV + kvh) * max_len) * HD;
+	const long base = (((long)(slot0 + s) * NKV + kvh) * max_len) * HD + 4 * lane; // this lane's 4 dims
+	const __nv_bfloat16 *kh = kc.h + base, *vh = vc.h + base;
+	const signed char *kq = kc.q + base, *vq = vc.q + base;
 	float4 qv[GRP];
 #pragma unroll
 	for (int g = 0; g < GRP; g++) qv[g] = ((const float4 *)(q + ((long)s * NQ + kvh * GRP + g) * HD))[lane];
 	float mx[GRP];
 #pragma unroll
 	for (int g = 0; g < GRP; g++) mx[g] = -INFINITY;
-	for (int p0 = warp * 4; p0 < len; p0 += 32) {
-		float4 kv[4];
+	for (int p0 = warp * DU; p0 < len; p0 += 8 * DU) {
+		uint2 khv[DU];
+		uint32_t kqv[DU];
 #pragma unroll
-		for (int u = 0; u < 4; u++) kv[u] = p0 + u < len ? ((const float4 *)(kb + (long)(p0 + u) * HD))[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+		for (int u = 0; u < DU; u++) {
+			const bool in = p0 + u < len;
+			khv[u] = in ? *(const uint2 *)(kh + (long)(p0 + u) * HD) : make_uint2(0u, 0u);
+			kqv[u] = in ? *(const uint32_t *)(kq + (long)(p0 + u) * HD) : 0u;
+		}
+		float4 kv[DU];
 #pragma unroll
-		for (int u = 0; u < 4; u++)
+		for (int u = 0; u < DU; u++) kv[u] = kv_decode4(khv[u], kqv[u]);
+		// The 8 dot products are summed over the warp by a halving butterfly: each exchange
+		// keeps half of the values and sends the other half, 9 shuffles for 8 positions (not
+		// 40). Lane L ends with position ((L >> 4) & 1) * 4 + ((L >> 3) & 1) * 2 + ((L >> 2) & 1).
+		const int pu = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
 #pragma unroll
-			for (int g = 0; g < GRP; g++) {
-				float d = fmaf(qv[g].x, kv[u].x, fmaf(qv[g].y, kv[u].y, fmaf(qv[g].z, kv[u].z, qv[g].w * kv[u].w)));
+		for (int g = 0; g < GRP; g++) {
+			float d[DU];
 #pragma unroll
-				for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-				if (p0 + u < len) {
-					d = __fmul_rn(d, scale);
-					if (lane == 0) sc[g * ((max_len + 3) & ~3) + p0 + u] = d;
-					mx[g] = fmaxf(mx[g], d);
-				}
+			for (int u = 0; u < DU; u++)
+				d[u] = fmaf(qv[g].x, kv[u].x, fmaf(qv[g].y, kv[u].y, fmaf(qv[g].z, kv[u].z, qv[g].w * kv[u].w)));
+			float v4[4], v2[2];
+#pragma unroll
+			for (int i = 0; i < 4; i++) {
+				const bool up = lane & 16;
+				v4[i] = (up ? d[i + 4] : d[i]) + __shfl_xor_sync(0xffffffffu, up ? d[i] : d[i + 4], 16);
 			}
+#pragma unroll
+			for (int i = 0; i < 2; i++) {
+				const bool up = lane & 8;
+				v2[i] = (up ? v4[i + 2] : v4[i]) + __shfl_xor_sync(0xffffffffu, up ? v4[i] : v4[i + 2], 8);
+			}
+			const bool up = lane & 4;
+			float v = (up ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, up ? v2[0] : v2[1], 4);
+			v += __shfl_xor_sync(0xffffffffu, v, 2);
+			v += __shfl_xor_sync(0xffffffffu, v, 1);
+			if (p0 + pu < len) {
+				v = __fmul_rn(v, scale);
+				if ((lane & 3) == 0) sc[g * ((max_len + 3) & ~3) + p0 + pu] = v;
+				mx[g] = fmaxf(mx[g], v);
+			}
+		}
 	}
+#pragma unroll
+	for (int g = 0; g < GRP; g++)
+#pragma unroll
+		for (int o = 16; o; o >>= 1) mx[g] = fmaxf(mx[g], __shfl_xor_sync(0xffffffffu, mx[g], o));
 	if (lane == 0)
 #pragma unroll
 		for (int g = 0; g < GRP; g++) wmax[warp][g] = mx[g];
@@ -252,12 +300,20 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 	float4 acc[GRP];
 #pragma unroll
 	for (int g = 0; g < GRP; g++) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-	for (int p0 = warp * 4; p0 < len; p0 += 32) {
-		float4 vv[4];
+	for (int p0 = warp * DU; p0 < len; p0 += 8 * DU) {
+		uint2 vhv[DU];
+		uint32_t vqv[DU];
 #pragma unroll
-		for (int u = 0; u < 4; u++) vv[u] = p0 + u < len ? ((const float4 *)(vb + (long)(p0 + u) * HD))[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+		for (int u = 0; u < DU; u++) {
+			const bool in = p0 + u < len;
+			vhv[u] = in ? *(const uint2 *)(vh + (long)(p0 + u) * HD) : make_uint2(0u, 0u);
+			vqv[u] = in ? *(const uint32_t *)(vq + (long)(p0 + u) * HD) : 0u;
+		}
+		float4 vv[DU];
 #pragma unroll
-		for (int u = 0; u < 4; u++) {
+		for (int u = 0; u < DU; u++) vv[u] = kv_decode4(vhv[u], vqv[u]);
+#pragma unroll
+		for (int u = 0; u < DU; u++) {
 			if (p0 + u >= len) break;
 #pragma unroll
 			for (int g = 0; g < GRP; g++) {
@@ -354,7 +410,7 @@ struct Engine {
 	float eps, scale;
 	DevBuf E, lnf, lmw, lms, cosT, sinT;
 	std::vector<std::unique_ptr<Layer>> layers;
-	DevBuf kc, vc;
+	DevBuf kh, kq, vh, vq; // the KV cache: bf16 and residual-byte planes (kv.cuh)
 	// activations
 	long rows_cap = 0;
 	DevBuf h, xhi, xlo, qkv, q, ahi, alo, ghi, glo, logits, tok, ids, status, out_tok, part;
@@ -575,8 +631,10 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 		    (rc = upload(Y.qn, d->qn[l], (size_t)HD * 4, dev, g.st)) || (rc = upload(Y.kn, d->kn[l], (size_t)HD * 4, dev, g.st)))
 			return rc;
 	}
-	size_t kv = (size_t)g.L * max_seqs * NKV * (size_t)max_len * HD * 4;
-	if ((rc = g.kc.alloc(kv, dev)) || (rc = g.vc.alloc(kv, dev))) return rc;
+	const size_t kv = (size_t)g.L * max_seqs * NKV * (size_t)max_len * HD; // elements per plane
+	if ((rc = g.kh.alloc(kv * 2, dev)) || (rc = g.kq.alloc(kv, dev)) || (rc = g.vh.alloc(kv * 2, dev)) ||
+	    (rc = g.vq.alloc(kv, dev)))
+		return rc;
 	long R = std::max<long>(PREFILL_ROWS, max_seqs);
 	g.rows_cap = R;
 	if ((rc = g.h.alloc((size_t)R * D * 4, dev)) || (rc = g.xhi.alloc((size_t)R * D * 2, dev)) ||
@@ -623,8 +681,10 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 	const unsigned warps_grid = (unsigned)((M * 32 + 255) / 256);
 	for (int l = 0; l < g.L; l++) {
 		Layer &Y = *g.layers[l];
-		float *kc = g.kc.as<float>() + (size_t)l * g.max_seqs * NKV * (size_t)g.max_len * HD;
-		float *vc = g.vc.as<float>() + (size_t)l * g.max_seqs * NKV * (size_t)g.max_len * HD;
+		const size_t lo = (size_t)l * g.max_seqs * NKV * (size_t)g.max_len * HD; // this layer's first element
+		const KvPlane kc{ g.kh.as<__nv_bfloat16>() + lo, g.kq.as<signed char>() + lo };
+		const KvPlane vc{ g.vh.as<__nv_bfloat16>() + lo, g.vq.as<signed char>() + lo };
+		const KvPlaneC kcc{ kc.h, kc.q }, vcc{ vc.h, vc.q };
 		g.launches += 3; // two norms and the q/k rope of this layer
 		k_rmsnorm_split<<<warps_grid, 256, 0, g.st>>>(g.h.as<float>(), M, D, Y.ln1.as<float>(), g.eps, 0,
 							     g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>());
@@ -640,7 +700,7 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 		if (!decode) {
 			dim3 grid((T + FA_Q - 1) / FA_Q, NQ, (unsigned)S);
 			int mk = mark_begin(g, MK_PREFILL, 4.0 * HD * (double)T * (T + 1) / 2 * NQ * S);
-			k_attn_prefill_tc<<<grid, FA_THREADS, FA_SMEM, g.st>>>(g.q.as<float>(), kc, vc, T, NQ, NKV, slot0, g.max_len,
+			k_attn_prefill_tc<<<grid, FA_THREADS, FA_SMEM, g.st>>>(g.q.as<float>(), kcc, vcc, T, NQ, NKV, slot0, g.max_len,
 									       g.scale, g.ahi.as<__nv_bfloat16>(),
 									       g.alo.as<__nv_bfloat16>(), status);
 			mark_end(g, mk);
@@ -648,13 +708,14 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 			// the key count (position + 1) is read on the device; bytes = per-key part * len + the rest
 			size_t smem = decode_smem(g);
 			dim3 grid(NKV, (unsigned)S);
-			int mk = mark_begin(g, MK_DECODE, (double)S * NQ * HD * 4 * 2, (double)S * NKV * HD * 4 * 2);
+			// per key: K and V rows of 3-byte elements
+			int mk = mark_begin(g, MK_DECODE, (double)S * NQ * HD * 4 * 2, (double)S * NKV * HD * 3 * 2);
 			if (NQ / NKV == 2)
-				k_attn_decode<2><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, 0, g.dpos.as<int>(), NQ, NKV, slot0,
+				k_attn_decode<2><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kcc, vcc, 0, g.dpos.as<int>(), NQ, NKV, slot0,
 									  g.max_len, g.scale, g.ahi.as<__nv_bfloat16>(),
 									  g.alo.as<__nv_bfloat16>());
 			else
-				k_attn_decode<1><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kc, vc, 0, g.dpos.as<int>(), NQ, NKV, slot0,
+				k_attn_decode<1><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kcc, vcc, 0, g.dpos.as<int>(), NQ, NKV, slot0,
 									  g.max_len, g.scale, g.ahi.as<__nv_bfloat16>(),
 									  g.alo.as<__nv_bfloat16>());
 			mark_end(g, mk);
