@@ -10,7 +10,7 @@ Workloads (seeded synthetic inputs of the stated shapes):
           does), greedy decode: 2048 sequences of 1024 uniform-random ids, each
           continued by 257 argmax tokens (the prefill's plus 256 decode steps over
           the KV cache). Sequences shard over ranks (2048/N each) and run in waves of
-          at most 256 per GPU; one step = one wave. Unit: generated tokens/s.
+          at most 512 per GPU; one step = one wave. Unit: generated tokens/s.
   lr      config 1: latent_reasoner int8 RTN (--min-size 1), 1,048,576 rows of f32[8]
           with Bernoulli(0.5) entries (seed 1) per GPU; unit rows/s.
   gemm    config 2: tg_cuda_matmul_q axis 0 (tg_matmul_qa) on W [4096, 4096] int4/int8
@@ -49,7 +49,7 @@ sys.path.insert(0, ROOT)
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # 74.4: 148 SMs x 128 FP32 lanes x FMA x 1965 MHz
-TOTAL_SEQS, PROMPT, NEW, WAVE = 2048, 1024, 257, 256
+TOTAL_SEQS, PROMPT, NEW, WAVE = 2048, 1024, 257, 512
 
 
 def peaks():
@@ -206,8 +206,9 @@ def bench_decode(args, world, rank, local):
                    f"REDUCED config5 shape (profiling): {total} seqs x {prompt} + {new - 1} steps, {cfg['layers']} layers",
                    "seqs_per_step_per_gpu": wave, "prompt": prompt, "new_tokens_per_seq": new,
                    "steps_for_full_job": (total // world + wave - 1) // wave,
-                   "kv_cache": "24-bit elements (bf16 + remainder byte, within 2^-16 of f32), 56 GB per GPU at "
-                               "256 seqs x 1280 positions",
+                   "kv_cache": f"24-bit elements (bf16 + remainder byte, within 2^-16 of f32), "
+                               f"{wave * (prompt + new - 1) * cfg['layers'] * 8 * 128 * 6 / 1e9:.0f} GB per GPU at "
+                               f"{wave} seqs x {prompt + new - 1} positions",
                    "l2": "inputs larger than L2 (KV cache of 75 GB streamed every decode step)",
                    "share_of_step": {"attn_decode": dec_ms / tot_ms, "gemm": sum(s["gemm_ms"] for s in stats) / tot_ms,
                                      "attn_prefill": sum(s["attn_prefill_ms"] for s in stats) / tot_ms},
