@@ -306,6 +306,214 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 	}
 }
 
+// ---- persistent variant: one CTA per SM walks many tiles ----------------------------------
+// The accumulator is double-buffered in TMEM (2 x BN columns): while the epilogue warps drain
+// tile i from one buffer, the MMA warp accumulates tile i + 1 into the other, and the
+// producer's ring runs on across tile boundaries. The epilogue stages its output in a
+// dedicated 32 KB buffer (two 16 KB halves: f32 chunks of 32 columns alternate between them;
+// a SwiGLU chunk of 64 channels uses both, bf16 hi then lo) and writes it by TMA store or
+// reduce-add. Tiles go column-block by column-block (m fastest), so the CTAs running at the
+// same time share the weight tile. Bf16 operands only, no split-K, outputs through TMA.
+constexpr int PSTG = 32768;
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(192, 1) gemm_tc_persistent(const __grid_constant__ TmaMaps maps, const GemmArgs p)
+{
+	extern __shared__ uint8_t smem_raw[];
+	uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+	constexpr int B_TILE = BN * BK * 2;
+	const int stage_bytes = p.na * A_TILE + p.nb * B_TILE;
+	uint8_t *stg = smem + STAGES * stage_bytes; // 1024-aligned: stage_bytes is a multiple of 1024
+	uint8_t *aux = stg + PSTG;
+	uint64_t *full = (uint64_t *)aux;
+	uint64_t *empty = full + STAGES;
+	uint64_t *acc_full = empty + STAGES; // [2]
+	uint64_t *acc_empty = acc_full + 2;  // [2]
+	uint32_t *tslot = (uint32_t *)(acc_empty + 2);
+	float *ssc = (float *)(aux + 256);   // max(BN, BM) scales of the current tile
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const int mtiles = (p.M + BM - 1) / BM, ntiles = (p.N + BN - 1) / BN, tiles = mtiles * ntiles;
+	const int KB = (p.K + BK - 1) / BK;
+
+	if (threadIdx.x == 0) {
+		for (int s = 0; s < STAGES; s++) {
+			mbar_init(&full[s], 1);
+			mbar_init(&empty[s], 1);
+		}
+		for (int b = 0; b < 2; b++) {
+			mbar_init(&acc_full[b], 1);
+			mbar_init(&acc_empty[b], 128);
+		}
+		fence_barrier_init();
+		for (int i = 0; i < p.na; i++) tma_prefetch_desc(&maps.a[i]);
+		for (int i = 0; i < p.nb; i++) tma_prefetch_desc(&maps.b[i]);
+		tma_prefetch_desc(&maps.o[0]);
+	}
+	if (warp == 1) tmem_alloc(tslot, 2 * BN);
+	__syncthreads();
+	tc_fence_after();
+	const uint32_t tmem = *tslot;
+
+	if (warp == 0 && lane == 0) { // ---- producer
+		int it = 0;
+		for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+			const int m0 = (t % mtiles) * BM, n0 = (t / mtiles) * BN;
+			bool ok = true;
+			for (int kb = 0; kb < KB; kb++, it++) {
+				const int s = it % STAGES;
+				const uint32_t ph = (it / STAGES) & 1;
+				if (!(ok = mbar_wait(&empty[s], ph ^ 1, p.status, ST_TIMEOUT_EMPTY))) break;
+				uint8_t *st = smem + s * stage_bytes;
+				mbar_expect_tx(&full[s], stage_bytes);
+				for (int i = 0; i < p.na; i++) tma_load_2d(st + i * A_TILE, &maps.a[i], &full[s], kb * BK, m0);
+				for (int j = 0; j < p.nb; j++) tma_load_2d(st + p.na * A_TILE + j * B_TILE, &maps.b[j], &full[s], kb * BK, n0);
+			}
+			if (!ok) break;
+		}
+	} else if (warp == 1 && lane == 0) { // ---- MMA issuer
+		constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+		int it = 0, i = 0;
+		bool ok = true;
+		for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, i++) {
+			const int b = i & 1;
+			if (!(ok = mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1, p.status, ST_TIMEOUT_ACC))) break;
+			tc_fence_after();
+			const uint32_t d = tmem + (uint32_t)(b * BN);
+			int issued = 0;
+			for (int kb = 0; kb < KB; kb++, it++) {
+				const int s = it % STAGES;
+				const uint32_t ph = (it / STAGES) & 1;
+				if (!(ok = mbar_wait(&full[s], ph, p.status, ST_TIMEOUT_FULL))) break;
+				tc_fence_after();
+				const uint32_t base = smem_u32(smem + s * stage_bytes);
+				for (int q = 0; q < p.npairs; q++) {
+					const uint32_t a = base + p.pa[q] * A_TILE, bb = base + p.na * A_TILE + p.pb[q] * B_TILE;
+#pragma unroll
+					for (int kk = 0; kk < BK / 16; kk++) {
+						tc_mma_f16(d, sw128_kmajor_desc(a + kk * 32), sw128_kmajor_desc(bb + kk * 32), idesc, issued);
+						issued = 1;
+					}
+				}
+				tc_commit(&empty[s]);
+			}
+			tc_commit(&acc_full[b]);
+		}
+	} else if (warp >= 2) { // ---- epilogue: TMEM lanes of quarter (warp % 4)
+		const int quarter = warp & 3;
+		const int r = quarter * 32 + lane; // tile row = TMEM lane
+		const int et = threadIdx.x - 64;   // 0..127
+		int i = 0, chunk = 0;
+		bool ok = true;
+		for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, i++) {
+			const int m0 = (t % mtiles) * BM, n0 = (t / mtiles) * BN, b = i & 1;
+			epilogue_sync(); // the previous tile's readers of ssc are done
+			if (EPI == EPI_SWIGLU) {
+				const int f0 = (t / mtiles) * (BN / 2);
+				for (int j = et; j < BN / 2; j += 128) {
+					ssc[j] = p.scale[f0 + j];
+					ssc[BN / 2 + j] = p.scale2[f0 + j];
+				}
+			} else if (p.scale_mode == 2) {
+				for (int j = et; j < BN; j += 128) ssc[j] = n0 + j < p.N ? p.scale[n0 + j] : 0.0f;
+			} else if (p.scale_mode == 1) {
+				ssc[et] = m0 + et < p.M ? p.scale[m0 + et] : 0.0f;
+			}
+			// one thread waits for the accumulator and the barrier hands the outcome to all 128, so
+			// they leave the loop together (the named barriers below need every one of them)
+			volatile int *flag = (volatile int *)(aux + 192);
+			if (et == 0) *flag = mbar_wait(&acc_full[b], (i >> 1) & 1, p.status, ST_TIMEOUT_ACC) ? 1 : 0;
+			epilogue_sync();
+			if (!(ok = *flag != 0)) break;
+			tc_fence_after();
+			const uint32_t trow = tmem + (uint32_t)(b * BN) + ((uint32_t)(quarter * 32) << 16);
+			if (EPI == EPI_SWIGLU) {
+				// 64 output channels per chunk: two blocks of 32 gate + 32 up columns; hi goes to the
+				// first half of the staging buffer, lo to the second, each 128-byte swizzled
+				const int f0 = (t / mtiles) * (BN / 2);
+				for (int c = 0; c < BN / 2; c += 64) {
+					if (et == 0) tma_store_wait_read();
+					epilogue_sync();
+					for (int hf = 0; hf < 2; hf++) {
+						const int cc = c + 32 * hf;
+						float g[32], u[32];
+						__syncwarp();
+						tmem_ld16(trow + 2 * cc, *(float(*)[16])g);
+						tmem_ld16(trow + 2 * cc + 16, *(float(*)[16])(g + 16));
+						tmem_ld16(trow + 2 * cc + 32, *(float(*)[16])u);
+						tmem_ld16(trow + 2 * cc + 48, *(float(*)[16])(u + 16));
+						uint32_t hi[16], lo[16];
+#pragma unroll
+						for (int k = 0; k < 32; k++) {
+							float gs = g[k] * ssc[cc + k], us = u[k] * ssc[BN / 2 + cc + k];
+							float y = __fmul_rn(__fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs))), us); // silu(g) * u
+							uint32_t h = bf16_bits(y);
+							uint32_t l = bf16_bits(y - __uint_as_float(h << 16));
+							if (k & 1) {
+								hi[k >> 1] |= h << 16;
+								lo[k >> 1] |= l << 16;
+							} else {
+								hi[k >> 1] = h;
+								lo[k >> 1] = l;
+							}
+						}
+						uint8_t *rh = stg + r * 128, *rl = stg + 16384 + r * 128;
+#pragma unroll
+						for (int q = 0; q < 4; q++) {
+							const int pu = ((4 * hf + q) ^ (r & 7)) * 16;
+							*(uint4 *)(rh + pu) = make_uint4(hi[4 * q], hi[4 * q + 1], hi[4 * q + 2], hi[4 * q + 3]);
+							*(uint4 *)(rl + pu) = make_uint4(lo[4 * q], lo[4 * q + 1], lo[4 * q + 2], lo[4 * q + 3]);
+						}
+					}
+					fence_async_smem();
+					epilogue_sync();
+					if (et == 0) {
+						tma_store_2d(&maps.o[0], stg, f0 + c, m0);
+						tma_store_2d(&maps.o[1], stg + 16384, f0 + c, m0);
+						tma_store_commit();
+					}
+				}
+			} else {
+				for (int c = 0; c < BN; c += 32, chunk++) {
+					uint8_t *buf = stg + (chunk & 1) * 16384;
+					if (et == 0) tma_store_wait_read1(); // the store that last read this half is done
+					epilogue_sync();
+					float v[32];
+					__syncwarp();
+					tmem_ld16(trow + c, *(float(*)[16])v);
+					tmem_ld16(trow + c + 16, *(float(*)[16])(v + 16));
+					const float rs = p.scale_mode == 1 ? ssc[r] : 1.0f;
+#pragma unroll
+					for (int k = 0; k < 32; k++) {
+						if (p.scale_mode == 1) v[k] = __fmul_rn(rs, v[k]);
+						else if (p.scale_mode == 2) v[k] = __fmul_rn(ssc[c + k], v[k]);
+					}
+					uint8_t *rp = buf + r * 128;
+#pragma unroll
+					for (int q = 0; q < 8; q++)
+						*(float4 *)(rp + ((q ^ (r & 7)) * 16)) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+					fence_async_smem();
+					epilogue_sync();
+					if (et == 0) {
+						if (n0 + c < p.N) {
+							if (EPI == EPI_ADD) tma_reduce_add_2d(&maps.o[0], buf, n0 + c, m0);
+							else tma_store_2d(&maps.o[0], buf, n0 + c, m0);
+						}
+						tma_store_commit(); // (an empty group when the chunk is past N)
+					}
+				}
+			}
+			tc_fence_before();
+			mbar_arrive(&acc_empty[b]); // this thread's TMEM loads of buffer b are complete
+		}
+		if (et == 0) tma_store_wait_all();
+	}
+	__syncthreads();
+	if (warp == 1) {
+		tc_fence_after();
+		tmem_dealloc(tmem, 2 * BN);
+	}
+}
+
 // ---- host ----------------------------------------------------------------------------------
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -368,6 +576,24 @@ static int launch_bn(const TmaMaps &maps, const GemmArgs &p, cudaStream_t st)
 	}
 	dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, p.kb_per_split ? (unsigned)(((p.K + BK - 1) / BK + p.kb_per_split - 1) / p.kb_per_split) : 1u);
 	gemm_tc<BN, STAGES, EPI><<<grid, 192, smem, st>>>(maps, p);
+	TGC_LAUNCH_CHECK();
+	return TG_CUDA_OK;
+}
+
+template <int BN, int STAGES, int EPI>
+static int launch_persistent(const TmaMaps &maps, const GemmArgs &p, int grid, cudaStream_t st)
+{
+	const int stage = p.na * A_TILE + p.nb * BN * BK * 2;
+	const size_t smem = (size_t)STAGES * stage + PSTG + 1024 + 256 + 1024; // ring, staging, alignment, barriers, scales
+	static bool attr_set[64] = {};
+	int dev;
+	cudaGetDevice(&dev);
+	if (!attr_set[dev]) {
+		cudaFuncSetAttribute(gemm_tc_persistent<BN, STAGES, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+		attr_set[dev] = true;
+	}
+	if (smem > 232448) return set_err(TG_CUDA_EINVAL, "gemm: persistent tiles do not fit shared memory");
+	gemm_tc_persistent<BN, STAGES, EPI><<<grid, 192, smem, st>>>(maps, p);
 	TGC_LAUNCH_CHECK();
 	return TG_CUDA_OK;
 }
@@ -487,6 +713,27 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 		p.tma_out = 1;
 	}
 	if (stages * stage > 220 * 1024) return set_err(TG_CUDA_EINVAL, "gemm: %d operand tiles do not fit", p.na + p.nb);
+	// More tiles than SMs, bf16 operands, a TMA-addressable output: the persistent kernel, whose
+	// epilogue overlaps the next tile's main loop
+	if (!p.cside && p.tma_out && BN >= 128 && tiles > sms) {
+		const int pst = std::min(4, (int)((232448 - 1024 - 256 - 1024 - PSTG) / stage));
+		const int grid = (int)std::min<long>(tiles, sms);
+		if (pst >= 2) {
+#define TGC_GEMM_PERSIST(E)                                                                            \
+	if (BN == 256) return pst >= 3 ? launch_persistent<256, 3, E>(maps, p, grid, st) : launch_persistent<256, 2, E>(maps, p, grid, st); \
+	return pst >= 4 ? launch_persistent<128, 4, E>(maps, p, grid, st) : launch_persistent<128, 3, E>(maps, p, grid, st);
+			if (pst >= 3 || BN == 256) {
+				if (p.epi == EPI_SWIGLU) {
+					TGC_GEMM_PERSIST(EPI_SWIGLU)
+				}
+				if (p.epi == EPI_ADD) {
+					TGC_GEMM_PERSIST(EPI_ADD)
+				}
+				TGC_GEMM_PERSIST(EPI_STORE)
+			}
+#undef TGC_GEMM_PERSIST
+		}
+	}
 #define TGC_GEMM_DISPATCH(E)                                                                 \
 	if (BN == 64) return launch_bn<64, 4, E>(maps, p, st); /* 40-48 KB stages: always 4 */ \
 	if (BN == 256)                                                                      \
