@@ -14,10 +14,12 @@
 //        probabilities (split hi/lo) to shared memory as the A operand of P.V, and at
 //        the end reads O from TMEM, divides by the sum and stores it split hi/lo (the
 //        o_proj GEMM's input).
-//   4-7  loaders: Q once, then per key tile K (warps 4-5; rows = keys, K-major over
-//        dims) and V^T (warps 6-7; rows = dims, K-major over keys): the cache's bf16
-//        part and the bf16 of its remainder (kv.cuh) as hi/lo, in the 128-byte-swizzled
-//        K-major layout of the UMMA descriptors.
+//   4-7  converters: Q once (from global); then per key tile, from a staging area that
+//        bulk copies fill with the tile's rows of the cache (bf16 part and remainder
+//        bytes of K and V, kv.cuh), K (rows = keys, K-major over dims) and V^T (rows =
+//        dims, K-major over keys) as bf16 hi/lo in the 128-byte-swizzled K-major layout
+//        of the UMMA descriptors. Thread 0 issues the next tile's bulk copies as soon as
+//        all converters have read the staging area, so global latency overlaps the tile.
 //   8    TMEM allocation and the MMA issue (one thread): S_j = Q.K_j^T into one of two
 //        TMEM score buffers, O += P_j.V_j into the TMEM accumulator. S_{j+1} is issued
 //        before P_j.V_j so the softmax of tile j+1 overlaps the P.V of tile j.
@@ -25,7 +27,8 @@
 // raised (and O, l rescaled in place) only when a tile's max exceeds it by more than
 // FA_RESCALE, so O is rarely touched between tiles; exp(s - m_ref) <= e^8 keeps the
 // sums well inside f32. The quotient O / l is the same as the reference's
-// exp(s - max) / sum, up to rounding.
+// exp(s - max) / sum, up to rounding (the exponentials use the hardware exp2, relative
+// error about 2^-21 here).
 //
 // Every wait is bounded (tc.cuh); a timeout sets the status word and all roles
 // leave their loops, waiting for their own MMAs before TMEM is released.
@@ -33,6 +36,7 @@
 
 #include <cuda_bf16.h>
 
+#include "kv.cuh"
 #include "tc.cuh"
 
 namespace tgc {
@@ -40,23 +44,27 @@ namespace tgc {
 constexpr int FA_Q = 128, FA_K = 64, FA_HD = 128;
 constexpr float FA_RESCALE = 8.0f;
 constexpr int FA_THREADS = 288;
-constexpr int FA_LB = 8; // items whose global loads a loader issues before converting them
+constexpr int FA_LB = 8; // Q items whose global loads a converter issues before converting them
 
-// shared-memory layout (byte offsets from a 1024-aligned base); each tile is K-major
-// with 128-byte swizzle: rows of 128 bytes, 8-row atoms of 1024 bytes
+// shared-memory layout (byte offsets from a 1024-aligned base); each operand tile is
+// K-major with 128-byte swizzle: rows of 128 bytes, 8-row atoms of 1024 bytes
 constexpr int FA_SQ_HI = 0;          // Q hi: [2 k-blocks][128 rows][128 B]
 constexpr int FA_SQ_LO = 32768;      // Q lo
 constexpr int FA_SK_HI = 65536;      // K hi: [2 k-blocks][64 rows][128 B]
 constexpr int FA_SK_LO = 81920;      // K lo
 constexpr int FA_SV_HI = 98304;      // V^T hi: [128 rows][128 B]
 constexpr int FA_SV_LO = 114688;     // V^T lo
-constexpr int FA_SP = 131072;        // P buffer b: hi at FA_SP + 32768 b, lo 16384 after it
-constexpr int FA_SBAR = 196608;      // barriers and the TMEM address
+constexpr int FA_SP = 131072;        // P: hi [128 rows][128 B], lo 16384 after it
+constexpr int FA_ST_KH = 163840;     // staging, the tile's rows as in the cache: K bf16 [64][128]
+constexpr int FA_ST_KQ = 180224;     //   K remainder bytes [64][128]
+constexpr int FA_ST_VH = 188416;     //   V bf16
+constexpr int FA_ST_VQ = 204800;     //   V remainder bytes
+constexpr int FA_SBAR = 212992;      // barriers and the TMEM address
 constexpr size_t FA_SMEM = FA_SBAR + 256 + 1024; // + alignment slack
 
 struct FaBars {
-	uint64_t q_full, k_full, k_empty, v_full, v_empty;
-	uint64_t s_full[2], s_free[2], p_full[2], p_empty[2], done;
+	uint64_t q_full, stg_full, stg_free, k_full, k_empty, v_full, v_empty;
+	uint64_t s_full[2], s_free[2], p_full, p_empty, done;
 	uint32_t tmem;
 	int abort;
 };
@@ -129,19 +137,22 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 	const int kvh = h / (NQ / NKV);
 	const int q0 = qt * FA_Q;
 	const int nkt = (min(q0 + FA_Q, T) + FA_K - 1) / FA_K;
+	const long cb = ((long)(slot0 + s) * NKV + kvh) * (long)max_len * FA_HD; // this (sequence, kv head)'s cache rows
 
 	if (threadIdx.x == 0) {
 		mbar_init(&B->q_full, 128);
-		mbar_init(&B->k_full, 64);
+		mbar_init(&B->stg_full, 1);
+		mbar_init(&B->stg_free, 128);
+		mbar_init(&B->k_full, 128);
 		mbar_init(&B->k_empty, 1);
-		mbar_init(&B->v_full, 64);
+		mbar_init(&B->v_full, 128);
 		mbar_init(&B->v_empty, 1);
 		for (int b = 0; b < 2; b++) {
 			mbar_init(&B->s_full[b], 1);
 			mbar_init(&B->s_free[b], 128);
-			mbar_init(&B->p_full[b], 128);
-			mbar_init(&B->p_empty[b], 1);
 		}
+		mbar_init(&B->p_full, 128);
+		mbar_init(&B->p_empty, 1);
 		mbar_init(&B->done, 1);
 		B->abort = 0;
 		fence_barrier_init();
@@ -153,14 +164,20 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 	const uint32_t tmem = B->tmem;
 
 	if (warp >= 4 && warp < 8) {
-		// ---------------- loaders ----------------
+		// ---------------- converters ----------------
 		const int t = threadIdx.x - 128;
+		// the bulk copies of key tile j into the staging area (rows past T are not copied)
+		auto stage = [&](int j) {
+			const int k0 = j * FA_K, rows = min(FA_K, T - k0);
+			mbar_expect_tx(&B->stg_full, (uint32_t)rows * (256 + 128) * 2);
+			bulk_load(sm + FA_ST_KH, kc.h + cb + (long)k0 * FA_HD, rows * 256, &B->stg_full);
+			bulk_load(sm + FA_ST_KQ, kc.q + cb + (long)k0 * FA_HD, rows * 128, &B->stg_full);
+			bulk_load(sm + FA_ST_VH, vc.h + cb + (long)k0 * FA_HD, rows * 256, &B->stg_full);
+			bulk_load(sm + FA_ST_VQ, vc.q + cb + (long)k0 * FA_HD, rows * 128, &B->stg_full);
+		};
+		int pending = -1; // thread 0: a staged tile whose copies nobody has waited for yet
+		if (t == 0) stage(0), pending = 0;
 		const float *qb = q + ((long)s * NQ + h) * (long)T * FA_HD;
-		const long cb = ((long)(slot0 + s) * NKV + kvh) * (long)max_len * FA_HD;
-		const __nv_bfloat16 *kh = kc.h + cb, *vh = vc.h + cb;
-		const signed char *kq = kc.q + cb, *vq = vc.q + cb;
-		// The loaders issue FA_LB items' global loads before converting any of them: the
-		// latency of a load round is paid once per batch, not once per item.
 		for (int i0 = t; i0 < FA_Q * 16; i0 += 128 * FA_LB) { // Q: 128 rows x 16 chunks of 8 dims
 			float4 a[FA_LB], b[FA_LB];
 #pragma unroll
@@ -184,81 +201,77 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 		}
 		fence_async_smem();
 		mbar_arrive(&B->q_full);
-		const int u = t & 63; // warps 4-5 load K tiles, warps 6-7 V tiles
 		for (int j = 0; j < nkt; j++) {
 			const int k0 = j * FA_K;
-			if (t < 64) {
-				if (j > 0 && !fa_wait(B, &B->k_empty, (j - 1) & 1, status)) break;
-				for (int i0 = u; i0 < FA_K * 16; i0 += 64 * FA_LB) { // K: 64 rows x 16 chunks of 8 dims
-					uint4 hv[FA_LB];
-					uint2 qv[FA_LB];
-#pragma unroll
-					for (int v = 0; v < FA_LB; v++) {
-						const int i = i0 + v * 64, r = i >> 4, c = i & 15;
-						const bool in = i < FA_K * 16 && k0 + r < T;
-						const long e = (long)(k0 + r) * FA_HD + c * 8;
-						hv[v] = in ? *(const uint4 *)(kh + e) : make_uint4(0u, 0u, 0u, 0u);
-						qv[v] = in ? *(const uint2 *)(kq + e) : make_uint2(0u, 0u);
-					}
-#pragma unroll
-					for (int v = 0; v < FA_LB; v++) {
-						const int i = i0 + v * 64, r = i >> 4, c = i & 15;
-						if (i >= FA_K * 16) break;
-						const uint32_t hw[4] = { hv[v].x, hv[v].y, hv[v].z, hv[v].w }, qw[2] = { qv[v].x, qv[v].y };
-						uint32_t lw[4];
-#pragma unroll
-						for (int w = 0; w < 4; w++) {
-							const uint32_t qq = qw[w >> 1] >> (16 * (w & 1)); // the two bytes of this word's elements
-							lw[w] = kv_lo_bits(hw[w] & 0xFFFF, (int)(int8_t)(qq & 0xFF)) |
-								(kv_lo_bits(hw[w] >> 16, (int)(int8_t)((qq >> 8) & 0xFF)) << 16);
-						}
-						uint32_t off = (uint32_t)((c >> 3) * 8192) + fa_sw(r, c & 7);
-						*(uint4 *)(sm + FA_SK_HI + off) = hv[v];
-						*(uint4 *)(sm + FA_SK_LO + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-					}
+			if (!fa_wait(B, &B->stg_full, j & 1, status)) break;
+			pending = -1;
+			// K: 64 rows x 16 chunks of 8 dims; the bf16 part as is, the remainder as lo
+			if (j > 0 && !fa_wait(B, &B->k_empty, (j - 1) & 1, status)) break;
+#pragma unroll 2
+			for (int i = t; i < FA_K * 16; i += 128) {
+				const int r = i >> 4, c = i & 15;
+				uint4 hv = make_uint4(0u, 0u, 0u, 0u);
+				uint2 qv = make_uint2(0u, 0u);
+				if (k0 + r < T) {
+					hv = *(const uint4 *)(sm + FA_ST_KH + r * 256 + c * 16);
+					qv = *(const uint2 *)(sm + FA_ST_KQ + r * 128 + c * 8);
 				}
-				fence_async_smem();
-				mbar_arrive(&B->k_full);
-			} else {
-				if (j > 0 && !fa_wait(B, &B->v_empty, (j - 1) & 1, status)) break;
-				for (int i0 = u; i0 < 256; i0 += 128) { // V^T: item = (8 keys, 4 dims) -> one chunk in 4 rows
-					uint2 hv[2][8];                   // two items' loads in flight at once
-					uint32_t qv[2][8];
+				const uint32_t hw[4] = { hv.x, hv.y, hv.z, hv.w }, qw[2] = { qv.x, qv.y };
+				uint32_t lw[4];
 #pragma unroll
-					for (int v = 0; v < 2; v++) {
-						const int i = i0 + v * 64, kg = i & 7, dg = i >> 3;
-#pragma unroll
-						for (int e = 0; e < 8; e++) {
-							const int key = k0 + kg * 8 + e;
-							const long o = (long)key * FA_HD + dg * 4;
-							hv[v][e] = key < T ? *(const uint2 *)(vh + o) : make_uint2(0u, 0u);
-							qv[v][e] = key < T ? *(const uint32_t *)(vq + o) : 0u;
-						}
-					}
-#pragma unroll
-					for (int v = 0; v < 2; v++) {
-						const int i = i0 + v * 64, kg = i & 7, dg = i >> 3;
-#pragma unroll
-						for (int dd = 0; dd < 4; dd++) {
-							uint32_t hb[8], lb[8]; // dim dg*4+dd of the 8 keys
-#pragma unroll
-							for (int e = 0; e < 8; e++) {
-								const uint32_t hw = dd < 2 ? hv[v][e].x : hv[v][e].y;
-								hb[e] = (dd & 1) ? hw >> 16 : hw & 0xFFFF;
-								lb[e] = kv_lo_bits(hb[e], (int)(int8_t)((qv[v][e] >> (8 * dd)) & 0xFF));
-							}
-							const uint4 hi = make_uint4(hb[0] | (hb[1] << 16), hb[2] | (hb[3] << 16), hb[4] | (hb[5] << 16), hb[6] | (hb[7] << 16));
-							const uint4 lo = make_uint4(lb[0] | (lb[1] << 16), lb[2] | (lb[3] << 16), lb[4] | (lb[5] << 16), lb[6] | (lb[7] << 16));
-							uint32_t off = fa_sw(dg * 4 + dd, kg);
-							*(uint4 *)(sm + FA_SV_HI + off) = hi;
-							*(uint4 *)(sm + FA_SV_LO + off) = lo;
-						}
-					}
+				for (int w = 0; w < 4; w++) {
+					const uint32_t qq = qw[w >> 1] >> (16 * (w & 1)); // the two bytes of this word's elements
+					lw[w] = kv_lo_bits(hw[w] & 0xFFFF, (int)(int8_t)(qq & 0xFF)) |
+						(kv_lo_bits(hw[w] >> 16, (int)(int8_t)((qq >> 8) & 0xFF)) << 16);
 				}
+				const uint32_t off = (uint32_t)((c >> 3) * 8192) + fa_sw(r, c & 7);
+				*(uint4 *)(sm + FA_SK_HI + off) = hv;
+				*(uint4 *)(sm + FA_SK_LO + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+			}
+			fence_async_smem();
+			mbar_arrive(&B->k_full);
+			// V^T: item = (8 keys, 4 dims) -> one 16-byte chunk in each of 4 rows
+			if (j > 0 && !fa_wait(B, &B->v_empty, (j - 1) & 1, status)) break;
+			for (int i = t; i < 256; i += 128) {
+				const int kg = i & 7, dg = i >> 3;
+				uint2 hv[8];
+				uint32_t qv[8];
+#pragma unroll
+				for (int e = 0; e < 8; e++) {
+					const int key = kg * 8 + e;
+					const bool in = k0 + key < T;
+					hv[e] = in ? *(const uint2 *)(sm + FA_ST_VH + key * 256 + dg * 8) : make_uint2(0u, 0u);
+					qv[e] = in ? *(const uint32_t *)(sm + FA_ST_VQ + key * 128 + dg * 4) : 0u;
+				}
+#pragma unroll
+				for (int dd = 0; dd < 4; dd++) {
+					uint32_t hb[8], lb[8]; // dim dg*4+dd of the 8 keys
+#pragma unroll
+					for (int e = 0; e < 8; e++) {
+						const uint32_t hw = dd < 2 ? hv[e].x : hv[e].y;
+						hb[e] = (dd & 1) ? hw >> 16 : hw & 0xFFFF;
+						lb[e] = kv_lo_bits(hb[e], (int)(int8_t)((qv[e] >> (8 * dd)) & 0xFF));
+					}
+					const uint4 hi = make_uint4(hb[0] | (hb[1] << 16), hb[2] | (hb[3] << 16), hb[4] | (hb[5] << 16), hb[6] | (hb[7] << 16));
+					const uint4 lo = make_uint4(lb[0] | (lb[1] << 16), lb[2] | (lb[3] << 16), lb[4] | (lb[5] << 16), lb[6] | (lb[7] << 16));
+					const uint32_t off = fa_sw(dg * 4 + dd, kg);
+					*(uint4 *)(sm + FA_SV_HI + off) = hi;
+					*(uint4 *)(sm + FA_SV_LO + off) = lo;
+				}
+			}
+			fence_async_smem();
+			mbar_arrive(&B->v_full);
+			// the staging area has been read: thread 0 refills it with the next tile
+			mbar_arrive(&B->stg_free);
+			if (t == 0 && j + 1 < nkt) {
+				if (!fa_wait(B, &B->stg_free, j & 1, status)) break;
 				fence_async_smem();
-				mbar_arrive(&B->v_full);
+				stage(j + 1);
+				pending = j + 1;
 			}
 		}
+		// after an abort: the copies still in flight land before the CTA's shared memory is released
+		if (pending >= 0) mbar_wait(&B->stg_full, pending & 1, nullptr, 0);
 	} else if (warp == 8) {
 		// ---------------- MMA issue ----------------
 		if (lane == 0) {
@@ -286,10 +299,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 			};
 			auto issue_pv = [&](int j) -> bool {
 				if (!fa_wait(B, &B->v_full, j & 1, status)) return false;
-				if (!fa_wait(B, &B->p_full[j & 1], (j >> 1) & 1, status)) return false;
+				if (!fa_wait(B, &B->p_full, j & 1, status)) return false;
 				tc_fence_after();
-				const uint32_t pbuf = base + FA_SP + (uint32_t)((j & 1) * 32768);
-				const uint32_t pa2[2] = { pbuf, pbuf + 16384 }, va[2] = { base + FA_SV_HI, base + FA_SV_LO };
+				const uint32_t pa2[2] = { base + FA_SP, base + FA_SP + 16384 }, va[2] = { base + FA_SV_HI, base + FA_SV_LO };
 				const int pa[3] = { 0, 0, 1 }, pb[3] = { 0, 1, 0 };
 				for (int kk = 0; kk < 4; kk++)
 					for (int pr = 0; pr < 3; pr++) {
@@ -297,7 +309,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 						tc_mma_f16(tmem + 128, sw128_kmajor_desc(a), sw128_kmajor_desc(b), idO,
 							   (j > 0 || kk > 0 || pr > 0) ? 1u : 0u);
 					}
-				tc_commit(&B->p_empty[j & 1]);
+				tc_commit(&B->p_empty);
 				tc_commit(&B->v_empty);
 				return true;
 			};
@@ -342,11 +354,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 			}
 			const bool raise = mt > m_ref + FA_RESCALE;
 			const float m_new = raise ? mt : m_ref;
+			// P's buffer (and O, for a rescale) is free once P_{j-1}.V has completed
+			if (j > 0 && !(ok = fa_wait_warp(B, &B->p_empty, (j - 1) & 1, status))) break;
 			if (__any_sync(0xffffffffu, raise && m_ref != -INFINITY)) {
-				// O holds P.V of tiles < j at the old reference max: wait for P_{j-1}.V, rescale in place
-				if (!(ok = fa_wait_warp(B, &B->p_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, status))) break;
+				// O holds P.V of tiles < j at the old reference max: rescale it in place
 				tc_fence_after();
-				const float f = raise && m_ref != -INFINITY ? expf(m_ref - m_new) : 1.0f;
+				const float f = raise && m_ref != -INFINITY ? __expf(m_ref - m_new) : 1.0f;
 #pragma unroll 1
 				for (int c = 0; c < FA_HD / 16; c++) {
 					float v[16];
@@ -362,14 +375,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 			float sum = 0.0f;
 #pragma unroll
 			for (int c = 0; c < FA_K; c++) {
-				float p = sc[c] == -INFINITY ? 0.0f : expf(sc[c] - m_ref);
+				float p = sc[c] == -INFINITY ? 0.0f : __expf(sc[c] - m_ref);
 				sc[c] = p;
 				sum += p;
 			}
 			l += sum;
-			// P buffer j&1 was last read by P_{j-2}.V
-			if (j >= 2 && !(ok = fa_wait_warp(B, &B->p_empty[j & 1], ((j >> 1) - 1) & 1, status))) break;
-			uint8_t *pb = sm + FA_SP + (j & 1) * 32768;
+			uint8_t *pb = sm + FA_SP;
 #pragma unroll
 			for (int c = 0; c < 8; c++) {
 				float x[8];
@@ -382,9 +393,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 			}
 			fence_async_smem();
 			tc_fence_before();
-			mbar_arrive(&B->p_full[j & 1]);
+			mbar_arrive(&B->p_full);
 		}
-		if (ok) ok = fa_wait_warp(B, &B->p_empty[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, status);
+		if (ok) ok = fa_wait_warp(B, &B->p_empty, (nkt - 1) & 1, status);
 		if (ok) {
 			tc_fence_after();
 			const float inv = 1.0f / l;

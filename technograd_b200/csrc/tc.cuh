@@ -72,6 +72,15 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
 		: "memory");
 }
 
+// Bulk copy of a contiguous global range into shared memory (no tensor map), completion
+// counted on bar. Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+{
+	asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+		     ::"r"(smem_u32(dst)), "l"((uint64_t)src), "r"(bytes), "r"(smem_u32(bar))
+		     : "memory");
+}
+
 // 2D TMA tile store / reduce-add from shared memory (bulk-group completion; no multicast).
 // The x coordinate must be 16-byte aligned and neither coordinate negative.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y)
