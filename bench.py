@@ -215,9 +215,9 @@ def bench_decode(args, world, rank, local):
                    "gemm_tflops": gemm_tf, "attn_prefill_tflops_f32": pre_tf, "build_s": t_build},
         "roofline": {"kernel": "k_attn_decode (KV-cache attention)", "bound": "hbm", "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "peak_source": src,
-                     # ncu dram read+write of a 64-sequence launch was 1.009x its algorithmic bytes
+                     # ncu dram read+write of a 64-sequence launch was 1.014x its algorithmic bytes
                      # (profiles/k_attn_decode_small.md); traffic grows with sequences x keys
-                     "traffic": 1.009 * dec_bytes / max(dec_launches, 1),
+                     "traffic": 1.014 * dec_bytes / max(dec_launches, 1),
                      "traffic_source": "ncu small-case ratio x algorithmic bytes per launch",
                      "bytes_per_launch": dec_bytes / max(dec_launches, 1),
                      "ms_per_launch": dec_ms / max(dec_launches, 1)},

@@ -123,15 +123,21 @@ __global__ void __launch_bounds__(128) k_ssm_scan(const float *__restrict__ dbc,
 #pragma unroll
 	for (int p = 0; p < R; p++) w[p] = wdt[(long)c * R + p]; // codes of column c of Wdt
 	const float sc = sdt[c], bias = dtb[c], dd = Dv[c];
+	// x and z of step t + 1 are loaded while step t computes (the loop is latency-bound otherwise)
+	float xn = xs[(long)s * Tc * DI + c], zn = xz[(long)s * Tc * 2 * DI + DI + c];
 	for (int t = 0; t < Tc; t++) {
 		const float *row = sd + t * W;
 		const long gr = (long)s * Tc + t;
+		const float x = xn, zt = zn;
+		if (t + 1 < Tc) {
+			xn = xs[(gr + 1) * DI + c];
+			zn = xz[(gr + 1) * 2 * DI + DI + c];
+		}
 		// dt = softplus(s * sum_p r[p] code[p] + dt_b), the sum in p order (runtime/tg_rt.h:143-151)
 		float acc = 0.0f;
 #pragma unroll
 		for (int p = 0; p < R; p++) acc = __fadd_rn(acc, __fmul_rn(row[p], w[p]));
 		const float dt = ssm_softplus(__fadd_rn(__fmul_rn(sc, acc), bias));
-		const float x = xs[gr * DI + c];
 		float m1 = 0.0f;
 		// the state update of the program, h = e*h + (1 - e)/a * (x*bt) with e = exp(-dt*a), in
 		// the fast forms: the hardware exp2 approximation (relative error about 2^-21 on this
@@ -145,7 +151,7 @@ __global__ void __launch_bounds__(128) k_ssm_scan(const float *__restrict__ dbc,
 #pragma unroll
 		for (int k = 0; k < DS; k++) m1 = fmaf(h[k], row[R + DS + k], m1);
 		const float y = __fadd_rn(m1, __fmul_rn(dd, x));
-		const float g = __fmul_rn(y, ssm_silu(xz[gr * 2 * DI + DI + c]));
+		const float g = __fmul_rn(y, ssm_silu(zt));
 		ssm_split(g, ghi[gr * DI + c], glo[gr * DI + c]);
 	}
 #pragma unroll
