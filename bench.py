@@ -654,6 +654,7 @@ def bench_lr(args, world, rank, local):
     rows = lr_inputs(LR_ROWS)
     _lib.init(0, [local])
     b = Batch(m)
+    spec, why = b.specialized
     L = _lib.lib()
     d_in = torch.from_numpy(rows).cuda()
     d_out = torch.empty((LR_ROWS, 4), device="cuda")
@@ -698,8 +699,10 @@ def bench_lr(args, world, rank, local):
         "ms_per_step": sum(ms) / len(ms), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
         "config": {"workload": "config1 latent_reasoner int8 RTN --min-size 1", "rows_per_gpu": LR_ROWS,
-                   "think_steps_mean": float(steps_np.mean()), "l2": L2Flush.NOTE},
-        "roofline": {"kernel": "vm_kernel", "bound": "fp32", "achieved": achieved, "peak": FP32_NOMINAL_TFLOPS,
+                   "think_steps_mean": float(steps_np.mean()), "l2": L2Flush.NOTE,
+                   "kernel": "generated for the program (NVRTC, sm_100a)" if spec else f"tape interpreter ({why})"},
+        "roofline": {"kernel": "tg_rowvm (generated for the program)" if spec else "vm_kernel (tape interpreter)",
+                     "bound": "fp32", "achieved": achieved, "peak": FP32_NOMINAL_TFLOPS,
                      "unit": "TFLOP/s", "frac": achieved / FP32_NOMINAL_TFLOPS, "traffic": None,
                      "peak_source": "nominal FP32 SIMT (148 SMs x 128 lanes x FMA x 1965 MHz); not in MEASURED_PEAKS"},
         "e2e": {"value": world * LR_ROWS * args.steps / te, "unit": "rows/s", "h2d_bytes_per_step": rows.nbytes,

@@ -164,6 +164,18 @@ int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int per, float 
  * asynchronous on stream). Used for measurements with inputs resident in HBM. */
 int tg_cuda_batch_device(tg_cuda_model *g, const float *all, long rows, float *out, int *steps, void *stream);
 void tg_cuda_free(tg_cuda_model *g);
+/* 1 when the model's rows run on a kernel generated for this program (compiled
+ * at load time with NVRTC for sm_100a), 0 when they run on the general tape
+ * interpreter kernel; then `why` (n bytes, may be NULL) receives the reason.
+ * TG_CUDA_ROWVM=interp in the environment at load time selects the interpreter.
+ * Both are GPU kernels with the same arithmetic. No reference counterpart: the
+ * reference's VM is the interpreter (src/vm.c:475-481). */
+int tg_cuda_model_jit(const tg_cuda_model *g, char *why, int n);
+/* The CUDA source generated for a program (written to src, n bytes, NUL-terminated,
+ * may be NULL; *len = its full length), and with compile != 0 its compilation for
+ * sm_100a. Needs neither tg_cuda_init nor a GPU. TG_CUDA_EUNSUPPORTED when the
+ * program is beyond the generator's limits (such a model runs on the interpreter). */
+int tg_cuda_program_kernel(const tg_cuda_program *p, char *src, long n, long *len, int compile);
 
 /* ---- decoder language models (the Qwen3 import) ---------------------------
  * Weights follow examples/qwen3/import.py:37-60: every linear weight is stored

@@ -61,6 +61,16 @@ class Batch:
         _lib.check(_lib.lib().tg_cuda_load(self.prog.ptr(), C.byref(h)))
         self.handle = h
 
+    @property
+    def specialized(self) -> tuple[bool, str]:
+        """(True, "") when rows run on the kernel generated for this program, else
+        (False, reason): they run on the tape interpreter kernel."""
+        why = C.create_string_buffer(512)
+        r = _lib.lib().tg_cuda_model_jit(self.handle, why, 512)
+        if r < 0:
+            _lib.check(r)
+        return r == 1, why.value.decode()
+
     def __del__(self):
         h = getattr(self, "handle", None)
         if h:

@@ -23,10 +23,12 @@
 
 #include <algorithm>
 #include <memory>
+#include <mutex>
 #include <thread>
 #include <vector>
 
 #include "common.cuh"
+#include "jit.cuh"
 #include "kernels.cuh"
 
 namespace tgc {
@@ -76,7 +78,14 @@ __device__ __forceinline__ Loc loc(int l, float *ar, const float *pb)
 	return { (float *)pb + (-(l + 1)), 1 };
 }
 
-__device__ float un_op(int op, float x)
+// The element functions. They are compiled here for the interpreter and handed as source
+// text to the run-time compiler for the specialised kernels, so both paths share one
+// definition.
+#define TGC_ROW_MATH(...) \
+	__VA_ARGS__       \
+	static const char kRowMathSrc[] = #__VA_ARGS__;
+TGC_ROW_MATH(
+__device__ __forceinline__ float un_op(int op, float x)
 {
 	switch (op) {
 	case TG_CUDA_OP_NEG: return -x;
@@ -113,6 +122,7 @@ __device__ __forceinline__ float bin_op(int op, float x, float y)
 	}
 	return 0.0f;
 }
+)
 
 // o[i,j] (+ per-group offsets) = sum_p a[i,p] b[p,j], in p order, scale after the sum.
 __device__ void vm_matmul(const DOp &op, float *ar, const float *pb)
@@ -338,16 +348,66 @@ __global__ void __launch_bounds__(VM_ROWS) vm_kernel(const DOp *__restrict__ tap
 
 // ---- host: program -> tape -------------------------------------------------------------------
 
+// Pinned host memory, grown on demand.
+struct HostBuf {
+	void *p = nullptr;
+	size_t bytes = 0;
+	HostBuf() = default;
+	HostBuf(const HostBuf &) = delete;
+	HostBuf &operator=(const HostBuf &) = delete;
+	~HostBuf()
+	{
+		if (p) cudaFreeHost(p);
+	}
+	int ensure(size_t n)
+	{
+		if (n <= bytes) return TG_CUDA_OK;
+		if (p) cudaFreeHost(p);
+		p = nullptr;
+		bytes = 0;
+		if (cudaHostAlloc(&p, n, cudaHostAllocDefault) != cudaSuccess) {
+			cudaGetLastError();
+			return set_err(TG_CUDA_ENOMEM, "cudaHostAlloc(%zu) failed", n);
+		}
+		bytes = n;
+		return TG_CUDA_OK;
+	}
+};
+
+// One stage of the host-buffer pipeline of tg_cuda_batch: pinned staging, the device
+// buffers of one chunk of rows and the stream that carries it.
+struct Slot {
+	HostBuf hin, hout, hsteps;
+	DevBuf din, dout, dsteps;
+	cudaStream_t st = nullptr;
+	cudaEvent_t done = nullptr;
+	long lo = 0, cnt = 0; // rows of the chunk in flight (offset within the device's shard)
+	bool busy = false;
+	Slot() = default;
+	Slot(const Slot &) = delete;
+	Slot &operator=(const Slot &) = delete;
+	~Slot()
+	{
+		if (done) cudaEventDestroy(done);
+		if (st) cudaStreamDestroy(st);
+	}
+};
+
 struct Model {
 	Prog prog;
 	struct PerDev {
 		DevBuf tape, blob, inloc, inlen, gar;
 		long gar_rows = 0;
+		JitModule jit; // the program's specialised kernel on this device
+		Slot slot[2];  // tg_cuda_batch pipeline
+		std::mutex mu; // one tg_cuda_batch at a time on this device's slots
 	};
 	std::vector<std::unique_ptr<PerDev>> dev;
 	bool blob_in_smem = true;
 	size_t smem = 0;
 	bool global_arena = false;
+	bool jit = false;    // rows run on the specialised kernel (else on vm_kernel)
+	std::string jit_why; // why not, when not
 };
 
 static long numel(const tg_cuda_value &v)
@@ -735,7 +795,7 @@ static int emit_block(Compiler &C, int from, int cnt, int depth)
 	return 0;
 }
 
-static int compile(const tg_cuda_program *p, Prog &out, std::string &err)
+static int compile_program(const tg_cuda_program *p, Prog &out, std::string &err)
 {
 	Compiler C;
 	C.p = p;
@@ -824,6 +884,285 @@ static int compile(const tg_cuda_program *p, Prog &out, std::string &err)
 	return TG_CUDA_OK;
 }
 
+// ---- run-time specialisation of the tape --------------------------------------------------
+//
+// The tape above is also turned into CUDA source for one kernel per program: every op
+// becomes straight-line code with its element indices resolved, so the arena is an
+// array of the thread's own registers (all indices are constants), params small enough
+// for the 64 KB constant bank are read from it as instruction operands, and op
+// dispatch, operand decoding and loop bookkeeping disappear. Control flow, rounding
+// and operation order are those of vm_kernel, op for op (the same element functions,
+// the same accumulation chains), with think loops as warp-uniform backward jumps.
+// Programs whose arena is indexed at run time (scan slices, take from a computed value)
+// run on vm_kernel: such a kernel would keep its arena in local memory, and one of them
+// (the nested_grad test program, every index checked in range) stopped with an illegal
+// address on the B200 for a cause not found; jit_build also refuses any generated kernel
+// that needs local memory.
+
+static const struct {
+	const char *name;
+	int v;
+} kOpNames[] = {
+#define TGC_OPNAME(x) { #x, x }
+	TGC_OPNAME(TG_CUDA_OP_ADD), TGC_OPNAME(TG_CUDA_OP_SUB), TGC_OPNAME(TG_CUDA_OP_MUL), TGC_OPNAME(TG_CUDA_OP_DIV),
+	TGC_OPNAME(TG_CUDA_OP_MAX), TGC_OPNAME(TG_CUDA_OP_MIN), TGC_OPNAME(TG_CUDA_OP_NEG), TGC_OPNAME(TG_CUDA_OP_TANH),
+	TGC_OPNAME(TG_CUDA_OP_RELU), TGC_OPNAME(TG_CUDA_OP_SIGMOID), TGC_OPNAME(TG_CUDA_OP_EXP), TGC_OPNAME(TG_CUDA_OP_SQRT),
+	TGC_OPNAME(TG_CUDA_OP_GELU), TGC_OPNAME(TG_CUDA_OP_SILU), TGC_OPNAME(TG_CUDA_OP_SOFTPLUS), TGC_OPNAME(TG_CUDA_OP_LOG),
+	TGC_OPNAME(TG_CUDA_OP_STEP), TGC_OPNAME(TG_CUDA_OP_SIN), TGC_OPNAME(TG_CUDA_OP_COS), TGC_OPNAME(TG_CUDA_OP_FLOOR),
+#undef TGC_OPNAME
+};
+
+constexpr long JIT_MAX_STMTS = 20000;   // larger programs stay on the interpreter (compile time)
+constexpr int JIT_MAX_ARENA = 192;      // floats per row: beyond this the arena no longer fits the registers
+constexpr size_t JIT_MAX_CPARAMS = 16000; // floats of params in the constant bank
+
+struct Gen {
+	const Prog &P;
+	bool cparams;
+	std::string s;
+	long stmts = 0;
+	std::vector<char> label;
+
+	explicit Gen(const Prog &p) : P(p), cparams(p.blob.size() <= JIT_MAX_CPARAMS), label(p.tape.size() + 1, 0) {}
+
+	static std::string num(long v) { return std::to_string(v); }
+	static std::string flt(float f)
+	{
+		uint32_t u;
+		memcpy(&u, &f, 4);
+		char b[32];
+		snprintf(b, sizeof b, "__uint_as_float(0x%08xu)", u);
+		return b;
+	}
+	// element e of a location, e a constant
+	std::string at(int l, long e) const
+	{
+		if (l >= 0) return "ar[" + num(l + e) + "]";
+		long i = -(long)(l + 1) + e;
+		return cparams ? "CP(" + num(i) + ")" : "__ldg(GP + " + num(i) + ")";
+	}
+	// element `e` (a run-time expression) of a param location
+	std::string atd(int l, const std::string &e) const { return "__ldg(GP + " + num(-(long)(l + 1)) + " + (" + e + "))"; }
+	void line(const std::string &x)
+	{
+		s += x;
+		s += '\n';
+		stmts++;
+	}
+	int op(int pc);
+};
+
+int Gen::op(int pc)
+{
+	const DOp &o = P.tape[pc];
+	const std::string D = num(o.depth);
+	if (label[pc]) line("L" + num(pc) + ":;");
+	switch (o.code) {
+	case D_CONST:
+		line("if (done == 0u) " + at(o.out, 0) + " = " + flt(o.f) + ";");
+		return 0;
+	case D_BIN:
+		line("if (done == 0u) {");
+		for (int e = 0; e < o.n; e++) {
+			long ia, ib;
+			if (o.rank == 0) {
+				ia = (long)e * o.sa[0];
+				ib = (long)e * o.sb[0];
+			} else {
+				int rem = e;
+				ia = ib = 0;
+				for (int d = o.rank - 1; d >= 0; d--) {
+					int idx = rem % o.dims[d];
+					rem /= o.dims[d];
+					ia += (long)idx * o.sa[d];
+					ib += (long)idx * o.sb[d];
+				}
+			}
+			line(at(o.out, e) + " = bin_op(" + num(o.sub) + ", " + at(o.a, ia) + ", " + at(o.b, ib) + ");");
+		}
+		line("}");
+		return 0;
+	case D_UN:
+		line("if (done == 0u) {");
+		for (int e = 0; e < o.n; e++) line(at(o.out, e) + " = un_op(" + num(o.sub) + ", " + at(o.a, e) + ");");
+		line("}");
+		return 0;
+	case D_MATMUL: {
+		line("if (done == 0u) {");
+		const int m = o.m, k = o.k, n = o.nn;
+		for (int g = 0; g < o.g; g++) {
+			long oo = (long)g * m * n, ao = (long)g * m * k, bo = (long)g * k * n;
+			for (int i = 0; i < m; i++)
+				for (int j = 0; j < n; j++) {
+					std::string x = "{ float acc = 0.0f;";
+					for (int p = 0; p < k; p++)
+						x += " acc = __fadd_rn(acc, __fmul_rn(" + at(o.a, ao + (long)i * k + p) + ", " + at(o.b, bo + (long)p * n + j) + "));";
+					if (o.scale == 1) x += " acc = __fmul_rn(" + at(o.c, i) + ", acc);";
+					else if (o.scale == 2) x += " acc = __fmul_rn(" + at(o.c, j) + ", acc);";
+					x += " " + at(o.out, oo + (long)i * n + j) + " = acc; }";
+					line(x);
+					stmts += k;
+				}
+		}
+		line("}");
+		return 0;
+	}
+	case D_ROW:
+		line("if (done == 0u) {");
+		for (int r = 0; r < o.m; r++) {
+			const long base = (long)r * o.k;
+			if (o.sub == TG_CUDA_OP_SOFTMAX) {
+				line("{ float mx = " + at(o.a, base) + ", s = 0.0f, v, y;");
+				for (int i = 1; i < o.k; i++) line("v = " + at(o.a, base + i) + "; if (v > mx) mx = v;");
+				for (int i = 0; i < o.k; i++)
+					line("y = expf(__fsub_rn(" + at(o.a, base + i) + ", mx)); " + at(o.out, base + i) + " = y; s = __fadd_rn(s, y);");
+				for (int i = 0; i < o.k; i++) line(at(o.out, base + i) + " = __fdiv_rn(" + at(o.out, base + i) + ", s);");
+				line("}");
+			} else {
+				line("{ float s = 0.0f, x;");
+				for (int i = 0; i < o.k; i++) line("x = " + at(o.a, base + i) + "; s = __fadd_rn(s, __fmul_rn(x, x));");
+				line("const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, " + flt((float)o.k) + "), 1e-6f)));");
+				for (int i = 0; i < o.k; i++) line(at(o.out, base + i) + " = __fmul_rn(" + at(o.a, base + i) + ", inv);");
+				line("}");
+			}
+		}
+		line("}");
+		return 0;
+	case D_RED: {
+		line("if (done == 0u) { float s = 0.0f;");
+		for (int e = 0; e < o.n; e++) line("s = __fadd_rn(s, " + at(o.a, e) + ");");
+		line(at(o.out, 0) + " = " + (o.sub == TG_CUDA_OP_MEAN ? "__fdiv_rn(s, " + flt((float)o.n) + ")" : std::string("s")) + "; }");
+		return 0;
+	}
+	case D_TRANS:
+		line("if (done == 0u) {");
+		for (int g = 0; g < o.g; g++)
+			for (int i = 0; i < o.m; i++)
+				for (int j = 0; j < o.k; j++)
+					line(at(o.out, (long)g * o.m * o.k + (long)j * o.m + i) + " = " + at(o.a, (long)g * o.m * o.k + (long)i * o.k + j) + ";");
+		line("}");
+		return 0;
+	case D_OUTER:
+		line("if (done == 0u) {");
+		for (int i = 0; i < o.m; i++)
+			for (int j = 0; j < o.k; j++)
+				line(at(o.out, (long)i * o.k + j) + " = __fmul_rn(" + at(o.a, i) + ", " + at(o.b, j) + ");");
+		line("}");
+		return 0;
+	case D_TAKE: // from a param table only (gen_source), in global memory
+		line("if (done == 0u) {");
+		for (int i = 0; i < o.m; i++) {
+			line("{ const float r = floorf(__fadd_rn(" + at(o.b, i) + ", 0.5f)); const int t = r >= 0.0f && r < " +
+			     flt((float)o.k) + " ? (int)r : -1;");
+			for (int j = 0; j < o.nn; j++)
+				line(at(o.out, (long)i * o.nn + j) + " = t >= 0 ? " + atd(o.a, "t * " + num(o.nn) + " + " + num(j)) + " : 0.0f;");
+			line("}");
+		}
+		line("}");
+		return 0;
+	case D_COPY:
+		if (o.out == o.a) return 0;
+		line("if (done == 0u) {");
+		for (int e = 0; e < o.n; e++) line(at(o.out, e) + " = " + at(o.a, e) + ";");
+		line("}");
+		return 0;
+	case D_THINK_BEGIN:
+		line("if (done == 0u) {");
+		if (o.out != o.a)
+			for (int e = 0; e < o.n; e++) line(at(o.out, e) + " = " + at(o.a, e) + ";");
+		line("it" + D + " = 0; surv" + D + " = 1.0f; }");
+		return 0;
+	case D_THINK_END: {
+		const std::string bit = num(1u << o.depth) + "u";
+		line("if (done == 0u) { it" + D + "++; float dd = 0.0f, v;");
+		for (int e = 0; e < o.n; e++)
+			line("v = fabsf(__fsub_rn(" + at(o.yield, e) + ", " + at(o.out, e) + ")); if (v > dd) dd = v;");
+		for (int e = 0; e < o.n; e++) line(at(o.out, e) + " = " + at(o.yield, e) + ";");
+		line("bool stop = it" + D + " >= " + num(o.maxit) + ";");
+		if (o.eps >= 0) line("if (dd <= " + flt(o.eps) + ") stop = true;");
+		if (o.halt != INT_MIN) {
+			line("{ const float p = " + at(o.halt, 0) + "; surv" + D + " = __fmul_rn(surv" + D +
+			     ", __fsub_rn(1.0f, p < 0.0f ? 0.0f : p > 1.0f ? 1.0f : p)); if (__fsub_rn(1.0f, surv" + D + ") > " + flt(o.hthr) +
+			     ") stop = true; }");
+		}
+		line("if (stop) { done |= " + bit + "; if (live && " + num(o.tid) + " < nt) steps[row * nt + " + num(o.tid) + "] = it" + D + "; }");
+		line("}");
+		line("if (__any_sync(0xffffffffu, done == 0u)) goto L" + num(o.target) + ";");
+		line("done &= ~" + bit + ";");
+		return 0;
+	}
+	}
+	return -1;
+}
+
+// CUDA source of the specialised kernel `tg_rowvm`, or an empty string when the program
+// is beyond the limits above (it then runs on vm_kernel).
+static std::string gen_source(const Prog &P, std::string &why)
+{
+	if (P.arena > JIT_MAX_ARENA) {
+		why = "arena larger than " + std::to_string(JIT_MAX_ARENA) + " floats per row";
+		return "";
+	}
+	// Every arena index must be a constant, so that the arena stays in registers: scans
+	// (a slice per step) and take from a computed value index it at run time and keep
+	// their programs on vm_kernel.
+	for (const DOp &o : P.tape)
+		if (o.code == D_SCAN_BEGIN || o.code == D_SCAN_SLICE || o.code == D_SCAN_END || (o.code == D_TAKE && o.a >= 0)) {
+			why = "run-time arena index (scan, or take from a computed value)";
+			return "";
+		}
+	Gen G(P);
+	for (const DOp &o : P.tape)
+		if (o.code == D_THINK_END) G.label[o.target] = 1;
+	std::string h;
+	for (auto &e : kOpNames) h += "#define " + std::string(e.name) + " " + std::to_string(e.v) + "\n";
+	h += kRowMathSrc;
+	h += "\n";
+	if (G.cparams) {
+		h += "__constant__ unsigned CPU_[" + std::to_string(std::max<size_t>(P.blob.size(), 1)) + "] = {";
+		for (size_t i = 0; i < P.blob.size(); i++) {
+			uint32_t u;
+			memcpy(&u, &P.blob[i], 4);
+			char b[16];
+			snprintf(b, sizeof b, "%s0x%xu", i ? "," : "", u);
+			h += b;
+			if (i % 16 == 15) h += "\n";
+		}
+		if (P.blob.empty()) h += "0u";
+		h += "};\n#define CP(i) __uint_as_float(CPU_[i])\n";
+	}
+	h += "extern \"C\" __global__ void __launch_bounds__(" + std::to_string(VM_ROWS) +
+	     ") tg_rowvm(const float *__restrict__ in, long rows, float *__restrict__ out, int *__restrict__ steps, int nt, "
+	     "const float *__restrict__ GP)\n{\n";
+	h += "const long row = (long)blockIdx.x * " + std::to_string(VM_ROWS) + " + threadIdx.x;\nconst bool live = row < rows;\n";
+	h += "float ar[" + std::to_string(std::max(P.arena, 1)) + "];\n#pragma unroll\nfor (int i = 0; i < " +
+	     std::to_string(std::max(P.arena, 1)) + "; i++) ar[i] = 0.0f;\n";
+	h += "unsigned done = live ? 0u : " + std::to_string(1u << VM_MAXDEPTH) + "u;\n";
+	for (int d = 0; d < VM_MAXDEPTH; d++) h += "int it" + std::to_string(d) + " = 0; float surv" + std::to_string(d) + " = 1.0f;\n";
+	h += "if (live) {\nconst float *src = in + row * " + std::to_string(P.per) + ";\n";
+	for (size_t i = 0, o = 0; i < P.in_off.size(); i++) {
+		for (int e = 0; e < P.in_len[i]; e++)
+			h += "ar[" + std::to_string(P.in_off[i] + e) + "] = src[" + std::to_string(o + e) + "];\n";
+		o += P.in_len[i];
+	}
+	h += "}\n";
+	G.s = h;
+	for (int pc = 0; pc < (int)P.tape.size(); pc++) {
+		if (G.op(pc)) {
+			why = "tape op without a generator";
+			return "";
+		}
+		if (G.stmts > JIT_MAX_STMTS) {
+			why = "program larger than " + std::to_string(JIT_MAX_STMTS) + " statements";
+			return "";
+		}
+	}
+	G.line("if (live) {");
+	for (int e = 0; e < P.nout; e++) G.line("out[row * " + std::to_string(P.nout) + " + " + std::to_string(e) + "] = " + G.at(P.out_loc, e) + ";");
+	G.line("}\n}");
+	return G.s;
+}
+
 } // namespace tgc
 
 using namespace tgc;
@@ -840,7 +1179,7 @@ extern "C" int tg_cuda_load(const tg_cuda_program *p, tg_cuda_model **out)
 	if (!inited()) return set_err(TG_CUDA_ENODEV, "tg_cuda_load: call tg_cuda_init first");
 	tg_cuda_model *g = new tg_cuda_model;
 	std::string err;
-	int rc = compile(p, g->m.prog, err);
+	int rc = compile_program(p, g->m.prog, err);
 	if (rc) {
 		delete g;
 		return set_err(rc, "tg_cuda_load: %s", err.c_str());
@@ -874,9 +1213,52 @@ extern "C" int tg_cuda_load(const tg_cuda_program *p, tg_cuda_model **out)
 		TGC_CUDA(cudaDeviceSynchronize());
 		TGC_CUDA(cudaFuncSetAttribute(vm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
 	}
+	// the specialised kernel, on every device or on none
+	const char *mode = getenv("TG_CUDA_ROWVM");
+	std::string src;
+	if (mode && !strcmp(mode, "interp")) g->m.jit_why = "TG_CUDA_ROWVM=interp";
+	else src = gen_source(P, g->m.jit_why);
+	if (!src.empty()) {
+		g->m.jit = true;
+		for (size_t i = 0; i < devices().size() && g->m.jit; i++) {
+			std::string log;
+			if (jit_build(src, "tg_rowvm", devices()[i].id, 0, g->m.dev[i]->jit, log)) {
+				g->m.jit = false;
+				g->m.jit_why = tg_cuda_error();
+				clear_err();
+			}
+		}
+	}
 	cudaSetDevice(devices()[0].id);
 	*out = g;
 	return TG_CUDA_OK;
+}
+
+extern "C" int tg_cuda_program_kernel(const tg_cuda_program *p, char *src, long n, long *len, int compile)
+{
+	clear_err();
+	if (!p) return set_err(TG_CUDA_EINVAL, "tg_cuda_program_kernel: NULL program");
+	Prog P;
+	std::string err, why;
+	int rc = compile_program(p, P, err);
+	if (rc) return set_err(rc, "tg_cuda_program_kernel: %s", err.c_str());
+	std::string s = gen_source(P, why);
+	if (s.empty()) return set_err(TG_CUDA_EUNSUPPORTED, "tg_cuda_program_kernel: %s", why.c_str());
+	if (len) *len = (long)s.size();
+	if (src && n > 0) snprintf(src, (size_t)n, "%s", s.c_str());
+	if (compile) {
+		std::vector<char> cubin;
+		std::string log;
+		if ((rc = jit_compile(s, cubin, log))) return rc;
+	}
+	return TG_CUDA_OK;
+}
+
+extern "C" int tg_cuda_model_jit(const tg_cuda_model *g, char *why, int n)
+{
+	if (!g) return set_err(TG_CUDA_EINVAL, "tg_cuda_model_jit: NULL model");
+	if (why && n > 0) snprintf(why, (size_t)n, "%s", g->m.jit ? "" : g->m.jit_why.c_str());
+	return g->m.jit ? 1 : 0;
 }
 
 static int run_rows(Model &M, size_t di, const float *d_in, long rows, float *d_out, int *d_steps, int nt, cudaStream_t st)
@@ -886,13 +1268,19 @@ static int run_rows(Model &M, size_t di, const float *d_in, long rows, float *d_
 	if (rows <= 0) return TG_CUDA_OK;
 	long ctas = (rows + VM_ROWS - 1) / VM_ROWS;
 	float *gar = nullptr;
-	if (M.global_arena) {
+	if (M.global_arena && !M.jit) {
 		size_t need = (size_t)ctas * P.arena * VM_ROWS * sizeof(float);
 		int rc = D.gar.ensure(need, devices()[di].id);
 		if (rc) return rc;
 		gar = D.gar.as<float>();
 	}
 	if (fault("launch")) return set_err(TG_CUDA_EFAULT, "injected launch failure (TG_CUDA_FAULT=launch)");
+	if (M.jit) {
+		const float *gp = D.blob.as<float>();
+		int ntv = nt;
+		void *args[] = { (void *)&d_in, (void *)&rows, (void *)&d_out, (void *)&d_steps, (void *)&ntv, (void *)&gp };
+		return jit_launch(D.jit, (unsigned)ctas, VM_ROWS, 0, st, args);
+	}
 	vm_kernel<<<(unsigned)ctas, VM_ROWS, M.smem, st>>>(D.tape.as<DOp>(), (int)P.tape.size(), D.blob.as<float>(),
 							   (int)P.blob.size(), M.blob_in_smem ? 1 : 0, P.arena, d_in, P.per,
 							   rows, d_out, P.nout, P.out_loc, d_steps, nt, D.inloc.as<int>(),
@@ -910,8 +1298,32 @@ extern "C" int tg_cuda_batch_device(tg_cuda_model *g, const float *all, long row
 	return run_rows(g->m, 0, all, rows, out, steps, g->m.prog.nthink, (cudaStream_t)stream);
 }
 
-// One host thread per GPU: copy its contiguous shard in, run, copy out. Output rows of a
-// shard land at the shard's own offset, so the gather keeps input order.
+// Host copies of a few MB and more split over up to 4 threads (one of them the caller).
+static void par_copy(void *dst, const void *src, size_t n)
+{
+	const int parts = (int)std::min<size_t>(4, n / (2 << 20));
+	if (parts <= 1) {
+		memcpy(dst, src, n);
+		return;
+	}
+	const size_t each = (n / parts + 63) / 64 * 64;
+	std::vector<std::thread> th;
+	for (int i = 1; i < parts; i++) {
+		size_t off = each * i;
+		if (off >= n) break;
+		th.emplace_back([=] { memcpy((char *)dst + off, (const char *)src + off, std::min(each, n - off)); });
+	}
+	memcpy(dst, src, std::min(each, n));
+	for (auto &t : th) t.join();
+}
+
+constexpr size_t BATCH_CHUNK_BYTES = 4 << 20; // input bytes per pipeline chunk
+
+// One host thread per GPU over its contiguous shard of rows. The shard goes through the
+// device in chunks of ~4 MB of input on two alternating slots: while the GPU copies in,
+// runs and copies out chunk k on one slot's stream, the host copies chunk k-1's results
+// out of the other slot's pinned buffers and chunk k+1's rows into them. Output rows
+// land at their own offsets, so the gather keeps input order.
 extern "C" int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int per, float *out, int n, int *steps, int nt)
 {
 	clear_err();
@@ -922,6 +1334,7 @@ extern "C" int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int 
 	if (P.nthink > 0 && (!steps || nt < P.nthink))
 		return set_err(TG_CUDA_EINVAL, "tg_cuda_batch: steps needs %d slots per row", P.nthink);
 	if (rows == 0) return TG_CUDA_OK;
+	const bool want_steps = nt > 0 && steps;
 	size_t G = devices().size();
 	std::vector<int> rcs(G, 0);
 	std::vector<std::string> errs(G);
@@ -930,27 +1343,66 @@ extern "C" int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int 
 		if (cnt <= 0) return;
 		Device &dv = devices()[di];
 		cudaSetDevice(dv.id);
-		DevBuf din, dout, dst;
-		int rc;
+		auto &D = *g->m.dev[di];
+		std::lock_guard<std::mutex> lk(D.mu);
+		const long chunk = std::max<long>(VM_ROWS, (long)(BATCH_CHUNK_BYTES / ((size_t)per * sizeof(float))) / VM_ROWS * VM_ROWS);
+		auto drain = [&] {
+			for (Slot &S : D.slot) {
+				if (S.st) cudaStreamSynchronize(S.st);
+				S.busy = false;
+			}
+		};
 		auto done = [&](int r) {
 			rcs[di] = r;
-			if (r) errs[di] = tg_cuda_error();
+			if (r) {
+				errs[di] = tg_cuda_error();
+				drain();
+			}
 		};
-		if ((rc = din.alloc((size_t)cnt * per * sizeof(float), dv.id)) || (rc = dout.alloc((size_t)cnt * n * sizeof(float), dv.id)) ||
-		    (rc = dst.alloc((size_t)cnt * (nt > 0 ? nt : 1) * sizeof(int), dv.id)))
-			return done(rc);
+		auto finish = [&](Slot &S) -> int {
+			cudaError_t e = cudaEventSynchronize(S.done);
+			if (e != cudaSuccess) return set_err(TG_CUDA_ECUDA, "device %d: %s", dv.id, cudaGetErrorString(e));
+			par_copy(out + (size_t)(lo + S.lo) * n, S.hout.p, (size_t)S.cnt * n * sizeof(float));
+			if (want_steps) par_copy(steps + (size_t)(lo + S.lo) * nt, S.hsteps.p, (size_t)S.cnt * nt * sizeof(int));
+			S.busy = false;
+			return TG_CUDA_OK;
+		};
+		int rc;
+		for (Slot &S : D.slot) {
+			if (!S.st && cudaStreamCreateWithFlags(&S.st, cudaStreamNonBlocking) != cudaSuccess)
+				return done(set_err(TG_CUDA_ECUDA, "cudaStreamCreate failed"));
+			if (!S.done && cudaEventCreateWithFlags(&S.done, cudaEventDisableTiming) != cudaSuccess)
+				return done(set_err(TG_CUDA_ECUDA, "cudaEventCreate failed"));
+			const long m = std::min(chunk, cnt);
+			if ((rc = S.hin.ensure((size_t)m * per * sizeof(float))) || (rc = S.hout.ensure((size_t)m * n * sizeof(float))) ||
+			    (rc = S.hsteps.ensure((size_t)m * std::max(nt, 1) * sizeof(int))) ||
+			    (rc = S.din.ensure((size_t)m * per * sizeof(float), dv.id)) || (rc = S.dout.ensure((size_t)m * n * sizeof(float), dv.id)) ||
+			    (rc = S.dsteps.ensure((size_t)m * std::max(nt, 1) * sizeof(int), dv.id)))
+				return done(rc);
+		}
 		if (fault("h2d")) return done(set_err(TG_CUDA_EFAULT, "injected copy failure (TG_CUDA_FAULT=h2d)"));
-		cudaError_t e = cudaMemcpyAsync(din.p, all + (size_t)lo * per, (size_t)cnt * per * sizeof(float), cudaMemcpyHostToDevice, dv.stream);
-		if (e != cudaSuccess) return done(set_err(TG_CUDA_ECUDA, "H2D: %s", cudaGetErrorString(e)));
-		if (nt > 0) cudaMemsetAsync(dst.p, 0, (size_t)cnt * nt * sizeof(int), dv.stream);
-		if ((rc = run_rows(g->m, di, din.as<float>(), cnt, dout.as<float>(), nt > 0 ? dst.as<int>() : nullptr, nt, dv.stream)))
-			return done(rc);
-		if (fault("gather")) return done(set_err(TG_CUDA_EFAULT, "injected gather failure (TG_CUDA_FAULT=gather)"));
-		e = cudaMemcpyAsync(out + (size_t)lo * n, dout.p, (size_t)cnt * n * sizeof(float), cudaMemcpyDeviceToHost, dv.stream);
-		if (e == cudaSuccess && nt > 0 && steps)
-			e = cudaMemcpyAsync(steps + (size_t)lo * nt, dst.p, (size_t)cnt * nt * sizeof(int), cudaMemcpyDeviceToHost, dv.stream);
-		if (e == cudaSuccess) e = cudaStreamSynchronize(dv.stream);
-		if (e != cudaSuccess) return done(set_err(TG_CUDA_ECUDA, "device %d: %s", dv.id, cudaGetErrorString(e)));
+		for (long c0 = 0, k = 0; c0 < cnt; c0 += chunk, k++) {
+			Slot &S = D.slot[k & 1];
+			if (S.busy && (rc = finish(S))) return done(rc);
+			const long m = std::min(chunk, cnt - c0);
+			par_copy(S.hin.p, all + (size_t)(lo + c0) * per, (size_t)m * per * sizeof(float));
+			cudaError_t e = cudaMemcpyAsync(S.din.p, S.hin.p, (size_t)m * per * sizeof(float), cudaMemcpyHostToDevice, S.st);
+			if (e == cudaSuccess && nt > 0) e = cudaMemsetAsync(S.dsteps.p, 0, (size_t)m * nt * sizeof(int), S.st);
+			if (e != cudaSuccess) return done(set_err(TG_CUDA_ECUDA, "H2D: %s", cudaGetErrorString(e)));
+			if ((rc = run_rows(g->m, di, S.din.as<float>(), m, S.dout.as<float>(), nt > 0 ? S.dsteps.as<int>() : nullptr, nt, S.st)))
+				return done(rc);
+			if (fault("gather")) return done(set_err(TG_CUDA_EFAULT, "injected gather failure (TG_CUDA_FAULT=gather)"));
+			e = cudaMemcpyAsync(S.hout.p, S.dout.p, (size_t)m * n * sizeof(float), cudaMemcpyDeviceToHost, S.st);
+			if (e == cudaSuccess && want_steps)
+				e = cudaMemcpyAsync(S.hsteps.p, S.dsteps.p, (size_t)m * nt * sizeof(int), cudaMemcpyDeviceToHost, S.st);
+			if (e == cudaSuccess) e = cudaEventRecord(S.done, S.st);
+			if (e != cudaSuccess) return done(set_err(TG_CUDA_ECUDA, "device %d: %s", dv.id, cudaGetErrorString(e)));
+			S.lo = c0;
+			S.cnt = m;
+			S.busy = true;
+		}
+		for (Slot &S : D.slot)
+			if (S.busy && (rc = finish(S))) return done(rc);
 		done(TG_CUDA_OK);
 	};
 	if (G == 1) work(0);
