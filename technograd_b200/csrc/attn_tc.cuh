@@ -140,18 +140,19 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 	const long cb = ((long)(slot0 + s) * NKV + kvh) * (long)max_len * FA_HD; // this (sequence, kv head)'s cache rows
 
 	if (threadIdx.x == 0) {
-		mbar_init(&B->q_full, 128);
+		// barriers the 128-thread groups arrive on count warps (mbar_arrive_warp)
+		mbar_init(&B->q_full, 4);
 		mbar_init(&B->stg_full, 1);
-		mbar_init(&B->stg_free, 128);
-		mbar_init(&B->k_full, 128);
+		mbar_init(&B->stg_free, 4);
+		mbar_init(&B->k_full, 4);
 		mbar_init(&B->k_empty, 1);
-		mbar_init(&B->v_full, 128);
+		mbar_init(&B->v_full, 4);
 		mbar_init(&B->v_empty, 1);
 		for (int b = 0; b < 2; b++) {
 			mbar_init(&B->s_full[b], 1);
-			mbar_init(&B->s_free[b], 128);
+			mbar_init(&B->s_free[b], 4);
 		}
-		mbar_init(&B->p_full, 128);
+		mbar_init(&B->p_full, 4);
 		mbar_init(&B->p_empty, 1);
 		mbar_init(&B->done, 1);
 		B->abort = 0;
@@ -200,13 +201,13 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 			}
 		}
 		fence_async_smem();
-		mbar_arrive(&B->q_full);
+		mbar_arrive_warp(&B->q_full);
 		for (int j = 0; j < nkt; j++) {
 			const int k0 = j * FA_K;
-			if (!fa_wait(B, &B->stg_full, j & 1, status)) break;
+			if (!fa_wait_warp(B, &B->stg_full, j & 1, status)) break;
 			pending = -1;
 			// K: 64 rows x 16 chunks of 8 dims; the bf16 part as is, the remainder as lo
-			if (j > 0 && !fa_wait(B, &B->k_empty, (j - 1) & 1, status)) break;
+			if (j > 0 && !fa_wait_warp(B, &B->k_empty, (j - 1) & 1, status)) break;
 #pragma unroll 2
 			for (int i = t; i < FA_K * 16; i += 128) {
 				const int r = i >> 4, c = i & 15;
@@ -229,9 +230,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 				*(uint4 *)(sm + FA_SK_LO + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
 			}
 			fence_async_smem();
-			mbar_arrive(&B->k_full);
+			mbar_arrive_warp(&B->k_full);
 			// V^T: item = (8 keys, 4 dims) -> one 16-byte chunk in each of 4 rows
-			if (j > 0 && !fa_wait(B, &B->v_empty, (j - 1) & 1, status)) break;
+			if (j > 0 && !fa_wait_warp(B, &B->v_empty, (j - 1) & 1, status)) break;
 			for (int i = t; i < 256; i += 128) {
 				const int kg = i & 7, dg = i >> 3;
 				uint2 hv[8];
@@ -260,14 +261,20 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 				}
 			}
 			fence_async_smem();
-			mbar_arrive(&B->v_full);
+			mbar_arrive_warp(&B->v_full);
 			// the staging area has been read: thread 0 refills it with the next tile
-			mbar_arrive(&B->stg_free);
-			if (t == 0 && j + 1 < nkt) {
-				if (!fa_wait(B, &B->stg_free, j & 1, status)) break;
-				fence_async_smem();
-				stage(j + 1);
-				pending = j + 1;
+			mbar_arrive_warp(&B->stg_free);
+			if (j + 1 < nkt) {
+				bool ok0 = true;
+				if (t == 0) {
+					ok0 = fa_wait(B, &B->stg_free, j & 1, status);
+					if (ok0) {
+						fence_async_smem();
+						stage(j + 1);
+						pending = j + 1;
+					}
+				}
+				if (!__shfl_sync(0xffffffffu, ok0, 0)) break; // thread 0's warp leaves together
 			}
 		}
 		// after an abort: the copies still in flight land before the CTA's shared memory is released
@@ -343,7 +350,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 				for (int e = 0; e < 16; e++) sc[c * 16 + e] = v[e];
 			}
 			tc_fence_before();
-			mbar_arrive(&B->s_free[j & 1]);
+			mbar_arrive_warp(&B->s_free[j & 1]);
 			float mt = -INFINITY;
 #pragma unroll
 			for (int c = 0; c < FA_K; c++) {
@@ -393,7 +400,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 			}
 			fence_async_smem();
 			tc_fence_before();
-			mbar_arrive(&B->p_full);
+			mbar_arrive_warp(&B->p_full);
 		}
 		if (ok) ok = fa_wait_warp(B, &B->p_empty, (nkt - 1) & 1, status);
 		if (ok) {

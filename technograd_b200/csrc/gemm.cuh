@@ -33,13 +33,15 @@ struct GemmArgs {
 	long partial_floats;     // its size in floats
 	int kb_per_split;        // set by gemm() for the split launch: K blocks per split
 	long mpad;               // set by gemm(): rows per split block of the partial buffer
-	// Dequant in the kernel: with cside 1 (A[0]) or 2 (B[0]) that operand is not loaded by
-	// TMA but built in shared memory from integer codes (K-major rows of cld bytes; int8 one
-	// code per byte, int4 two per byte low nibble first), which are exact in bf16. K must be
-	// a multiple of 64, cld and the base 16-byte aligned.
+	// Dequant in the kernel: with cside 1 (A[0]) or 2 (B[0]) that operand is built in shared
+	// memory from integer codes (K-major rows of cld bytes; int8 one code per byte, int4 two
+	// per byte low nibble first), which are exact in bf16: TMA brings each K block of raw
+	// codes into its ring stage, four warps expand them in place. K must be a multiple of
+	// 64, cld and the base 16-byte aligned.
 	const signed char *codes;
 	int cbits, cside;
 	long cld;
+	int raw_bytes; // set by gemm(): bytes of one K block of codes (TMA-loaded into each ring stage)
 };
 
 // Launch on stream. SwiGLU: B rows come in blocks of 64 (32 gate rows then the

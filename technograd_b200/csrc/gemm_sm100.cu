@@ -8,13 +8,15 @@
 // Weights whose scale cannot stay in the epilogue (per-head o_proj scales) are
 // pre-scaled and split too, and use hi*hi + hi*lo + lo*hi.
 //
-// Kernel: 6 warps. Warp 0 lane 0 issues TMA tile loads (128-byte swizzle, K
+// Kernel: 10 warps. Warp 0 lane 0 issues TMA tile loads (128-byte swizzle, K
 // blocks of 64) into a STAGES-deep shared-memory ring; warp 1 owns the TMEM
 // accumulator (BN f32 columns) and lane 0 issues tcgen05.mma (M=128, N=BN,
-// K=16 per instruction), committing each stage back to the producer; warps 2-5
-// drain TMEM with tcgen05.ld and run the epilogue (scale, residual add, SwiGLU
-// with a bf16 hi/lo split of the result). Every mbarrier wait is bounded and
-// reports into a device status word instead of hanging.
+// K=16 per instruction), committing each stage back to the producer; warps 2-9
+// expand integer codes into the ring (in-kernel dequant only); warps 2-5 drain
+// TMEM with tcgen05.ld and run the epilogue (scale, residual add, SwiGLU with a
+// bf16 hi/lo split of the result). Every mbarrier wait is bounded and reports
+// into a device status word instead of hanging. The persistent variant below
+// keeps 6 warps (bf16 operands only).
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -33,6 +35,8 @@ constexpr int A_TILE = BM * BK * 2; // 16 KB
 struct TmaMaps {
 	CUtensorMap a[2], b[2];
 	CUtensorMap o[2]; // the output (SwiGLU: the bf16 hi and lo outputs), when p.tma_out
+	CUtensorMap c;    // raw codes (p.cside): uint8 [rows, K * bits / 8], unswizzled boxes
+	CUtensorMap cpf;  // the same codes in boxes of 256 bytes per row, for L2 prefetches
 };
 
 __device__ __forceinline__ uint32_t bf16_bits(float x) { return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x)); }
@@ -41,20 +45,55 @@ __device__ __forceinline__ uint32_t bf16x2(float a, float b) { return bf16_bits(
 // row rr of a 128-byte-swizzled K-major tile: rows of 128 bytes, 8-row atoms of 1024 bytes
 __device__ __forceinline__ uint8_t *smem_row(uint8_t *tile, int rr) { return tile + rr * 128; }
 
+// Integer codes -> bf16 without int-to-float conversions. int4: the nibble n of code c
+// (n ^ 8 = c + 8, 0..15) below the bf16 pattern of 128.0 reads as 128 + c + 8, exact with
+// bf16's 8-bit significand; one packed bf16 subtraction of 136 leaves c, two codes at a
+// time. int8: the byte b (b ^ 0x80 = c + 128) below the f32 pattern of 2^23 reads as
+// 2^23 + c + 128; subtracting 2^23 + 128 leaves c, whose f32 pattern truncates exactly to
+// bf16 (|c| <= 128 needs 8 significant bits).
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b)
+{
+	__nv_bfloat162 r = __hsub2(*(__nv_bfloat162 *)&a, *(__nv_bfloat162 *)&b);
+	return *(uint32_t *)&r;
+}
+// 8 int4 codes of one word (code 2e in bits 8e..8e+3, 2e+1 in bits 8e+4..8e+7) -> 4 bf16 pairs
+__device__ __forceinline__ void int4x8_bf16(uint32_t w, uint32_t h[4])
+{
+	const uint32_t lo = (w & 0x0F0F0F0Fu) ^ 0x08080808u, hi = ((w >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+#pragma unroll
+	for (int e = 0; e < 4; e++) {
+		const uint32_t t = __byte_perm(lo, hi, e | ((4 + e) << 8)) & 0x00FF00FFu; // [lo byte e, -, hi byte e, -]
+		h[e] = bf16x2_sub(t | 0x43004300u, 0x43084308u);
+	}
+}
+// 4 int8 codes of one word -> 2 bf16 pairs
+__device__ __forceinline__ void int8x4_bf16(uint32_t w, uint32_t h[2])
+{
+	const uint32_t x = w ^ 0x80808080u;
+	float f[4];
+#pragma unroll
+	for (int e = 0; e < 4; e++) f[e] = __fsub_rn(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540u | e)), 8388736.0f);
+	h[0] = __byte_perm(__float_as_uint(f[0]), __float_as_uint(f[1]), 0x7632u);
+	h[1] = __byte_perm(__float_as_uint(f[2]), __float_as_uint(f[3]), 0x7632u);
+}
+
 template <int BN, int STAGES, int EPI>
-__global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMaps maps, const GemmArgs p)
+__global__ void __launch_bounds__(320, 1) gemm_tc(const __grid_constant__ TmaMaps maps, const GemmArgs p)
 {
 	extern __shared__ uint8_t smem_raw[];
 	uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
 	constexpr int B_TILE = BN * BK * 2;
-	const int stage_bytes = p.na * A_TILE + p.nb * B_TILE;
+	const int ops_bytes = p.na * A_TILE + p.nb * B_TILE;
+	const int stage_bytes = ops_bytes + p.raw_bytes; // operand tiles, then the raw codes (cside)
 	uint64_t *full = (uint64_t *)(smem + STAGES * stage_bytes);
 	uint64_t *empty = full + STAGES;
-	uint64_t *accf = empty + STAGES;
+	uint64_t *rawf = empty + STAGES; // raw codes of the stage landed (cside)
+	uint64_t *accf = rawf + STAGES;
 	uint32_t *tslot = (uint32_t *)(accf + 1);
 	float *ssc = (float *)(accf + 2); // BN floats: the tile's scales (SwiGLU: gate then up)
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+	const int kbytes = p.cbits == 8 ? BK : BK / 2; // code bytes per row of a K block
 	// split-K (EPI_PARTIAL): this CTA takes K blocks [kb0, kb0 + KB) and stores its raw sums
 	const int KBall = (p.K + BK - 1) / BK;
 	const int kb0 = p.kb_per_split ? blockIdx.z * p.kb_per_split : 0;
@@ -62,13 +101,20 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 
 	if (threadIdx.x == 0) {
 		for (int s = 0; s < STAGES; s++) {
-			mbar_init(&full[s], p.cside ? 1 + 128 : 1); // + the 128 converting threads
+			mbar_init(&full[s], p.cside ? 1 + 8 : 1); // + one arrival per converting warp
 			mbar_init(&empty[s], 1);
+			mbar_init(&rawf[s], 1);
 		}
 		mbar_init(accf, 1);
 		fence_barrier_init();
-		for (int i = 0; i < p.na; i++) tma_prefetch_desc(&maps.a[i]);
-		for (int i = 0; i < p.nb; i++) tma_prefetch_desc(&maps.b[i]);
+		for (int i = 0; i < p.na; i++)
+			if (!(i == 0 && p.cside == 1)) tma_prefetch_desc(&maps.a[i]);
+		for (int i = 0; i < p.nb; i++)
+			if (!(i == 0 && p.cside == 2)) tma_prefetch_desc(&maps.b[i]);
+		if (p.cside) {
+			tma_prefetch_desc(&maps.c);
+			tma_prefetch_desc(&maps.cpf);
+		}
 	}
 	if (warp == 1) tmem_alloc(tslot, BN);
 	__syncthreads();
@@ -76,12 +122,21 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 	const uint32_t tmem = *tslot;
 
 	if (warp == 0 && lane == 0) { // ---- producer
+		// the codes of this CTA's whole K range into L2 up front, 256 contiguous bytes per row
+		// per request: the stage loads below (one K block of 32 or 64 bytes per row) then hit L2
+		if (p.cside)
+			for (int x = kb0 * kbytes; x < (kb0 + KB) * kbytes; x += 256)
+				tma_prefetch_l2_2d(&maps.cpf, x, p.cside == 1 ? m0 : n0);
 		for (int kb = 0; kb < KB; kb++) {
 			const int s = kb % STAGES;
 			const uint32_t ph = (kb / STAGES) & 1;
 			if (!mbar_wait(&empty[s], ph ^ 1, p.status, ST_TIMEOUT_EMPTY)) break;
 			uint8_t *st = smem + s * stage_bytes;
-			mbar_expect_tx(&full[s], stage_bytes - (p.cside == 1 ? A_TILE : p.cside == 2 ? B_TILE : 0));
+			if (p.cside) { // the raw codes first: the converting warps start on them
+				mbar_expect_tx(&rawf[s], p.raw_bytes);
+				tma_load_2d(st + ops_bytes, &maps.c, &rawf[s], (kb0 + kb) * kbytes, p.cside == 1 ? m0 : n0);
+			}
+			mbar_expect_tx(&full[s], ops_bytes - (p.cside == 1 ? A_TILE : p.cside == 2 ? B_TILE : 0));
 			for (int i = p.cside == 1 ? 1 : 0; i < p.na; i++) tma_load_2d(st + i * A_TILE, &maps.a[i], &full[s], (kb0 + kb) * BK, m0);
 			for (int j = p.cside == 2 ? 1 : 0; j < p.nb; j++)
 				tma_load_2d(st + p.na * A_TILE + j * B_TILE, &maps.b[j], &full[s], (kb0 + kb) * BK, n0);
@@ -106,13 +161,15 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 			tc_commit(&empty[s]);
 		}
 		tc_commit(accf);
-	} else if (warp >= 2) { // ---- epilogue: TMEM lanes of quarter (warp % 4)
+	} else if (warp >= 2) { // ---- warps 2-9 expand codes (cside); 2-5 then run the epilogue
 		const int quarter = warp & 3;
 		const int r = quarter * 32 + lane; // tile row = TMEM lane
 		const int row = m0 + r;
-		const int et = threadIdx.x - 64;   // 0..127 over the epilogue warps
+		const int et = threadIdx.x - 64;   // 0..127 over the epilogue warps, 0..255 over the converters
+		const bool epi_warp = warp < 6;
 		// scales of this tile into shared memory while the main loop runs
-		if (EPI == EPI_SWIGLU) {
+		if (!epi_warp) {
+		} else if (EPI == EPI_SWIGLU) {
 			const int f0 = blockIdx.x * (BN / 2);
 			for (int j = et; j < BN / 2; j += 128) {
 				ssc[j] = p.scale[f0 + j];
@@ -124,64 +181,55 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 			ssc[et] = m0 + et < p.M ? p.scale[m0 + et] : 0.0f;
 		}
 		if (p.cside) {
-			// Build the code operand of every K block in its ring slot while the producer's TMA
-			// brings the others: integer codes (exact in bf16) in the 128-byte-swizzled K-major
-			// layout; rows past the matrix are zero, like TMA's out-of-bounds fill. Each thread
-			// owns `per` 16-byte code chunks of a block; those of block kb + 1 are loaded while
-			// block kb is written, so up to 8 loads per thread are in flight.
+			// Expand the raw codes of every K block (TMA'd into the end of its ring stage) into
+			// the stage's code operand: exact bf16 in the 128-byte-swizzled K-major layout. Rows
+			// past the matrix arrive as zero bytes (TMA's out-of-bounds fill), which expand to
+			// code 0. The stage's raw codes landing implies the producer saw the stage free, so
+			// the operand slot may be written.
+			// Each of the 256 threads owns up to 4 chunks of a block; all are read before any is
+			// converted, so the conversions of different chunks overlap.
 			const int R = p.cside == 1 ? BM : BN;
-			const int row0 = p.cside == 1 ? m0 : n0, valid = p.cside == 1 ? p.M : p.N;
-			const int cpr = p.cbits == 8 ? 4 : 2;       // 16-byte code chunks per row of a K block
-			const int kbytes = p.cbits == 8 ? BK : BK / 2;
-			const int per = R * cpr / 128;              // 1, 2, 4 or 8
-			uint4 buf[8];
-			auto load = [&](int kb) {
-				const signed char *src = p.codes + (long)(kb0 + kb) * kbytes;
-#pragma unroll
-				for (int i = 0; i < 8; i++)
-					if (i < per) {
-						const int it = et + i * 128, rr = it / cpr, c = it % cpr, grow = row0 + rr;
-						buf[i] = grow < valid ? __ldg((const uint4 *)(src + (long)grow * p.cld + c * 16)) : make_uint4(0u, 0u, 0u, 0u);
-					}
-			};
-			if (KB > 0) load(0);
+			const int cpr = kbytes / 16;                // 16-byte code chunks per row of a K block
+			const int chunks = R * cpr;                 // per K block, 128 .. 1024
 			for (int kb = 0; kb < KB; kb++) {
 				const int s = kb % STAGES;
 				const uint32_t ph = (kb / STAGES) & 1;
-				if (!mbar_wait(&empty[s], ph ^ 1, p.status, ST_TIMEOUT_EMPTY)) break;
-				uint8_t *slot = smem + s * stage_bytes + (p.cside == 1 ? 0 : p.na * A_TILE);
+				if (!__all_sync(0xffffffffu, mbar_wait(&rawf[s], ph, p.status, ST_TIMEOUT_FULL))) break; // the warp leaves together
+				uint8_t *stg = smem + s * stage_bytes;
+				uint8_t *slot = stg + (p.cside == 1 ? 0 : p.na * A_TILE);
+				const uint8_t *raw = stg + ops_bytes;
+				uint4 vv[4];
 #pragma unroll
-				for (int i = 0; i < 8; i++) {
-					if (i >= per) break;
-					const int it = et + i * 128, rr = it / cpr, c = it % cpr, sw = rr & 7;
-					const uint32_t w[4] = { buf[i].x, buf[i].y, buf[i].z, buf[i].w };
+				for (int i = 0; i < 4; i++)
+					if (et + i * 256 < chunks) vv[i] = *(const uint4 *)(raw + (et + i * 256) * 16);
+#pragma unroll
+				for (int i = 0; i < 4; i++) {
+					const int it = et + i * 256;
+					if (it >= chunks) break;
+					const int rr = it / cpr, c = it % cpr, sw = rr & 7;
 					uint8_t *dst = smem_row(slot, rr);
+					const uint4 v = vv[i];
+					const uint32_t w[4] = { v.x, v.y, v.z, v.w };
 					if (p.cbits == 8) { // 16 codes -> swizzle units 2c, 2c + 1
 						uint32_t h[8];
 #pragma unroll
-						for (int j = 0; j < 4; j++) {
-							h[2 * j] = bf16x2((float)(int8_t)(w[j] & 0xff), (float)(int8_t)((w[j] >> 8) & 0xff));
-							h[2 * j + 1] = bf16x2((float)(int8_t)((w[j] >> 16) & 0xff), (float)(int8_t)(w[j] >> 24));
-						}
+						for (int j = 0; j < 4; j++) int8x4_bf16(w[j], h + 2 * j);
 						*(uint4 *)(dst + (((2 * c) ^ sw) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
 						*(uint4 *)(dst + (((2 * c + 1) ^ sw) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
 					} else { // 32 codes -> units 4c .. 4c + 3, one 32-bit word (8 codes) each
 #pragma unroll
 						for (int j = 0; j < 4; j++) {
 							uint32_t h[4];
-#pragma unroll
-							for (int e = 0; e < 4; e++)
-								h[e] = bf16x2((float)((int32_t)(w[j] << (28 - 8 * e)) >> 28),
-									      (float)((int32_t)(w[j] << (24 - 8 * e)) >> 28));
+							int4x8_bf16(w[j], h);
 							*(uint4 *)(dst + (((4 * c + j) ^ sw) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
 						}
 					}
 				}
 				fence_async_smem();
-				mbar_arrive(&full[s]);
-				if (kb + 1 < KB) load(kb + 1);
+				mbar_arrive_warp(&full[s]);
 			}
 		}
+		if (epi_warp) {
 		epilogue_sync();
 		const bool ok = mbar_wait(accf, 0, p.status, ST_TIMEOUT_ACC);
 		const bool live = ok && row < p.M;
@@ -298,6 +346,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc(const __grid_constant__ TmaMap
 			}
 		}
 		tc_fence_before();
+		}
 	}
 	__syncthreads();
 	if (warp == 1) {
@@ -342,7 +391,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_persistent(const __grid_consta
 		}
 		for (int b = 0; b < 2; b++) {
 			mbar_init(&acc_full[b], 1);
-			mbar_init(&acc_empty[b], 128);
+			mbar_init(&acc_empty[b], 4); // one arrival per epilogue warp
 		}
 		fence_barrier_init();
 		for (int i = 0; i < p.na; i++) tma_prefetch_desc(&maps.a[i]);
@@ -503,7 +552,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_persistent(const __grid_consta
 				}
 			}
 			tc_fence_before();
-			mbar_arrive(&acc_empty[b]); // this thread's TMEM loads of buffer b are complete
+			mbar_arrive_warp(&acc_empty[b]); // this warp's TMEM loads of buffer b are complete
 		}
 		if (et == 0) tma_store_wait_all();
 	}
@@ -562,10 +611,25 @@ static int make_out_map(CUtensorMap *m, CUtensorMapDataType dt, int esize, const
 	return TG_CUDA_OK;
 }
 
+// Raw int8 / int4 codes [rows, K * bits / 8] bytes (row pitch ld bytes), boxes of one K block
+// (64 codes) x box_rows rows, unswizzled: a row of the box is 32 or 64 contiguous bytes.
+static int make_codes_map(CUtensorMap *m, const void *base, long rows, long row_bytes, long ld, int kbytes, int box_rows)
+{
+	if (((uintptr_t)base & 15) || ld % 16) return set_err(TG_CUDA_EINVAL, "code rows not 16-byte aligned (ld %ld)", ld);
+	cuuint64_t dims[2] = { (cuuint64_t)row_bytes, (cuuint64_t)rows };
+	cuuint64_t strides[1] = { (cuuint64_t)ld };
+	cuuint32_t box[2] = { (cuuint32_t)kbytes, (cuuint32_t)box_rows };
+	cuuint32_t es[2] = { 1, 1 };
+	CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+			      CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+	if (r != CUDA_SUCCESS) return set_err(TG_CUDA_ECUDA, "cuTensorMapEncodeTiled (codes) failed (%d)", (int)r);
+	return TG_CUDA_OK;
+}
+
 template <int BN, int STAGES, int EPI>
 static int launch_bn(const TmaMaps &maps, const GemmArgs &p, cudaStream_t st)
 {
-	int stage = p.na * A_TILE + p.nb * BN * BK * 2;
+	int stage = p.na * A_TILE + p.nb * BN * BK * 2 + p.raw_bytes;
 	size_t smem = (size_t)STAGES * stage + 1024 + 256 + BN * 4; // ring, alignment, barriers, scales
 	static bool attr_set[64] = {};
 	int dev;
@@ -575,7 +639,7 @@ static int launch_bn(const TmaMaps &maps, const GemmArgs &p, cudaStream_t st)
 		attr_set[dev] = true;
 	}
 	dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, p.kb_per_split ? (unsigned)(((p.K + BK - 1) / BK + p.kb_per_split - 1) / p.kb_per_split) : 1u);
-	gemm_tc<BN, STAGES, EPI><<<grid, 192, smem, st>>>(maps, p);
+	gemm_tc<BN, STAGES, EPI><<<grid, 320, smem, st>>>(maps, p);
 	TGC_LAUNCH_CHECK();
 	return TG_CUDA_OK;
 }
@@ -600,6 +664,7 @@ static int launch_persistent(const TmaMaps &maps, const GemmArgs &p, int grid, c
 
 static int launch_split(int BN, int stages, const TmaMaps &maps, const GemmArgs &q, dim3, cudaStream_t st)
 {
+	if (BN == 32) return stages >= 6 ? launch_bn<32, 6, EPI_PARTIAL>(maps, q, st) : launch_bn<32, 4, EPI_PARTIAL>(maps, q, st);
 	if (BN == 64) return launch_bn<64, 4, EPI_PARTIAL>(maps, q, st);
 	if (BN == 256)
 		return stages >= 4 ? launch_bn<256, 4, EPI_PARTIAL>(maps, q, st)
@@ -656,22 +721,35 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 	const long mtiles = (p.M + BM - 1) / BM;
 	int BN = p.epi == EPI_SWIGLU || p.N >= 256 ? 256 : 128;
 	if (((p.N + BN - 1) / BN) * mtiles * 2 <= sms && p.N % 64 == 0 && mtiles <= 4) BN = 64;
+	if (p.N <= 32 && p.epi != EPI_SWIGLU) BN = 32; // a batch of up to 32 (drop-in axis 0): one narrow MMA
+	// In-kernel dequant adds the raw code block to each stage; keep at least 3 stages of
+	// TMA in flight rather than the widest tile
+	const int kbytes = p.cbits == 8 ? BK : BK / 2;
+	auto stage_of = [&](int bn) { return p.na * A_TILE + p.nb * bn * BK * 2 + (p.cside ? (p.cside == 1 ? BM : bn) * kbytes : 0); };
+	if (p.cside && BN == 256 && p.epi != EPI_SWIGLU && (220 * 1024) / stage_of(256) < 3) BN = 128;
+	p.raw_bytes = p.cside ? (p.cside == 1 ? BM : BN) * kbytes : 0;
 	TmaMaps maps;
 	memset(&maps, 0, sizeof maps);
+	if (p.cside &&
+	    ((rc = make_codes_map(&maps.c, p.codes, p.cside == 1 ? p.M : p.N, (long)p.K * p.cbits / 8, p.cld, kbytes, p.cside == 1 ? BM : BN)) ||
+	     (rc = make_codes_map(&maps.cpf, p.codes, p.cside == 1 ? p.M : p.N, (long)p.K * p.cbits / 8, p.cld,
+				  (int)std::min<long>(256, (long)p.K * p.cbits / 8), p.cside == 1 ? BM : BN))))
+		return rc;
 	for (int i = 0; i < p.na; i++)
 		if (!(i == 0 && p.cside == 1) && (rc = make_map(&maps.a[i], ops.a[i], p.M, p.K, ops.lda, BM))) return rc;
 	for (int j = 0; j < p.nb; j++)
 		if (!(j == 0 && p.cside == 2) && (rc = make_map(&maps.b[j], ops.b[j], p.N, p.K, ops.ldb, BN))) return rc;
-	// as many ring stages (2..4) as fit in 220 KB of shared memory
-	const int stage = p.na * A_TILE + p.nb * BN * BK * 2;
-	const int stages = std::min(4, std::max(2, (220 * 1024) / stage));
+	// as many ring stages (2..4; 6 for the narrow tile) as fit in 220 KB of shared memory
+	const int stage = stage_of(BN);
+	const int stages = std::min(BN == 32 ? 6 : 4, std::max(2, (220 * 1024) / stage));
 	// Split K when the tiles would leave most SMs idle (small-batch decode): each split stores raw
 	// f32 sums into the caller's partial buffer, then k_split_reduce adds them in a fixed order.
 	const long tiles = (long)((p.N + BN - 1) / BN) * ((p.M + BM - 1) / BM);
 	const int KBall = (p.K + BK - 1) / BK;
 	int splits = 1;
 	if (p.partial && tiles * 2 <= sms && KBall >= 8 && p.N % 4 == 0) {
-		splits = (int)std::min<long>((sms + tiles - 1) / tiles, KBall / 4);
+		// one wave: the ring takes most of an SM's shared memory, so one CTA per SM
+		splits = (int)std::min<long>(sms / tiles, KBall / 4);
 		const long mpad = (long)(p.M + BM - 1) / BM * BM;
 		while (splits > 1 && (long)splits * mpad * p.N > p.partial_floats) splits--;
 	}
@@ -734,6 +812,8 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 #undef TGC_GEMM_PERSIST
 		}
 	}
+#define TGC_GEMM_NARROW(E) \
+	if (BN == 32) return stages >= 6 ? launch_bn<32, 6, E>(maps, p, st) : launch_bn<32, 4, E>(maps, p, st);
 #define TGC_GEMM_DISPATCH(E)                                                                 \
 	if (BN == 64) return launch_bn<64, 4, E>(maps, p, st); /* 40-48 KB stages: always 4 */ \
 	if (BN == 256)                                                                      \
@@ -745,9 +825,12 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 		TGC_GEMM_DISPATCH(EPI_SWIGLU)
 	}
 	if (p.epi == EPI_ADD) {
+		TGC_GEMM_NARROW(EPI_ADD)
 		TGC_GEMM_DISPATCH(EPI_ADD)
 	}
+	TGC_GEMM_NARROW(EPI_STORE)
 	TGC_GEMM_DISPATCH(EPI_STORE)
+#undef TGC_GEMM_NARROW
 #undef TGC_GEMM_DISPATCH
 }
 
@@ -830,8 +913,9 @@ int codes_to_bf16(const signed char *q, int bits, long rows, long cols, bool tra
 // The drop-in call stays asynchronous: the GEMM's device status word is copied into a
 // pinned host word after each call, and a later call on the device reports it.
 struct TcScratch {
-	DevBuf buf, status, part; // part: split-K partial sums of small-batch calls (64 MB)
-	int *h_status = nullptr; // pinned
+	DevBuf buf, part;        // part: split-K partial sums of small-batch calls (64 MB)
+	int *h_status = nullptr; // pinned, mapped: the kernels' status word (written only by a wait that timed out)
+	int *d_status = nullptr; // its device address
 };
 static TcScratch g_tc[64];
 
@@ -859,19 +943,19 @@ int matmul_q_tc(int axis, float *o, const float *act, const signed char *q, int 
 	size_t wbytes = (size_t)wrows * k * 2, abytes = (size_t)brows * k * 2;
 	int rc;
 	if (!S.h_status) {
-		TGC_CUDA(cudaHostAlloc((void **)&S.h_status, sizeof(int), cudaHostAllocDefault));
+		TGC_CUDA(cudaHostAlloc((void **)&S.h_status, sizeof(int), cudaHostAllocMapped));
 		*S.h_status = 0;
+		TGC_CUDA(cudaHostGetDevicePointer((void **)&S.d_status, S.h_status, 0));
 	}
 	if (int prev = *(volatile int *)S.h_status) { // an earlier call's kernel gave up waiting
 		*S.h_status = 0;
 		return set_err(TG_CUDA_EDEVICE, "a tensor-core kernel of an earlier call on this device gave up waiting (status %d)",
 			       prev);
 	}
-	if ((rc = S.buf.ensure(wbytes + 2 * abytes + 256, dev)) || (rc = S.status.ensure(64, dev))) return rc;
+	if ((rc = S.buf.ensure(wbytes + 2 * abytes + 256, dev))) return rc;
 	__nv_bfloat16 *wq = (__nv_bfloat16 *)S.buf.p;
 	__nv_bfloat16 *ahi = (__nv_bfloat16 *)((uint8_t *)S.buf.p + ((wbytes + 127) & ~(size_t)127));
 	__nv_bfloat16 *alo = (__nv_bfloat16 *)((uint8_t *)ahi + ((abytes + 127) & ~(size_t)127));
-	cudaMemsetAsync(S.status.p, 0, sizeof(int), st);
 	GemmOperands ops;
 	GemmArgs p;
 	memset(&p, 0, sizeof p);
@@ -882,7 +966,7 @@ int matmul_q_tc(int axis, float *o, const float *act, const signed char *q, int 
 	p.pa[0] = 0, p.pb[0] = 0, p.pa[1] = 0, p.pb[1] = 1;
 	p.epi = EPI_STORE;
 	p.out = o;
-	p.status = S.status.as<int>();
+	p.status = S.d_status; // no per-call reset or copy: a timeout writes the host word directly
 	// small batches leave most SMs idle with one tile per weight slab: let gemm() split K
 	if ((rc = S.part.ensure((size_t)64 << 20, dev))) return rc;
 	p.partial = S.part.as<float>(), p.partial_floats = (long)((64 << 20) / sizeof(float));
@@ -908,7 +992,6 @@ int matmul_q_tc(int axis, float *o, const float *act, const signed char *q, int 
 	}
 	ops.lda = k, ops.ldb = k;
 	if ((rc = gemm(ops, p, st))) return rc;
-	TGC_CUDA(cudaMemcpyAsync(S.h_status, p.status, sizeof(int), cudaMemcpyDeviceToHost, st));
 	*done = true;
 	return TG_CUDA_OK;
 }

@@ -22,6 +22,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <condition_variable>
 #include <memory>
 #include <mutex>
 #include <thread>
@@ -1298,23 +1299,82 @@ extern "C" int tg_cuda_batch_device(tg_cuda_model *g, const float *all, long row
 	return run_rows(g->m, 0, all, rows, out, steps, g->m.prog.nthink, (cudaStream_t)stream);
 }
 
-// Host copies of a few MB and more split over up to 4 threads (one of them the caller).
+// Host copies of a few MB and more split over up to 4 threads: the caller and three
+// workers that live as long as the process (thread start-up would cost more than the
+// copy of a 4 MB chunk).
+class CopyPool {
+	std::mutex mu;
+	std::condition_variable cv, idle;
+	struct Job {
+		void *dst;
+		const void *src;
+		size_t n;
+	};
+	std::vector<Job> jobs;
+	int running = 0;
+	std::vector<std::thread> th;
+	bool stop = false;
+
+public:
+	static constexpr int WORKERS = 3;
+	CopyPool()
+	{
+		for (int i = 0; i < WORKERS; i++)
+			th.emplace_back([this] {
+				std::unique_lock<std::mutex> lk(mu);
+				for (;;) {
+					cv.wait(lk, [this] { return stop || !jobs.empty(); });
+					if (stop) return;
+					Job j = jobs.back();
+					jobs.pop_back();
+					running++;
+					lk.unlock();
+					memcpy(j.dst, j.src, j.n);
+					lk.lock();
+					running--;
+					if (jobs.empty() && running == 0) idle.notify_all();
+				}
+			});
+	}
+	~CopyPool()
+	{
+		{
+			std::lock_guard<std::mutex> lk(mu);
+			stop = true;
+		}
+		cv.notify_all();
+		for (auto &t : th) t.join();
+	}
+	// copies [0, first) on the calling thread, the rest as `parts - 1` jobs, then waits
+	void copy(void *dst, const void *src, size_t n, int parts)
+	{
+		const size_t each = (n / parts + 63) / 64 * 64;
+		{
+			std::lock_guard<std::mutex> lk(mu);
+			for (int i = 1; i < parts; i++) {
+				size_t off = each * i;
+				if (off >= n) break;
+				jobs.push_back({ (char *)dst + off, (const char *)src + off, std::min(each, n - off) });
+			}
+		}
+		cv.notify_all();
+		memcpy(dst, src, std::min(each, n));
+		std::unique_lock<std::mutex> lk(mu);
+		idle.wait(lk, [this] { return jobs.empty() && running == 0; });
+	}
+};
+
 static void par_copy(void *dst, const void *src, size_t n)
 {
-	const int parts = (int)std::min<size_t>(4, n / (2 << 20));
+	static CopyPool pool;
+	static std::mutex one; // one split copy at a time (several GPUs' host threads share the pool)
+	const int parts = (int)std::min<size_t>(CopyPool::WORKERS + 1, n / (1 << 20));
 	if (parts <= 1) {
 		memcpy(dst, src, n);
 		return;
 	}
-	const size_t each = (n / parts + 63) / 64 * 64;
-	std::vector<std::thread> th;
-	for (int i = 1; i < parts; i++) {
-		size_t off = each * i;
-		if (off >= n) break;
-		th.emplace_back([=] { memcpy((char *)dst + off, (const char *)src + off, std::min(each, n - off)); });
-	}
-	memcpy(dst, src, std::min(each, n));
-	for (auto &t : th) t.join();
+	std::lock_guard<std::mutex> lk(one);
+	pool.copy(dst, src, n, parts);
 }
 
 constexpr size_t BATCH_CHUNK_BYTES = 4 << 20; // input bytes per pipeline chunk

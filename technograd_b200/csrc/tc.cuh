@@ -34,6 +34,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar)
 	asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// One arrival for a whole warp (the barrier counts warps): __syncwarp orders every lane's
+// preceding shared-memory writes, proxy fences and TMEM loads before lane 0's arrive. 32
+// threads arriving one by one serialize on the barrier word and delay every other barrier
+// operation of the CTA. All 32 lanes must call it at the same point.
+__device__ __forceinline__ void mbar_arrive_warp(uint64_t *bar)
+{
+	__syncwarp();
+	if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
 __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity)
 {
 	uint32_t ok;
@@ -47,7 +57,8 @@ __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity)
 	return ok != 0;
 }
 
-// Bounded wait: false (and *status set) if the phase did not complete in time.
+// Bounded wait: false (and *status set to code; any nonzero code reports the failure) if the
+// phase did not complete in time.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status, int code)
 {
 	if (mbar_try(bar, parity)) return true;
@@ -56,7 +67,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *s
 		if (mbar_try(bar, parity)) return true;
 		if ((i & 63) == 0 && clock64() - t0 > WAIT_CYCLES) break;
 	}
-	if (status) atomicExch(status, code);
+	if (status) *(volatile int *)status = code; // a plain store: the word may be mapped host memory
 	return false;
 }
 
@@ -111,6 +122,13 @@ __device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map)
 {
 	asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)map) : "memory");
+}
+
+// Prefetch of a 2D tile into L2 (no shared memory, no completion); x 16-byte aligned.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int x, int y)
+{
+	asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"((uint64_t)map), "r"(x), "r"(y)
+		     : "memory");
 }
 
 // ---- TMEM -------------------------------------------------------------------------------

@@ -62,6 +62,8 @@ def test_matmul_q_vs_oracle(cuda, axis, m, k, n, bits):
 @pytest.mark.parametrize("axis,m,k,n", [
     (0, 128, 64, 128), (0, 200, 72, 130), (1, 130, 200, 136), (1, 9, 64, 128), (0, 4096, 4096, 256),
     (1, 2048, 1024, 3072), (0, 1024, 4096, 4096),
+    # narrow batches (32-column tiles, split K) and ragged rows / columns of the code operand
+    (0, 4096, 4096, 9), (0, 300, 1024, 32), (0, 129, 128, 17), (0, 1000, 512, 40), (0, 4096, 1024, 33),
 ])
 def test_matmul_q_tensor_cores_vs_oracle(cuda, axis, m, k, n, bits):
     """Batches above 8 take the tcgen05 GEMM; large shapes are checked on sampled outputs."""
