@@ -53,8 +53,9 @@ __device__ __forceinline__ uint8_t *smem_row(uint8_t *tile, int rr) { return til
 // bf16 (|c| <= 128 needs 8 significant bits).
 __device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b)
 {
-	__nv_bfloat162 r = __hsub2(*(__nv_bfloat162 *)&a, *(__nv_bfloat162 *)&b);
-	return *(uint32_t *)&r;
+	uint32_t d;
+	asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+	return d;
 }
 // 8 int4 codes of one word (code 2e in bits 8e..8e+3, 2e+1 in bits 8e+4..8e+7) -> 4 bf16 pairs
 __device__ __forceinline__ void int4x8_bf16(uint32_t w, uint32_t h[4])
