@@ -18,11 +18,13 @@
 //        bulk copies fill with the tile's rows of the cache (bf16 part and remainder
 //        bytes of K and V, kv.cuh), K (rows = keys, K-major over dims) and V^T (rows =
 //        dims, K-major over keys) as bf16 hi/lo in the 128-byte-swizzled K-major layout
-//        of the UMMA descriptors. Thread 0 issues the next tile's bulk copies as soon as
-//        all converters have read the staging area, so global latency overlaps the tile.
+//        of the UMMA descriptors. The K and V halves of the staging area refill
+//        separately: thread 0 issues tile j+1's K copies once K_j is converted, so they
+//        land while V_j is converted, and V_{j+1}'s once V_j is.
 //   8    TMEM allocation and the MMA issue (one thread): S_j = Q.K_j^T into one of two
-//        TMEM score buffers, O += P_j.V_j into the TMEM accumulator. S_{j+1} is issued
-//        before P_j.V_j so the softmax of tile j+1 overlaps the P.V of tile j.
+//        TMEM score buffers, O += P_j.V_j into the TMEM accumulator, each issued as soon
+//        as its operands are ready, so the softmax of tile j+1 overlaps the P.V of tile j
+//        and P_j.V_j does not wait for K_{j+1}.
 // O stays in TMEM across tiles. The probabilities use a running reference max that is
 // raised (and O, l rescaled in place) only when a tile's max exceeds it by more than
 // FA_RESCALE, so O is rarely touched between tiles; exp(s - m_ref) <= e^8 keeps the
@@ -63,7 +65,7 @@ constexpr int FA_SBAR = 212992;      // barriers and the TMEM address
 constexpr size_t FA_SMEM = FA_SBAR + 256 + 1024; // + alignment slack
 
 struct FaBars {
-	uint64_t q_full, stg_full, stg_free, k_full, k_empty, v_full, v_empty;
+	uint64_t q_full, stgk_full, stgk_free, stgv_full, stgv_free, k_full, k_empty, v_full, v_empty;
 	uint64_t s_full[2], s_free[2], p_full, p_empty, done;
 	uint32_t tmem;
 	int abort;
@@ -142,8 +144,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 	if (threadIdx.x == 0) {
 		// barriers the 128-thread groups arrive on count warps (mbar_arrive_warp)
 		mbar_init(&B->q_full, 4);
-		mbar_init(&B->stg_full, 1);
-		mbar_init(&B->stg_free, 4);
+		mbar_init(&B->stgk_full, 1);
+		mbar_init(&B->stgk_free, 4);
+		mbar_init(&B->stgv_full, 1);
+		mbar_init(&B->stgv_free, 4);
 		mbar_init(&B->k_full, 4);
 		mbar_init(&B->k_empty, 1);
 		mbar_init(&B->v_full, 4);
@@ -167,17 +171,22 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 	if (warp >= 4 && warp < 8) {
 		// ---------------- converters ----------------
 		const int t = threadIdx.x - 128;
-		// the bulk copies of key tile j into the staging area (rows past T are not copied)
-		auto stage = [&](int j) {
+		// the bulk copies of key tile j's K rows (and, separately, its V rows) into their halves
+		// of the staging area (rows past T are not copied)
+		auto stage_k = [&](int j) {
 			const int k0 = j * FA_K, rows = min(FA_K, T - k0);
-			mbar_expect_tx(&B->stg_full, (uint32_t)rows * (256 + 128) * 2);
-			bulk_load(sm + FA_ST_KH, kc.h + cb + (long)k0 * FA_HD, rows * 256, &B->stg_full);
-			bulk_load(sm + FA_ST_KQ, kc.q + cb + (long)k0 * FA_HD, rows * 128, &B->stg_full);
-			bulk_load(sm + FA_ST_VH, vc.h + cb + (long)k0 * FA_HD, rows * 256, &B->stg_full);
-			bulk_load(sm + FA_ST_VQ, vc.q + cb + (long)k0 * FA_HD, rows * 128, &B->stg_full);
+			mbar_expect_tx(&B->stgk_full, (uint32_t)rows * (256 + 128));
+			bulk_load(sm + FA_ST_KH, kc.h + cb + (long)k0 * FA_HD, rows * 256, &B->stgk_full);
+			bulk_load(sm + FA_ST_KQ, kc.q + cb + (long)k0 * FA_HD, rows * 128, &B->stgk_full);
 		};
-		int pending = -1; // thread 0: a staged tile whose copies nobody has waited for yet
-		if (t == 0) stage(0), pending = 0;
+		auto stage_v = [&](int j) {
+			const int k0 = j * FA_K, rows = min(FA_K, T - k0);
+			mbar_expect_tx(&B->stgv_full, (uint32_t)rows * (256 + 128));
+			bulk_load(sm + FA_ST_VH, vc.h + cb + (long)k0 * FA_HD, rows * 256, &B->stgv_full);
+			bulk_load(sm + FA_ST_VQ, vc.q + cb + (long)k0 * FA_HD, rows * 128, &B->stgv_full);
+		};
+		int pendk = -1, pendv = -1; // thread 0: staged tiles whose copies nobody has waited for yet
+		if (t == 0) stage_k(0), stage_v(0), pendk = 0, pendv = 0;
 		const float *qb = q + ((long)s * NQ + h) * (long)T * FA_HD;
 		for (int i0 = t; i0 < FA_Q * 16; i0 += 128 * FA_LB) { // Q: 128 rows x 16 chunks of 8 dims
 			float4 a[FA_LB], b[FA_LB];
@@ -204,8 +213,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 		mbar_arrive_warp(&B->q_full);
 		for (int j = 0; j < nkt; j++) {
 			const int k0 = j * FA_K;
-			if (!fa_wait_warp(B, &B->stg_full, j & 1, status)) break;
-			pending = -1;
+			if (!fa_wait_warp(B, &B->stgk_full, j & 1, status)) break;
+			pendk = -1;
 			// K: 64 rows x 16 chunks of 8 dims; the bf16 part as is, the remainder as lo
 			if (j > 0 && !fa_wait_warp(B, &B->k_empty, (j - 1) & 1, status)) break;
 #pragma unroll 2
@@ -231,7 +240,24 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 			}
 			fence_async_smem();
 			mbar_arrive_warp(&B->k_full);
+			// the K half of the staging area has been read: thread 0 refills it with the next
+			// tile's K rows, which then land while V is converted
+			mbar_arrive_warp(&B->stgk_free);
+			if (j + 1 < nkt) {
+				bool ok0 = true;
+				if (t == 0) {
+					ok0 = fa_wait(B, &B->stgk_free, j & 1, status);
+					if (ok0) {
+						fence_async_smem();
+						stage_k(j + 1);
+						pendk = j + 1;
+					}
+				}
+				if (!__shfl_sync(0xffffffffu, ok0, 0)) break; // thread 0's warp leaves together
+			}
 			// V^T: item = (8 keys, 4 dims) -> one 16-byte chunk in each of 4 rows
+			if (!fa_wait_warp(B, &B->stgv_full, j & 1, status)) break;
+			pendv = -1;
 			if (j > 0 && !fa_wait_warp(B, &B->v_empty, (j - 1) & 1, status)) break;
 			for (int i = t; i < 256; i += 128) {
 				const int kg = i & 7, dg = i >> 3;
@@ -262,32 +288,30 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 			}
 			fence_async_smem();
 			mbar_arrive_warp(&B->v_full);
-			// the staging area has been read: thread 0 refills it with the next tile
-			mbar_arrive_warp(&B->stg_free);
+			mbar_arrive_warp(&B->stgv_free);
 			if (j + 1 < nkt) {
 				bool ok0 = true;
 				if (t == 0) {
-					ok0 = fa_wait(B, &B->stg_free, j & 1, status);
+					ok0 = fa_wait(B, &B->stgv_free, j & 1, status);
 					if (ok0) {
 						fence_async_smem();
-						stage(j + 1);
-						pending = j + 1;
+						stage_v(j + 1);
+						pendv = j + 1;
 					}
 				}
 				if (!__shfl_sync(0xffffffffu, ok0, 0)) break; // thread 0's warp leaves together
 			}
 		}
 		// after an abort: the copies still in flight land before the CTA's shared memory is released
-		if (pending >= 0) mbar_wait(&B->stg_full, pending & 1, nullptr, 0);
+		if (pendk >= 0) mbar_wait(&B->stgk_full, pendk & 1, nullptr, 0);
+		if (pendv >= 0) mbar_wait(&B->stgv_full, pendv & 1, nullptr, 0);
 	} else if (warp == 8) {
 		// ---------------- MMA issue ----------------
 		if (lane == 0) {
 			const uint32_t idS = idesc_bf16_f32(FA_Q, FA_K), idO = idesc_bf16_f32(FA_Q, FA_HD);
 			const uint32_t base = smem_u32(sm);
 			bool ok = fa_wait(B, &B->q_full, 0, status);
-			auto issue_s = [&](int j) -> bool {
-				if (!fa_wait(B, &B->k_full, j & 1, status)) return false;
-				if (j >= 2 && !fa_wait(B, &B->s_free[j & 1], ((j >> 1) - 1) & 1, status)) return false;
+			auto issue_s = [&](int j) {
 				tc_fence_after();
 				const uint32_t d = tmem + (uint32_t)((j & 1) * FA_K);
 				const uint32_t qa[2] = { base + FA_SQ_HI, base + FA_SQ_LO }, ka[2] = { base + FA_SK_HI, base + FA_SK_LO };
@@ -302,11 +326,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 						}
 				tc_commit(&B->s_full[j & 1]);
 				tc_commit(&B->k_empty);
-				return true;
 			};
-			auto issue_pv = [&](int j) -> bool {
-				if (!fa_wait(B, &B->v_full, j & 1, status)) return false;
-				if (!fa_wait(B, &B->p_full, j & 1, status)) return false;
+			auto issue_pv = [&](int j) {
 				tc_fence_after();
 				const uint32_t pa2[2] = { base + FA_SP, base + FA_SP + 16384 }, va[2] = { base + FA_SV_HI, base + FA_SV_LO };
 				const int pa[3] = { 0, 0, 1 }, pb[3] = { 0, 1, 0 };
@@ -318,12 +339,36 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 					}
 				tc_commit(&B->p_empty);
 				tc_commit(&B->v_empty);
-				return true;
 			};
-			if (ok) ok = issue_s(0);
-			for (int j = 0; ok && j < nkt; j++) {
-				if (j + 1 < nkt) ok = issue_s(j + 1);
-				if (ok) ok = issue_pv(j);
+			// S_j and P_j.V_j in the order their operands become ready: S_j once K_j is
+			// converted and its score buffer is free (the softmax has read S_{j-2}), P_j.V_j once
+			// P_j and V_j are in shared memory. Neither chain waits behind the other; each
+			// barrier polled can be at most one phase ahead of the one asked for, because its
+			// next phase depends on the MMA not yet issued.
+			int ns = 0, npv = 0;
+			long long idle0 = clock64();
+			for (uint32_t spins = 0; ok && npv < nkt;) {
+				bool did = false;
+				if (ns < nkt && mbar_try(&B->k_full, ns & 1) && (ns < 2 || mbar_try(&B->s_free[ns & 1], ((ns >> 1) - 1) & 1))) {
+					issue_s(ns++);
+					did = true;
+				}
+				if (npv < ns && mbar_try(&B->v_full, npv & 1) && mbar_try(&B->p_full, npv & 1)) {
+					issue_pv(npv++);
+					did = true;
+				}
+				if (did) {
+					idle0 = clock64();
+					spins = 0;
+				} else if ((++spins & 63) == 0) {
+					if (*(volatile int *)&B->abort) {
+						ok = false;
+					} else if (clock64() - idle0 > WAIT_CYCLES) {
+						if (status) *(volatile int *)status = ST_TIMEOUT_FULL;
+						*(volatile int *)&B->abort = 1;
+						ok = false;
+					}
+				}
 			}
 			// every MMA issued has completed before TMEM is released (also after an abort)
 			tc_commit(&B->done);
