@@ -44,6 +44,13 @@ const char *tg_cuda_error(void);
 int tg_cuda_init(int ngpus, const int *devices);
 /* Number of devices selected by tg_cuda_init (0 before it). */
 int tg_cuda_ngpus(void);
+/* Failure-path self-test on device 0 of the selection: a kernel waits on an mbarrier
+ * that nothing arrives on, with a limit of `cycles` SM clock cycles (the same bounded
+ * wait every tcgen05 kernel uses, whose default limit is about 2 s). The wait gives
+ * up, the kernel writes its status word and returns: TG_CUDA_EDEVICE with *status =
+ * the kernel's status code (1, a timed-out full-barrier wait). Any other return means
+ * the mechanism failed. The context stays usable. No reference counterpart. */
+int tg_cuda_selftest_wait(long long cycles, int *status);
 /* Release every device resource the library holds. */
 void tg_cuda_shutdown(void);
 

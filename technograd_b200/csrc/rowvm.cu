@@ -1299,9 +1299,10 @@ extern "C" int tg_cuda_batch_device(tg_cuda_model *g, const float *all, long row
 	return run_rows(g->m, 0, all, rows, out, steps, g->m.prog.nthink, (cudaStream_t)stream);
 }
 
-// Host copies of a few MB and more split over up to 4 threads: the caller and three
-// workers that live as long as the process (thread start-up would cost more than the
-// copy of a 4 MB chunk).
+// Host copies of a few MB and more split over up to 4 threads: the caller and up to three
+// workers (fewer on hosts with fewer hardware threads) that live as long as the process
+// (thread start-up would cost more than the copy of a 4 MB chunk). More threads measured
+// no faster: four saturate the host's copy bandwidth.
 class CopyPool {
 	std::mutex mu;
 	std::condition_variable cv, idle;
@@ -1316,10 +1317,10 @@ class CopyPool {
 	bool stop = false;
 
 public:
-	static constexpr int WORKERS = 3;
-	CopyPool()
+	const int workers;
+	CopyPool() : workers((int)std::min(3u, std::max(2u, std::thread::hardware_concurrency()) - 1))
 	{
-		for (int i = 0; i < WORKERS; i++)
+		for (int i = 0; i < workers; i++)
 			th.emplace_back([this] {
 				std::unique_lock<std::mutex> lk(mu);
 				for (;;) {
@@ -1368,7 +1369,7 @@ static void par_copy(void *dst, const void *src, size_t n)
 {
 	static CopyPool pool;
 	static std::mutex one; // one split copy at a time (several GPUs' host threads share the pool)
-	const int parts = (int)std::min<size_t>(CopyPool::WORKERS + 1, n / (1 << 20));
+	const int parts = (int)std::min<size_t>((size_t)pool.workers + 1, n / (1 << 20));
 	if (parts <= 1) {
 		memcpy(dst, src, n);
 		return;

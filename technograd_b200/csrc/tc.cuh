@@ -58,17 +58,22 @@ __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity)
 }
 
 // Bounded wait: false (and *status set to code; any nonzero code reports the failure) if the
-// phase did not complete in time.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status, int code)
+// phase did not complete within `limit` SM clock cycles.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, int *status, int code, long long limit)
 {
 	if (mbar_try(bar, parity)) return true;
 	const long long t0 = clock64();
 	for (uint32_t i = 1;; i++) {
 		if (mbar_try(bar, parity)) return true;
-		if ((i & 63) == 0 && clock64() - t0 > WAIT_CYCLES) break;
+		if ((i & 63) == 0 && clock64() - t0 > limit) break;
 	}
 	if (status) *(volatile int *)status = code; // a plain store: the word may be mapped host memory
 	return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status, int code)
+{
+	return mbar_wait_for(bar, parity, status, code, WAIT_CYCLES);
 }
 
 __device__ __forceinline__ void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
