@@ -86,8 +86,11 @@ Driver &driver()
 JitModule::~JitModule()
 {
 	if (mod && driver().ok) {
-		cudaSetDevice(dev);
+		int cur = -1;
+		cudaGetDevice(&cur);
+		cudaSetDevice(dev); // the module belongs to this device's primary context
 		driver().unload((CUmodule)mod);
+		if (cur >= 0) cudaSetDevice(cur);
 	}
 }
 

@@ -14,6 +14,9 @@ struct JitModule {
 	void *mod = nullptr;  // CUmodule
 	void *func = nullptr; // CUfunction
 	int dev = -1;
+	JitModule() = default;
+	JitModule(const JitModule &) = delete; // owns the module: unloaded once, by the destructor
+	JitModule &operator=(const JitModule &) = delete;
 	~JitModule();
 };
 
