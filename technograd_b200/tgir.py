@@ -11,14 +11,18 @@ keeps `data = code * scale`, as src/ir.c:495-507 does.
 from __future__ import annotations
 
 import ctypes as C
+import mmap
 import re
+import warnings
 from dataclasses import dataclass, field
 
 import numpy as np
 
 from . import _lib
 
-_TOKEN = re.compile(r'\s+|;[^\n]*|(\()|(\))|"([^"\n]*)"|([^\s();"]+)')
+_TOKEN = re.compile(rb'\s+|;[^\n]*|(\()|(\))|"([^"\n]*)"|([^\s();"]+)')
+# the number lists of params: read straight into arrays (no object per number)
+_PAYLOAD = re.compile(rb'\(\s*(data|codes|scale)(?=[\s)])')
 
 
 class TgirError(ValueError):
@@ -39,14 +43,50 @@ class Sym(str):
     pass
 
 
-def read_sexp(src: str) -> list:
+def _payload(span: bytes, head: str) -> np.ndarray:
+    """The numbers of a (data ...), (codes ...) or (scale ...) list, parsed in C. Codes are
+    integers (src/ir.c:478-509); data and scales are read as doubles and later rounded to
+    f32, as the reference's strtod + (float) does (src/sexp.c:112-121)."""
+    if not span.strip():
+        return np.zeros(0, np.int32 if head == "codes" else np.float64)
+    with warnings.catch_warnings():
+        warnings.simplefilter("error", DeprecationWarning)  # a partial parse is an error
+        try:
+            if head == "codes":
+                try:
+                    return np.fromstring(span, dtype=np.int32, sep=" ")
+                except (ValueError, DeprecationWarning):
+                    pass  # not plain integers: let the generic check below decide
+            return np.fromstring(span, dtype=np.float64, sep=" ")
+        except (ValueError, DeprecationWarning) as e:
+            raise TgirError(f"bad number in ({head} ...)") from e
+
+
+def read_sexp(src, fast: bool = True) -> list:
+    """S-expressions of `src` (str, bytes or a read-only mmap). With `fast`, the number
+    lists of params become [Sym(head), ndarray] without a Python object per number, so a
+    quantized model of hundreds of millions of codes reads in bounded memory; without it,
+    every number is an atom, as the reference's reader builds its Sx nodes."""
+    buf = src.encode("utf-8") if isinstance(src, str) else src
     stack: list[list] = [[]]
     pos = 0
-    n = len(src)
+    n = len(buf)
     while pos < n:
-        m = _TOKEN.match(src, pos)
+        m = _TOKEN.match(buf, pos)
         if not m:
             raise TgirError(f"bad character at offset {pos}")
+        if m.group(1) and fast:
+            pm = _PAYLOAD.match(buf, pos)
+            if pm:
+                end = buf.find(b")", pm.end())
+                if end < 0:
+                    raise TgirError("unterminated list")
+                span = buf[pm.end():end]
+                if b"(" not in span and b";" not in span:
+                    head = pm.group(1).decode()
+                    stack[-1].append([Sym(head), _payload(span, head)])
+                    pos = end + 1
+                    continue
         pos = m.end()
         if m.group(1):
             stack.append([])
@@ -56,12 +96,19 @@ def read_sexp(src: str) -> list:
             done = stack.pop()
             stack[-1].append(done)
         elif m.group(3) is not None:
-            stack[-1].append(m.group(3))
+            stack[-1].append(m.group(3).decode("utf-8"))
         elif m.group(4):
-            stack[-1].append(_atom(m.group(4)))
+            stack[-1].append(_atom(m.group(4).decode("utf-8")))
     if len(stack) != 1:
         raise TgirError("unterminated list")
     return stack[0]
+
+
+def _numbers(node) -> np.ndarray:
+    """The values of a number list, parsed fast (an array) or as atoms."""
+    if len(node) == 2 and isinstance(node[1], np.ndarray):
+        return node[1]
+    return np.array(node[1:], dtype=np.float64)
 
 
 @dataclass
@@ -138,7 +185,9 @@ class Module:
 def pack_codes(codes: np.ndarray, bits: int) -> np.ndarray:
     """Reference packing (runtime/tg_rt.h:124-129): int8 as is; int4 element i in
     byte i/2, low nibble first."""
-    codes = np.asarray(codes, dtype=np.int64).ravel()
+    codes = np.asarray(codes).ravel()
+    if codes.dtype.kind not in "iu":
+        codes = codes.astype(np.int64)
     if bits == 8:
         return codes.astype(np.int8)
     if codes.size % 2:
@@ -287,8 +336,8 @@ class _Reader:
         return PIns(_lib.OP["scan"], s.c[0], body=body, scan=s, tid=tid)
 
 
-def read(src: str) -> Module:
-    forms = read_sexp(src)
+def read(src, fast: bool = True) -> Module:
+    forms = read_sexp(src, fast)
     if len(forms) != 1 or not isinstance(forms[0], list) or forms[0][:2] != ["tgir", 1.0]:
         raise TgirError("expected (tgir 1 ...)")
     m = None
@@ -304,8 +353,12 @@ def read(src: str) -> Module:
         if h in ("param", "state") and isinstance(f[3], list) and f[3] and f[3][0] == "quant":
             shape = _shape(f[2])
             bits, axis = int(f[3][1]), int(f[3][2])
-            sc = np.array(f[3][3][1:], dtype=np.float64).astype(np.float32)
-            codes = np.array(f[3][4][1:], dtype=np.int64)
+            sc = _numbers(f[3][3]).astype(np.float32)
+            codes = _numbers(f[3][4])
+            if codes.dtype.kind == "f":
+                if not np.array_equal(codes, np.round(codes)):
+                    raise TgirError(f"param '{f[1]}': codes must be integers")
+                codes = codes.astype(np.int32)
             n = int(np.prod(shape))
             if codes.size != n or sc.size != shape[axis]:
                 raise TgirError(f"param '{f[1]}': quant sizes")
@@ -317,12 +370,13 @@ def read(src: str) -> Module:
             pv.qbits, pv.qaxis = bits, axis
             pv.q = pack_codes(codes, bits)
             pv.qs = sc
-            ch = (np.arange(n) // shape[1]) if axis == 0 else (np.arange(n) % shape[1])
-            pv.data = (codes.astype(np.float32) * sc[ch]).astype(np.float32)
+            # data = code * scale of the element's channel (src/ir.c:495-507), one f32 rounding
+            c2 = codes.reshape(shape[0], -1).astype(np.float32)
+            pv.data = (c2 * (sc[:, None] if axis == 0 else sc[None, :])).astype(np.float32).ravel()
             rd.define(f[1], v)
         elif h in ("param", "state"):
             shape = _shape(f[2])
-            data = np.array(f[3][1:], dtype=np.float64).astype(np.float32)
+            data = _numbers(f[3]).astype(np.float32)
             if data.size != int(np.prod(shape)):
                 raise TgirError(f"param '{f[1]}' needs {int(np.prod(shape))} values, has {data.size}")
             v = m.value(_lib.PARAM if h == "param" else _lib.STATE, shape, str(f[1]))
@@ -346,9 +400,16 @@ def read(src: str) -> Module:
     return m
 
 
-def load(path: str) -> Module:
-    with open(path, encoding="utf-8") as f:
-        return read(f.read())
+def load(path: str, fast: bool = True) -> Module:
+    """Reads a TGIR file through a read-only memory map: the text is never held as a
+    Python string, and the params' number lists are parsed straight into arrays."""
+    with open(path, "rb") as f:
+        try:
+            mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+        except ValueError:  # an empty file cannot be mapped
+            return read(b"", fast)
+        with mm:
+            return read(mm, fast)
 
 
 class CProgram:
