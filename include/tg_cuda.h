@@ -15,6 +15,7 @@
  *   tg_cuda_lm_*       <- `tgc batch` over the Qwen3 program that examples/qwen3/import.py:51-131
  *                         emits (per-head tg_matmul_qb, rmsnorm, softmax, take), run per sequence
  *   tg_cuda_quantize_rtn <- the RTN branch of quantize_param, src/quant.c:176-200,258-316
+ *   tg_cuda_batcher_*  <- vm_run_into per request line in run_line, src/serve.c:129-149
  */
 #ifndef TG_CUDA_H
 #define TG_CUDA_H
@@ -178,6 +179,20 @@ void tg_cuda_free(tg_cuda_model *g);
  * Both are GPU kernels with the same arithmetic. No reference counterpart: the
  * reference's VM is the interpreter (src/vm.c:475-481). */
 int tg_cuda_model_jit(const tg_cuda_model *g, char *why, int n);
+
+/* Micro-batching for servers (`tgc serve` / `tgc stream`, src/serve.c:129-149): many
+ * threads each submit one row (tg_cuda_batcher_run blocks until that row's output and
+ * think steps are written); one dispatcher thread gathers the waiting rows -- up to
+ * max_rows, or those that arrive within max_wait_us of the first -- into one
+ * tg_cuda_batch call. Host buffers; rows sized as the model's (per values in, n out,
+ * nthink steps; steps may be NULL when nthink == 0). A failed batch returns its status
+ * to every row in it. tg_cuda_batcher_free answers the rows already queued, then stops;
+ * the model must outlive the batcher. */
+typedef struct tg_cuda_batcher tg_cuda_batcher;
+int tg_cuda_batcher_new(tg_cuda_model *g, int max_rows, int max_wait_us, tg_cuda_batcher **out);
+int tg_cuda_batcher_run(tg_cuda_batcher *b, const float *row, float *out, int *steps);
+int tg_cuda_batcher_stats(tg_cuda_batcher *b, long *rows, long *batches);
+void tg_cuda_batcher_free(tg_cuda_batcher *b);
 /* The CUDA source generated for a program (written to src, n bytes, NUL-terminated,
  * may be NULL; *len = its full length), and with compile != 0 its compilation for
  * sm_100a. Needs neither tg_cuda_init nor a GPU. TG_CUDA_EUNSUPPORTED when the

@@ -25,7 +25,8 @@ PARAM, INPUT, TMP, STATE = 0, 1, 2, 3
 SYMBOLS = ["tg_cuda_error", "tg_cuda_init", "tg_cuda_ngpus", "tg_cuda_selftest_wait", "tg_cuda_shutdown", "tg_cuda_matmul_q",
            "tg_cuda_matmul_qb_noalloc",
            "tg_cuda_quantize_rtn", "tg_cuda_gptq_prepare", "tg_cuda_quantize_gptq", "tg_cuda_gptq_free", "tg_cuda_load", "tg_cuda_batch", "tg_cuda_batch_device", "tg_cuda_free",
-           "tg_cuda_model_jit", "tg_cuda_program_kernel",
+           "tg_cuda_model_jit", "tg_cuda_program_kernel", "tg_cuda_batcher_new", "tg_cuda_batcher_run",
+           "tg_cuda_batcher_stats", "tg_cuda_batcher_free",
            "tg_cuda_lm_load", "tg_cuda_lm_forward", "tg_cuda_lm_generate", "tg_cuda_lm_free", "tg_cuda_lm_profile",
            "tg_cuda_lm_get_stats", "tg_cuda_ssm_load", "tg_cuda_ssm_forward", "tg_cuda_ssm_forward_device",
            "tg_cuda_ssm_free", "tg_cuda_ssm_profile", "tg_cuda_ssm_get_stats"]
@@ -127,6 +128,10 @@ def lib() -> C.CDLL:
             "tg_cuda_batch_device": ([vp, vp, l, vp, vp, vp], i),
             "tg_cuda_free": ([vp], None),
             "tg_cuda_model_jit": ([vp, C.c_char_p, i], i),
+            "tg_cuda_batcher_new": ([vp, i, i, C.POINTER(vp)], i),
+            "tg_cuda_batcher_run": ([vp, vp, vp, vp], i),
+            "tg_cuda_batcher_stats": ([vp, C.POINTER(l), C.POINTER(l)], i),
+            "tg_cuda_batcher_free": ([vp], None),
             "tg_cuda_program_kernel": ([C.POINTER(Program), C.c_char_p, l, C.POINTER(l), i], i),
             "tg_cuda_lm_load": ([C.POINTER(LmDesc), i, i, C.POINTER(vp)], i),
             "tg_cuda_lm_forward": ([vp, vp, l, i, vp], i),

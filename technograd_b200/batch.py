@@ -88,6 +88,39 @@ class Batch:
         return out, steps[:, :m.nthink]
 
 
+class Batcher:
+    """Micro-batching of single-row requests from many threads (tg_cuda_batcher_*), the
+    device side of `tgc serve`: each run() blocks until its row has gone through the GPU
+    in a batch with whatever other rows were waiting."""
+
+    def __init__(self, batch: Batch, max_rows: int = 8192, max_wait_us: int = 1000):
+        self.batch = batch  # keeps the model alive as long as the batcher
+        h = C.c_void_p()
+        _lib.check(_lib.lib().tg_cuda_batcher_new(batch.handle, max_rows, max_wait_us, C.byref(h)))
+        self.handle = h
+
+    def run(self, row) -> tuple[np.ndarray, np.ndarray]:
+        m = self.batch.module
+        row = np.ascontiguousarray(row, np.float32).reshape(m.per)
+        out = np.empty(m.nout, np.float32)
+        steps = np.zeros(max(m.nthink, 1), np.int32)
+        _lib.check(_lib.lib().tg_cuda_batcher_run(self.handle, row.ctypes.data, out.ctypes.data, steps.ctypes.data))
+        return out, steps[:m.nthink]
+
+    def stats(self) -> tuple[int, int]:
+        rows, batches = C.c_long(), C.c_long()
+        _lib.check(_lib.lib().tg_cuda_batcher_stats(self.handle, C.byref(rows), C.byref(batches)))
+        return rows.value, batches.value
+
+    def close(self):
+        if getattr(self, "handle", None):
+            _lib.lib().tg_cuda_batcher_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+
 def write_rows(path: str | None, out: np.ndarray, steps: np.ndarray) -> None:
     if path and is_binary(path):
         out.astype("<f4").tofile(path)

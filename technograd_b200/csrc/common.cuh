@@ -27,6 +27,9 @@ struct Device {
 	cudaStream_t stream;
 };
 
+// Row sizes of a loaded model (values per row, outputs per row, think-step slots).
+int model_shape(const tg_cuda_model *g, int *per, int *nout, int *nthink);
+
 // Devices chosen by tg_cuda_init, in shard order.
 std::vector<Device> &devices();
 bool inited();

@@ -1255,6 +1255,13 @@ extern "C" int tg_cuda_program_kernel(const tg_cuda_program *p, char *src, long 
 	return TG_CUDA_OK;
 }
 
+// Row sizes of a loaded model, for the micro-batcher (batcher.cu).
+int tgc::model_shape(const tg_cuda_model *g, int *per, int *nout, int *nthink)
+{
+	*per = g->m.prog.per, *nout = g->m.prog.nout, *nthink = g->m.prog.nthink;
+	return TG_CUDA_OK;
+}
+
 extern "C" int tg_cuda_model_jit(const tg_cuda_model *g, char *why, int n)
 {
 	if (!g) return set_err(TG_CUDA_EINVAL, "tg_cuda_model_jit: NULL model");
