@@ -361,6 +361,184 @@ static void obin(int op, float *o, const tg_cuda_value *vo, const float *a, cons
 	}
 }
 
+/* Rounded table index or -1 (runtime/tg_rt.h:200-204, tg_ell_idx). */
+static int oell(float v, int d)
+{
+	float r = floorf(v + 0.5f);
+	return r >= 0.0f && r < (float)d ? (int)r : -1;
+}
+
+/* spmm / spmm with a quantized table (runtime/tg_rt.h:206-235): rows of ELLPACK (index,
+ * value) pairs against a table [d, h], entries in order, padding (value 0) and
+ * out-of-range indices skipped; a quantized table multiplies its codes by value * scale
+ * of the entry's row. */
+static void ospmm(float *o, const float *x, const float *w, const tg_cuda_value *wv, int r, int k, int d, int h)
+{
+	const int quant = wv->qbits && wv->qaxis == 0;
+	for (int i = 0; i < r; i++) {
+		float *y = o + (long)i * h;
+		for (int j = 0; j < h; j++) y[j] = 0.0f;
+		for (int e = 0; e < k; e++) {
+			const float *pr = x + ((long)i * k + e) * 2;
+			const int t = oell(pr[0], d);
+			if (t < 0 || pr[1] == 0.0f) continue;
+			if (quant) {
+				const float v = pr[1] * wv->qs[t];
+				for (int j = 0; j < h; j++) y[j] += v * (float)tgo_qget(wv->q, wv->qbits, (long)t * h + j);
+			} else {
+				for (int j = 0; j < h; j++) y[j] += pr[1] * w[(long)t * h + j];
+			}
+		}
+	}
+}
+
+/* topk (runtime/tg_rt.h:445-483): per row, the indices of the k largest entries, largest
+ * first, ties to the lower index, NaN never chosen, -1 past the row's non-NaN entries.
+ * Restated as repeated selection of the next entry in the order (value descending,
+ * index ascending), which picks the same indices as the reference's insertion buffer. */
+static void otopk(float *o, const float *a, int rows, int n, int k)
+{
+	for (int r = 0; r < rows; r++) {
+		const float *x = a + (long)r * n;
+		float lv = 0.0f;
+		int li = -1; /* the last pick: (value lv, index li); -1 = none yet */
+		for (int i = 0; i < k; i++) {
+			int bi = -1;
+			float bv = 0.0f;
+			for (int j = 0; j < n; j++) {
+				const float v = x[j];
+				if (v != v) continue;
+				if (li >= 0 && !(v < lv || (v == lv && j > li))) continue; /* not after the last pick */
+				if (bi < 0 || v > bv) bi = j, bv = v;                     /* first index wins a tie */
+			}
+			o[(long)r * k + i] = (float)bi;
+			if (bi < 0) {
+				for (int q = i + 1; q < k; q++) o[(long)r * k + q] = -1.0f;
+				break;
+			}
+			lv = bv, li = bi;
+		}
+	}
+}
+
+/* memscan (runtime/tg_rt.h:485-516): a delta-rule memory M (rows, dv), initially m0,
+ * read and written by tn steps of k entries (row, read weight a, write weight c[, delta
+ * read weight dd]); per step, in entry order: r = sum a M[row], rd = sum dd M[row]
+ * (dd = a with 3 fields), then M[row] += c (v - rd) for c != 0. Output: the reads r
+ * (tn, dv), the delta reads rd (tn, dv), the final M. */
+static void omemscan(float *o, const float *m0, const float *p, const float *v, int tn, int kq, int rows, int dv)
+{
+	const int k = kq / 2, q = 3 + (kq & 1);
+	float *M = o + 2L * tn * dv;
+	memmove(M, m0, (size_t)rows * dv * sizeof *M);
+	for (long st = 0; st < tn; st++) {
+		const float *e = p + st * k * q, *x = v + st * dv;
+		float *r = o + st * dv, *rd = o + ((long)tn + st) * dv;
+		for (int j = 0; j < dv; j++) r[j] = rd[j] = 0.0f;
+		for (int i = 0; i < k; i++) {
+			const int t = oell(e[i * q], rows);
+			if (t < 0) continue;
+			const float a = e[i * q + 1], dd = q == 4 ? e[i * q + 3] : a;
+			for (int j = 0; j < dv; j++) {
+				r[j] += a * M[(long)t * dv + j];
+				rd[j] += dd * M[(long)t * dv + j];
+			}
+		}
+		for (int i = 0; i < k; i++) {
+			const int t = oell(e[i * q], rows);
+			const float c = e[i * q + 2];
+			if (t < 0 || c == 0.0f) continue;
+			for (int j = 0; j < dv; j++) M[(long)t * dv + j] += c * (x[j] - rd[j]);
+		}
+	}
+}
+
+/* sufmatch (runtime/tg_rt.h:579-666): per stream, a suffix automaton of the tokens read
+ * so far; at step t, the state reached by the longest suffix of x[..t] seen before t, and
+ * the token that followed that suffix's first occurrence. The automaton lives in the
+ * output's workspace exactly as the reference lays it out (per state: len, link, first
+ * end, edge list head; per edge slot of an open-addressing table of H = the first power of
+ * two >= max(16, 6T + 6): state, symbol, target, next edge of the state), so the whole
+ * output matches, workspace included. */
+static long osm_cap(long T)
+{
+	long h = 16;
+	while (h < 6 * T + 6) h *= 2;
+	return h;
+}
+static long osm_slot(const float *E, long H, long st, long c)
+{
+	unsigned long h = ((unsigned long)st * 2654435761UL ^ (unsigned long)c * 40503UL) & (unsigned long)(H - 1);
+	for (;; h = (h + 1) & (unsigned long)(H - 1))
+		if (E[h * 4] < 0.0f || ((long)E[h * 4] == st && (long)E[h * 4 + 1] == c)) return (long)h;
+}
+static long osm_get(const float *E, long H, long st, long c)
+{
+	const long h = osm_slot(E, H, st, c);
+	return E[h * 4] < 0.0f ? -1 : (long)E[h * 4 + 2];
+}
+static void osm_put(float *E, float *S, long H, long st, long c, long to)
+{
+	const long h = osm_slot(E, H, st, c);
+	if (E[h * 4] < 0.0f) { /* a new edge of st: push it on st's edge list */
+		E[h * 4] = (float)st, E[h * 4 + 1] = (float)c, E[h * 4 + 3] = S[st * 4 + 3];
+		S[st * 4 + 3] = (float)h;
+	}
+	E[h * 4 + 2] = (float)to;
+}
+static void osufmatch(float *o, const float *x, int T, int n)
+{
+	const long H = osm_cap(T);
+	float *S = o + 2L * T * n, *E = S + 4 * (2L * T + 2);
+	for (int g = 0; g < n; g++) {
+		long nst = 1, last = 0, m = 0, l = 0;
+		for (long i = 0; i < H; i++) E[i * 4] = -1.0f;
+		S[0] = 0.0f, S[1] = -1.0f, S[2] = -1.0f, S[3] = -1.0f;
+		for (long t = 0; t < T; t++) {
+			const float xv = x[t * n + g];
+			const long c = xv >= 0.0f ? (long)(xv + 0.5f) : -1;
+			float *out = o + (t * n + g) * 2;
+			if (c < 0) { /* a negative id: no match across it, not added */
+				m = 0, l = 0;
+				out[0] = -1.0f, out[1] = 0.0f;
+				continue;
+			}
+			/* the longest suffix of x[..t] that occurs before t */
+			while (m != 0 && osm_get(E, H, m, c) < 0) {
+				m = (long)S[m * 4 + 1];
+				l = (long)S[m * 4];
+			}
+			const long tr = osm_get(E, H, m, c);
+			if (tr >= 0) m = tr, l++;
+			else m = 0, l = 0;
+			const long fe = l > 0 ? (long)S[m * 4 + 2] : -1;
+			out[0] = fe >= 0 && fe + 1 <= t ? x[(fe + 1) * n + g] : -1.0f;
+			out[1] = (float)l;
+			/* extend the automaton by c */
+			const long cur = nst++;
+			long pp = last;
+			S[cur * 4] = S[last * 4] + 1.0f, S[cur * 4 + 2] = (float)t, S[cur * 4 + 3] = -1.0f;
+			for (; pp != -1 && osm_get(E, H, pp, c) < 0; pp = (long)S[pp * 4 + 1]) osm_put(E, S, H, pp, c, cur);
+			if (pp == -1) {
+				S[cur * 4 + 1] = 0.0f;
+			} else {
+				const long qs = osm_get(E, H, pp, c);
+				if (S[pp * 4] + 1.0f == S[qs * 4]) {
+					S[cur * 4 + 1] = (float)qs;
+				} else { /* split qs: a clone of length len(pp) + 1 */
+					const long cl = nst++;
+					S[cl * 4] = S[pp * 4] + 1.0f, S[cl * 4 + 1] = S[qs * 4 + 1], S[cl * 4 + 2] = S[qs * 4 + 2], S[cl * 4 + 3] = -1.0f;
+					for (long h = (long)S[qs * 4 + 3]; h >= 0; h = (long)E[h * 4 + 3]) osm_put(E, S, H, cl, (long)E[h * 4 + 1], (long)E[h * 4 + 2]);
+					for (; pp != -1 && osm_get(E, H, pp, c) == qs; pp = (long)S[pp * 4 + 1]) osm_put(E, S, H, pp, c, cl);
+					S[qs * 4 + 1] = (float)cl, S[cur * 4 + 1] = (float)cl;
+					if (m == qs && l <= (long)S[cl * 4]) m = cl;
+				}
+			}
+			last = cur;
+		}
+	}
+}
+
 static int oexec(OVM *vm, int from, int count);
 
 /* src/ops.c:60-73 matmul_dims / matmul_groups, src/ops.c:310-320 q_axis_for,
@@ -453,6 +631,28 @@ static int oone(OVM *vm, const tg_cuda_ins *in)
 	case TG_CUDA_OP_RESHAPE:
 		ocopy(o, a, n);
 		return 0;
+	case TG_CUDA_OP_SPMM: { /* src/vm.c:307-313, src/ops.c:82-88 spmm_dims */
+		const tg_cuda_value *x = &p->val[in->a[0]], *w = &p->val[in->a[1]];
+		ospmm(o, a, c, w, x->rank == 3 ? x->dim[0] : 1, x->dim[x->rank - 2], w->dim[0], w->dim[1]);
+		return 0;
+	}
+	case TG_CUDA_OP_TOPK: { /* src/vm.c:340-345 */
+		const tg_cuda_value *x = &p->val[in->a[0]];
+		const int cols = x->rank ? x->dim[x->rank - 1] : 1;
+		otopk(o, a, (int)(numel(x) / cols), cols, vo->dim[vo->rank - 1]);
+		return 0;
+	}
+	case TG_CUDA_OP_MEMSCAN: { /* src/vm.c:351-357, src/util.c:455-467 memscan_dims */
+		const tg_cuda_value *m0 = &p->val[in->a[0]], *pe = &p->val[in->a[1]];
+		const float *v = optr(vm, in->a[2]);
+		omemscan(o, a, c, v, pe->dim[0] * pe->dim[1], 2 * pe->dim[2] + (pe->dim[3] == 4), m0->dim[0], m0->dim[1]);
+		return 0;
+	}
+	case TG_CUDA_OP_SUFMATCH: { /* src/vm.c:346-350 */
+		const tg_cuda_value *x = &p->val[in->a[0]];
+		osufmatch(o, a, x->dim[0], x->rank == 2 ? x->dim[1] : 1);
+		return 0;
+	}
 	case TG_CUDA_OP_THINK: { /* src/vm.c:383-411 */
 		ocopy(o, optr(vm, in->init), n);
 		int it = 0;

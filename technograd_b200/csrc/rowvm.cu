@@ -38,7 +38,7 @@ namespace tgc {
 
 enum : int {
 	D_CONST = 1, D_BIN, D_UN, D_MATMUL, D_ROW, D_RED, D_TRANS, D_OUTER, D_TAKE, D_COPY,
-	D_THINK_BEGIN, D_THINK_END, D_SCAN_BEGIN, D_SCAN_SLICE, D_SCAN_END,
+	D_THINK_BEGIN, D_THINK_END, D_SCAN_BEGIN, D_SCAN_SLICE, D_SCAN_END, D_SPMM, D_TOPK, D_MEMSCAN, D_SUFMATCH,
 };
 
 // An operand: >= 0 an arena slot (per row), < 0 a param offset -(loc + 1) in the param blob.
@@ -142,6 +142,186 @@ __device__ void vm_matmul(const DOp &op, float *ar, const float *pb)
 				else if (op.scale == 2) acc = __fmul_rn(sc[j], acc);
 				o.p[(oo + (long)i * n + j) * o.st] = acc;
 			}
+	}
+}
+
+// Rounded table index or -1 (runtime/tg_rt.h:200-204).
+__device__ __forceinline__ int ell_idx(float v, int d)
+{
+	const float r = floorf(__fadd_rn(v, 0.5f));
+	return r >= 0.0f && r < (float)d ? (int)r : -1;
+}
+
+// spmm (runtime/tg_rt.h:206-235): ELLPACK rows of (index, value) pairs against a table
+// [d, h], entries in order; a quantized table (sc != nullptr) holds exact codes and
+// multiplies them by value * scale of the entry's row.
+__device__ void vm_spmm(const DOp &op, float *ar, const float *pb)
+{
+	Loc o = loc(op.out, ar, pb), x = loc(op.a, ar, pb), w = loc(op.b, ar, pb);
+	const float *sc = op.scale ? loc(op.c, ar, pb).p : nullptr;
+	const int h = op.nn;
+	for (int i = 0; i < op.m; i++) {
+		for (int j = 0; j < h; j++) o.p[((long)i * h + j) * o.st] = 0.0f;
+		for (int e = 0; e < op.k; e++) {
+			const long xe = ((long)i * op.k + e) * 2;
+			const float val = x.p[(xe + 1) * x.st];
+			const int t = ell_idx(x.p[xe * x.st], op.g);
+			if (t < 0 || val == 0.0f) continue;
+			const float v = sc ? __fmul_rn(val, sc[t]) : val;
+			for (int j = 0; j < h; j++) {
+				float &y = o.p[((long)i * h + j) * o.st];
+				y = __fadd_rn(y, __fmul_rn(v, w.p[((long)t * h + j) * w.st]));
+			}
+		}
+	}
+}
+
+// topk (runtime/tg_rt.h:445-483): per row, the indices of the k largest entries, largest
+// first, ties to the lower index, NaN never chosen, -1 past the row's other entries; by
+// repeated selection of the next entry in the order (value descending, index ascending).
+__device__ void vm_topk(const DOp &op, float *ar, const float *pb)
+{
+	Loc o = loc(op.out, ar, pb), x = loc(op.a, ar, pb);
+	const int n = op.k, k = op.nn;
+	for (int r = 0; r < op.m; r++) {
+		float lv = 0.0f;
+		int li = -1;
+		for (int i = 0; i < k; i++) {
+			int bi = -1;
+			float bv = 0.0f;
+			for (int j = 0; j < n; j++) {
+				const float v = x.p[((long)r * n + j) * x.st];
+				if (v != v) continue;
+				if (li >= 0 && !(v < lv || (v == lv && j > li))) continue;
+				if (bi < 0 || v > bv) bi = j, bv = v;
+			}
+			o.p[((long)r * k + i) * o.st] = (float)bi;
+			if (bi >= 0) lv = bv, li = bi;
+		}
+	}
+}
+
+// memscan (runtime/tg_rt.h:485-516): the delta-rule memory, initially m0 (rows, dv), read
+// and written by tn steps of k entries (row, a, c[, dd]); per step in entry order the reads
+// r = sum a M[row] and rd = sum dd M[row], then M[row] += c (v - rd). Output: r, rd, final M.
+__device__ void vm_memscan(const DOp &op, float *ar, const float *pb)
+{
+	Loc o = loc(op.out, ar, pb), m0 = loc(op.a, ar, pb), p = loc(op.b, ar, pb), v = loc(op.c, ar, pb);
+	const int tn = op.m, k = op.k / 2, q = 3 + (op.k & 1), rows = op.nn, dv = op.g;
+	const long mo = 2L * tn * dv; // M's offset in the output
+	for (long i = 0; i < (long)rows * dv; i++) o.p[(mo + i) * o.st] = m0.p[i * m0.st];
+	for (long st = 0; st < tn; st++) {
+		const long e0 = st * k * q, ro = st * dv, rdo = ((long)tn + st) * dv;
+		for (int j = 0; j < dv; j++) o.p[(ro + j) * o.st] = o.p[(rdo + j) * o.st] = 0.0f;
+		for (int i = 0; i < k; i++) {
+			const int t = ell_idx(p.p[(e0 + (long)i * q) * p.st], rows);
+			if (t < 0) continue;
+			const float a = p.p[(e0 + (long)i * q + 1) * p.st], dd = q == 4 ? p.p[(e0 + (long)i * q + 3) * p.st] : a;
+			for (int j = 0; j < dv; j++) {
+				const float mv = o.p[(mo + (long)t * dv + j) * o.st];
+				o.p[(ro + j) * o.st] = __fadd_rn(o.p[(ro + j) * o.st], __fmul_rn(a, mv));
+				o.p[(rdo + j) * o.st] = __fadd_rn(o.p[(rdo + j) * o.st], __fmul_rn(dd, mv));
+			}
+		}
+		for (int i = 0; i < k; i++) {
+			const int t = ell_idx(p.p[(e0 + (long)i * q) * p.st], rows);
+			const float c = p.p[(e0 + (long)i * q + 2) * p.st];
+			if (t < 0 || c == 0.0f) continue;
+			for (int j = 0; j < dv; j++) {
+				float &mv = o.p[(mo + (long)t * dv + j) * o.st];
+				mv = __fadd_rn(mv, __fmul_rn(c, __fsub_rn(v.p[(st * dv + j) * v.st], o.p[(rdo + j) * o.st])));
+			}
+		}
+	}
+}
+
+// sufmatch (runtime/tg_rt.h:579-666): per stream, a suffix automaton of the tokens so far;
+// at step t the token that followed the first occurrence of the longest suffix of x[..t]
+// seen before t (or -1) and that suffix's length. The automaton lives in the output's
+// workspace as the reference lays it out -- per state (len, link, first end, edge list),
+// per slot of an open-addressing edge table of H slots (state, symbol, target, next edge)
+// -- so the whole output matches, workspace included.
+struct SufWs {
+	float *base;
+	int st;
+	long S0, E0, H;
+	__device__ float &s(long i) const { return base[(S0 + i) * st]; }
+	__device__ float &e(long i) const { return base[(E0 + i) * st]; }
+	__device__ long slot(long state, long c) const
+	{
+		unsigned long h = ((unsigned long)state * 2654435761UL ^ (unsigned long)c * 40503UL) & (unsigned long)(H - 1);
+		for (long probe = 0; probe < H; probe++, h = (h + 1) & (unsigned long)(H - 1))
+			if (e(h * 4) < 0.0f || ((long)e(h * 4) == state && (long)e(h * 4 + 1) == c)) break;
+		return (long)h; // the table holds fewer edges than slots, so an empty slot is reached
+	}
+	__device__ long get(long state, long c) const
+	{
+		const long h = slot(state, c);
+		return e(h * 4) < 0.0f ? -1 : (long)e(h * 4 + 2);
+	}
+	__device__ void put(long state, long c, long to) const
+	{
+		const long h = slot(state, c);
+		if (e(h * 4) < 0.0f) {
+			e(h * 4) = (float)state, e(h * 4 + 1) = (float)c, e(h * 4 + 3) = s(state * 4 + 3);
+			s(state * 4 + 3) = (float)h;
+		}
+		e(h * 4 + 2) = (float)to;
+	}
+};
+
+__device__ void vm_sufmatch(const DOp &op, float *ar, const float *pb)
+{
+	Loc o = loc(op.out, ar, pb), x = loc(op.a, ar, pb);
+	const long T = op.m, n = op.k;
+	long H = 16;
+	while (H < 6 * T + 6) H *= 2;
+	const SufWs W{ o.p, o.st, 2 * T * n, 2 * T * n + 4 * (2 * T + 2), H };
+	for (long g = 0; g < n; g++) {
+		long nst = 1, last = 0, m = 0, l = 0;
+		for (long i = 0; i < H; i++) W.e(i * 4) = -1.0f;
+		W.s(0) = 0.0f, W.s(1) = -1.0f, W.s(2) = -1.0f, W.s(3) = -1.0f;
+		for (long t = 0; t < T; t++) {
+			const float xv = x.p[(t * n + g) * x.st];
+			const long c = xv >= 0.0f ? (long)__fadd_rn(xv, 0.5f) : -1;
+			float &o0 = o.p[((t * n + g) * 2) * o.st], &o1 = o.p[((t * n + g) * 2 + 1) * o.st];
+			if (c < 0) {
+				m = 0, l = 0;
+				o0 = -1.0f, o1 = 0.0f;
+				continue;
+			}
+			while (m != 0 && W.get(m, c) < 0) {
+				m = (long)W.s(m * 4 + 1);
+				l = (long)W.s(m * 4);
+			}
+			const long tr = W.get(m, c);
+			if (tr >= 0) m = tr, l++;
+			else m = 0, l = 0;
+			const long fe = l > 0 ? (long)W.s(m * 4 + 2) : -1;
+			o0 = fe >= 0 && fe + 1 <= t ? x.p[((fe + 1) * n + g) * x.st] : -1.0f;
+			o1 = (float)l;
+			const long cur = nst++;
+			long pp = last;
+			W.s(cur * 4) = __fadd_rn(W.s(last * 4), 1.0f), W.s(cur * 4 + 2) = (float)t, W.s(cur * 4 + 3) = -1.0f;
+			for (; pp != -1 && W.get(pp, c) < 0; pp = (long)W.s(pp * 4 + 1)) W.put(pp, c, cur);
+			if (pp == -1) {
+				W.s(cur * 4 + 1) = 0.0f;
+			} else {
+				const long qs = W.get(pp, c);
+				if (__fadd_rn(W.s(pp * 4), 1.0f) == W.s(qs * 4)) {
+					W.s(cur * 4 + 1) = (float)qs;
+				} else {
+					const long cl = nst++;
+					W.s(cl * 4) = __fadd_rn(W.s(pp * 4), 1.0f), W.s(cl * 4 + 1) = W.s(qs * 4 + 1), W.s(cl * 4 + 2) = W.s(qs * 4 + 2),
+						 W.s(cl * 4 + 3) = -1.0f;
+					for (long h = (long)W.s(qs * 4 + 3); h >= 0; h = (long)W.e(h * 4 + 3)) W.put(cl, (long)W.e(h * 4 + 1), (long)W.e(h * 4 + 2));
+					for (; pp != -1 && W.get(pp, c) == qs; pp = (long)W.s(pp * 4 + 1)) W.put(pp, c, cl);
+					W.s(qs * 4 + 1) = (float)cl, W.s(cur * 4 + 1) = (float)cl;
+					if (m == qs && l <= (long)W.s(cl * 4)) m = cl;
+				}
+			}
+			last = cur;
+		}
 	}
 }
 
@@ -272,6 +452,18 @@ __global__ void __launch_bounds__(VM_ROWS) vm_kernel(const DOp *__restrict__ tap
 						o.p[((long)i * op.nn + j) * o.st] = t >= 0 ? a.p[((long)t * op.nn + j) * a.st] : 0.0f;
 				}
 			}
+			break;
+		case D_SPMM:
+			if (act) vm_spmm(op, ar, blob);
+			break;
+		case D_TOPK:
+			if (act) vm_topk(op, ar, blob);
+			break;
+		case D_MEMSCAN:
+			if (act) vm_memscan(op, ar, blob);
+			break;
+		case D_SUFMATCH:
+			if (act) vm_sufmatch(op, ar, blob);
 			break;
 		case D_COPY:
 			if (act && op.out != op.a) {
@@ -689,6 +881,51 @@ static int emit_ins(Compiler &C, int idx, int depth)
 		T.push_back(d);
 		return 0;
 	}
+	case TG_CUDA_OP_SPMM: { // src/vm.c:307-313, src/ops.c:82-88 spmm_dims
+		const tg_cuda_value &X = p->val[in.a[0]], &W = p->val[in.a[1]];
+		d.code = D_SPMM;
+		d.m = X.rank == 3 ? X.dim[0] : 1;
+		d.k = X.dim[X.rank - 2];
+		d.g = W.dim[0];
+		d.nn = W.dim[1];
+		if (W.qbits && W.qaxis == 0) { // the table's exact codes, times value * scale of the row
+			d.scale = 1;
+			d.b = -(C.pslot[in.a[1]] + 1);
+			d.c = -(C.sslot[in.a[1]] + 1);
+		} else if (W.qbits) { // quantized on the other axis: its dequantized values
+			d.b = -(C.pslot[in.a[1]] + 1 + (int)numel(W) + W.dim[W.qaxis]);
+		}
+		T.push_back(d);
+		return 0;
+	}
+	case TG_CUDA_OP_TOPK: { // src/vm.c:340-345 with row_dims, src/ops.c:90-94
+		const tg_cuda_value &X = p->val[in.a[0]];
+		d.code = D_TOPK;
+		d.k = X.rank ? X.dim[X.rank - 1] : 1;
+		d.m = (int)(numel(X) / d.k);
+		d.nn = vo.dim[vo.rank - 1];
+		T.push_back(d);
+		return 0;
+	}
+	case TG_CUDA_OP_MEMSCAN: { // src/vm.c:351-357, src/util.c:455-467 memscan_dims
+		const tg_cuda_value &M0 = p->val[in.a[0]], &P = p->val[in.a[1]];
+		d.code = D_MEMSCAN;
+		d.c = C.L(in.a[2]);
+		d.m = P.dim[0] * P.dim[1];
+		d.k = 2 * P.dim[2] + (P.dim[3] == 4);
+		d.nn = M0.dim[0];
+		d.g = M0.dim[1];
+		T.push_back(d);
+		return 0;
+	}
+	case TG_CUDA_OP_SUFMATCH: { // src/vm.c:346-350
+		const tg_cuda_value &X = p->val[in.a[0]];
+		d.code = D_SUFMATCH;
+		d.m = X.dim[0];
+		d.k = X.rank == 2 ? X.dim[1] : 1;
+		T.push_back(d);
+		return 0;
+	}
 	case TG_CUDA_OP_RESHAPE:
 		d.code = D_COPY;
 		d.n = (int)numel(vo);
@@ -1061,6 +1298,39 @@ int Gen::op(int pc)
 		}
 		line("}");
 		return 0;
+	case D_SPMM: // from a param table only (gen_source): run-time rows of it in global memory
+		line("if (done == 0u) {");
+		for (int i = 0; i < o.m; i++) {
+			for (int j = 0; j < o.nn; j++) line(at(o.out, (long)i * o.nn + j) + " = 0.0f;");
+			for (int e = 0; e < o.k; e++) {
+				const long xe = ((long)i * o.k + e) * 2;
+				line("{ const float val = " + at(o.a, xe + 1) + ", rr = floorf(__fadd_rn(" + at(o.a, xe) + ", 0.5f)); const int t = rr >= 0.0f && rr < " +
+				     flt((float)o.g) + " ? (int)rr : -1;");
+				line("if (t >= 0 && val != 0.0f) { const float v = " + (o.scale ? "__fmul_rn(val, " + atd(o.c, "t") + ")" : std::string("val")) + ";");
+				for (int j = 0; j < o.nn; j++)
+					line(at(o.out, (long)i * o.nn + j) + " = __fadd_rn(" + at(o.out, (long)i * o.nn + j) + ", __fmul_rn(v, " +
+					     atd(o.b, "t * " + num(o.nn) + " + " + num(j)) + "));");
+				line("} }");
+				stmts += o.nn;
+			}
+		}
+		line("}");
+		return 0;
+	case D_TOPK: // repeated selection in the order (value descending, index ascending)
+		line("if (done == 0u) {");
+		for (int r = 0; r < o.m; r++) {
+			line("{ float lv = 0.0f; int li = -1;");
+			for (int i = 0; i < o.nn; i++) {
+				line("{ int bi = -1; float bv = 0.0f, v;");
+				for (int j = 0; j < o.k; j++)
+					line("v = " + at(o.a, (long)r * o.k + j) + "; if (v == v && (li < 0 || v < lv || (v == lv && " + num(j) +
+					     " > li)) && (bi < 0 || v > bv)) bi = " + num(j) + ", bv = v;");
+				line(at(o.out, (long)r * o.nn + i) + " = (float)bi; if (bi >= 0) lv = bv, li = bi; }");
+			}
+			line("}");
+		}
+		line("}");
+		return 0;
 	case D_COPY:
 		if (o.out == o.a) return 0;
 		line("if (done == 0u) {");
@@ -1108,8 +1378,9 @@ static std::string gen_source(const Prog &P, std::string &why)
 	// (a slice per step) and take from a computed value index it at run time and keep
 	// their programs on vm_kernel.
 	for (const DOp &o : P.tape)
-		if (o.code == D_SCAN_BEGIN || o.code == D_SCAN_SLICE || o.code == D_SCAN_END || (o.code == D_TAKE && o.a >= 0)) {
-			why = "run-time arena index (scan, or take from a computed value)";
+		if (o.code == D_SCAN_BEGIN || o.code == D_SCAN_SLICE || o.code == D_SCAN_END || o.code == D_MEMSCAN ||
+		    o.code == D_SUFMATCH || (o.code == D_TAKE && o.a >= 0) || (o.code == D_SPMM && o.b >= 0)) {
+			why = "run-time arena index (scan, memscan, sufmatch, or take / spmm from a computed table)";
 			return "";
 		}
 	Gen G(P);

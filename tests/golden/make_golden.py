@@ -359,6 +359,59 @@ def programs(tgc: str) -> None:
         sh(tgc, "batch", ir, rp, "-j", "1", "-o", os.path.join(out, f"{name}_out.csv"))
 
 
+# Programs of the reference's tests with the ops of the sparse and memory models: name ->
+# (source, rows, how rows are drawn, quantize flags or None for `tgc ir`)
+SPARSE_MEMORY = {
+    "topk": ("tests/memory/topk.tg", 200, "ties", None),
+    "topk_pad": ("tests/memory/topk_pad.tg", 100, "ties", None),
+    "memscan": ("tests/memory/scan.tg", 200, "uniform", None),
+    "sufmatch": ("tests/memory/sufmatch.tg", 200, "tokens", None),
+    "mlp_f32": ("tests/quant/mlp.tg", 300, "sparse", None),
+    "mlp_q8": ("tests/quant/mlp.tg", 300, "sparse", ["--bits", "8"]),
+    "mlp_q4": ("tests/quant/mlp.tg", 300, "sparse", ["--bits", "4"]),
+}
+# tests/run.sh:33-48: the inputs the reference's own suite runs these programs on
+SPARSE_MEMORY_ROWS = {
+    "topk": [[0, 5, 3, 4, -1, 2, 0, 0, 0, 0, 0, 0, 6, 5, 4, 3, 2, 1]],
+    "topk_pad": [[2, 3, 1]],
+    "memscan": [list(np.round(np.arange(-1.1, 1.25, 0.1), 1))],
+    "sufmatch": [[1, 5, 2, 6, 3, 5, 1, 6, 2, 5, 3, 6, 1, -1, 2, 5, 3, 6, 9, 7, 1, 6, 2, 5]],
+}
+
+
+def sparse_memory(tgc: str) -> None:
+    from technograd_b200 import tgir
+    out = os.path.join(HERE, "programs")
+    os.makedirs(out, exist_ok=True)
+    for name, (src, n, kind, qflags) in SPARSE_MEMORY.items():
+        ir = os.path.join(out, f"{name}.tgir")
+        if qflags is None:
+            with open(ir, "w") as f:
+                f.write(sh(tgc, "ir", os.path.join(REF, src)))
+        else:
+            sh(tgc, "quantize", os.path.join(REF, src), *qflags, "-o", ir)
+        m = tgir.load(ir)
+        rng = np.random.default_rng(sum(map(ord, name)))
+        if kind == "ties":  # small integers: many equal values, and a NaN now and then
+            rows = rng.integers(-3, 4, size=(n, m.per)).astype(np.float32)
+            rows[rng.uniform(size=rows.shape) < 0.05] = np.nan
+        elif kind == "tokens":  # token ids with repeats and breaks (negative ids)
+            rows = rng.integers(-1, 7, size=(n, m.per)).astype(np.float32)
+        elif kind == "sparse":  # x f32[16], then 3 (index, value) pairs into a 64-row table
+            rows = np.round(rng.uniform(-1.5, 1.5, size=(n, m.per)), 3).astype(np.float32)
+            idx = rng.integers(-3, 68, size=(n, 3)).astype(np.float32) + np.round(rng.uniform(-0.45, 0.45, size=(n, 3)), 2)
+            val = np.round(rng.uniform(-2, 2, size=(n, 3)), 3)
+            val[rng.uniform(size=val.shape) < 0.15] = 0.0  # padding
+            rows[:, 16::2], rows[:, 17::2] = idx, val
+        else:
+            rows = np.round(rng.uniform(-1.5, 1.5, size=(n, m.per)), 3).astype(np.float32)
+        if name in SPARSE_MEMORY_ROWS:
+            rows = np.concatenate([np.array(SPARSE_MEMORY_ROWS[name], np.float32), rows])
+        rp = os.path.join(out, f"{name}_rows.csv")
+        np.savetxt(rp, rows, fmt="%.9g", delimiter=",")
+        sh(tgc, "batch", ir, rp, "-j", "1", "-o", os.path.join(out, f"{name}_out.csv"))
+
+
 def main() -> None:
     tgo.build()
     tgc = tgo.REF_TGC
@@ -370,6 +423,7 @@ def main() -> None:
     quant()
     nano(tgc)
     programs(tgc)
+    sparse_memory(tgc)
     print("golden fixtures written to", HERE)
 
 

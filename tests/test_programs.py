@@ -1,5 +1,7 @@
 """The reference's control-flow test programs (tests/scan/scan.tg, tests/think/halt.tg,
-tests/scan/nested_grad.tg, tests/attn/window.tg) on the oracle VM and on the device
+tests/scan/nested_grad.tg, tests/attn/window.tg) and the programs of its sparse and
+memory tests (tests/memory/topk.tg, topk_pad.tg, scan.tg, sufmatch.tg; tests/quant/mlp.tg
+as f32 and quantized to int8 / int4, an spmm table) on the oracle VM and on the device
 row executor, against `tgc batch` output of the reference (tests/golden/programs).
 
 The oracle follows the reference's arithmetic order with the same libm, so it must
@@ -15,7 +17,9 @@ from technograd_b200 import tgir
 from technograd_b200.batch import Batch, load_samples
 
 RTOL, ATOL = 1e-3, 1e-4
-NAMES = ["scan", "halt", "nested_grad", "window"]
+NAMES = ["scan", "halt", "nested_grad", "window",
+         # the sparse and memory models' ops: spmm (f32 and quantized tables), topk, memscan, sufmatch
+         "topk", "topk_pad", "memscan", "sufmatch", "mlp_f32", "mlp_q8", "mlp_q4"]
 
 
 def fixture(golden, name):
@@ -33,6 +37,16 @@ def test_oracle_vm_matches_tgc_batch(golden, name):
     assert steps.shape == want_steps.shape
     assert np.array_equal(steps, want_steps)
     assert np.array_equal(out.view(np.uint32), want.view(np.uint32))
+
+
+def test_known_answers_of_the_reference_suite(golden):
+    """tests/run.sh:33-36 expect_run rows: topk, topk with k past the row, suffix match."""
+    for name, want in [("topk", [1, 3, 2, 5, 0, 1, 2, 3, 0, 1, 2, 3]), ("topk_pad", [1, 0, 2, -1, -1]),
+                       ("sufmatch", [-1, 0, -1, 0, -1, 0, -1, 0, -1, 0, 6, 1, 2, 1, 5, 2, 3, 2, 6, 3, 1, 3, 5, 4, 2, 4,
+                                     -1, 0, 3, 5, 6, 1, 1, 6, 5, 2, -1, 0, -1, 0, 2, 1, 5, 1, 3, 2, 6, 2])]:
+        m, rows, ref, _ = fixture(golden, name)
+        out, _ = tgo.program_run(tgir.CProgram(m), rows[:1])
+        assert out[0].tolist() == want == ref[0].tolist()
 
 
 def test_halt_step_counts(golden):

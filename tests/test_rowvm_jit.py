@@ -22,6 +22,15 @@ PROGRAMS = {
     "programs/scan.tgir": False,  # scans index the arena at run time: interpreter
     "programs/nested_grad.tgir": False,
     "programs/window.tgir": False,  # 400 floats per row: interpreter
+    "programs/topk.tgir": True,
+    "programs/topk_pad.tgir": True,
+    "programs/memscan.tgir": False,  # the memory is indexed at run time: interpreter
+    "programs/sufmatch.tgir": False,
+    # spmm from a param table is generated; whether the compiled kernel needs a few bytes
+    # of local memory (then jit_build refuses it and the interpreter runs) is the compiler's
+    "programs/mlp_f32.tgir": None,
+    "programs/mlp_q8.tgir": None,
+    "programs/mlp_q4.tgir": None,
 }
 
 # take from a param table by rounded index (runtime/tg_rt.h:316-322), with indices out of range
@@ -53,7 +62,7 @@ def kernel_source(m, compile_: bool):
 def test_generated_kernel_compiles(golden, name):
     m = tgir.load(os.path.join(golden, name))
     rc, src = kernel_source(m, True)
-    if PROGRAMS[name]:
+    if PROGRAMS[name] is not False:
         assert rc == 0, _lib.lib().tg_cuda_error().decode()
         assert 'extern "C" __global__' in src and "tg_rowvm" in src
     else:
@@ -87,7 +96,8 @@ def test_generated_kernel_equals_interpreter(cuda, golden, name, monkeypatch):
     rng = np.random.default_rng(7)
     rows = rng.uniform(-2, 2, size=(1000, m.per)).astype(np.float32)
     jit, (o1, s1), (o2, s2) = _both(m, rows, monkeypatch)
-    assert jit.specialized[0] == PROGRAMS[name], jit.specialized[1]
+    if PROGRAMS[name] is not None:
+        assert jit.specialized[0] == PROGRAMS[name], jit.specialized[1]
     assert np.array_equal(o1.view(np.uint32), o2.view(np.uint32))
     assert np.array_equal(s1, s2)
 
