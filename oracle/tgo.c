@@ -539,6 +539,141 @@ static void osufmatch(float *o, const float *x, int T, int n)
 	}
 }
 
+/* The iteration space of an operand broadcast to `out` (src/util.c:172-212, bcast_desc
+ * with one operand): size-1 axes of out dropped, adjacent axes merged where the operand's
+ * strides allow (both broadcast, or contiguous); d = rank, dims, the operand's strides. */
+static void odesc(const tg_cuda_value *out, const tg_cuda_value *a, int *d)
+{
+	int r = out->rank, dim[4], st[4], nr = 0;
+	long acc = 1;
+	for (int i = r - 1; i >= 0; i--) {
+		const int j = i - (r - a->rank), n = j >= 0 ? a->dim[j] : 1;
+		st[i] = n == 1 ? 0 : (int)acc;
+		acc *= n;
+	}
+	int md[4], ms[4];
+	for (int i = 0; i < r; i++) {
+		if (out->dim[i] == 1) continue;
+		if (nr > 0) {
+			const int p = nr - 1;
+			const long merged = (long)st[i] * out->dim[i];
+			if ((ms[p] == 0 && st[i] == 0) || (st[i] != 0 && ms[p] == merged)) {
+				md[p] *= out->dim[i];
+				ms[p] = st[i];
+				continue;
+			}
+		}
+		md[nr] = out->dim[i], ms[nr] = st[i], nr++;
+	}
+	if (nr == 0) md[0] = 1, ms[0] = 0, nr = 1;
+	(void)dim;
+	d[0] = nr;
+	for (int i = 0; i < nr; i++) d[1 + i] = md[i], d[1 + nr + i] = ms[i];
+}
+
+/* sum_to (runtime/tg_rt.h:419-438): o (no elements) = the sum of x over its broadcast
+ * axes, in the iteration order of the merged space; a broadcast innermost axis is summed
+ * by rows first. */
+static void osum_to(float *o, const float *x, long no, const int *d)
+{
+	const int r = d[0];
+	const int *dim = d + 1, *so = d + 1 + r;
+	const int w = dim[r - 1];
+	int idx[4] = { 0 };
+	long n = 1, io = 0;
+	for (long i = 0; i < no; i++) o[i] = 0.0f;
+	for (int i = 0; i < r - 1; i++) n *= dim[i];
+	for (long i = 0; i < n; i++) {
+		const float *px = x + i * w;
+		if (so[r - 1]) {
+			for (int j = 0; j < w; j++) o[io + j] += px[j];
+		} else {
+			float sacc = 0.0f;
+			for (int j = 0; j < w; j++) sacc += px[j];
+			o[io] += sacc;
+		}
+		for (int q = r - 2; q >= 0; q--) {
+			io += so[q];
+			if (++idx[q] < dim[q]) break;
+			io -= (long)so[q] * dim[q];
+			idx[q] = 0;
+		}
+	}
+}
+
+/* take_t (runtime/tg_rt.h:324-333): o [d, h] = 0, then the rows of g added at rows r. */
+static void otake_t(float *o, const float *r, const float *g, int n, int d, int h)
+{
+	for (long i = 0; i < (long)d * h; i++) o[i] = 0.0f;
+	for (int i = 0; i < n; i++) {
+		const int t = oell(r[i], d);
+		if (t >= 0)
+			for (int j = 0; j < h; j++) o[(long)t * h + j] += g[(long)i * h + j];
+	}
+}
+
+/* memscan_t (runtime/tg_rt.h:517-578): memscan's derivatives, replaying the steps backwards
+ * from the final memory and undoing each write. y is memscan's output, pv (tn, 4k + dv) the
+ * entries (row, a, c, d) then the step's value, g the adjoint of y. o: dP (tn k 4) at 0, dM0
+ * (rows, dv) at o1, dV (tn, dv) at o2, the working memory at o3, padded to N (the layout's
+ * rounding: o1 up to a multiple of dv, N up to a multiple of dv, 2 dv or 4 dv, whichever
+ * is a multiple of 4). */
+static void omemscan_layout(long tn, int k, int rows, int dv, long *o1, long *o2, long *o3, long *N)
+{
+	const long np = tn * k * 4, L = dv % 4 == 0 ? dv : dv % 2 == 0 ? 2L * dv : 4L * dv;
+	*o1 = (np + dv - 1) / dv * dv;
+	*o2 = *o1 + (long)rows * dv;
+	*o3 = *o2 + tn * dv;
+	*N = (*o3 + (long)rows * dv + L - 1) / L * L;
+}
+static void omemscan_t(float *o, const float *y, const float *pv, const float *g, int tn, int k, int rows, int dv)
+{
+	const long w = 4L * k + dv;
+	long o1, o2, o3, N;
+	omemscan_layout(tn, k, rows, dv, &o1, &o2, &o3, &N);
+	float *dP = o, *dM = o + o1, *dV = o + o2, *M = o + o3;
+	for (long i = 0; i < N; i++) o[i] = 0.0f;
+	for (long i = 0; i < (long)rows * dv; i++) M[i] = y[2L * tn * dv + i], dM[i] = g[2L * tn * dv + i];
+	for (long st = (long)tn - 1; st >= 0; st--) {
+		const float *e = pv + st * w, *x = e + 4 * k, *rd = y + ((long)tn + st) * dv, *gr = g + st * dv,
+			    *grd = g + ((long)tn + st) * dv;
+		float *dp = dP + st * k * 4, *dx = dV + st * dv;
+		for (int i = k - 1; i >= 0; i--) { /* the memory as this step read it */
+			const int t = oell(e[i * 4], rows);
+			const float c = e[i * 4 + 2];
+			if (t < 0 || c == 0.0f) continue;
+			for (int j = 0; j < dv; j++) M[(long)t * dv + j] -= c * (x[j] - rd[j]);
+		}
+		for (int i = 0; i < k; i++) { /* the writes: dc_i, and the value's gradient */
+			const int t = oell(e[i * 4], rows);
+			const float c = e[i * 4 + 2];
+			float dc = 0.0f;
+			if (t < 0) continue;
+			for (int j = 0; j < dv; j++) {
+				dc += dM[(long)t * dv + j] * (x[j] - rd[j]);
+				dx[j] += c * dM[(long)t * dv + j];
+			}
+			dp[i * 4 + 2] = dc;
+		}
+		for (int i = 0; i < k; i++) { /* the reads: da_i and dd_i */
+			const int t = oell(e[i * 4], rows);
+			float da = 0.0f, dd = 0.0f;
+			if (t < 0) continue;
+			for (int j = 0; j < dv; j++) {
+				da += gr[j] * M[(long)t * dv + j];
+				dd += (grd[j] - dx[j]) * M[(long)t * dv + j];
+			}
+			dp[i * 4 + 1] = da, dp[i * 4 + 3] = dd;
+		}
+		for (int i = 0; i < k; i++) { /* the memory's adjoint before this step */
+			const int t = oell(e[i * 4], rows);
+			const float a = e[i * 4 + 1], d = e[i * 4 + 3];
+			if (t < 0) continue;
+			for (int j = 0; j < dv; j++) dM[(long)t * dv + j] += a * gr[j] + d * (grd[j] - dx[j]);
+		}
+	}
+}
+
 static int oexec(OVM *vm, int from, int count);
 
 /* src/ops.c:60-73 matmul_dims / matmul_groups, src/ops.c:310-320 q_axis_for,
@@ -646,6 +781,23 @@ static int oone(OVM *vm, const tg_cuda_ins *in)
 		const tg_cuda_value *m0 = &p->val[in->a[0]], *pe = &p->val[in->a[1]];
 		const float *v = optr(vm, in->a[2]);
 		omemscan(o, a, c, v, pe->dim[0] * pe->dim[1], 2 * pe->dim[2] + (pe->dim[3] == 4), m0->dim[0], m0->dim[1]);
+		return 0;
+	}
+	case TG_CUDA_OP_SUM_TO: { /* src/vm.c:358-363 */
+		int d[13];
+		odesc(&p->val[in->a[0]], &p->val[in->a[1]], d);
+		osum_to(o, a, n, d);
+		return 0;
+	}
+	case TG_CUDA_OP_TAKE_T: { /* src/vm.c:320-323 */
+		const tg_cuda_value *w = &p->val[in->a[2]];
+		otake_t(o, a, c, p->val[in->a[0]].dim[0], w->dim[0], (int)(numel(w) / w->dim[0]));
+		return 0;
+	}
+	case TG_CUDA_OP_MEMSCAN_T: { /* src/vm.c:351-357, src/util.c:455-467 memscan_dims */
+		const tg_cuda_value *y = &p->val[in->a[0]], *pv = &p->val[in->a[1]];
+		const int dv = y->dim[1], tn = pv->dim[0] * pv->dim[1];
+		omemscan_t(o, a, c, optr(vm, in->a[2]), tn, (pv->dim[2] - dv) / 4, y->dim[0] - 2 * tn, dv);
 		return 0;
 	}
 	case TG_CUDA_OP_SUFMATCH: { /* src/vm.c:346-350 */

@@ -38,7 +38,7 @@ namespace tgc {
 
 enum : int {
 	D_CONST = 1, D_BIN, D_UN, D_MATMUL, D_ROW, D_RED, D_TRANS, D_OUTER, D_TAKE, D_COPY,
-	D_THINK_BEGIN, D_THINK_END, D_SCAN_BEGIN, D_SCAN_SLICE, D_SCAN_END, D_SPMM, D_TOPK, D_MEMSCAN, D_SUFMATCH,
+	D_THINK_BEGIN, D_THINK_END, D_SCAN_BEGIN, D_SCAN_SLICE, D_SCAN_END, D_SPMM, D_TOPK, D_MEMSCAN, D_SUFMATCH, D_SUMTO, D_TAKE_T, D_MEMSCAN_T,
 };
 
 // An operand: >= 0 an arena slot (per row), < 0 a param offset -(loc + 1) in the param blob.
@@ -231,6 +231,111 @@ __device__ void vm_memscan(const DOp &op, float *ar, const float *pb)
 				float &mv = o.p[(mo + (long)t * dv + j) * o.st];
 				mv = __fadd_rn(mv, __fmul_rn(c, __fsub_rn(v.p[(st * dv + j) * v.st], o.p[(rdo + j) * o.st])));
 			}
+		}
+	}
+}
+
+// sum_to (runtime/tg_rt.h:419-438): out (n elements) = the sum of x over its broadcast axes,
+// walking the merged iteration space the compiler describes (rank, dims, out's strides); a
+// broadcast innermost axis is summed by rows first, as the reference does.
+__device__ void vm_sum_to(const DOp &op, float *ar, const float *pb)
+{
+	Loc o = loc(op.out, ar, pb), x = loc(op.a, ar, pb);
+	const int r = op.rank, w = op.dims[r - 1];
+	for (int i = 0; i < op.n; i++) o.p[(long)i * o.st] = 0.0f;
+	long outer = 1, io = 0;
+	for (int i = 0; i < r - 1; i++) outer *= op.dims[i];
+	int idx[4] = { 0, 0, 0, 0 };
+	for (long i = 0; i < outer; i++) {
+		const long xo = i * w;
+		if (op.sa[r - 1]) {
+			for (int j = 0; j < w; j++) o.p[(io + j) * o.st] = __fadd_rn(o.p[(io + j) * o.st], x.p[(xo + j) * x.st]);
+		} else {
+			float acc = 0.0f;
+			for (int j = 0; j < w; j++) acc = __fadd_rn(acc, x.p[(xo + j) * x.st]);
+			o.p[io * o.st] = __fadd_rn(o.p[io * o.st], acc);
+		}
+		for (int q = r - 2; q >= 0; q--) {
+			io += op.sa[q];
+			if (++idx[q] < op.dims[q]) break;
+			io -= (long)op.sa[q] * op.dims[q];
+			idx[q] = 0;
+		}
+	}
+}
+
+// take_t (runtime/tg_rt.h:324-333): out [d, h] = 0, then g's rows added at the rows r names.
+__device__ void vm_take_t(const DOp &op, float *ar, const float *pb)
+{
+	Loc o = loc(op.out, ar, pb), r = loc(op.a, ar, pb), g = loc(op.b, ar, pb);
+	const int h = op.nn;
+	for (long i = 0; i < (long)op.k * h; i++) o.p[i * o.st] = 0.0f;
+	for (int i = 0; i < op.m; i++) {
+		const int t = ell_idx(r.p[(long)i * r.st], op.k);
+		if (t < 0) continue;
+		for (int j = 0; j < h; j++) {
+			float &y = o.p[((long)t * h + j) * o.st];
+			y = __fadd_rn(y, g.p[((long)i * h + j) * g.st]);
+		}
+	}
+}
+
+// memscan_t (runtime/tg_rt.h:517-578): memscan's derivatives by replaying the steps backwards
+// from the final memory, undoing each write. y is memscan's output, pv (tn, 4k + dv) the
+// entries (row, a, c, d) then the step's value, g y's adjoint. Out: dP (tn k 4) at 0, dM0 at
+// o1, dV at o2, the working memory at o3, zero-padded to n.
+__device__ void vm_memscan_t(const DOp &op, float *ar, const float *pb)
+{
+	Loc o = loc(op.out, ar, pb), y = loc(op.a, ar, pb), pv = loc(op.b, ar, pb), g = loc(op.c, ar, pb);
+	const long tn = op.m, k = op.k, rows = op.nn, dv = op.g, w = 4 * k + dv;
+	const long o1 = (tn * k * 4 + dv - 1) / dv * dv, o2 = o1 + rows * dv, o3 = o2 + tn * dv;
+	auto O = [&](long i) -> float & { return o.p[i * o.st]; };
+	for (long i = 0; i < op.n; i++) O(i) = 0.0f;
+	for (long i = 0; i < rows * dv; i++) O(o3 + i) = y.p[(2 * tn * dv + i) * y.st], O(o1 + i) = g.p[(2 * tn * dv + i) * g.st];
+	for (long st = tn - 1; st >= 0; st--) {
+		const long e = st * w, xo = e + 4 * k, rdo = (tn + st) * dv, gro = st * dv, grdo = (tn + st) * dv, dpo = st * k * 4,
+			   dxo = o2 + st * dv;
+		auto E = [&](long i) { return pv.p[(e + i) * pv.st]; };
+		auto X = [&](long j) { return pv.p[(xo + j) * pv.st]; };
+		auto RD = [&](long j) { return y.p[(rdo + j) * y.st]; };
+		auto GR = [&](long j) { return g.p[(gro + j) * g.st]; };
+		auto GRD = [&](long j) { return g.p[(grdo + j) * g.st]; };
+		for (long i = k - 1; i >= 0; i--) { // the memory as this step read it
+			const int t = ell_idx(E(i * 4), (int)rows);
+			const float c = E(i * 4 + 2);
+			if (t < 0 || c == 0.0f) continue;
+			for (long j = 0; j < dv; j++) O(o3 + t * dv + j) = __fsub_rn(O(o3 + t * dv + j), __fmul_rn(c, __fsub_rn(X(j), RD(j))));
+		}
+		for (long i = 0; i < k; i++) { // the writes: dc_i and the value's gradient
+			const int t = ell_idx(E(i * 4), (int)rows);
+			const float c = E(i * 4 + 2);
+			float dc = 0.0f;
+			if (t < 0) continue;
+			for (long j = 0; j < dv; j++) {
+				const float dm = O(o1 + t * dv + j);
+				dc = __fadd_rn(dc, __fmul_rn(dm, __fsub_rn(X(j), RD(j))));
+				O(dxo + j) = __fadd_rn(O(dxo + j), __fmul_rn(c, dm));
+			}
+			O(dpo + i * 4 + 2) = dc;
+		}
+		for (long i = 0; i < k; i++) { // the reads: da_i and dd_i
+			const int t = ell_idx(E(i * 4), (int)rows);
+			float da = 0.0f, dd = 0.0f;
+			if (t < 0) continue;
+			for (long j = 0; j < dv; j++) {
+				const float m = O(o3 + t * dv + j);
+				da = __fadd_rn(da, __fmul_rn(GR(j), m));
+				dd = __fadd_rn(dd, __fmul_rn(__fsub_rn(GRD(j), O(dxo + j)), m));
+			}
+			O(dpo + i * 4 + 1) = da, O(dpo + i * 4 + 3) = dd;
+		}
+		for (long i = 0; i < k; i++) { // the memory's adjoint before this step
+			const int t = ell_idx(E(i * 4), (int)rows);
+			const float a = E(i * 4 + 1), d = E(i * 4 + 3);
+			if (t < 0) continue;
+			for (long j = 0; j < dv; j++)
+				O(o1 + t * dv + j) = __fadd_rn(O(o1 + t * dv + j),
+							      __fadd_rn(__fmul_rn(a, GR(j)), __fmul_rn(d, __fsub_rn(GRD(j), O(dxo + j)))));
 		}
 	}
 }
@@ -464,6 +569,15 @@ __global__ void __launch_bounds__(VM_ROWS) vm_kernel(const DOp *__restrict__ tap
 			break;
 		case D_SUFMATCH:
 			if (act) vm_sufmatch(op, ar, blob);
+			break;
+		case D_SUMTO:
+			if (act) vm_sum_to(op, ar, blob);
+			break;
+		case D_TAKE_T:
+			if (act) vm_take_t(op, ar, blob);
+			break;
+		case D_MEMSCAN_T:
+			if (act) vm_memscan_t(op, ar, blob);
 			break;
 		case D_COPY:
 			if (act && op.out != op.a) {
@@ -759,6 +873,36 @@ static int plan_arena(Compiler &C)
 
 static int emit_block(Compiler &C, int from, int cnt, int depth);
 
+// The iteration space of sum_to (src/util.c:172-212, bcast_desc with one operand): x's
+// shape with its size-1 axes dropped and adjacent axes merged where the target's strides
+// allow (both broadcast, or contiguous); rank, dims and the target's strides into d.
+static void sumto_desc(const tg_cuda_value &x, const tg_cuda_value &tgt, DOp &d)
+{
+	const int r = x.rank;
+	int st[4];
+	long acc = 1;
+	for (int i = r - 1; i >= 0; i--) {
+		const int j = i - (r - tgt.rank), n = j >= 0 ? tgt.dim[j] : 1;
+		st[i] = n == 1 ? 0 : (int)acc;
+		acc *= n;
+	}
+	int nr = 0;
+	for (int i = 0; i < r; i++) {
+		if (x.dim[i] == 1) continue;
+		if (nr > 0) {
+			const int p = nr - 1;
+			if ((d.sa[p] == 0 && st[i] == 0) || (st[i] != 0 && (long)d.sa[p] == (long)st[i] * x.dim[i])) {
+				d.dims[p] *= x.dim[i];
+				d.sa[p] = st[i];
+				continue;
+			}
+		}
+		d.dims[nr] = x.dim[i], d.sa[nr] = st[i], nr++;
+	}
+	if (nr == 0) d.dims[0] = 1, d.sa[0] = 0, nr = 1;
+	d.rank = nr;
+}
+
 static void bcast(const tg_cuda_value &o, const tg_cuda_value &a, const tg_cuda_value &b, DOp &d)
 {
 	long n = numel(o), na = numel(a), nb = numel(b);
@@ -915,6 +1059,33 @@ static int emit_ins(Compiler &C, int idx, int depth)
 		d.k = 2 * P.dim[2] + (P.dim[3] == 4);
 		d.nn = M0.dim[0];
 		d.g = M0.dim[1];
+		T.push_back(d);
+		return 0;
+	}
+	case TG_CUDA_OP_SUM_TO: // src/vm.c:358-363
+		d.code = D_SUMTO;
+		d.n = (int)numel(vo);
+		sumto_desc(p->val[in.a[0]], p->val[in.a[1]], d);
+		T.push_back(d);
+		return 0;
+	case TG_CUDA_OP_TAKE_T: { // src/vm.c:320-323: take_t(r, g, w) -> the shape of w
+		const tg_cuda_value &W = p->val[in.a[2]];
+		d.code = D_TAKE_T;
+		d.m = p->val[in.a[0]].dim[0];
+		d.k = W.dim[0];
+		d.nn = (int)(numel(W) / W.dim[0]);
+		T.push_back(d);
+		return 0;
+	}
+	case TG_CUDA_OP_MEMSCAN_T: { // src/vm.c:351-357, src/util.c:455-467 memscan_dims
+		const tg_cuda_value &Y = p->val[in.a[0]], &PV = p->val[in.a[1]];
+		d.code = D_MEMSCAN_T;
+		d.c = C.L(in.a[2]);
+		d.g = Y.dim[1];
+		d.m = PV.dim[0] * PV.dim[1];
+		d.k = (PV.dim[2] - d.g) / 4;
+		d.nn = Y.dim[0] - 2 * d.m;
+		d.n = (int)numel(vo);
 		T.push_back(d);
 		return 0;
 	}
@@ -1316,6 +1487,32 @@ int Gen::op(int pc)
 		}
 		line("}");
 		return 0;
+	case D_SUMTO: { // the merged iteration space walked at generation time: constant indices
+		line("if (done == 0u) {");
+		for (int i = 0; i < o.n; i++) line(at(o.out, i) + " = 0.0f;");
+		const int r = o.rank, w = o.dims[r - 1];
+		long outer = 1, io = 0;
+		for (int i = 0; i < r - 1; i++) outer *= o.dims[i];
+		int idx[4] = { 0, 0, 0, 0 };
+		for (long i = 0; i < outer; i++) {
+			if (o.sa[r - 1]) {
+				for (int j = 0; j < w; j++) line(at(o.out, io + j) + " = __fadd_rn(" + at(o.out, io + j) + ", " + at(o.a, i * w + j) + ");");
+			} else {
+				std::string x = "{ float acc = 0.0f;";
+				for (int j = 0; j < w; j++) x += " acc = __fadd_rn(acc, " + at(o.a, i * w + j) + ");";
+				line(x + " " + at(o.out, io) + " = __fadd_rn(" + at(o.out, io) + ", acc); }");
+				stmts += w;
+			}
+			for (int q = r - 2; q >= 0; q--) {
+				io += o.sa[q];
+				if (++idx[q] < o.dims[q]) break;
+				io -= (long)o.sa[q] * o.dims[q];
+				idx[q] = 0;
+			}
+		}
+		line("}");
+		return 0;
+	}
 	case D_TOPK: // repeated selection in the order (value descending, index ascending)
 		line("if (done == 0u) {");
 		for (int r = 0; r < o.m; r++) {
@@ -1379,8 +1576,9 @@ static std::string gen_source(const Prog &P, std::string &why)
 	// their programs on vm_kernel.
 	for (const DOp &o : P.tape)
 		if (o.code == D_SCAN_BEGIN || o.code == D_SCAN_SLICE || o.code == D_SCAN_END || o.code == D_MEMSCAN ||
-		    o.code == D_SUFMATCH || (o.code == D_TAKE && o.a >= 0) || (o.code == D_SPMM && o.b >= 0)) {
-			why = "run-time arena index (scan, memscan, sufmatch, or take / spmm from a computed table)";
+		    o.code == D_MEMSCAN_T || o.code == D_SUFMATCH || o.code == D_TAKE_T || (o.code == D_TAKE && o.a >= 0) ||
+		    (o.code == D_SPMM && o.b >= 0)) {
+			why = "run-time arena index (scan, memscan, sufmatch, take_t, or take / spmm from a computed table)";
 			return "";
 		}
 	Gen G(P);

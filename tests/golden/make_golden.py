@@ -369,6 +369,9 @@ SPARSE_MEMORY = {
     "mlp_f32": ("tests/quant/mlp.tg", 300, "sparse", None),
     "mlp_q8": ("tests/quant/mlp.tg", 300, "sparse", ["--bits", "8"]),
     "mlp_q4": ("tests/quant/mlp.tg", 300, "sparse", ["--bits", "4"]),
+    "memscan_grad": ("tests/memory/scan_grad.tg", 200, "uniform", None),
+    "memscan4": ("tests/memory/scan4.tg", 200, "uniform", None),
+    "broadcast": ("tests/native/broadcast.tg", 200, "uniform", None),
 }
 # tests/run.sh:33-48: the inputs the reference's own suite runs these programs on
 SPARSE_MEMORY_ROWS = {
@@ -376,6 +379,9 @@ SPARSE_MEMORY_ROWS = {
     "topk_pad": [[2, 3, 1]],
     "memscan": [list(np.round(np.arange(-1.1, 1.25, 0.1), 1))],
     "sufmatch": [[1, 5, 2, 6, 3, 5, 1, 6, 2, 5, 3, 6, 1, -1, 2, 5, 3, 6, 9, 7, 1, 6, 2, 5]],
+    "memscan_grad": [list(np.round(np.arange(-1.1, 1.25, 0.1), 1))],
+    "memscan4": [list(np.round(np.arange(-1.1, 1.25, 0.1), 1))],
+    "broadcast": [[1, 2, 3, 0.5, -1, 2, 0] + list(np.round(np.arange(-1, 1.35, 0.1), 1))],
 }
 
 

@@ -19,7 +19,10 @@ from technograd_b200.batch import Batch, load_samples
 RTOL, ATOL = 1e-3, 1e-4
 NAMES = ["scan", "halt", "nested_grad", "window",
          # the sparse and memory models' ops: spmm (f32 and quantized tables), topk, memscan, sufmatch
-         "topk", "topk_pad", "memscan", "sufmatch", "mlp_f32", "mlp_q8", "mlp_q4"]
+         "topk", "topk_pad", "memscan", "sufmatch", "mlp_f32", "mlp_q8", "mlp_q4",
+         # gradients inside forward programs: memscan_t and take_t (tests/memory/scan_grad.tg,
+         # scan4.tg), sum_to with batched matmuls and rank-3 transposes (tests/native/broadcast.tg)
+         "memscan_grad", "memscan4", "broadcast"]
 
 
 def fixture(golden, name):

@@ -31,7 +31,20 @@ PROGRAMS = {
     "programs/mlp_f32.tgir": None,
     "programs/mlp_q8.tgir": None,
     "programs/mlp_q4.tgir": None,
+    "programs/memscan_grad.tgir": False,  # arenas past the register budget
+    "programs/memscan4.tgir": False,
+    "programs/broadcast.tgir": False,
 }
+
+# sum_to over the broadcast patterns of src/util.c:172-212: rows, columns, rank 3, scalars
+SUM_TO_CASES = [((3, 4), (1, 4)), ((3, 4), (3, 1)), ((2, 3, 4), (3, 1)), ((2, 3, 4), (4,)), ((2, 3, 4), (2, 1, 4)),
+                ((2, 3, 4), (1,)), ((2, 3, 4), (2, 3, 1))]
+
+
+def sum_to_src(xs, ts):
+    sh = lambda s: " ".join(map(str, s))
+    return (f"(tgir 1 (model st) (input x (f32 {sh(xs)})) (input y (f32 {sh(ts)}))"
+            f" (block (%2 (f32 {sh(ts)}) (sum_to x y))) (output %2))")
 
 # take from a param table by rounded index (runtime/tg_rt.h:316-322), with indices out of range
 TAKE_SRC = """(tgir 1
@@ -173,3 +186,21 @@ def test_host_pipeline_many_chunks(cuda, golden):
     # a second call reuses the staging buffers
     out2, steps2 = b.run(rows[:1000])
     assert np.array_equal(out2, out[:1000]) and np.array_equal(steps2, steps[:1000])
+
+
+@pytest.mark.parametrize("xs,ts", SUM_TO_CASES)
+def test_sum_to_generates(xs, ts):
+    rc, src = kernel_source(tgir.read(sum_to_src(xs, ts)), True)
+    assert rc == 0, _lib.lib().tg_cuda_error().decode()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("xs,ts", SUM_TO_CASES)
+def test_sum_to_on_generated_kernel(cuda, xs, ts, monkeypatch):
+    m = tgir.read(sum_to_src(xs, ts))
+    rows = np.random.default_rng(3).normal(size=(300, m.per)).astype(np.float32)
+    jit, (o1, _), (o2, _) = _both(m, rows, monkeypatch)
+    assert jit.specialized == (True, "")
+    assert np.array_equal(o1.view(np.uint32), o2.view(np.uint32))
+    want, _ = tgo.program_run(tgir.CProgram(m), rows)
+    np.testing.assert_allclose(o1, want, rtol=RTOL, atol=ATOL)
