@@ -188,6 +188,11 @@ struct Engine {
 	std::vector<std::unique_ptr<Block>> blocks;
 	DevBuf nf, u, nhi, nlo, xz, xs, xhi, xlo, dbc, ghi, glo, state, carry, status, io;
 	cudaEvent_t e0 = nullptr, e1 = nullptr;
+	// host rows: a second chunk buffer and copy streams, so that chunk c+1 comes in and
+	// chunk c-1 goes out while chunk c computes (created on the first host call)
+	DevBuf u2;
+	cudaStream_t cp_in = nullptr, cp_out = nullptr;
+	cudaEvent_t in_ready[2] = {}, done[2] = {}, wave_start = nullptr, out_done = nullptr;
 	long launches = 0;
 	// profiling: an event pair around every GEMM / scan launch, reused across calls
 	bool prof = false;
@@ -208,6 +213,10 @@ struct Engine {
 		}
 		if (e0) cudaEventDestroy(e0);
 		if (e1) cudaEventDestroy(e1);
+		for (cudaEvent_t e : { in_ready[0], in_ready[1], done[0], done[1], wave_start, out_done })
+			if (e) cudaEventDestroy(e);
+		if (cp_in) cudaStreamDestroy(cp_in);
+		if (cp_out) cudaStreamDestroy(cp_out);
 		if (st) cudaStreamDestroy(st);
 	}
 };
@@ -348,8 +357,9 @@ int launch_scan(Engine &g, Block &Y, int S, int Tc, int b)
 	return TG_CUDA_OK;
 }
 
-// One chunk of Tc steps of S sequences: u holds the chunk's rows; the output rows go to out.
-int run_chunk(Engine &g, int S, int Tc, int T, int t0, float *out)
+// One chunk of Tc steps of S sequences: u holds the chunk's rows (and is the residual stream the
+// blocks add into); the output rows go to out.
+int run_chunk(Engine &g, float *u, int S, int Tc, int T, int t0, float *out)
 {
 	int rc;
 	const int DM = g.DM, DI = g.DI;
@@ -358,7 +368,7 @@ int run_chunk(Engine &g, int S, int Tc, int T, int t0, float *out)
 	const unsigned warps_grid = (unsigned)((M * 32 + 255) / 256);
 	for (int b = 0; b < g.B; b++) {
 		Block &Y = *g.blocks[b];
-		k_ssm_norm<<<warps_grid, 256, 0, g.st>>>(g.u.as<float>(), M, DM, Y.norm.as<float>(), g.eps, g.nhi.as<__nv_bfloat16>(),
+		k_ssm_norm<<<warps_grid, 256, 0, g.st>>>(u, M, DM, Y.norm.as<float>(), g.eps, g.nhi.as<__nv_bfloat16>(),
 							g.nlo.as<__nv_bfloat16>(), nullptr, Tc, T, t0);
 		TGC_LAUNCH_CHECK();
 		GemmOperands op;
@@ -386,14 +396,82 @@ int run_chunk(Engine &g, int S, int Tc, int T, int t0, float *out)
 		GemmOperands oo;
 		oo.a[0] = g.ghi.p, oo.a[1] = g.glo.p, oo.b[0] = Y.wo.p, oo.lda = DI, oo.ldb = DI;
 		GemmArgs po = gemm_args((int)M, DM, DI, status);
-		po.epi = EPI_ADD, po.scale = Y.so.as<float>(), po.out = g.u.as<float>(), po.ldo = DM;
+		po.epi = EPI_ADD, po.scale = Y.so.as<float>(), po.out = u, po.ldo = DM;
 		if ((rc = gemm_marked(g, oo, po, DM))) return rc;
 		g.launches += 6;
 	}
-	k_ssm_norm<<<warps_grid, 256, 0, g.st>>>(g.u.as<float>(), M, DM, g.nf.as<float>(), g.eps, nullptr, nullptr, out, Tc, T, t0);
+	k_ssm_norm<<<warps_grid, 256, 0, g.st>>>(u, M, DM, g.nf.as<float>(), g.eps, nullptr, nullptr, out, Tc, T, t0);
 	TGC_LAUNCH_CHECK();
 	g.launches += 1;
 	return TG_CUDA_OK;
+}
+
+// The host path's copy streams and events, made on first use.
+int host_pipe(Engine &g)
+{
+	if (!g.cp_in) TGC_CUDA(cudaStreamCreateWithFlags(&g.cp_in, cudaStreamNonBlocking));
+	if (!g.cp_out) TGC_CUDA(cudaStreamCreateWithFlags(&g.cp_out, cudaStreamNonBlocking));
+	for (cudaEvent_t *e : { &g.in_ready[0], &g.in_ready[1], &g.done[0], &g.done[1], &g.wave_start, &g.out_done })
+		if (!*e) TGC_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+	return TG_CUDA_OK;
+}
+
+// Host rows: chunk c computes in buffer c % 2 on the compute stream while chunk c+1's rows
+// come into the other buffer on cp_in (once chunk c-1 has finished with it) and chunk c-1's
+// output rows go back on cp_out. The compute stream ends the wave waiting for the last copy,
+// so a synchronize on it covers the copies, and the next wave reuses the buffers safely.
+int run_wave_host(Engine &g, const float *u, int S, int T, float *out)
+{
+	int rc;
+	const int DM = g.DM;
+	const size_t pitch = (size_t)T * DM * 4;
+	if ((rc = host_pipe(g)) || (rc = g.u2.ensure(g.u.bytes, g.dev)) || (rc = g.io.ensure((size_t)S * pitch, g.dev)))
+		return rc;
+	float *ub[2] = { g.u.as<float>(), g.u2.as<float>() };
+	float *dout = g.io.as<float>();
+	const int nch = (T + g.chunk - 1) / g.chunk;
+	auto rows = [&](int c) { return std::min(g.chunk, T - c * g.chunk); };
+	auto copy_in = [&](int c) -> int { // rows (s, t0 .. t0 + Tc) of every sequence -> the chunk, sequence-major
+		const size_t w = (size_t)rows(c) * DM * 4;
+		TGC_CUDA(cudaMemcpy2DAsync(ub[c & 1], w, u + (size_t)c * g.chunk * DM, pitch, w, S, cudaMemcpyHostToDevice, g.cp_in));
+		TGC_CUDA(cudaEventRecord(g.in_ready[c & 1], g.cp_in));
+		return TG_CUDA_OK;
+	};
+	auto copy_out = [&](int c) -> int {
+		const size_t off = (size_t)c * g.chunk * DM;
+		TGC_CUDA(cudaStreamWaitEvent(g.cp_out, g.done[c & 1], 0));
+		TGC_CUDA(cudaMemcpy2DAsync(out + off, pitch, dout + off, pitch, (size_t)rows(c) * DM * 4, S, cudaMemcpyDeviceToHost,
+					   g.cp_out));
+		return TG_CUDA_OK;
+	};
+	auto body = [&]() -> int {
+		int rc;
+		TGC_CUDA(cudaEventRecord(g.wave_start, g.st)); // the previous wave is done with both buffers
+		TGC_CUDA(cudaStreamWaitEvent(g.cp_in, g.wave_start, 0));
+		if ((rc = copy_in(0))) return rc;
+		for (int c = 0; c < nch; c++) {
+			TGC_CUDA(cudaStreamWaitEvent(g.st, g.in_ready[c & 1], 0));
+			if ((rc = run_chunk(g, ub[c & 1], S, rows(c), T, c * g.chunk, dout))) return rc;
+			TGC_CUDA(cudaEventRecord(g.done[c & 1], g.st));
+			if (c + 1 < nch) {
+				// the other buffer was chunk c-1's: its done event is that chunk's latest record
+				if (c >= 1) TGC_CUDA(cudaStreamWaitEvent(g.cp_in, g.done[(c + 1) & 1], 0));
+				if ((rc = copy_in(c + 1))) return rc;
+			}
+			// chunk c-1's rows leave only now, after chunk c is queued: a pageable destination
+			// makes the copy call wait for its chunk, and the GPU has chunk c to run meanwhile
+			if (c >= 1 && (rc = copy_out(c - 1))) return rc;
+		}
+		if ((rc = copy_out(nch - 1))) return rc;
+		TGC_CUDA(cudaEventRecord(g.out_done, g.cp_out));
+		TGC_CUDA(cudaStreamWaitEvent(g.st, g.out_done, 0));
+		return TG_CUDA_OK;
+	};
+	if ((rc = body())) { // no copy may still use the caller's buffers after an error return
+		cudaStreamSynchronize(g.cp_in);
+		cudaStreamSynchronize(g.cp_out);
+	}
+	return rc;
 }
 
 // nseq sequences of T steps: u, out [nseq][T][DM], on the device (device == true) or host.
@@ -403,19 +481,14 @@ int run_wave(Engine &g, const float *u, int S, int T, float *out, bool device)
 	const int DM = g.DM, DI = g.DI, DS = g.DS;
 	TGC_CUDA(cudaMemsetAsync(g.state.p, 0, (size_t)g.B * g.max_seqs * DI * DS * 4, g.st));
 	TGC_CUDA(cudaMemsetAsync(g.carry.p, 0, (size_t)g.B * g.max_seqs * 3 * DI * 4, g.st));
-	float *dout = out;
-	if (!device) { // the output rows of the wave gather in a device buffer, then one copy
-		if ((rc = g.io.ensure((size_t)S * T * DM * 4, g.dev))) return rc;
-		dout = g.io.as<float>();
-	}
+	if (!device) return run_wave_host(g, u, S, T, out);
 	for (int t0 = 0; t0 < T; t0 += g.chunk) {
 		const int Tc = std::min(g.chunk, T - t0);
 		// rows (s, t0 .. t0 + Tc) of every sequence -> the chunk, sequence-major
 		TGC_CUDA(cudaMemcpy2DAsync(g.u.p, (size_t)Tc * DM * 4, u + (size_t)t0 * DM, (size_t)T * DM * 4, (size_t)Tc * DM * 4, S,
-					   device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, g.st));
-		if ((rc = run_chunk(g, S, Tc, T, t0, dout))) return rc;
+					   cudaMemcpyDeviceToDevice, g.st));
+		if ((rc = run_chunk(g, g.u.as<float>(), S, Tc, T, t0, out))) return rc;
 	}
-	if (!device) TGC_CUDA(cudaMemcpyAsync(out, dout, (size_t)S * T * DM * 4, cudaMemcpyDeviceToHost, g.st));
 	return TG_CUDA_OK;
 }
 
