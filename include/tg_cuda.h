@@ -16,6 +16,8 @@
  *                         emits (per-head tg_matmul_qb, rmsnorm, softmax, take), run per sequence
  *   tg_cuda_quantize_rtn <- the RTN branch of quantize_param, src/quant.c:176-200,258-316
  *   tg_cuda_batcher_*  <- vm_run_into per request line in run_line, src/serve.c:129-149
+ *   tg_cuda_host_register <- no counterpart: pins the batch branch's sample array (load_samples,
+ *                         src/main.c:175-214) and output block for direct DMA
  */
 #ifndef TG_CUDA_H
 #define TG_CUDA_H
@@ -168,6 +170,17 @@ int tg_cuda_load(const tg_cuda_program *p, tg_cuda_model **out);
  * call blocks until out and steps are written. Rows are sharded across the
  * selected GPUs in contiguous blocks. */
 int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int per, float *out, int n, int *steps, int nt);
+/* Page-lock [p, p + bytes) of the caller's host memory for every selected GPU
+ * (after tg_cuda_init). A tg_cuda_batch whose input rows, output rows and steps
+ * each lie inside one registered range copies straight between those buffers and
+ * the GPUs; otherwise it goes through the library's own page-locked staging
+ * buffers. For long-lived buffers such as the batch branch's sample array and
+ * output block (src/main.c:400-444); registration costs far more than one copy.
+ * Unregister (by the same p) before the memory is freed, and not while a call
+ * uses it; tg_cuda_shutdown unregisters what is left. EINVAL for a range that
+ * overlaps one already registered. */
+int tg_cuda_host_register(void *p, size_t bytes);
+int tg_cuda_host_unregister(void *p);
 /* Same, with every buffer already on device 0 of the selection (device pointers,
  * asynchronous on stream). Used for measurements with inputs resident in HBM. */
 int tg_cuda_batch_device(tg_cuda_model *g, const float *all, long rows, float *out, int *steps, void *stream);

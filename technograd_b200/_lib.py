@@ -25,6 +25,7 @@ PARAM, INPUT, TMP, STATE = 0, 1, 2, 3
 SYMBOLS = ["tg_cuda_error", "tg_cuda_init", "tg_cuda_ngpus", "tg_cuda_selftest_wait", "tg_cuda_shutdown", "tg_cuda_matmul_q",
            "tg_cuda_matmul_qb_noalloc",
            "tg_cuda_quantize_rtn", "tg_cuda_gptq_prepare", "tg_cuda_quantize_gptq", "tg_cuda_gptq_free", "tg_cuda_load", "tg_cuda_batch", "tg_cuda_batch_device", "tg_cuda_free",
+           "tg_cuda_host_register", "tg_cuda_host_unregister",
            "tg_cuda_model_jit", "tg_cuda_program_kernel", "tg_cuda_batcher_new", "tg_cuda_batcher_run",
            "tg_cuda_batcher_stats", "tg_cuda_batcher_free",
            "tg_cuda_lm_load", "tg_cuda_lm_forward", "tg_cuda_lm_generate", "tg_cuda_lm_free", "tg_cuda_lm_profile",
@@ -127,6 +128,8 @@ def lib() -> C.CDLL:
             "tg_cuda_batch": ([vp, vp, l, i, vp, i, vp, i], i),
             "tg_cuda_batch_device": ([vp, vp, l, vp, vp, vp], i),
             "tg_cuda_free": ([vp], None),
+            "tg_cuda_host_register": ([vp, C.c_size_t], i),
+            "tg_cuda_host_unregister": ([vp], i),
             "tg_cuda_model_jit": ([vp, C.c_char_p, i], i),
             "tg_cuda_batcher_new": ([vp, i, i, C.POINTER(vp)], i),
             "tg_cuda_batcher_run": ([vp, vp, vp, vp], i),
@@ -167,3 +170,29 @@ def init(ngpus: int = 0, devices=None) -> int:
     else:
         check(L.tg_cuda_init(ngpus, None))
     return L.tg_cuda_ngpus()
+
+
+class HostRegistered:
+    """Page-locks numpy arrays for direct DMA by tg_cuda_batch for the length of a `with`
+    block (tg_cuda_host_register / tg_cuda_host_unregister)."""
+
+    def __init__(self, *arrays):
+        self.arrays = [a for a in arrays if a is not None and a.nbytes]
+        self.done = []
+
+    def __enter__(self):
+        try:
+            for a in self.arrays:
+                if not a.flags.c_contiguous:
+                    raise ValueError("tg_cuda_host_register: the array must be C-contiguous")
+                check(lib().tg_cuda_host_register(a.ctypes.data, a.nbytes))
+                self.done.append(a)
+        except BaseException:
+            self.__exit__(None, None, None)
+            raise
+        return self
+
+    def __exit__(self, *exc):
+        while self.done:
+            check(lib().tg_cuda_host_unregister(self.done.pop().ctypes.data))
+        return False

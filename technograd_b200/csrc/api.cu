@@ -3,6 +3,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <map>
 #include <mutex>
 
 #include "common.cuh"
@@ -32,6 +33,22 @@ bool fault(const char *step)
 
 std::vector<Device> &devices() { return g_devs; }
 bool inited() { return !g_devs.empty(); }
+
+// Caller ranges page-locked through tg_cuda_host_register: start -> bytes.
+static std::map<uintptr_t, size_t> g_host;
+static std::mutex g_host_mu;
+
+bool host_registered(const void *p, size_t n)
+{
+	if (n == 0) return true;
+	const uintptr_t a = (uintptr_t)p;
+	std::lock_guard<std::mutex> lk(g_host_mu);
+	auto it = g_host.upper_bound(a);
+	if (it == g_host.begin()) return false;
+	--it;
+	const size_t off = a - it->first;
+	return off < it->second && n <= it->second - off;
+}
 
 int DevBuf::alloc(size_t n, int device)
 {
@@ -113,8 +130,44 @@ extern "C" int tg_cuda_init(int ngpus, const int *devs)
 
 extern "C" int tg_cuda_ngpus(void) { return (int)g_devs.size(); }
 
+extern "C" int tg_cuda_host_register(void *p, size_t bytes)
+{
+	clear_err();
+	if (!p || bytes == 0) return set_err(TG_CUDA_EINVAL, "tg_cuda_host_register: NULL or empty range");
+	if (!inited()) return set_err(TG_CUDA_ENODEV, "tg_cuda_host_register: call tg_cuda_init first");
+	std::lock_guard<std::mutex> lk(g_host_mu);
+	cudaError_t e = cudaHostRegister(p, bytes, cudaHostRegisterPortable);
+	if (e != cudaSuccess) {
+		cudaGetLastError();
+		return set_err(e == cudaErrorHostMemoryAlreadyRegistered ? TG_CUDA_EINVAL : TG_CUDA_ECUDA,
+			       "tg_cuda_host_register(%zu bytes): %s", bytes, cudaGetErrorString(e));
+	}
+	g_host[(uintptr_t)p] = bytes;
+	return TG_CUDA_OK;
+}
+
+extern "C" int tg_cuda_host_unregister(void *p)
+{
+	clear_err();
+	std::lock_guard<std::mutex> lk(g_host_mu);
+	auto it = g_host.find((uintptr_t)p);
+	if (it == g_host.end()) return set_err(TG_CUDA_EINVAL, "tg_cuda_host_unregister: %p is not the start of a registered range", p);
+	g_host.erase(it);
+	cudaError_t e = cudaHostUnregister(p);
+	if (e != cudaSuccess) {
+		cudaGetLastError();
+		return set_err(TG_CUDA_ECUDA, "cudaHostUnregister: %s", cudaGetErrorString(e));
+	}
+	return TG_CUDA_OK;
+}
+
 extern "C" void tg_cuda_shutdown(void)
 {
+	{
+		std::lock_guard<std::mutex> lk(g_host_mu);
+		for (auto &r : g_host) cudaHostUnregister((void *)r.first);
+		g_host.clear();
+	}
 	std::lock_guard<std::mutex> lk(g_mu);
 	for (auto &d : g_devs) {
 		cudaSetDevice(d.id);

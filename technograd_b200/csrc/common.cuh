@@ -34,6 +34,9 @@ int model_shape(const tg_cuda_model *g, int *per, int *nout, int *nthink);
 std::vector<Device> &devices();
 bool inited();
 
+// True when [p, p + n) lies inside one range registered with tg_cuda_host_register.
+bool host_registered(const void *p, size_t n);
+
 #define TGC_CUDA(call)                                                                                    \
 	do {                                                                                              \
 		cudaError_t e_ = (call);                                                                  \

@@ -1860,7 +1860,10 @@ constexpr size_t BATCH_CHUNK_BYTES = 4 << 20; // input bytes per pipeline chunk
 // device in chunks of ~4 MB of input on two alternating slots: while the GPU copies in,
 // runs and copies out chunk k on one slot's stream, the host copies chunk k-1's results
 // out of the other slot's pinned buffers and chunk k+1's rows into them. Output rows
-// land at their own offsets, so the gather keeps input order.
+// land at their own offsets, so the gather keeps input order. When the caller's buffers
+// are page-locked (tg_cuda_host_register) the staging copies drop out: each chunk is
+// copied in, run and copied out on its slot's stream straight from and to the caller's
+// memory, and the host thread only queues work and waits at the end.
 extern "C" int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int per, float *out, int n, int *steps, int nt)
 {
 	clear_err();
@@ -1872,6 +1875,9 @@ extern "C" int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int 
 		return set_err(TG_CUDA_EINVAL, "tg_cuda_batch: steps needs %d slots per row", P.nthink);
 	if (rows == 0) return TG_CUDA_OK;
 	const bool want_steps = nt > 0 && steps;
+	const bool direct = host_registered(all, (size_t)rows * per * sizeof(float)) &&
+			    host_registered(out, (size_t)rows * n * sizeof(float)) &&
+			    (!want_steps || host_registered(steps, (size_t)rows * nt * sizeof(int)));
 	size_t G = devices().size();
 	std::vector<int> rcs(G, 0);
 	std::vector<std::string> errs(G);
@@ -1911,13 +1917,37 @@ extern "C" int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int 
 			if (!S.done && cudaEventCreateWithFlags(&S.done, cudaEventDisableTiming) != cudaSuccess)
 				return done(set_err(TG_CUDA_ECUDA, "cudaEventCreate failed"));
 			const long m = std::min(chunk, cnt);
-			if ((rc = S.hin.ensure((size_t)m * per * sizeof(float))) || (rc = S.hout.ensure((size_t)m * n * sizeof(float))) ||
-			    (rc = S.hsteps.ensure((size_t)m * std::max(nt, 1) * sizeof(int))) ||
-			    (rc = S.din.ensure((size_t)m * per * sizeof(float), dv.id)) || (rc = S.dout.ensure((size_t)m * n * sizeof(float), dv.id)) ||
+			if (!direct && ((rc = S.hin.ensure((size_t)m * per * sizeof(float))) || (rc = S.hout.ensure((size_t)m * n * sizeof(float))) ||
+					(rc = S.hsteps.ensure((size_t)m * std::max(nt, 1) * sizeof(int)))))
+				return done(rc);
+			if ((rc = S.din.ensure((size_t)m * per * sizeof(float), dv.id)) || (rc = S.dout.ensure((size_t)m * n * sizeof(float), dv.id)) ||
 			    (rc = S.dsteps.ensure((size_t)m * std::max(nt, 1) * sizeof(int), dv.id)))
 				return done(rc);
 		}
 		if (fault("h2d")) return done(set_err(TG_CUDA_EFAULT, "injected copy failure (TG_CUDA_FAULT=h2d)"));
+		if (direct) {
+			for (long c0 = 0, k = 0; c0 < cnt; c0 += chunk, k++) {
+				Slot &S = D.slot[k & 1];
+				const long m = std::min(chunk, cnt - c0);
+				const size_t r0 = (size_t)(lo + c0);
+				cudaError_t e = cudaMemcpyAsync(S.din.p, all + r0 * per, (size_t)m * per * sizeof(float), cudaMemcpyHostToDevice, S.st);
+				if (e == cudaSuccess && nt > 0) e = cudaMemsetAsync(S.dsteps.p, 0, (size_t)m * nt * sizeof(int), S.st);
+				if (e != cudaSuccess) return done(set_err(TG_CUDA_ECUDA, "H2D: %s", cudaGetErrorString(e)));
+				if ((rc = run_rows(g->m, di, S.din.as<float>(), m, S.dout.as<float>(), nt > 0 ? S.dsteps.as<int>() : nullptr, nt,
+						   S.st)))
+					return done(rc);
+				if (fault("gather")) return done(set_err(TG_CUDA_EFAULT, "injected gather failure (TG_CUDA_FAULT=gather)"));
+				e = cudaMemcpyAsync(out + r0 * n, S.dout.p, (size_t)m * n * sizeof(float), cudaMemcpyDeviceToHost, S.st);
+				if (e == cudaSuccess && want_steps)
+					e = cudaMemcpyAsync(steps + r0 * nt, S.dsteps.p, (size_t)m * nt * sizeof(int), cudaMemcpyDeviceToHost, S.st);
+				if (e != cudaSuccess) return done(set_err(TG_CUDA_ECUDA, "device %d: %s", dv.id, cudaGetErrorString(e)));
+			}
+			for (Slot &S : D.slot) {
+				cudaError_t e = cudaStreamSynchronize(S.st);
+				if (e != cudaSuccess) return done(set_err(TG_CUDA_ECUDA, "device %d: %s", dv.id, cudaGetErrorString(e)));
+			}
+			return done(TG_CUDA_OK);
+		}
 		for (long c0 = 0, k = 0; c0 < cnt; c0 += chunk, k++) {
 			Slot &S = D.slot[k & 1];
 			if (S.busy && (rc = finish(S))) return done(rc);

@@ -1,5 +1,6 @@
 """The C ABI: the library loads and exports every entry point include/tg_cuda.h
 declares; calls that need a device fail cleanly without one."""
+import ctypes as C
 import os
 import re
 
@@ -38,3 +39,17 @@ def test_no_device_is_an_error_not_a_crash():
     assert rc == _lib.ENODEV
     assert L.tg_cuda_error()
     assert L.tg_cuda_ngpus() == 0
+
+
+def test_host_register_checks_arguments_first():
+    """No GPU needed: a NULL or empty range is EINVAL, a range before tg_cuda_init is
+    ENODEV, an unknown pointer cannot be unregistered."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    L = _lib.lib()
+    assert L.tg_cuda_host_register(None, 64) == _lib.EINVAL
+    buf = (C.c_char * 64)()
+    assert L.tg_cuda_host_register(C.addressof(buf), 0) == _lib.EINVAL
+    assert L.tg_cuda_host_register(C.addressof(buf), 64) == _lib.ENODEV
+    assert L.tg_cuda_host_unregister(C.addressof(buf)) == _lib.EINVAL

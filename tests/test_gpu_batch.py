@@ -98,3 +98,35 @@ def test_empty_and_single_rows(cuda, golden):
         out, steps = b.run(rows)
         want, want_steps, margin = tgo.program_run(tgir.CProgram(m), rows, margins=True)
         check_rows(out, steps, want, want_steps, margin)
+
+
+def test_registered_host_buffers_match_staged(cuda, golden):
+    """Caller buffers page-locked with tg_cuda_host_register are copied straight to and
+    from the GPU: the same bits as through the staging buffers. 300,001 rows span two full
+    4 MB input chunks per slot and a partial one; a buffer only partly registered goes
+    through staging; an overlapping registration and an unknown pointer are refused."""
+    m = tgir.load(os.path.join(golden, "latent_reasoner.q8.tgir"))
+    b = Batch(m)
+    rows = np.random.default_rng(7).uniform(-2, 2, size=(300001, 8)).astype(np.float32)
+    want, want_steps = b.run(rows)
+    L = _lib.lib()
+
+    def call(o, s):
+        _lib.check(L.tg_cuda_batch(b.handle, rows.ctypes.data, rows.shape[0], 8, o.ctypes.data, 4, s.ctypes.data, 1))
+
+    out = np.full((rows.shape[0], 4), np.nan, np.float32)
+    steps = np.full((rows.shape[0], 1), -1, np.int32)
+    with _lib.HostRegistered(rows, out, steps):
+        call(out, steps)
+        with pytest.raises(_lib.TgCudaError) as e:
+            _lib.check(L.tg_cuda_host_register(rows.ctypes.data + 4096, 64))
+        assert e.value.status == _lib.EINVAL
+    assert np.array_equal(out, want) and np.array_equal(steps, want_steps)
+    out2 = np.full_like(out, np.nan)
+    steps2 = np.full_like(steps, -1)
+    with _lib.HostRegistered(rows[:150000], out2, steps2):
+        call(out2, steps2)
+    assert np.array_equal(out2, want) and np.array_equal(steps2, want_steps)
+    with pytest.raises(_lib.TgCudaError) as e:
+        _lib.check(L.tg_cuda_host_unregister(rows.ctypes.data))
+    assert e.value.status == _lib.EINVAL
