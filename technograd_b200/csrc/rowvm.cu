@@ -706,7 +706,7 @@ struct Model {
 		DevBuf tape, blob, inloc, inlen, gar;
 		long gar_rows = 0;
 		JitModule jit; // the program's specialised kernel on this device
-		Slot slot[2];  // tg_cuda_batch pipeline
+		Slot slot[3];  // tg_cuda_batch pipeline: two with staging, three straight from the caller's buffers
 		std::mutex mu; // one tg_cuda_batch at a time on this device's slots
 	};
 	std::vector<std::unique_ptr<PerDev>> dev;
@@ -1854,7 +1854,8 @@ static void par_copy(void *dst, const void *src, size_t n)
 	pool.copy(dst, src, n, parts);
 }
 
-constexpr size_t BATCH_CHUNK_BYTES = 4 << 20; // input bytes per pipeline chunk
+constexpr size_t BATCH_CHUNK_BYTES = 4 << 20;  // input bytes per pipeline chunk through staging
+constexpr size_t DIRECT_CHUNK_BYTES = 2 << 20; // ... and straight from page-locked caller buffers
 
 // One host thread per GPU over its contiguous shard of rows. The shard goes through the
 // device in chunks of ~4 MB of input on two alternating slots: while the GPU copies in,
@@ -1888,7 +1889,11 @@ extern "C" int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int 
 		cudaSetDevice(dv.id);
 		auto &D = *g->m.dev[di];
 		std::lock_guard<std::mutex> lk(D.mu);
-		const long chunk = std::max<long>(VM_ROWS, (long)(BATCH_CHUNK_BYTES / ((size_t)per * sizeof(float))) / VM_ROWS * VM_ROWS);
+		// direct: three slots keep the copy-in engine busy (a slot's next chunk waits for its
+		// previous copy-out), smaller chunks shorten the pipeline's fill and drain
+		const int nslot = direct ? 3 : 2;
+		const long chunk = std::max<long>(
+			VM_ROWS, (long)((direct ? DIRECT_CHUNK_BYTES : BATCH_CHUNK_BYTES) / ((size_t)per * sizeof(float))) / VM_ROWS * VM_ROWS);
 		auto drain = [&] {
 			for (Slot &S : D.slot) {
 				if (S.st) cudaStreamSynchronize(S.st);
@@ -1911,7 +1916,8 @@ extern "C" int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int 
 			return TG_CUDA_OK;
 		};
 		int rc;
-		for (Slot &S : D.slot) {
+		for (int si = 0; si < nslot; si++) {
+			Slot &S = D.slot[si];
 			if (!S.st && cudaStreamCreateWithFlags(&S.st, cudaStreamNonBlocking) != cudaSuccess)
 				return done(set_err(TG_CUDA_ECUDA, "cudaStreamCreate failed"));
 			if (!S.done && cudaEventCreateWithFlags(&S.done, cudaEventDisableTiming) != cudaSuccess)
@@ -1927,7 +1933,7 @@ extern "C" int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int 
 		if (fault("h2d")) return done(set_err(TG_CUDA_EFAULT, "injected copy failure (TG_CUDA_FAULT=h2d)"));
 		if (direct) {
 			for (long c0 = 0, k = 0; c0 < cnt; c0 += chunk, k++) {
-				Slot &S = D.slot[k & 1];
+				Slot &S = D.slot[k % nslot];
 				const long m = std::min(chunk, cnt - c0);
 				const size_t r0 = (size_t)(lo + c0);
 				cudaError_t e = cudaMemcpyAsync(S.din.p, all + r0 * per, (size_t)m * per * sizeof(float), cudaMemcpyHostToDevice, S.st);
@@ -1942,8 +1948,8 @@ extern "C" int tg_cuda_batch(tg_cuda_model *g, const float *all, long rows, int 
 					e = cudaMemcpyAsync(steps + r0 * nt, S.dsteps.p, (size_t)m * nt * sizeof(int), cudaMemcpyDeviceToHost, S.st);
 				if (e != cudaSuccess) return done(set_err(TG_CUDA_ECUDA, "device %d: %s", dv.id, cudaGetErrorString(e)));
 			}
-			for (Slot &S : D.slot) {
-				cudaError_t e = cudaStreamSynchronize(S.st);
+			for (int si = 0; si < nslot; si++) {
+				cudaError_t e = cudaStreamSynchronize(D.slot[si].st);
 				if (e != cudaSuccess) return done(set_err(TG_CUDA_ECUDA, "device %d: %s", dv.id, cudaGetErrorString(e)));
 			}
 			return done(TG_CUDA_OK);

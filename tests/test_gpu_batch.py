@@ -102,9 +102,10 @@ def test_empty_and_single_rows(cuda, golden):
 
 def test_registered_host_buffers_match_staged(cuda, golden):
     """Caller buffers page-locked with tg_cuda_host_register are copied straight to and
-    from the GPU: the same bits as through the staging buffers. 300,001 rows span two full
-    4 MB input chunks per slot and a partial one; a buffer only partly registered goes
-    through staging; an overlapping registration and an unknown pointer are refused."""
+    from the GPU: the same bits as through the staging buffers. 300,001 rows are four full
+    2 MB input chunks and a partial one, so each of the three slots is reused; a buffer only
+    partly registered goes through staging; an overlapping registration and an unknown
+    pointer are refused."""
     m = tgir.load(os.path.join(golden, "latent_reasoner.q8.tgir"))
     b = Batch(m)
     rows = np.random.default_rng(7).uniform(-2, 2, size=(300001, 8)).astype(np.float32)
