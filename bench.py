@@ -1,6 +1,6 @@
 """Benchmark of the batch backend (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|lr|prefill|gemm] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|lr|prefill|gemm|ssm] [--impl ours|reference]
 
 Workloads (seeded synthetic inputs of the stated shapes):
   decode  config 5, the headline: Qwen3-0.6B architecture (28 layers, hidden 1024,
@@ -354,6 +354,9 @@ def cpu_baseline_prefill(built, T: int = 16):
 
 # ---- config 3: stacked selective-SSM blocks ------------------------------------------------------
 SSM_SEQS, SSM_T = 1024, 4096
+# DRAM bytes / algorithmic bytes of one k_ssm_scan launch, from ncu (91.3 MB of 103.8 MB on the
+# 256 x 512 case: the g writes are partly still in L2 when the kernel ends)
+SSM_SCAN_TRAFFIC_RATIO = 91.3 / 103.8
 
 
 def ssm_inputs(seqs: int, T: int, lo: int, hi: int) -> np.ndarray:
@@ -421,6 +424,9 @@ def bench_ssm(args, world, rank, local):
     scan_tf = sum(s["scan_flops"] for s in stats) / (scan_ms / 1e3) / 1e12
     gemm_tf = sum(s["gemm_flops"] for s in stats) / (gemm_ms / 1e3) / 1e12
     full = (seqs, T, cfg["blocks"]) == (SSM_SEQS, SSM_T, 4)
+    # k_ssm_scan reads xs, z and the [dt | B | C] rows and writes g as bf16 hi/lo, per launch
+    # (S sequences x one chunk of 64 steps)
+    scan_bytes = float(S * 64 * (cfg["d_inner"] * 12 + (cfg["dt_rank"] + 2 * cfg["d_state"]) * 4))
     line = {
         "metric": "int8 stacked selective-SSM tokens/s (config 3)", "value": world * tok * args.steps / t_dev,
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
@@ -430,11 +436,13 @@ def bench_ssm(args, world, rank, local):
                    if full else f"REDUCED config3 shape: {seqs} seqs x {T} steps, {cfg['blocks']} blocks",
                    "seqs_per_gpu": S, "steps_per_seq": T, "chunk": 64,
                    "share_of_step": {"scan": scan_ms / tot_ms, "gemm": gemm_ms / tot_ms}, "gemm_tflops": gemm_tf,
-                   "l2": "inputs larger than L2 (4.3 GB in, 4.3 GB out per step)", "build_s": t_build},
+                   "l2": f"inputs larger than L2 ({u.nbytes / 1e9:.2f} GB in, {u.nbytes / 1e9:.2f} GB out per step)",
+                   "build_s": t_build},
         "roofline": {"kernel": "k_ssm_scan (FP32 pipe + SFU)", "bound": "fp32", "achieved": scan_tf,
                      "peak": FP32_NOMINAL_TFLOPS, "unit": "TFLOP/s", "frac": scan_tf / FP32_NOMINAL_TFLOPS,
                      "peak_source": "nominal FP32 SIMT (148 SMs x 128 lanes x FMA x 1965 MHz); not in MEASURED_PEAKS",
-                     "traffic": None},
+                     "traffic": SSM_SCAN_TRAFFIC_RATIO * scan_bytes, "bytes_per_launch": scan_bytes,
+                     "traffic_source": "ncu small-case ratio (profiles/k_ssm_scan_config3_small.md) x algorithmic bytes per launch"},
         "e2e": {"value": world * tok * args.steps / t_wall, "unit": "tokens/s", "h2d_bytes_per_step": u.nbytes,
                 "d2h_bytes_per_step": u.nbytes},
         "gpu_launches": int(sum(s["launches"] for s in stats)), "clocks": clocks,
