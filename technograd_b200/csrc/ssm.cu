@@ -66,20 +66,21 @@ __global__ void k_ssm_norm(const float *__restrict__ x, long M, int D, const flo
 }
 
 // Causal conv + silu. Thread = (sequence, channel); carries c[3][DI] per sequence hold
-// x_{t-1}, x_{t-2}, x_{t-3} across chunks. xz rows: [x (DI) | z (DI)].
+// x_{t-1}, x_{t-2}, x_{t-3} across chunks. xz rows: [x (DI) | z (DI)]. The inputs of 8
+// steps are loaded before any of them is used: one load in flight per thread would leave
+// HBM latency-bound at these thread counts.
 __global__ void k_ssm_conv(const float *__restrict__ xz, int S, int Tc, int DI, const float *__restrict__ cw,
 			   const float *__restrict__ cb, float *__restrict__ carry, float *__restrict__ xs,
 			   __nv_bfloat16 *__restrict__ hi, __nv_bfloat16 *__restrict__ lo)
 {
+	constexpr int U = 8;
 	long tid = (long)blockIdx.x * blockDim.x + threadIdx.x;
 	if (tid >= (long)S * DI) return;
 	const int s = (int)(tid / DI), c = (int)(tid % DI);
 	float *cr = carry + (long)s * 3 * DI;
 	float c1 = cr[c], c2 = cr[DI + c], c3 = cr[2 * DI + c];
 	const float w0 = cw[c], w1 = cw[DI + c], w2 = cw[2 * DI + c], w3 = cw[3 * DI + c], b = cb[c];
-	for (int t = 0; t < Tc; t++) {
-		const long row = (long)s * Tc + t;
-		const float x = xz[row * 2 * DI + c];
+	auto step = [&](long row, float x) {
 		float a = __fadd_rn(__fmul_rn(c3, w0), __fmul_rn(c2, w1));
 		a = __fadd_rn(a, __fmul_rn(c1, w2));
 		a = __fadd_rn(a, __fmul_rn(x, w3));
@@ -88,7 +89,17 @@ __global__ void k_ssm_conv(const float *__restrict__ xz, int S, int Tc, int DI, 
 		const float v = ssm_silu(a);
 		xs[row * DI + c] = v;
 		ssm_split(v, hi[row * DI + c], lo[row * DI + c]);
+	};
+	const long row0 = (long)s * Tc;
+	int t = 0;
+	for (; t + U <= Tc; t += U) {
+		float x[U];
+#pragma unroll
+		for (int u = 0; u < U; u++) x[u] = xz[(row0 + t + u) * 2 * DI + c];
+#pragma unroll
+		for (int u = 0; u < U; u++) step(row0 + t + u, x[u]);
 	}
+	for (; t < Tc; t++) step(row0 + t, xz[(row0 + t) * 2 * DI + c]);
 	cr[c] = c1, cr[DI + c] = c2, cr[2 * DI + c] = c3;
 }
 
