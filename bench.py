@@ -477,6 +477,8 @@ def cpu_baseline_ssm(model, T: int = 96):
 
 # ---- config 2: weight-only dequant GEMM microbench ---------------------------------------------
 GEMM_N = GEMM_K = 4096
+# DRAM bytes (read + write) of one gemm_tc launch, from an ncu capture: (M, bits) -> bytes
+GEMM_TC_TRAFFIC = {(256, 4): 12625920.0}
 
 
 def gemm_inputs(bits: int, M: int):
@@ -592,7 +594,9 @@ def bench_gemm(args, world, rank, local, M: int, bits: int):
                    "algorithmic_bytes": byts, "flops": flops},
         "roofline": {"kernel": path, "bound": "hbm" if hbm else "tensor", "achieved": achieved, "peak": peak,
                      "unit": unit, "frac": achieved / peak, "peak_source": src + (" hbm_gbs" if hbm else " bf16 burst"),
-                     "traffic": None},
+                     "traffic": GEMM_TC_TRAFFIC.get((M, bits)),
+                     "traffic_source": "ncu dram bytes of one gemm_tc launch (profiles/gemm_tc_config2_m256.md)"
+                     if (M, bits) in GEMM_TC_TRAFFIC else None},
         "e2e": {"value": world * args.steps / te, "unit": "GEMM/s", "h2d_bytes_per_step": b.nbytes,
                 "d2h_bytes_per_step": GEMM_N * M * 4},
         # GEMV: one kernel; tensor cores: the activation split, the GEMM, and the fixed-order
