@@ -144,20 +144,23 @@ __global__ void __launch_bounds__(128) k_ssm_scan(const float *__restrict__ dbc,
 			xn = xs[(gr + 1) * DI + c];
 			zn = xz[(gr + 1) * 2 * DI + DI + c];
 		}
-		// dt = softplus(s * sum_p r[p] code[p] + dt_b), the sum in p order (runtime/tg_rt.h:143-151)
+		// dt = softplus(s * sum_p r[p] code[p] + dt_b), the sum in p order (runtime/tg_rt.h:143-151),
+		// each term fused into the running sum (one rounding per term instead of two)
 		float acc = 0.0f;
 #pragma unroll
-		for (int p = 0; p < R; p++) acc = __fadd_rn(acc, __fmul_rn(row[p], w[p]));
+		for (int p = 0; p < R; p++) acc = fmaf(row[p], w[p], acc);
 		const float dt = ssm_softplus(__fadd_rn(__fmul_rn(sc, acc), bias));
 		float m1 = 0.0f;
 		// the state update of the program, h = e*h + (1 - e)/a * (x*bt) with e = exp(-dt*a), in
 		// the fast forms: the hardware exp2 approximation (relative error about 2^-21 on this
-		// range) and a multiply by 1/a (within an ulp of the division); the per-state work is
-		// the inner loop of the whole SSM
+		// range) and a multiply by 1/a (within an ulp of the division). Written as
+		// h = q + e*(h - q) with q = (x*bt)/a, the same value in one instruction fewer per
+		// state: the per-state work is the inner loop of the whole SSM
 #pragma unroll
 		for (int k = 0; k < DS; k++) {
 			const float e = __expf(-(dt * a[k]));
-			h[k] = fmaf((1.0f - e) * ia[k], x * row[R + k], e * h[k]);
+			const float q = (x * row[R + k]) * ia[k];
+			h[k] = fmaf(e, h[k] - q, q);
 		}
 #pragma unroll
 		for (int k = 0; k < DS; k++) m1 = fmaf(h[k], row[R + DS + k], m1);
