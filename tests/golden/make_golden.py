@@ -17,6 +17,15 @@ Fixtures:
   nano/                            a Qwen3-structured program (examples/qwen3/import.py layout) at toy
                                    sizes: weights, quantized TGIR (int8 RTN, int4 RTN, int4 GPTQ) and
                                    `tgc batch` logits of 4 sequences
+  nano_ssm/                        a stacked selective-SSM program at toy sizes, quantized int8 and
+                                   int4, with `tgc batch` outputs
+  programs/                        `tgc ir` (or `tgc quantize`) of the reference's own test and
+                                   example programs, seeded rows (the inputs tests/run.sh uses
+                                   first) and `tgc batch` outputs: control flow (PROGRAMS), the
+                                   sparse and memory ops (SPARSE_MEMORY), every other stateless one
+                                   (SMALL)
+
+`python make_golden.py PART ...` regenerates only the named parts (PARTS).
 """
 from __future__ import annotations
 
@@ -418,18 +427,80 @@ def sparse_memory(tgc: str) -> None:
         sh(tgc, "batch", ir, rp, "-j", "1", "-o", os.path.join(out, f"{name}_out.csv"))
 
 
+# The other stateless programs of the reference's tests and examples: name -> (source, rows,
+# how rows are drawn). Imports and file() params are resolved by `tgc ir`.
+SMALL = {
+    "xor": ("examples/xor.tg", 100, "bits"),
+    "newton": ("examples/newton.tg", 200, "positive"),
+    "use_import": ("examples/use_import.tg", 200, "uniform"),
+    "bcast": ("tests/bcast/broadcast.tg", 200, "uniform"),
+    "file_param": ("tests/cases/file_param.tg", 200, "uniform"),
+    "multi_input": ("tests/cases/multi_input.tg", 200, "uniform"),
+    "nested": ("tests/cases/nested.tg", 200, "uniform"),
+    "cycle": ("tests/imports/cycle.tg", 100, "uniform"),
+    "diamond": ("tests/imports/diamond.tg", 100, "uniform"),
+    "take_along": ("tests/memory/take_along.tg", 200, "take"),
+    "native_matmul": ("tests/native/matmul.tg", 200, "uniform"),
+}  # tests/par/wide.tg is left out: its TGIR (a large param for the parallel-matmul test) is 16 MB
+# tests/run.sh:26-47,334,427-428: the inputs the reference's own suite runs them on (a
+# program's inputs concatenated, as `tgc batch` reads a row)
+SMALL_ROWS = {
+    "xor": [[0, 0], [1, 0], [0, 1], [1, 1]],
+    "newton": [[2, 9, 16]],
+    "use_import": [[1, -1, 2, -2]],
+    "bcast": [[0.1, -0.2, 0.3, 1, 2, -1, 0, 0, 0, -3, 0.5, 0.25]],
+    "file_param": [[1, 2]],
+    "multi_input": [[1, 2, 3, 0.5]],
+    "nested": [[0.3, -0.7]],
+    "cycle": [[10, 20]],
+    "diamond": [[10, 20]],
+    "take_along": [[1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 3, 0, -1, 1, 4, 2]],
+    "native_matmul": [[1, 2, 3, 4, 5, 6, 7] + [round(0.1 * i, 1) for i in range(1, 36)] + [1, -1, 2, -2, 0.5, 0.5, 1, 2, 3]],
+}
+
+
+def small_programs(tgc: str) -> None:
+    from technograd_b200 import tgir
+    out = os.path.join(HERE, "programs")
+    os.makedirs(out, exist_ok=True)
+    for name, (src, n, kind) in SMALL.items():
+        ir = os.path.join(out, f"{name}.tgir")
+        with open(ir, "w") as f:
+            f.write(sh(tgc, "ir", os.path.join(REF, src)))
+        m = tgir.load(ir)
+        rng = np.random.default_rng(sum(map(ord, name)))
+        if kind == "bits":
+            rows = rng.integers(0, 2, size=(n, m.per)).astype(np.float32)
+        elif kind == "positive":  # square roots by a think loop: 0.001 .. 100
+            rows = np.round(10 ** rng.uniform(-3, 2, size=(n, m.per)), 4).astype(np.float32)
+        elif kind == "take":  # 12 values, then 6 indices, some out of range or fractional
+            vals = np.round(rng.uniform(-5, 5, size=(n, 12)), 3)
+            idx = rng.integers(-2, 7, size=(n, 6)) + np.round(rng.uniform(-0.45, 0.45, size=(n, 6)), 2)
+            rows = np.concatenate([vals, idx], axis=1).astype(np.float32)
+        else:
+            rows = np.round(rng.uniform(-1.5, 1.5, size=(n, m.per)), 3).astype(np.float32)
+        if name in SMALL_ROWS:
+            rows = np.concatenate([np.array(SMALL_ROWS[name], np.float32), rows])
+        rp = os.path.join(out, f"{name}_rows.csv")
+        np.savetxt(rp, rows, fmt="%.9g", delimiter=",")
+        sh(tgc, "batch", ir, rp, "-j", "1", "-o", os.path.join(out, f"{name}_out.csv"))
+
+
+PARTS = {"latent_reasoner": latent_reasoner, "ops": ops, "kernels": kernels, "quant": quant, "nano": nano,
+         "nano_ssm": nano_ssm, "programs": programs, "sparse_memory": sparse_memory, "small_programs": small_programs}
+
+
 def main() -> None:
+    """python make_golden.py [PART ...]: every fixture, or only the named parts."""
     tgo.build()
     tgc = tgo.REF_TGC
     if not os.path.exists(tgc) or tgo.ref() is None:
         sys.exit("oracle/_ref was not built: the reference sources are needed")
-    latent_reasoner(tgc)
-    ops(tgc)
-    kernels()
-    quant()
-    nano(tgc)
-    programs(tgc)
-    sparse_memory(tgc)
+    for part in sys.argv[1:] or list(PARTS):
+        if part not in PARTS:
+            sys.exit(f"unknown part {part!r}; parts: {', '.join(PARTS)}")
+        f = PARTS[part]
+        f() if part in ("kernels", "quant") else f(tgc)
     print("golden fixtures written to", HERE)
 
 

@@ -2,7 +2,8 @@
 tests/scan/nested_grad.tg, tests/attn/window.tg) and the programs of its sparse and
 memory tests (tests/memory/topk.tg, topk_pad.tg, scan.tg, sufmatch.tg; tests/quant/mlp.tg
 as f32 and quantized to int8 / int4, an spmm table) on the oracle VM and on the device
-row executor, against `tgc batch` output of the reference (tests/golden/programs).
+row executor, against `tgc batch` output of the reference (tests/golden/programs); the
+reference's remaining stateless programs on the oracle VM.
 
 The oracle follows the reference's arithmetic order with the same libm, so it must
 agree bit for bit. The device path: values within 1e-4 + 1e-3 |ref|; think steps
@@ -50,6 +51,36 @@ def test_known_answers_of_the_reference_suite(golden):
         m, rows, ref, _ = fixture(golden, name)
         out, _ = tgo.program_run(tgir.CProgram(m), rows[:1])
         assert out[0].tolist() == want == ref[0].tolist()
+
+
+# Every other stateless program of the reference's tests and examples (tests/golden/make_golden.py
+# SMALL): plain ops, imports (diamond and cycle), file() params, several inputs, broadcasts,
+# take_along, a think loop (newton) and the native matmul forms.
+SMALL_NAMES = ["xor", "newton", "use_import", "bcast", "file_param", "multi_input", "nested", "cycle", "diamond",
+               "take_along", "native_matmul"]
+
+
+@pytest.mark.parametrize("name", SMALL_NAMES)
+def test_oracle_vm_matches_tgc_batch_small(golden, name):
+    m, rows, want, want_steps = fixture(golden, name)
+    out, steps = tgo.program_run(tgir.CProgram(m), rows)
+    assert np.array_equal(steps, want_steps)
+    assert np.array_equal(out.view(np.uint32), want.view(np.uint32))
+
+
+def test_known_answers_of_the_small_programs(golden):
+    """tests/run.sh:26-35,427-428: xor's truth table, newton's square roots and 5 steps,
+    take_along, and the import diamond and cycle."""
+    cases = [("xor", 4, [[0], [1], [1], [0]], None), ("newton", 1, [[1.41421354, 3, 4]], [[5]]),
+             ("take_along", 1, [[4, 1, 0, 6, 0, 11]], None), ("diamond", 1, [[23, 43]], None),
+             ("cycle", 1, [[11, 21]], None)]
+    for name, k, want, want_steps in cases:
+        m, rows, ref, ref_steps = fixture(golden, name)
+        out, steps = tgo.program_run(tgir.CProgram(m), rows[:k])
+        np.testing.assert_array_equal(out, np.array(want, np.float32))
+        np.testing.assert_array_equal(ref[:k], np.array(want, np.float32))
+        if want_steps is not None:
+            assert steps.tolist() == want_steps == ref_steps[:k].tolist()
 
 
 def test_halt_step_counts(golden):
