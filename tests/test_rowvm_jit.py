@@ -71,6 +71,34 @@ def kernel_source(m, compile_: bool):
     return rc, buf.value.decode()
 
 
+# The reference's other stateless programs: whether the generator takes them (NVRTC compiles
+# them here, without a GPU)
+SMALL_PROGRAMS = {
+    "programs/xor.tgir": True,
+    "programs/newton.tgir": True,
+    "programs/use_import.tgir": True,
+    "programs/bcast.tgir": True,
+    "programs/file_param.tgir": True,
+    "programs/multi_input.tgir": True,
+    "programs/nested.tgir": True,
+    "programs/cycle.tgir": True,
+    "programs/diamond.tgir": True,
+    "programs/take_along.tgir": False,  # the gather indexes the arena at run time: interpreter
+    "programs/native_matmul.tgir": False,  # more than 192 floats per row: interpreter
+}
+
+
+@pytest.mark.parametrize("name", sorted(SMALL_PROGRAMS))
+def test_generated_kernel_compiles_small(golden, name):
+    m = tgir.load(os.path.join(golden, name))
+    rc, src = kernel_source(m, True)
+    if SMALL_PROGRAMS[name]:
+        assert rc == 0, _lib.lib().tg_cuda_error().decode()
+        assert 'extern "C" __global__' in src and "tg_rowvm" in src
+    else:
+        assert rc == _lib.EUNSUPPORTED
+
+
 @pytest.mark.parametrize("name", sorted(PROGRAMS))
 def test_generated_kernel_compiles(golden, name):
     m = tgir.load(os.path.join(golden, name))
