@@ -187,12 +187,20 @@ class HostRegistered:
                     raise ValueError("tg_cuda_host_register: the array must be C-contiguous")
                 check(lib().tg_cuda_host_register(a.ctypes.data, a.nbytes))
                 self.done.append(a)
-        except BaseException:
-            self.__exit__(None, None, None)
+        except BaseException as e:
+            self.__exit__(type(e), e, e.__traceback__)  # releases what was registered, keeps e
             raise
         return self
 
-    def __exit__(self, *exc):
+    def __exit__(self, exc_type, exc, tb):
+        # every range is released even if one fails; a failure is raised only when no other
+        # exception is already leaving the block
+        first = None
         while self.done:
-            check(lib().tg_cuda_host_unregister(self.done.pop().ctypes.data))
+            try:
+                check(lib().tg_cuda_host_unregister(self.done.pop().ctypes.data))
+            except TgCudaError as e:
+                first = first or e
+        if first is not None and exc_type is None:
+            raise first
         return False
