@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import argparse
 import ctypes as C
+import re
 import sys
 import time
 
@@ -23,31 +24,94 @@ from . import _lib, tgir
 
 
 def is_binary(path: str) -> bool:
-    return path.endswith(".bin") or path.endswith(".f32")
+    """src/io.c:17-21: the extension after the last dot is .bin or .f32."""
+    dot = path.rfind(".")
+    return dot >= 0 and path[dot:] in (".bin", ".f32")
 
 
-def load_samples(path: str, per: int) -> np.ndarray:
-    """src/main.c:175-214 load_samples: raw f32 streams or text rows of exactly `per` numbers."""
+# One number as glibc's strtof reads it (C locale): its own leading white space, a sign, then a
+# hex float, a decimal, inf/infinity or nan/nan(chars). A match ends where strtof stops.
+_NUMBER = re.compile(r"""[ \t\n\v\f\r]*(?P<num>[+-]?(?:
+      0[xX](?:[0-9a-fA-F]+(?:\.[0-9a-fA-F]*)?|\.[0-9a-fA-F]+)(?:[pP][+-]?[0-9]+)?
+    | (?:[0-9]+(?:\.[0-9]*)?|\.[0-9]+)(?:[eE][+-]?[0-9]+)?
+    | [iI][nN][fF](?:[iI][nN][iI][tT][yY])?
+    | [nN][aA][nN](?:\([0-9A-Za-z_]*\))?))""", re.X)
+_SEPARATORS = " \t,\r\n"
+_libc_strtof = None
+
+
+def _strtof(tok: str) -> np.float32:
+    global _libc_strtof
+    if _libc_strtof is None:
+        f = C.CDLL(None).strtof
+        f.restype, f.argtypes = C.c_float, [C.c_char_p, C.c_void_p]
+        _libc_strtof = f
+    return np.float32(_libc_strtof(tok.encode("latin-1"), None))
+
+
+def parse_row(line: str) -> tuple[list, list] | int:
+    """io_parse_row (src/io.c:25-41): the numbers of one line up to its end or a '#', as
+    (doubles, tokens); or the offset of the first bad number. A number must end at a
+    separator (space, tab, comma, CR, LF), a '#' or the end of the line."""
+    vals, toks, i, n = [], [], 0, len(line)
+    while True:
+        while i < n and line[i] in _SEPARATORS:
+            i += 1
+        if i >= n or line[i] == "#":
+            return vals, toks
+        m = _NUMBER.match(line, i)
+        if m is None or (m.end() < n and line[m.end()] not in _SEPARATORS + "#"):
+            return i
+        tok = m.group("num")
+        try:
+            v = float.fromhex(tok) if "x" in tok or "X" in tok else float(tok)
+        except (ValueError, OverflowError):  # nan(chars), or a hex float past the double range
+            v = None
+        vals.append(v)
+        toks.append(tok)
+        i = m.end()
+
+
+def _narrow(vals: list, toks: list) -> np.ndarray:
+    """Doubles of correctly rounded tokens -> the f32 values strtof gives. Rounding the double
+    to f32 gives strtof's result unless the double sits exactly on a midpoint between two f32
+    values (the decimal may lie on either side of it), overflowed, or is a NaN (whose sign and
+    payload strtof sets); those few tokens are read by strtof itself."""
+    d = np.array([np.nan if v is None else v for v in vals], np.float64)
+    with np.errstate(over="ignore", invalid="ignore"):
+        f = d.astype(np.float32)
+        other = np.nextafter(f, np.where(f.astype(np.float64) > d, np.float32(-np.inf), np.float32(np.inf)))
+        mid = (f.astype(np.float64) + other.astype(np.float64)) / 2
+    redo = np.isnan(d) | (np.isinf(f) & ~np.isinf(d)) | ((f.astype(np.float64) != d) & (mid == d))
+    for i in np.flatnonzero(redo):
+        f[i] = _strtof(toks[i])
+    return f
+
+
+def load_samples(path: str, per: int, model: str = "model") -> np.ndarray:
+    """src/main.c:175-214 load_samples: raw little-endian f32 streams, or text rows of exactly
+    `per` numbers (blank and comment-only lines skipped). Everything is validated before
+    anything is returned; errors carry the reference's wording."""
+    with open(path, "rb") as fh:
+        raw = fh.read()
     if is_binary(path):
-        raw = np.fromfile(path, dtype="<f4")
-        if raw.size % per:
-            raise ValueError(f"'{path}': {raw.size} values is not a multiple of the {per} per sample")
-        return raw.reshape(-1, per).astype(np.float32)
-    rows = []
-    with open(path, encoding="utf-8") as f:
-        for lineno, line in enumerate(f, 1):
-            line = line.split("#", 1)[0]
-            toks = [t for t in line.replace(",", " ").split()]
-            if not toks:
-                continue
-            try:
-                vals = [float(t) for t in toks]
-            except ValueError as e:
-                raise ValueError(f"{path}:{lineno}: bad number") from e
-            if len(vals) != per:
-                raise ValueError(f"{path}:{lineno}: row has {len(vals)} values, the model needs {per} per sample")
-            rows.append(vals)
-    return np.array(rows, dtype=np.float64).astype(np.float32).reshape(-1, per)
+        if len(raw) % 4:  # src/io.c:49
+            raise ValueError(f"'{path}': {len(raw)} bytes is not a whole number of f32 values")
+        v = np.frombuffer(raw, dtype="<f4")
+        if v.size % per:
+            raise ValueError(f"'{path}': {v.size} values is not a multiple of the {per} per sample")
+        return v.astype(np.float32).reshape(-1, per)
+    text = raw.split(b"\0", 1)[0].decode("latin-1")  # the C loop stops at a NUL byte
+    vals, toks = [], []
+    for lineno, line in enumerate(text.split("\n"), 1):
+        r = parse_row(line)
+        if isinstance(r, int):
+            raise ValueError(f"{path}:{lineno}: bad number near '{line[r:r + 20]}'")
+        if r[0] and len(r[0]) != per:
+            raise ValueError(f"{path}:{lineno}: row has {len(r[0])} values, model {model} needs {per} per sample")
+        vals += r[0]
+        toks += r[1]
+    return _narrow(vals, toks).reshape(-1, per)
 
 
 class Batch:
@@ -121,13 +185,21 @@ class Batcher:
         self.close()
 
 
+def _g9(v) -> str:
+    """printf("%.9g", (double)v) as glibc writes it: NaN with its sign ("-nan")."""
+    v = float(v)
+    if v != v:
+        return "-nan" if np.signbit(v) else "nan"
+    return f"{v:.9g}"
+
+
 def write_rows(path: str | None, out: np.ndarray, steps: np.ndarray) -> None:
     if path and is_binary(path):
         out.astype("<f4").tofile(path)
         return
     lines = []
     for r in range(out.shape[0]):
-        vals = ",".join(f"{float(v):.9g}" for v in out[r])
+        vals = ",".join(_g9(v) for v in out[r])
         extra = "".join(f",{int(s)}" for s in steps[r])
         lines.append(vals + extra)
     text = "\n".join(lines) + ("\n" if lines else "")
@@ -148,7 +220,7 @@ def main(argv=None) -> int:
     a = ap.parse_args(argv)
     t0 = time.perf_counter()
     m = tgir.load(a.model)
-    rows = load_samples(a.data, m.per)  # everything validated before compute or output
+    rows = load_samples(a.data, m.per, m.name)  # everything validated before compute or output
     b = Batch(m, a.gpus)
     out, steps = b.run(rows)
     write_rows(a.out, out, steps)
