@@ -20,7 +20,7 @@ import time
 
 import numpy as np
 
-from . import _lib, tgir
+from . import _lib, cnum, tgir
 
 
 def is_binary(path: str) -> bool:
@@ -29,24 +29,10 @@ def is_binary(path: str) -> bool:
     return dot >= 0 and path[dot:] in (".bin", ".f32")
 
 
-# One number as glibc's strtof reads it (C locale): its own leading white space, a sign, then a
-# hex float, a decimal, inf/infinity or nan/nan(chars). A match ends where strtof stops.
-_NUMBER = re.compile(r"""[ \t\n\v\f\r]*(?P<num>[+-]?(?:
-      0[xX](?:[0-9a-fA-F]+(?:\.[0-9a-fA-F]*)?|\.[0-9a-fA-F]+)(?:[pP][+-]?[0-9]+)?
-    | (?:[0-9]+(?:\.[0-9]*)?|\.[0-9]+)(?:[eE][+-]?[0-9]+)?
-    | [iI][nN][fF](?:[iI][nN][iI][tT][yY])?
-    | [nN][aA][nN](?:\([0-9A-Za-z_]*\))?))""", re.X)
+# One field as strtof reads it: its own leading white space, then a number in the C library's
+# grammar; the match ends where strtof stops.
+_NUMBER = re.compile(r"[ \t\n\v\f\r]*(?P<num>" + cnum.PATTERN + ")", re.X)
 _SEPARATORS = " \t,\r\n"
-_libc_strtof = None
-
-
-def _strtof(tok: str) -> np.float32:
-    global _libc_strtof
-    if _libc_strtof is None:
-        f = C.CDLL(None).strtof
-        f.restype, f.argtypes = C.c_float, [C.c_char_p, C.c_void_p]
-        _libc_strtof = f
-    return np.float32(_libc_strtof(tok.encode("latin-1"), None))
 
 
 def parse_row(line: str) -> tuple[list, list] | int:
@@ -63,11 +49,7 @@ def parse_row(line: str) -> tuple[list, list] | int:
         if m is None or (m.end() < n and line[m.end()] not in _SEPARATORS + "#"):
             return i
         tok = m.group("num")
-        try:
-            v = float.fromhex(tok) if "x" in tok or "X" in tok else float(tok)
-        except (ValueError, OverflowError):  # nan(chars), or a hex float past the double range
-            v = None
-        vals.append(v)
+        vals.append(cnum.strtod(tok))
         toks.append(tok)
         i = m.end()
 
@@ -77,14 +59,14 @@ def _narrow(vals: list, toks: list) -> np.ndarray:
     to f32 gives strtof's result unless the double sits exactly on a midpoint between two f32
     values (the decimal may lie on either side of it), overflowed, or is a NaN (whose sign and
     payload strtof sets); those few tokens are read by strtof itself."""
-    d = np.array([np.nan if v is None else v for v in vals], np.float64)
+    d = np.array(vals, np.float64)
     with np.errstate(over="ignore", invalid="ignore"):
         f = d.astype(np.float32)
         other = np.nextafter(f, np.where(f.astype(np.float64) > d, np.float32(-np.inf), np.float32(np.inf)))
         mid = (f.astype(np.float64) + other.astype(np.float64)) / 2
     redo = np.isnan(d) | (np.isinf(f) & ~np.isinf(d)) | ((f.astype(np.float64) != d) & (mid == d))
     for i in np.flatnonzero(redo):
-        f[i] = _strtof(toks[i])
+        f[i] = cnum.strtof(toks[i])
     return f
 
 

@@ -18,7 +18,7 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
-from . import _lib
+from . import _lib, cnum
 
 _TOKEN = re.compile(rb'\s+|;[^\n]*|(\()|(\))|"([^"\n]*)"|([^\s();"]+)')
 # the number lists of params: read straight into arrays (no object per number)
@@ -31,16 +31,22 @@ class TgirError(ValueError):
 
 def _atom(tok: str):
     # src/sexp.c:112-121: a number when strtod consumes it all and it starts like one
-    if tok[0].isdigit() or (tok[0] in "+-." and len(tok) > 1):
-        try:
-            return float(tok)
-        except ValueError:
-            pass
-    return Sym(tok)
+    v = cnum.atom_number(tok)
+    return Sym(tok) if v is None else v
 
 
 class Sym(str):
     pass
+
+
+_DECIMAL_BYTES = b"0123456789eE+-. \t\n\r\v\f"
+_BARE_SIGN = re.compile(rb"[+-](?![0-9.])")
+
+
+def _plain_decimals(span) -> bool:
+    """Whether a number list holds only decimal forms numpy parses as strtod does. Lists with
+    anything else (hex floats, inf/nan, symbols) or a bare sign go atom by atom."""
+    return not bytes(span).translate(None, _DECIMAL_BYTES) and _BARE_SIGN.search(span) is None
 
 
 def _payload(span: bytes, head: str) -> np.ndarray:
@@ -82,7 +88,7 @@ def read_sexp(src, fast: bool = True) -> list:
                 if end < 0:
                     raise TgirError("unterminated list")
                 span = buf[pm.end():end]
-                if b"(" not in span and b";" not in span:
+                if b"(" not in span and b";" not in span and _plain_decimals(span):
                     head = pm.group(1).decode()
                     stack[-1].append([Sym(head), _payload(span, head)])
                     pos = end + 1
@@ -108,6 +114,8 @@ def _numbers(node) -> np.ndarray:
     """The values of a number list, parsed fast (an array) or as atoms."""
     if len(node) == 2 and isinstance(node[1], np.ndarray):
         return node[1]
+    if any(isinstance(x, (str, list)) for x in node[1:]):  # a symbol, string or list among the numbers
+        raise TgirError(f"bad number in ({node[0]} ...)")
     return np.array(node[1:], dtype=np.float64)
 
 
@@ -353,7 +361,8 @@ def read(src, fast: bool = True) -> Module:
         if h in ("param", "state") and isinstance(f[3], list) and f[3] and f[3][0] == "quant":
             shape = _shape(f[2])
             bits, axis = int(f[3][1]), int(f[3][2])
-            sc = _numbers(f[3][3]).astype(np.float32)
+            with np.errstate(over="ignore"):  # (float) of a double past the f32 range is inf, as in C
+                sc = _numbers(f[3][3]).astype(np.float32)
             codes = _numbers(f[3][4])
             if codes.dtype.kind == "f":
                 if not np.array_equal(codes, np.round(codes)):
@@ -376,7 +385,8 @@ def read(src, fast: bool = True) -> Module:
             rd.define(f[1], v)
         elif h in ("param", "state"):
             shape = _shape(f[2])
-            data = _numbers(f[3]).astype(np.float32)
+            with np.errstate(over="ignore"):
+                data = _numbers(f[3]).astype(np.float32)
             if data.size != int(np.prod(shape)):
                 raise TgirError(f"param '{f[1]}' needs {int(np.prod(shape))} values, has {data.size}")
             v = m.value(_lib.PARAM if h == "param" else _lib.STATE, shape, str(f[1]))
