@@ -1204,6 +1204,389 @@ static int emit_block(Compiler &C, int from, int cnt, int depth)
 	return 0;
 }
 
+// ---- program verification -------------------------------------------------------------------
+//
+// tg_cuda_load trusts nothing about the program it is handed. Every index is in range, every
+// instruction belongs to exactly one block, and every declared shape is the one its operands
+// give by the reference's own rules: op_infer (src/ops.c:96-295) and the instruction, think
+// and scan checks of its TGIR reader (src/ir.c:258-447). So no kernel indexes past a value,
+// whatever the caller passes.
+
+struct VShape {
+	int rank = 0, dim[4] = { 1, 1, 1, 1 };
+};
+
+static VShape vshape(const tg_cuda_value &v)
+{
+	VShape s;
+	s.rank = v.rank;
+	for (int d = 0; d < v.rank && d < 4; d++) s.dim[d] = v.dim[d];
+	return s;
+}
+
+static bool veq(const VShape &a, const VShape &b)
+{
+	if (a.rank != b.rank) return false;
+	for (int d = 0; d < a.rank; d++)
+		if (a.dim[d] != b.dim[d]) return false;
+	return true;
+}
+
+static long vnumel(const VShape &s)
+{
+	long n = 1;
+	for (int d = 0; d < s.rank; d++) n *= s.dim[d];
+	return n;
+}
+
+static std::string vstr(const VShape &s)
+{
+	std::string r = "(f32";
+	for (int d = 0; d < s.rank; d++) r += " " + std::to_string(s.dim[d]);
+	return r + ")";
+}
+
+// src/util.c:154-165: dimensions compared from the right, each pair equal or one of them 1
+static bool vbroadcast(const VShape &a, const VShape &b, VShape &o)
+{
+	o = VShape();
+	o.rank = std::max(a.rank, b.rank);
+	for (int i = 1; i <= o.rank; i++) {
+		int x = i <= a.rank ? a.dim[a.rank - i] : 1, y = i <= b.rank ? b.dim[b.rank - i] : 1;
+		if (x != y && x != 1 && y != 1) return false;
+		o.dim[o.rank - i] = x == 1 ? y : x;
+	}
+	return true;
+}
+
+// operand counts of the reference's op table (src/ops.c:7-50), in TG_CUDA_OP_* order
+static const signed char kArity[TG_CUDA_OP_COUNT] = {
+	0, 2, 2, 2, 2, 2, 2, // const add sub mul div max min
+	1, 1, 1, 1, 1, 1, 1, // neg tanh relu sigmoid exp sqrt gelu
+	1, 1, 1, 2, 1, 1,    // silu softplus log matmul softmax rmsnorm
+	1, 1, 1, 2, 1, 2,    // sum mean transpose outer step spmm
+	3, 3, 2, 2, 3, 3,    // spmm_t spmm_dx active take take_t spmm_tc
+	1, 1, 1, 1, 2, 1,    // sin cos reshape floor sum_to topk
+	3, 3, 1, 0, 0        // memscan memscan_t sufmatch think scan
+};
+
+// sufmatch's output length (src/util.c:469-474): 2 T n results, then the automaton's workspace
+static long vsufmatch_size(long T, long n)
+{
+	long h = 16;
+	while (h < 6 * T + 6) h *= 2;
+	return 2 * T * n + 4 * (2 * T + 2) + 4 * h;
+}
+
+// memscan_t's output length (runtime/tg_rt.h:524-532, tg_memscan_layout)
+static long vmemscan_t_size(long tn, long k, long rows, long dv)
+{
+	long np = tn * k * 4, L = dv % 4 == 0 ? dv : dv % 2 == 0 ? 2 * dv : 4 * dv;
+	long o1 = (np + dv - 1) / dv * dv, o2 = o1 + rows * dv, o3 = o2 + tn * dv, end = o3 + rows * dv;
+	return (end + L - 1) / L * L;
+}
+
+// The shape a value op yields from its operands' shapes (src/ops.c:96-295), or false with err.
+static bool vinfer(int op, const VShape *a, VShape &o, std::string &err)
+{
+	o = VShape();
+	switch (op) {
+	case TG_CUDA_OP_ADD: case TG_CUDA_OP_SUB: case TG_CUDA_OP_MUL: case TG_CUDA_OP_DIV: case TG_CUDA_OP_MAX:
+	case TG_CUDA_OP_MIN:
+		if (vbroadcast(a[0], a[1], o)) return true;
+		err = "shape mismatch " + vstr(a[0]) + " vs " + vstr(a[1]);
+		return false;
+	case TG_CUDA_OP_SUM_TO: {
+		VShape b;
+		if (!vbroadcast(a[0], a[1], b) || !veq(b, a[0])) {
+			err = "'sum_to' cannot reduce " + vstr(a[0]) + " to " + vstr(a[1]);
+			return false;
+		}
+		o = a[1];
+		return true;
+	}
+	case TG_CUDA_OP_NEG: case TG_CUDA_OP_TANH: case TG_CUDA_OP_RELU: case TG_CUDA_OP_SIGMOID: case TG_CUDA_OP_EXP:
+	case TG_CUDA_OP_SQRT: case TG_CUDA_OP_GELU: case TG_CUDA_OP_SILU: case TG_CUDA_OP_SOFTPLUS: case TG_CUDA_OP_LOG:
+	case TG_CUDA_OP_STEP: case TG_CUDA_OP_SIN: case TG_CUDA_OP_COS: case TG_CUDA_OP_FLOOR:
+		o = a[0];
+		return true;
+	case TG_CUDA_OP_MATMUL: {
+		int ra = a[0].rank, rb = a[1].rank;
+		int ka = ra >= 1 ? a[0].dim[ra - 1] : -1, kb = rb == 3 ? a[1].dim[1] : rb >= 1 ? a[1].dim[0] : -1;
+		if (ra < 1 || ra > 3 || rb < 1 || rb > 3 || ka != kb || (rb == 3 && (ra != 3 || a[0].dim[0] != a[1].dim[0]))) {
+			err = "'matmul' incompatible operands " + vstr(a[0]) + " @ " + vstr(a[1]);
+			return false;
+		}
+		for (int i = 0; i < ra - 1; i++) o.dim[o.rank++] = a[0].dim[i];
+		if (rb >= 2) o.dim[o.rank++] = a[1].dim[rb - 1];
+		return true;
+	}
+	case TG_CUDA_OP_SOFTMAX: case TG_CUDA_OP_RMSNORM:
+		if (a[0].rank == 0) {
+			err = "row op needs rank >= 1";
+			return false;
+		}
+		o = a[0];
+		return true;
+	case TG_CUDA_OP_SUM: case TG_CUDA_OP_MEAN:
+		return true; // a scalar
+	case TG_CUDA_OP_TRANSPOSE:
+		if (a[0].rank != 2 && a[0].rank != 3) {
+			err = "'transpose' needs rank 2 or 3";
+			return false;
+		}
+		o = a[0];
+		o.dim[o.rank - 2] = a[0].dim[a[0].rank - 1];
+		o.dim[o.rank - 1] = a[0].dim[a[0].rank - 2];
+		return true;
+	case TG_CUDA_OP_OUTER:
+		if (a[0].rank != 1 || a[1].rank != 1) {
+			err = "'outer' needs two vectors, got " + vstr(a[0]) + " and " + vstr(a[1]);
+			return false;
+		}
+		o.rank = 2, o.dim[0] = a[0].dim[0], o.dim[1] = a[1].dim[0];
+		return true;
+	case TG_CUDA_OP_SPMM: case TG_CUDA_OP_SPMM_T: case TG_CUDA_OP_SPMM_DX: {
+		const VShape &x = a[0], &w = a[op == TG_CUDA_OP_SPMM_T ? 2 : 1];
+		if ((x.rank != 2 && x.rank != 3) || x.dim[x.rank - 1] != 2 || w.rank != 2) {
+			err = "spmm needs sparse rows (K, 2) or (B, K, 2) and a matrix (D, H), got " + vstr(x) + " and " + vstr(w);
+			return false;
+		}
+		VShape y;
+		if (x.rank == 3) y.dim[y.rank++] = x.dim[0];
+		y.dim[y.rank++] = w.dim[1];
+		if (op == TG_CUDA_OP_SPMM) {
+			o = y;
+			return true;
+		}
+		if (!veq(a[op == TG_CUDA_OP_SPMM_T ? 1 : 2], y)) {
+			err = "spmm gradient does not match the product shape " + vstr(y);
+			return false;
+		}
+		o = op == TG_CUDA_OP_SPMM_T ? w : x;
+		return true;
+	}
+	case TG_CUDA_OP_TAKE_T: {
+		VShape want = a[2];
+		bool ok = a[0].rank == 1 && want.rank >= 1;
+		if (ok) want.dim[0] = a[0].dim[0];
+		if (!ok || !veq(a[1], want)) {
+			err = "'take_t' needs rows (n), a gradient (n, ...) and the table it scatters into";
+			return false;
+		}
+		o = a[2];
+		return true;
+	}
+	case TG_CUDA_OP_TAKE:
+		if (a[0].rank < 1 || a[1].rank != 1) {
+			err = "'take' needs a tensor (D, ...) and row indices (n), got " + vstr(a[0]) + " and " + vstr(a[1]);
+			return false;
+		}
+		o = a[0];
+		o.dim[0] = a[1].dim[0];
+		return true;
+	case TG_CUDA_OP_ACTIVE: case TG_CUDA_OP_SPMM_TC: {
+		const VShape &x = a[0];
+		if ((x.rank != 2 && x.rank != 3) || x.dim[x.rank - 1] != 2) {
+			err = "sparse rows (K, 2) or (B, K, 2) expected, got " + vstr(x);
+			return false;
+		}
+		int n = x.rank == 3 ? x.dim[0] * x.dim[1] : x.dim[0];
+		if (op == TG_CUDA_OP_ACTIVE) {
+			if (a[1].rank < 1) {
+				err = "'active' needs the table the rows index";
+				return false;
+			}
+			o.rank = 1, o.dim[0] = n;
+			return true;
+		}
+		const VShape &g = a[1], &r = a[2];
+		int gr = x.rank == 3 ? 2 : 1;
+		if (g.rank != gr || (gr == 2 && g.dim[0] != x.dim[0]) || r.rank != 1 || r.dim[0] != n) {
+			err = "'spmm_tc' operand shapes do not fit";
+			return false;
+		}
+		o.rank = 2, o.dim[0] = n, o.dim[1] = g.dim[g.rank - 1];
+		return true;
+	}
+	case TG_CUDA_OP_MEMSCAN: {
+		const VShape &m0 = a[0], &pp = a[1], &v = a[2];
+		if (m0.rank != 2 || pp.rank != 4 || (pp.dim[3] != 3 && pp.dim[3] != 4) || v.rank != 3 || v.dim[0] != pp.dim[0] ||
+		    v.dim[1] != pp.dim[1] || v.dim[2] != m0.dim[1]) {
+			err = "'memscan' needs a memory (rows, dv), entries (T, n, k, 3 or 4) and values (T, n, dv)";
+			return false;
+		}
+		o.rank = 2, o.dim[0] = 2 * pp.dim[0] * pp.dim[1] + m0.dim[0], o.dim[1] = m0.dim[1];
+		return true;
+	}
+	case TG_CUDA_OP_MEMSCAN_T: {
+		const VShape &y = a[0], &pv = a[1], &g = a[2];
+		long dv = y.rank == 2 ? y.dim[1] : 0, tn = pv.rank == 3 ? (long)pv.dim[0] * pv.dim[1] : 0;
+		if (!dv || !tn || !veq(y, g) || y.dim[0] <= 2 * tn || pv.dim[2] <= dv || (pv.dim[2] - dv) % 4) {
+			err = "'memscan_t' needs memscan's output, the packed entries and values, and the output's adjoint";
+			return false;
+		}
+		long N = vmemscan_t_size(tn, (pv.dim[2] - dv) / 4, y.dim[0] - 2 * tn, dv);
+		if (N > INT32_MAX) {
+			err = "'memscan_t' output too large";
+			return false;
+		}
+		o.rank = 1, o.dim[0] = (int)N;
+		return true;
+	}
+	case TG_CUDA_OP_SUFMATCH: {
+		const VShape &x = a[0];
+		if (x.rank != 1 && x.rank != 2) {
+			err = "'sufmatch' needs token ids (T) or (T, n), got " + vstr(x);
+			return false;
+		}
+		long N = vsufmatch_size(x.dim[0], x.rank == 2 ? x.dim[1] : 1);
+		if (N > INT32_MAX) {
+			err = "'sufmatch' output too large";
+			return false;
+		}
+		o.rank = 1, o.dim[0] = (int)N;
+		return true;
+	}
+	default:
+		err = "not a value operation";
+		return false;
+	}
+}
+
+struct Verifier {
+	const tg_cuda_program *p;
+	std::vector<char> seen;
+	std::string err;
+	int status = TG_CUDA_OK;
+
+	bool fail(int st, int i, const std::string &why)
+	{
+		status = st;
+		err = "instruction " + std::to_string(i) + ": " + why;
+		return false;
+	}
+	bool val(int v) const { return v >= 0 && v < p->nval; }
+	VShape sh(int v) const { return vshape(p->val[v]); }
+
+	bool block(int from, int cnt, int depth)
+	{
+		if (from < 0 || cnt < 0 || from > p->nins || cnt > p->nins - from) return fail(TG_CUDA_EINVAL, from, "block out of range");
+		if (depth > VM_MAXDEPTH) return fail(TG_CUDA_EUNSUPPORTED, from, "think/scan nesting deeper than 4");
+		for (int i = from; i < from + cnt; i++)
+			if (!ins(i, depth)) return false;
+		return true;
+	}
+
+	bool ins(int i, int depth)
+	{
+		const tg_cuda_ins &in = p->ins[i];
+		if (seen[i]) return fail(TG_CUDA_EINVAL, i, "belongs to two blocks");
+		seen[i] = 1;
+		if (in.op < 0 || in.op >= TG_CUDA_OP_COUNT) return fail(TG_CUDA_EINVAL, i, "unknown op");
+		if (!val(in.out)) return fail(TG_CUDA_EINVAL, i, "result out of range");
+		const VShape decl = sh(in.out);
+		if (in.op == TG_CUDA_OP_THINK) {
+			if (!val(in.init) || !val(in.yield) || (in.halt != -1 && !val(in.halt)) || in.maxit < 1 || in.tid < 0 ||
+			    in.tid >= p->nthink)
+				return fail(TG_CUDA_EINVAL, i, "malformed think");
+			if (!veq(sh(in.init), decl) || !veq(sh(in.yield), decl))
+				return fail(TG_CUDA_EINVAL, i, "think state, initial value and yield differ in shape");
+			if (in.halt >= 0 && sh(in.halt).rank != 0) return fail(TG_CUDA_EINVAL, i, "halting value must be a scalar");
+			return block(in.body, in.nbody, depth + 1);
+		}
+		if (in.op == TG_CUDA_OP_SCAN) {
+			if (in.scan < 0 || in.scan >= p->nscan || !p->scans) return fail(TG_CUDA_EINVAL, i, "scan out of range");
+			const tg_cuda_scan &s = p->scans[in.scan];
+			if (s.T < 1 || s.nc < 1 || s.nx < 0 || s.ny < 0 || !s.c || !s.init || !s.next || (s.nx && (!s.x || !s.xt)) ||
+			    (s.ny && (!s.y || !s.ys)) || (s.tid != -1 && (s.tid < 0 || s.tid >= p->nthink)))
+				return fail(TG_CUDA_EINVAL, i, "malformed scan");
+			for (int k = 0; k < s.nc; k++) {
+				if (!val(s.c[k]) || !val(s.init[k]) || !val(s.next[k])) return fail(TG_CUDA_EINVAL, i, "scan carry out of range");
+				if (!veq(sh(s.c[k]), sh(s.init[k])) || !veq(sh(s.c[k]), sh(s.next[k])))
+					return fail(TG_CUDA_EINVAL, i, "scan carry, initial and next values differ in shape");
+			}
+			for (int j = 0; j < s.nx; j++) {
+				if (!val(s.x[j]) || !val(s.xt[j])) return fail(TG_CUDA_EINVAL, i, "scan sequence out of range");
+				VShape want = sh(s.x[j]);
+				if (want.rank < 1 || want.dim[0] != s.T)
+					return fail(TG_CUDA_EINVAL, i, "sequence does not have T steps along its first axis");
+				for (int d = 1; d < want.rank; d++) want.dim[d - 1] = want.dim[d];
+				want.rank--;
+				if (!veq(sh(s.xt[j]), want)) return fail(TG_CUDA_EINVAL, i, "slice type differs from a row of its sequence");
+			}
+			for (int y = 0; y < s.ny; y++) {
+				if (!val(s.y[y]) || !val(s.ys[y])) return fail(TG_CUDA_EINVAL, i, "scan stack out of range");
+				VShape want = sh(s.y[y]);
+				if (want.rank >= 4) return fail(TG_CUDA_EINVAL, i, "stack rank exceeds 4");
+				for (int d = want.rank; d > 0; d--) want.dim[d] = want.dim[d - 1];
+				want.dim[0] = s.T;
+				want.rank++;
+				if (!veq(sh(s.ys[y]), want)) return fail(TG_CUDA_EINVAL, i, "emit stack differs from T rows of its value");
+			}
+			return block(in.body, in.nbody, depth + 1);
+		}
+		if (in.na != kArity[in.op])
+			return fail(TG_CUDA_EINVAL, i,
+				    "op takes " + std::to_string(kArity[in.op]) + " operand(s), got " + std::to_string(in.na));
+		VShape a[3], got;
+		for (int j = 0; j < in.na; j++) a[j] = sh(in.a[j]); // operand indices were range-checked
+		switch (in.op) {
+		case TG_CUDA_OP_CONST:
+			return true;
+		case TG_CUDA_OP_TOPK: { // the declared type carries k in its last dimension (src/ir.c:389-399)
+			bool ok = a[0].rank >= 1 && decl.rank == a[0].rank && decl.dim[decl.rank - 1] >= 1 &&
+				  decl.dim[decl.rank - 1] <= 256;
+			for (int d = 0; ok && d < a[0].rank - 1; d++) ok = decl.dim[d] == a[0].dim[d];
+			return ok || fail(TG_CUDA_EINVAL, i, "topk: the declared type must keep the leading dimensions and set the last to k (1 to 256)");
+		}
+		case TG_CUDA_OP_RESHAPE: // only the element count is checked (src/ir.c:400-407)
+			return vnumel(a[0]) == vnumel(decl) || fail(TG_CUDA_EINVAL, i, "reshape changes the element count");
+		default:
+			if (!vinfer(in.op, a, got, err)) return fail(TG_CUDA_EINVAL, i, err);
+			if (!veq(got, decl)) return fail(TG_CUDA_EINVAL, i, "declared " + vstr(decl) + " but operation yields " + vstr(got));
+			return true;
+		}
+	}
+};
+
+static int verify_program(const tg_cuda_program *p, std::string &err)
+{
+	for (int v = 0; v < p->nval; v++) {
+		const tg_cuda_value &x = p->val[v];
+		long n = 1;
+		bool ok = x.rank >= 0 && x.rank <= 4;
+		for (int d = 0; ok && d < x.rank; d++) {
+			ok = x.dim[d] >= 1;
+			n *= ok ? x.dim[d] : 1;
+			ok = ok && n <= INT32_MAX;
+		}
+		if (!ok) {
+			err = "value " + std::to_string(v) + ": bad rank or dimension";
+			return TG_CUDA_EINVAL;
+		}
+		if (x.qbits && (x.rank != 2 || x.qaxis < 0 || x.qaxis > 1)) {
+			err = "value " + std::to_string(v) + ": quantized params are rank 2 with axis 0 or 1";
+			return TG_CUDA_EINVAL;
+		}
+	}
+	if (p->ninputs < 0 || (p->ninputs && !p->inputs) || p->nthink < 0 || p->nscan < 0 || (p->nins && !p->ins)) {
+		err = "malformed program";
+		return TG_CUDA_EINVAL;
+	}
+	for (int i = 0; i < p->ninputs; i++)
+		if (p->inputs[i] < 0 || p->inputs[i] >= p->nval || p->val[p->inputs[i]].kind != TG_CUDA_INPUT) {
+			err = "entry input " + std::to_string(i) + " is not an input value";
+			return TG_CUDA_EINVAL;
+		}
+	Verifier V{ p, std::vector<char>(p->nins, 0), "", TG_CUDA_OK };
+	if (!V.block(0, p->ntop, 0)) {
+		err = V.err;
+		return V.status;
+	}
+	return TG_CUDA_OK;
+}
+
 static int compile_program(const tg_cuda_program *p, Prog &out, std::string &err)
 {
 	Compiler C;
@@ -1229,6 +1612,7 @@ static int compile_program(const tg_cuda_program *p, Prog &out, std::string &err
 				return TG_CUDA_EINVAL;
 			}
 	}
+	if (int rc = verify_program(p, err)) return rc;
 	// params: f32 values; quantized params additionally keep codes (exact, in f32) and scales
 	C.pslot.assign(p->nval, -1);
 	C.sslot.assign(p->nval, -1);
