@@ -243,6 +243,11 @@ class _Reader:
         raise TgirError(f"undefined value '{name}'")
 
     def define(self, name, v: int) -> None:
+        # src/ir.c:223-227: a name, defined once in the scope
+        if not isinstance(name, Sym):
+            raise TgirError("expected value name")
+        if any(n == name for n, _ in self.scope):
+            raise TgirError(f"redefinition of '{name}'")
         self.scope.append((str(name), v))
 
     def block(self, forms) -> list:
@@ -350,16 +355,27 @@ def read(src, fast: bool = True) -> Module:
         raise TgirError("expected (tgir 1 ...)")
     m = None
     rd = None
+    seen_block = seen_out = False  # the order of src/ir.c:462-548
     for f in forms[0][2:]:
+        if not (isinstance(f, list) and f and isinstance(f[0], Sym)):
+            raise TgirError("malformed top-level form")
         h = f[0]
         if h == "model":
+            if m is not None or len(f) != 2 or not isinstance(f[1], Sym):
+                raise TgirError("malformed model")
             m = Module(str(f[1]))
             rd = _Reader(m)
             continue
         if m is None:
             raise TgirError("(model ...) must come first")
-        if h in ("param", "state") and isinstance(f[3], list) and f[3] and f[3][0] == "quant":
+        if h in ("param", "state", "input") and seen_block:
+            raise TgirError(f"malformed {h} (after the block)")
+        if h in ("param", "state") and len(f) == 4 and isinstance(f[3], list) and f[3] and f[3][0] == "quant":
             shape = _shape(f[2])
+            if len(f[3]) != 5 or f[3][1] not in (8.0, 4.0):
+                raise TgirError("malformed quant bits (8 or 4)")
+            if len(shape) != 2 or f[3][2] not in (0.0, 1.0):
+                raise TgirError("malformed quant axis (0 or 1, rank-2 param)")
             bits, axis = int(f[3][1]), int(f[3][2])
             with np.errstate(over="ignore"):  # (float) of a double past the f32 range is inf, as in C
                 sc = _numbers(f[3][3]).astype(np.float32)
@@ -398,10 +414,18 @@ def read(src, fast: bool = True) -> Module:
             m.inputs.append(v)
             rd.define(f[1], v)
         elif h == "block":
+            if seen_block:
+                raise TgirError("malformed block (duplicate)")
+            seen_block = True
             m.top = rd.block(f[1:])
         elif h == "output":
+            if not seen_block or seen_out or len(f) != 2:
+                raise TgirError("malformed output")
+            seen_out = True
             m.output = rd.get(f[1])
         elif h == "update":
+            if not seen_block:
+                raise TgirError("malformed update (before the block)")
             m.nupd += 1
         else:
             raise TgirError(f"unknown top-level form '{h}'")
