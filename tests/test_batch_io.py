@@ -5,6 +5,7 @@ an f32 rounding midpoint -- and rejected where the reference rejects them, binar
 hold whole f32 values, and text output is printf's "%.9g" (src/io.c:79-92)."""
 import os
 import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -119,3 +120,30 @@ def test_every_golden_rows_file_reads_as_before(golden):
         plain = np.loadtxt(p, delimiter=",", dtype=np.float64, ndmin=2).astype(np.float32)
         got = batch.load_samples(p, per)
         assert np.array_equal(got.view(np.uint32), plain.view(np.uint32)) or np.array_equal(got, plain, equal_nan=True)
+
+
+@pytest.mark.parametrize("rows,msg", [("1 2\n1 x\n", "bad number near 'x'"),
+                                      ("1 2\n1 2 3\n", "row has 3 values, model ident needs 2 per sample")])
+def test_bad_input_fails_before_the_output_exists(tmp_path, rows, msg):
+    """src/main.c:414-419: the whole input is validated before any compute and before the
+    output file is created, so a failed run leaves no partial output."""
+    mp, dp, op = tmp_path / "m.tgir", tmp_path / "rows.csv", tmp_path / "out.csv"
+    mp.write_text(IDENT)
+    dp.write_text(rows)
+    r = subprocess.run([sys.executable, "-m", "technograd_b200.batch", str(mp), str(dp), "-o", str(op)],
+                       capture_output=True, text=True, timeout=120, cwd=ROOT)
+    assert r.returncode == 1 and msg in r.stderr and r.stderr.startswith("error: ")
+    assert not op.exists()
+    if os.path.exists(TGC):
+        r = subprocess.run([TGC, "batch", str(mp), str(dp), "-o", str(op)], capture_output=True, text=True, timeout=60)
+        assert r.returncode != 0 and msg in r.stderr and not op.exists()
+
+
+def test_bad_model_fails_before_the_output_exists(tmp_path):
+    mp, dp, op = tmp_path / "m.tgir", tmp_path / "rows.csv", tmp_path / "out.csv"
+    mp.write_text(IDENT.replace("(data 0 0)", "(data 0 0 0)"))
+    dp.write_text("1 2\n")
+    r = subprocess.run([sys.executable, "-m", "technograd_b200.batch", str(mp), str(dp), "-o", str(op)],
+                       capture_output=True, text=True, timeout=120, cwd=ROOT)
+    assert r.returncode == 1 and "needs 2 values, has 3" in r.stderr
+    assert not op.exists()
