@@ -74,8 +74,14 @@ def load_samples(path: str, per: int, model: str = "model") -> np.ndarray:
     """src/main.c:175-214 load_samples: raw little-endian f32 streams, or text rows of exactly
     `per` numbers (blank and comment-only lines skipped). Everything is validated before
     anything is returned; errors carry the reference's wording."""
-    with open(path, "rb") as fh:
-        raw = fh.read()
+    if path == "-":  # src/util.c:100-103: "-" is standard input
+        raw = sys.stdin.buffer.read()
+    else:
+        try:
+            with open(path, "rb") as fh:
+                raw = fh.read()
+        except OSError as e:
+            raise ValueError(f"cannot open '{path}'") from e
     if is_binary(path):
         if len(raw) % 4:  # src/io.c:49
             raise ValueError(f"'{path}': {len(raw)} bytes is not a whole number of f32 values")
@@ -201,7 +207,10 @@ def main(argv=None) -> int:
     ap.add_argument("-v", action="store_true")
     a = ap.parse_args(argv)
     t0 = time.perf_counter()
-    m = tgir.load(a.model)
+    try:
+        m = tgir.load(a.model)
+    except OSError as e:
+        raise ValueError(f"cannot open '{a.model}'") from e
     rows = load_samples(a.data, m.per, m.name)  # everything validated before compute or output
     b = Batch(m, a.gpus)
     out, steps = b.run(rows)

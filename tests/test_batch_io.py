@@ -147,3 +147,25 @@ def test_bad_model_fails_before_the_output_exists(tmp_path):
                        capture_output=True, text=True, timeout=120, cwd=ROOT)
     assert r.returncode == 1 and "needs 2 values, has 3" in r.stderr
     assert not op.exists()
+
+
+def test_rows_from_standard_input_and_missing_files(tmp_path):
+    """src/util.c:100-103: DATA "-" is standard input; a missing file is "cannot open"."""
+    mp = tmp_path / "m.tgir"
+    mp.write_text(IDENT)
+    r = subprocess.run([sys.executable, "-m", "technograd_b200.batch", str(mp), "-"], input="1 2\n1 y\n",
+                       capture_output=True, text=True, timeout=120, cwd=ROOT)
+    assert r.returncode == 1 and "-:2: bad number near 'y'" in r.stderr
+    r = subprocess.run([sys.executable, "-m", "technograd_b200.batch", str(mp), str(tmp_path / "none.csv")],
+                       capture_output=True, text=True, timeout=120, cwd=ROOT)
+    assert r.returncode == 1 and r.stderr.startswith("error: cannot open '")
+    r = subprocess.run([sys.executable, "-m", "technograd_b200.batch", str(tmp_path / "none.tgir"), "-"], input="1 2\n",
+                       capture_output=True, text=True, timeout=120, cwd=ROOT)
+    assert r.returncode == 1 and r.stderr.startswith("error: cannot open '")
+    import io
+    old = sys.stdin
+    try:
+        sys.stdin = io.TextIOWrapper(io.BytesIO(b"0x1p1, 3 # rows from stdin\n"))
+        assert batch.load_samples("-", 2).tolist() == [[2.0, 3.0]]
+    finally:
+        sys.stdin = old
