@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import argparse
 import ctypes as C
+import os
 import re
 import sys
 import time
@@ -198,6 +199,14 @@ def write_rows(path: str | None, out: np.ndarray, steps: np.ndarray) -> None:
         sys.stdout.write(text)
 
 
+def _writable(path: str) -> bool:
+    if os.path.isdir(path):
+        return False
+    if os.path.exists(path):
+        return os.access(path, os.W_OK)
+    return os.access(os.path.dirname(os.path.abspath(path)), os.W_OK)
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="tgc batch --device cuda")
     ap.add_argument("model")
@@ -212,9 +221,14 @@ def main(argv=None) -> int:
     except OSError as e:
         raise ValueError(f"cannot open '{a.model}'") from e
     rows = load_samples(a.data, m.per, m.name)  # everything validated before compute or output
+    if a.out and not _writable(a.out):  # src/main.c:64-68, checked without creating the file
+        raise ValueError(f"cannot write '{a.out}'")
     b = Batch(m, a.gpus)
     out, steps = b.run(rows)
-    write_rows(a.out, out, steps)
+    try:
+        write_rows(a.out, out, steps)
+    except OSError as e:
+        raise ValueError(f"write failed '{a.out}'") from e
     if a.v:
         ms = (time.perf_counter() - t0) * 1e3
         sys.stderr.write(f"[batch] {rows.shape[0]} row(s) in {ms:.2f} ms on {_lib.lib().tg_cuda_ngpus()} GPU(s)\n")

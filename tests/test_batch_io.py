@@ -169,3 +169,15 @@ def test_rows_from_standard_input_and_missing_files(tmp_path):
         assert batch.load_samples("-", 2).tolist() == [[2.0, 3.0]]
     finally:
         sys.stdin = old
+
+
+def test_unwritable_output_fails_before_compute(tmp_path):
+    """src/main.c:64-68: an output path that cannot be written ends the run before any
+    compute (here: before a GPU is touched), with the reference's wording."""
+    mp, dp = tmp_path / "m.tgir", tmp_path / "rows.csv"
+    mp.write_text(IDENT)
+    dp.write_text("1 2\n")
+    for bad in (tmp_path / "no_such_dir" / "out.csv", tmp_path):
+        r = subprocess.run([sys.executable, "-m", "technograd_b200.batch", str(mp), str(dp), "-o", str(bad)],
+                           capture_output=True, text=True, timeout=120, cwd=ROOT)
+        assert r.returncode == 1 and r.stderr.startswith("error: cannot write '"), r.stderr
