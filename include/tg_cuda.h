@@ -77,9 +77,13 @@ int tg_cuda_matmul_q(int axis, float *o, const float *act, const signed char *q,
  * Its split-K partial sums use a 4 MiB static device array that every GPU
  * loading the library keeps until exit, so m * n may be at most 1,048,576; n a
  * multiple of 8 (int4) or 4 (int8), q 4-byte aligned. The first call on a
- * device looks the array's address up (make it before any stream capture).
- * Calls overlapping on one device share the array and race. Device pointers,
- * asynchronous on stream; larger shapes are rejected with TG_CUDA_EINVAL. */
+ * device looks the array's address up (make it before any stream capture) and
+ * caches it for the life of the process, so cudaDeviceReset is not supported
+ * while the library is loaded. Every call on a device shares the array: calls
+ * from several host threads on the same stream are serialised (a per-device
+ * lock covers the enqueue of both kernels), calls on different streams that
+ * overlap on the GPU race. Device pointers, asynchronous on stream; larger
+ * shapes are rejected with TG_CUDA_EINVAL. */
 int tg_cuda_matmul_qb_noalloc(float *o, const float *act, const signed char *q, int bits, const float *s, int m, int k,
 			      int n, void *stream);
 

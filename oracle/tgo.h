@@ -54,6 +54,12 @@ int tgo_program_run(const tg_cuda_program *p, const float *row, float *out, int 
  * Scratch is allocated inside. */
 int tgo_lm_forward(const tg_cuda_lm_desc *d, const float *ids, int T, float *logits);
 
+/* The same results, bit for bit, from vectorised kernels on `threads` threads
+ * (0: every online CPU); tgo_mt.c says why the bits cannot differ. */
+void tgo_matmul_qb_mt(float *o, const float *a, const signed char *q, int bits, const float *s, int m, int k, int n,
+		      int threads);
+int tgo_lm_forward_mt(const tg_cuda_lm_desc *d, const float *ids, int T, float *logits, int threads);
+
 /* The stacked selective-SSM program (tg_cuda_ssm_desc) over one sequence of T
  * steps, u and out [T][d_model]. Scratch is allocated inside. */
 int tgo_ssm_forward(const tg_cuda_ssm_desc *d, const float *u, int T, float *out);

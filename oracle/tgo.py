@@ -55,6 +55,9 @@ def tgo() -> C.CDLL:
         L.tgo_program_run.restype = C.c_int
         L.tgo_lm_forward.argtypes = [C.c_void_p, FP, C.c_int, FP]
         L.tgo_lm_forward.restype = C.c_int
+        L.tgo_matmul_qb_mt.argtypes = [FP, FP, BP, C.c_int, FP, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.tgo_lm_forward_mt.argtypes = [C.c_void_p, FP, C.c_int, FP, C.c_int]
+        L.tgo_lm_forward_mt.restype = C.c_int
         L.tgo_ssm_forward.argtypes = [C.c_void_p, FP, C.c_int, FP]
         L.tgo_ssm_forward.restype = C.c_int
         _tgo = L
