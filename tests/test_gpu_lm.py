@@ -77,7 +77,10 @@ def test_generate_teacher_forced(micro):
 
 
 def test_generate_consistent_with_prefill(micro):
-    """The decode path (KV cache, one token per step) agrees with a fresh prefill of the same prefix."""
+    """The decode path (KV cache, one token per step) agrees with a fresh prefill of the same
+    prefix: every token is the prefill's argmax, or (both paths being within the logit
+    tolerance of the oracle, so within twice it of each other) one of the prefill's top two
+    whose logits lie within twice the tolerance."""
     rng = np.random.default_rng(8)
     ids = rng.integers(0, MICRO["vocab"], size=(4, 9)).astype(np.float32)
     eng = lm.Engine(micro, max_seqs=4, max_len=32)
@@ -85,7 +88,12 @@ def test_generate_consistent_with_prefill(micro):
     for step in range(6):
         prefix = np.concatenate([ids, tok[:, :step].astype(np.float32)], axis=1)
         lg = eng.forward(prefix)
-        assert (lg.argmax(axis=1) == tok[:, step]).mean() >= 0.75
+        for s in range(ids.shape[0]):
+            t = int(tok[s, step])
+            if t == int(lg[s].argmax()):
+                continue
+            top2 = np.sort(lg[s])[-2:]
+            assert lg[s][t] >= top2[0] and top2[1] - top2[0] <= 2 * (ATOL + RTOL * abs(top2[1])), f"seq {s} step {step}"
 
 
 def test_lm_rejects_bad_shapes(cuda):

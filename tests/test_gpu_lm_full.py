@@ -1,0 +1,113 @@
+"""The decoder engine at the benchmarked shapes, against the oracle (GPU).
+
+Config 5 (the headline): the Qwen3-0.6B architecture (28 layers, hidden 1024, 16/8
+heads x 128, SwiGLU 3072, vocab 151,936) built exactly as bench.py builds it --
+random N(0, 0.02) weights quantized to int4 by GPTQ on the device against 256 seeded
+N(0,1) calibration rows (the 3072-wide down projection by RTN, src/quant.c:346) --
+over the first 40 of bench.py's 1024-token prompts (seed 5). The engine runs them in
+waves of 20 sequences, and each wave's prefill in chunks of 16,384 rows (16 sequences),
+so the sampled sequences 0, 15, 16, 19, 20, 35, 36, 39 sit on both sides of every wave
+and chunk boundary. For each sampled sequence:
+
+- the last position's logits of the 1024-token prefill are within 1e-3 relative +
+  1e-4 absolute of the oracle's over all 151,936 entries (north_star's tolerance);
+- each of three greedy tokens (the prefill's argmax, then two decode steps through the
+  24-bit KV cache at positions 1024 and 1025) equals the argmax of the oracle's forward
+  of the GPU's own prefix (teacher forcing), or the oracle's top-2 logits lie within
+  that tolerance of each other.
+
+Config 4: int8 RTN weights (seed 4), the bench's 64 x 512-token prompts in one wave
+(prefill chunks of 32 sequences), logits of sequences 0, 31, 32, 63.
+
+The oracle is tgo_lm_forward_mt: the scalar restatement of the program the reference
+runs (examples/qwen3/import.py through src/vm.c), vectorised and threaded with the
+same bits (tests/test_oracle_mt.py); about 1 TFLOP per 1024-token forward, a few
+seconds on the box's host cores. Sample: 8 sequences x 3 forwards (config 5) and 4
+forwards (config 4). The GPTQ codes themselves are checked bit for bit on layer 0's
+q projection (GPTQ) and down projection (RTN) against the oracle's quantizer."""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import tgo
+from technograd_b200 import lm
+
+pytestmark = pytest.mark.gpu
+RTOL, ATOL = 1e-3, 1e-4
+V = lm.QWEN3_0_6B["vocab"]
+
+
+def oracle_logits(desc, ids: np.ndarray) -> np.ndarray:
+    out = np.zeros(V, np.float32)
+    ids = np.ascontiguousarray(ids, np.float32)
+    assert tgo.tgo().tgo_lm_forward_mt(C.addressof(desc), tgo.f32p(ids), ids.size, tgo.f32p(out), 0) == 0
+    return out
+
+
+def argmax_ok(tok: int, want: np.ndarray) -> bool:
+    if tok == int(want.argmax()):
+        return True
+    top2 = np.sort(want)[-2:]
+    return bool(top2[1] - top2[0] <= ATOL + RTOL * abs(top2[1]) and want[tok] >= top2[0])
+
+
+@pytest.fixture(scope="module")
+def config5(cuda):
+    built = lm.DeviceBuilt(lm.QWEN3_0_6B, bits=4, method="gptq", seed=5)
+    return built, built.desc()
+
+
+def test_config5_gptq_codes_bit_exact(config5):
+    """Layer 0's weights regenerated from the same device generator, quantized by the oracle."""
+    built, _ = config5
+    c = lm.QWEN3_0_6B
+    D, NQ, NKV, HD, FF = c["hidden"], c["nq"], c["nkv"], c["head_dim"], c["ffn"]
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    draws = [(V, D), (D, V), (D, NQ * HD), (D, NKV * HD), (D, NKV * HD), (NQ * HD, D), (D, FF), (D, FF), (FF, D)]
+    w = [torch.randn(*s, generator=gen, device="cuda", dtype=torch.float32) * 0.02 for s in draws]
+    rng = np.random.default_rng(5)
+    rng.standard_normal((256, HD)).astype(np.float32)  # DeviceBuilt draws the 128-wide calibration first
+    x = rng.standard_normal((256, D)).astype(np.float32)
+    H = np.zeros((D, D))
+    tgo.tgo().tgo_hessian_add(H.ctypes.data_as(tgo.DP), tgo.f32p(x), 256, D)
+    q, s = tgo.quantize(tgo.tgo(), "tgo_", w[2].cpu().numpy(), 1, 4, H)  # q projection: GPTQ (K = 1024)
+    assert np.array_equal(built.layers[0]["wq"][0], q)
+    assert np.array_equal(built.layers[0]["wq"][1].view(np.uint32), s.view(np.uint32))
+    q, s = tgo.quantize(tgo.tgo(), "tgo_", w[8].cpu().numpy(), 1, 4)  # down projection: RTN (K = 3072)
+    assert np.array_equal(built.layers[0]["wd"][0], q)
+    assert np.array_equal(built.layers[0]["wd"][1].view(np.uint32), s.view(np.uint32))
+
+
+def test_config5_prefill_and_decode_vs_oracle(config5):
+    built, (desc, keep) = config5
+    S, T, NEW = 40, 1024, 3
+    ids = np.random.default_rng(5).integers(0, V, size=(2048, T)).astype(np.float32)[:S]  # bench.py's first prompts
+    eng = lm.Engine(built, max_seqs=20, max_len=T + NEW - 1)
+    logits = eng.forward(ids)
+    tok = eng.generate(ids, NEW)
+    assert tok.shape == (S, NEW) and (tok >= 0).all() and (tok < V).all()
+    checked = bad = 0
+    for s in (0, 15, 16, 19, 20, 35, 36, 39):
+        want = oracle_logits(desc, ids[s])
+        np.testing.assert_allclose(logits[s], want, rtol=RTOL, atol=ATOL, err_msg=f"sequence {s}")
+        for step in range(NEW):
+            if step:
+                want = oracle_logits(desc, np.concatenate([ids[s], tok[s, :step].astype(np.float32)]))
+            checked += 1
+            bad += not argmax_ok(int(tok[s, step]), want)
+    assert bad == 0, f"{bad} of {checked} greedy tokens differ from the oracle's argmax beyond the tie tolerance"
+
+
+def test_config4_prefill_vs_oracle(cuda):
+    built = lm.DeviceBuilt(lm.QWEN3_0_6B, bits=8, method="rtn", seed=4)
+    desc, keep = built.desc()
+    S, T = 64, 512
+    ids = np.random.default_rng(4).integers(0, V, size=(S, T)).astype(np.float32)  # bench.py's prompts
+    logits = lm.Engine(built, max_seqs=S, max_len=T).forward(ids)
+    for s in (0, 31, 32, 63):
+        want = oracle_logits(desc, ids[s])
+        np.testing.assert_allclose(logits[s], want, rtol=RTOL, atol=ATOL, err_msg=f"sequence {s}")
+        assert int(logits[s].argmax()) == int(want.argmax()) or argmax_ok(int(logits[s].argmax()), want)

@@ -2,14 +2,18 @@
 allocate device memory (GPU).
 
 It must agree with tg_cuda_matmul_q, the entry point that allocates its scratch,
-within the float tolerance of the other GPU tests (1e-3 relative + 1e-4
-absolute), on two calls in a row: the second call reuses the fixed scratch the
-first one left behind. This file is collected last so that a failure here never
-hides another test's result."""
+and with the CPU oracle's x @ W (the reference's tg_matmul_qb arithmetic), within
+the float tolerance of the other GPU tests (1e-3 relative + 1e-4 absolute), on two
+calls in a row: the second call reuses the fixed scratch the first one left
+behind. The large shapes make the fixed array decide the split count: m*n = 2^19
+leaves room for two K splits where four CTAs per SM would want three, and
+m*n = 2^20 fills the array to its last float with a single split. This file is
+collected last so that a failure here never hides another test's result."""
 import numpy as np
 import pytest
 import torch
 
+from oracle import tgo
 from technograd_b200 import _lib, tgir
 
 pytestmark = pytest.mark.gpu
@@ -24,7 +28,8 @@ def _case(rng, bits, m, k, n):
     return q, s, a
 
 
-@pytest.mark.parametrize("bits,m,k,n", [(4, 1, 1024, 3072), (8, 5, 3072, 1024), (4, 8, 1024, 2048), (4, 3, 200, 24)])
+@pytest.mark.parametrize("bits,m,k,n", [(4, 1, 1024, 3072), (8, 5, 3072, 1024), (4, 8, 1024, 2048), (4, 3, 200, 24),
+                                        (4, 8, 4096, 1 << 16), (4, 8, 1024, 1 << 17), (8, 1, 256, 1 << 20)])
 def test_no_alloc_matches_allocating_entry_point(cuda, bits, m, k, n):
     L = _lib.lib()
     rng = np.random.default_rng(100 + m)
@@ -36,7 +41,13 @@ def test_no_alloc_matches_allocating_entry_point(cuda, bits, m, k, n):
         _lib.check(L.tg_cuda_matmul_qb_noalloc(got[call].data_ptr(), a.data_ptr(), q.data_ptr(), bits, s.data_ptr(), m, k,
                                                n, None))
         torch.cuda.synchronize()
-        np.testing.assert_allclose(got[call].cpu().numpy(), want.cpu().numpy(), rtol=RTOL, atol=ATOL)
+        mine = got[call].cpu().numpy()
+        np.testing.assert_allclose(mine, want.cpu().numpy(), rtol=RTOL, atol=ATOL)
+        # the oracle: the reference's x @ W arithmetic on the CPU (threaded, bit-identical to the scalar form)
+        oracle = np.zeros(m * n, np.float32)
+        qh, sh, ah = q.cpu().numpy(), s.cpu().numpy(), a.cpu().numpy()
+        tgo.tgo().tgo_matmul_qb_mt(tgo.f32p(oracle), tgo.f32p(ah), tgo.i8p(qh), bits, tgo.f32p(sh), m, k, n, 0)
+        np.testing.assert_allclose(mine, oracle, rtol=RTOL, atol=ATOL)
 
 
 def test_no_alloc_rejects_sizes_beyond_its_scratch(cuda):
