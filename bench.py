@@ -1,32 +1,43 @@
-"""Benchmark of the batch backend (one JSON line on rank 0).
+"""Benchmark of the batch backend (one JSON line per workload on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|lr|prefill|gemm|ssm] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload all|decode|lr|prefill|gemm|ssm] [--impl ours|reference]
 
-Workloads (seeded synthetic inputs of the stated shapes):
-  decode  config 5, the headline: Qwen3-0.6B architecture (28 layers, hidden 1024,
-          16/8 heads x 128, SwiGLU 3072, vocab 151936), random init N(0, 0.02),
-          int4 GPTQ per output column against 256 seeded N(0,1) calibration rows
-          per input width (the 3072-wide down projection RTN, as src/quant.c:346
-          does), greedy decode: 2048 sequences of 1024 uniform-random ids, each
-          continued by 257 argmax tokens (the prefill's plus 256 decode steps over
-          the KV cache). Sequences shard over ranks (2048/N each) and run in waves of
-          at most 512 per GPU; one step = one wave. Unit: generated tokens/s.
+With no --workload every config runs, one line each, in the order lr, gemm (M = 1, 16,
+256, 4096), ssm, prefill, decode; the last line is config 5, the headline metric
+BASELINE.json names. Workloads (seeded synthetic inputs of the
+stated shapes):
+  decode  config 5: Qwen3-0.6B architecture (28 layers, hidden 1024, 16/8 heads x 128,
+          SwiGLU 3072, vocab 151936), random init N(0, 0.02), int4 GPTQ per output column
+          against 256 seeded N(0,1) calibration rows per input width (the 3072-wide down
+          projection RTN, as src/quant.c:346 does), greedy decode: 2048 sequences of 1024
+          uniform-random ids, each continued by 257 argmax tokens (the prefill's plus 256
+          decode steps over the KV cache). The 2048-sequence job is fixed: rank r of N takes
+          2048/N sequences and runs them in waves of at most 512 (strong scaling); one step
+          = one wave on every rank. Unit: generated tokens/s.
   lr      config 1: latent_reasoner int8 RTN (--min-size 1), 1,048,576 rows of f32[8]
           with Bernoulli(0.5) entries (seed 1) per GPU; unit rows/s.
   gemm    config 2: tg_cuda_matmul_q axis 0 (tg_matmul_qa) on W [4096, 4096] int4/int8
           codes and X^T [4096, M], --m 1,16,256,4096 (one JSON line per M), --bits 4|8;
           unit GEMMs/s, roofline HBM for M <= 16, bf16 tensor above.
-  prefill config 4: the Qwen3-0.6B shape with int8 RTN weights (seed 4), 64 sequences x
-          512 uniform-random ids, last-position logits; unit prompt tokens/s.
   ssm     config 3: 4 selective-SSM blocks (d_model 256, d_inner 512, d_state 16, dt_rank
           16, conv 4), int8 RTN, 1024 sequences x 4096 steps of N(0,1) f32[256] (seed 3);
           unit tokens (sequence steps)/s.
+  prefill config 4: the Qwen3-0.6B shape with int8 RTN weights (seed 4), 64 sequences x
+          512 uniform-random ids, last-position logits; unit prompt tokens/s.
 
 value: the device time of each step (CUDA events on the stream the library
 launches on, first to last launch), summed over steps, max over ranks. e2e: the
 same steps timed around the synchronous C-ABI call with host buffers (ids in,
-tokens out). Under torchrun every rank runs its own shard (weak scaling: the
-per-GPU work of a step is fixed), no collective on the data path.
+tokens out). Under torchrun every rank runs its own shard, with no collective on
+the data path.
+
+--impl reference times the reference's own CPU implementation on the host cores (rank
+0 only; other ranks exit without work) and prints config 5's line, or the --workload
+given: its `tgc batch -j auto` (config 1), its tg_matmul_qa kernel (config 2), and its
+VM -- load_module, quantize_param, plan, vm_run_into, compiled from its sources into
+oracle/_ref -- on the config-3 program and on pieces of the config-4/5 Qwen3 forward at
+the config's sequence length (oracle/refvm.py says how a forward is pieced). Nothing of
+this repository's product (technograd_b200, libtgcuda) is imported on that path.
 """
 from __future__ import annotations
 
@@ -111,7 +122,17 @@ def dist_setup():
     return world, rank, local
 
 
-from technograd_b200.shard import gather_in_order, max_over_ranks, shard_range  # noqa: E402
+
+def shard_range(total: int, world: int, rank: int):
+    from technograd_b200.shard import shard_range as f
+    return f(total, world, rank)
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return float(x)
+    from technograd_b200.shard import max_over_ranks as f
+    return f(x, world)
 
 
 class L2Flush:
@@ -137,6 +158,52 @@ def barrier(world: int) -> None:
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
+
+
+# ---- the workloads as both arms name them (static: no measured values) --------------------------
+
+METRICS = {
+    "decode": ("int4 Qwen3-0.6B-shape greedy decode tokens/s (config 5)", "tokens/s"),
+    "prefill": ("int8 Qwen3-0.6B-shape batched prefill tokens/s (config 4)", "tokens/s"),
+    "ssm": ("int8 stacked selective-SSM tokens/s (config 3)", "tokens/s"),
+    "lr": ("latent_reasoner int8 batch rows/s (config 1)", "rows/s"),
+}
+
+
+def gemm_metric(bits: int, M: int):
+    return f"int{bits} dequant GEMM [4096x4096] x [4096, M={M}] GEMMs/s (config 2)", "GEMM/s"
+
+
+def workload_config(workload: str, args, M: int = 0) -> dict:
+    """The line's `config`: what was run, identical in both arms for the same flags."""
+    if workload == "decode":
+        total, prompt, new, layers = args.seqs or TOTAL_SEQS, args.prompt or PROMPT, args.new or NEW, args.layers or 28
+        full = (total, prompt, new, layers) == (TOTAL_SEQS, PROMPT, NEW, 28)
+        return {"workload": "config5 int4 GPTQ Qwen3-0.6B-shape: 2048 seqs x 1024-token prompts + 256 decode steps"
+                if full else f"REDUCED config5 shape (profiling): {total} seqs x {prompt} + {new - 1} steps, {layers} layers",
+                "seqs": total, "prompt": prompt, "new_tokens_per_seq": new, "max_seqs_per_wave": WAVE,
+                "parallelism": "sequences sharded over ranks, waves of <= 512 per GPU",
+                "l2": "inputs larger than L2 (the KV cache, tens of GB, is streamed every decode step)"}
+    if workload == "prefill":
+        seqs, T, layers = args.seqs or PF_SEQS, args.prompt or PF_T, args.layers or 28
+        return {"workload": "config4 int8 RTN Qwen3-0.6B-shape prefill: 64 seqs x 512 tokens, last-position logits"
+                if (seqs, T, layers) == (PF_SEQS, PF_T, 28) else f"REDUCED config4 shape: {seqs} seqs x {T} tokens, {layers} layers",
+                "seqs": seqs, "tokens_per_seq": T, "parallelism": "sequences sharded over ranks",
+                "l2": "inputs larger than L2 (activations 64x512x3072 f32 and weights stream every layer)"}
+    if workload == "ssm":
+        seqs, T, blocks = args.seqs or SSM_SEQS, args.prompt or SSM_T, args.layers or 4
+        return {"workload": "config3 4 SSM blocks d_model 256, d_inner 512, d_state 16, conv 4: 1024 seqs x 4096 steps"
+                if (seqs, T, blocks) == (SSM_SEQS, SSM_T, 4) else f"REDUCED config3 shape: {seqs} seqs x {T} steps, {blocks} blocks",
+                "seqs": seqs, "steps_per_seq": T, "parallelism": "sequences sharded over ranks",
+                "l2": "inputs larger than L2 (4.3 GB in, 4.3 GB out per step)"}
+    if workload == "lr":
+        return {"workload": "config1 latent_reasoner int8 RTN --min-size 1", "rows_per_gpu": LR_ROWS,
+                "parallelism": "each rank its own rows", "l2": "flushed between calls: 256 MB written, then 256 MB read"}
+    if workload == "gemm":
+        return {"workload": f"config2 M={M} int{args.bits}", "M": M, "N": GEMM_N, "K": GEMM_K,
+                "parallelism": "replicas (each rank its own GEMM)",
+                "l2": "inputs larger than L2: step i uses weight copy i mod n (together > 256 MB); the K steps run as one CUDA graph"}
+    raise ValueError(workload)
 
 
 # ---- config 5: int4 GPTQ Qwen3-0.6B-shape greedy decode ----------------------------------------
@@ -197,28 +264,25 @@ def bench_decode(args, world, rank, local):
     pre_tf = sum(s["attn_prefill_flops"] for s in stats) / (sum(s["attn_prefill_ms"] for s in stats) / 1e3) / 1e12
     tot_ms = sum(dev_ms)
     line = {
-        "metric": "int4 Qwen3-0.6B-shape greedy decode tokens/s (config 5)", "value": value, "unit": "tokens/s",
+        "metric": METRICS["decode"][0], "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
         "data": "synthetic: random-init weights N(0,0.02), uniform-random prompt ids (seed 5)",
-        "config": {"workload": "config5 int4 GPTQ Qwen3-0.6B-shape: 2048 seqs x 1024-token prompts + 256 decode steps"
-                   if (total, prompt, new, cfg["layers"]) == (TOTAL_SEQS, PROMPT, NEW, 28) else
-                   f"REDUCED config5 shape (profiling): {total} seqs x {prompt} + {new - 1} steps, {cfg['layers']} layers",
-                   "seqs_per_step_per_gpu": wave, "prompt": prompt, "new_tokens_per_seq": new,
-                   "steps_for_full_job": (total // world + wave - 1) // wave,
-                   "kv_cache": f"24-bit elements (bf16 + remainder byte, within 2^-16 of f32), "
-                               f"{wave * (prompt + new - 1) * cfg['layers'] * 8 * 128 * 6 / 1e9:.0f} GB per GPU at "
-                               f"{wave} seqs x {prompt + new - 1} positions",
-                   "l2": "inputs larger than L2 (KV cache of 75 GB streamed every decode step)",
-                   "share_of_step": {"attn_decode": dec_ms / tot_ms, "gemm": sum(s["gemm_ms"] for s in stats) / tot_ms,
-                                     "attn_prefill": sum(s["attn_prefill_ms"] for s in stats) / tot_ms},
-                   "gemm_tflops": gemm_tf, "attn_prefill_tflops_f32": pre_tf, "build_s": t_build},
+        "config": workload_config("decode", args),
+        "breakdown": {"seqs_per_step_per_gpu": wave, "steps_for_full_job": nwaves,
+                      "kv_cache": f"24-bit elements (bf16 + remainder byte, within 2^-16 of f32), "
+                                  f"{wave * (prompt + new - 1) * cfg['layers'] * 8 * 128 * 6 / 1e9:.0f} GB per GPU at "
+                                  f"{wave} seqs x {prompt + new - 1} positions",
+                      "share_of_step": {"attn_decode": dec_ms / tot_ms, "gemm": sum(s["gemm_ms"] for s in stats) / tot_ms,
+                                        "attn_prefill": sum(s["attn_prefill_ms"] for s in stats) / tot_ms},
+                      "gemm_tflops": gemm_tf, "attn_prefill_tflops_f32": pre_tf, "build_s": t_build},
         "roofline": {"kernel": "k_attn_decode (KV-cache attention)", "bound": "hbm", "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "peak_source": src,
-                     # ncu dram read+write of a 64-sequence launch was 1.014x its algorithmic bytes
-                     # (profiles/k_attn_decode_small.md); traffic grows with sequences x keys
+                     # ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_attn_decode launch over 64
+                     # sequences was 1.014x its algorithmic bytes; the bytes grow with sequences x keys
                      "traffic": 1.014 * dec_bytes / max(dec_launches, 1),
-                     "traffic_source": "ncu small-case ratio x algorithmic bytes per launch",
+                     "traffic_source": "ncu dram read+write of a 64-sequence k_attn_decode launch (1.014x its "
+                                       "algorithmic bytes), scaled to this launch's sequences x keys",
                      "bytes_per_launch": dec_bytes / max(dec_launches, 1),
                      "ms_per_launch": dec_ms / max(dec_launches, 1)},
         "e2e": {"value": world * tokens_step * args.steps / t_wall, "unit": "tokens/s",
@@ -228,33 +292,40 @@ def bench_decode(args, world, rank, local):
     return line, built, tok
 
 
-def cpu_baseline_decode(built, seconds_budget: float = 30.0):
-    """The oracle port of the reference VM (tgo_lm_forward: the same arithmetic as `tgc batch`
-    over the Qwen3 program, pinned bit-exact to the reference in tests/test_oracle.py) on the
-    host cores: one teacher-forced next token per sequence. The reference has no KV cache, so
-    each new token costs a full forward of the prefix; the sample uses a 16-token prefix."""
-    from oracle import tgo
-    d, keep = built.desc()
-    L = tgo.tgo()
-    threads = os.cpu_count() or 1
-    T = 16
-    ids = np.random.default_rng(5).integers(0, 151936, size=(threads, T)).astype(np.float32)
-    out = np.zeros((threads, 151936), np.float32)
+def ref_qwen3(T: int, bits: int, gptq: bool, seed: int):
+    """The config-4/5 forward on the reference's own VM, in pieces (oracle/refvm.py)."""
+    from oracle import refvm
+    return refvm.Qwen3Pieces(T, bits, gptq, seed)
 
-    def work(r):
-        L.tgo_lm_forward(C.addressof(d), tgo.f32p(np.ascontiguousarray(ids[r])), T, out[r].ctypes.data_as(tgo.FP))
 
-    t0 = time.perf_counter()
-    th = [threading.Thread(target=work, args=(r,)) for r in range(threads)]
-    for t in th:
-        t.start()
-    for t in th:
-        t.join()
-    dt = time.perf_counter() - t0
-    return {"value": threads / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{threads} sequences x 1 teacher-forced token at a {T}-token prefix (full Qwen3-0.6B shape, "
-                      f"int4 GPTQ codes), one thread per sequence, {dt:.1f} s; at the config's 1024-1280-token "
-                      f"prefixes each token costs ~64-80x more"}
+def ref_qwen3_line(P, per_seq_tokens: int, what: str) -> dict:
+    """The rate the piece medians so far give: every host core runs one sequence's forward."""
+    from oracle import refvm
+    fwd = P.forward_seconds()
+    n = {p: len(v) for p, v in P.times.items()}
+    return {"value": P.threads * per_seq_tokens / fwd, "unit": "tokens/s", "cores": P.threads, "kind": "reference",
+            "sample": f"{what}: the reference's VM (load_module, quantize_param, plan, vm_run_into from its own "
+                      f"sources) on pieces of the Qwen3-0.6B-shape forward at T = {P.T}, one sequence per core on "
+                      f"{P.threads} cores at once: one decoder layer's attention half, its gate/up half, its down "
+                      f"projection, and the LM head on {refvm.HEAD_ROWS} of the {P.T} rows (timed {n['attn']}, "
+                      f"{n['gate']}, {n['down']}, {n['head']} times, medians "
+                      + ", ".join(f"{statistics.median(v):.2f}" for v in P.times.values()) +
+                      f" s); one forward = 28 x (attn + gate + down) + {P.T // refvm.HEAD_ROWS} x head = {fwd:.0f} s "
+                      f"per core; setup (writing, loading, quantizing the pieces) {P.setup_s:.0f} s, not timed",
+            "forward_s_per_core": fwd}
+
+
+def cpu_baseline_decode():
+    """One pass over the pieces of a 1024-token forward (config 5: int4 GPTQ): the reference
+    has no KV cache, so every generated token costs a forward of its whole prefix."""
+    P = ref_qwen3(PROMPT, 4, True, 5)
+    try:
+        for piece in ("attn", "gate", "down", "head"):
+            P.run(piece)
+        return ref_qwen3_line(P, 1, "1 generated token per sequence at the prompt's 1024-token prefix "
+                                    "(a lower bound of the cost: later tokens see up to 1280)")
+    finally:
+        P.close()
 
 
 # ---- config 4: int8 RTN Qwen3-0.6B-shape batched prefill ---------------------------------------
@@ -301,20 +372,16 @@ def bench_prefill(args, world, rank, local):
     gemm_fl = sum(s["gemm_flops"] for s in stats)
     achieved = gemm_fl / (gemm_ms / 1e3) / 1e12
     tot_ms = sum(dev_ms)
-    full = (seqs, T, cfg["layers"]) == (PF_SEQS, PF_T, 28)
     line = {
-        "metric": "int8 Qwen3-0.6B-shape batched prefill tokens/s (config 4)", "value": world * tok * args.steps / t_dev,
+        "metric": METRICS["prefill"][0], "value": world * tok * args.steps / t_dev,
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
         "data": "synthetic: random-init weights N(0,0.02), uniform-random ids (seed 4)",
-        "config": {"workload": "config4 int8 RTN Qwen3-0.6B-shape prefill: 64 seqs x 512 tokens, last-position logits"
-                   if full else f"REDUCED config4 shape: {seqs} seqs x {T} tokens, {cfg['layers']} layers",
-                   "seqs_per_gpu": shard, "tokens_per_seq": T,
-                   "share_of_step": {"gemm": gemm_ms / tot_ms, "attn_prefill": sum(s["attn_prefill_ms"] for s in stats) / tot_ms},
-                   "attn_prefill_tflops_f32": sum(s["attn_prefill_flops"] for s in stats) /
-                   max(sum(s["attn_prefill_ms"] for s in stats) / 1e3, 1e-9) / 1e12,
-                   "l2": "inputs larger than L2 (activations 64x512x3072 f32 and weights stream every layer)",
-                   "build_s": t_build},
+        "config": workload_config("prefill", args),
+        "breakdown": {"seqs_per_gpu": shard,
+                      "share_of_step": {"gemm": gemm_ms / tot_ms, "attn_prefill": sum(s["attn_prefill_ms"] for s in stats) / tot_ms},
+                      "attn_prefill_tflops_f32": sum(s["attn_prefill_flops"] for s in stats) /
+                      max(sum(s["attn_prefill_ms"] for s in stats) / 1e3, 1e-9) / 1e12, "build_s": t_build},
         "roofline": {"kernel": "gemm_tc (tcgen05 dequant GEMM, all linear layers)", "bound": "tensor",
                      "achieved": achieved, "peak": pk["bf16_tflops_sustained"] if "bf16_tflops_sustained" in pk
                      else pk["bf16_tflops"], "unit": "TFLOP/s", "peak_source": src + " bf16 sustained",
@@ -327,35 +394,23 @@ def bench_prefill(args, world, rank, local):
     return line, built
 
 
-def cpu_baseline_prefill(built, T: int = 16):
-    """The oracle port (tgo_lm_forward, the reference VM's arithmetic over the Qwen3 program) on
-    the host cores: one T-token prefill per thread."""
-    from oracle import tgo
-    d, keep = built.desc()
-    L = tgo.tgo()
-    threads = os.cpu_count() or 1
-    ids = np.random.default_rng(4).integers(0, 151936, size=(threads, T)).astype(np.float32)
-    out = np.zeros((threads, 151936), np.float32)
-
-    def work(r):
-        L.tgo_lm_forward(C.addressof(d), tgo.f32p(np.ascontiguousarray(ids[r])), T, out[r].ctypes.data_as(tgo.FP))
-
-    t0 = time.perf_counter()
-    th = [threading.Thread(target=work, args=(r,)) for r in range(threads)]
-    for t in th:
-        t.start()
-    for t in th:
-        t.join()
-    dt = time.perf_counter() - t0
-    return {"value": threads * T / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{threads} sequences x {T}-token prefill (full Qwen3-0.6B shape, int8 RTN codes), one thread "
-                      f"per sequence, {dt:.1f} s; at 512 tokens the attention share grows from ~0.2% to ~6%"}
+def cpu_baseline_prefill():
+    """One pass over the pieces of a 512-token forward (config 4: int8 RTN), the prefill of
+    one sequence per core."""
+    P = ref_qwen3(PF_T, 8, False, 4)
+    try:
+        for piece in ("attn", "gate", "down", "head"):
+            P.run(piece)
+        return ref_qwen3_line(P, PF_T, "a 512-token prefill per sequence")
+    finally:
+        P.close()
 
 
 # ---- config 3: stacked selective-SSM blocks ------------------------------------------------------
 SSM_SEQS, SSM_T = 1024, 4096
-# DRAM bytes / algorithmic bytes of one k_ssm_scan launch, from ncu (91.3 MB of 103.8 MB on the
-# 256 x 512 case: the g writes are partly still in L2 when the kernel ends)
+# DRAM bytes / algorithmic bytes of one k_ssm_scan launch, from ncu dram__bytes_read.sum +
+# dram__bytes_write.sum (91.3 MB of 103.8 MB on 256 sequences x 512 channels: the g writes are
+# partly still in L2 when the kernel ends)
 SSM_SCAN_TRAFFIC_RATIO = 91.3 / 103.8
 
 
@@ -428,21 +483,19 @@ def bench_ssm(args, world, rank, local):
     # (S sequences x one chunk of 64 steps)
     scan_bytes = float(S * 64 * (cfg["d_inner"] * 12 + (cfg["dt_rank"] + 2 * cfg["d_state"]) * 4))
     line = {
-        "metric": "int8 stacked selective-SSM tokens/s (config 3)", "value": world * tok * args.steps / t_dev,
+        "metric": METRICS["ssm"][0], "value": world * tok * args.steps / t_dev,
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
         "data": "synthetic: random-init weights N(0,0.02) int8 RTN, inputs N(0,1) (seed 3)",
-        "config": {"workload": "config3 4 SSM blocks d_model 256, d_inner 512, d_state 16, conv 4: 1024 seqs x 4096 steps"
-                   if full else f"REDUCED config3 shape: {seqs} seqs x {T} steps, {cfg['blocks']} blocks",
-                   "seqs_per_gpu": S, "steps_per_seq": T, "chunk": 64,
-                   "share_of_step": {"scan": scan_ms / tot_ms, "gemm": gemm_ms / tot_ms}, "gemm_tflops": gemm_tf,
-                   "l2": f"inputs larger than L2 ({u.nbytes / 1e9:.2f} GB in, {u.nbytes / 1e9:.2f} GB out per step)",
-                   "build_s": t_build},
+        "config": workload_config("ssm", args),
+        "breakdown": {"seqs_per_gpu": S, "chunk": 64, "share_of_step": {"scan": scan_ms / tot_ms, "gemm": gemm_ms / tot_ms},
+                      "gemm_tflops": gemm_tf, "build_s": t_build},
         "roofline": {"kernel": "k_ssm_scan (FP32 pipe + SFU)", "bound": "fp32", "achieved": scan_tf,
                      "peak": FP32_NOMINAL_TFLOPS, "unit": "TFLOP/s", "frac": scan_tf / FP32_NOMINAL_TFLOPS,
                      "peak_source": "nominal FP32 SIMT (148 SMs x 128 lanes x FMA x 1965 MHz); not in MEASURED_PEAKS",
                      "traffic": SSM_SCAN_TRAFFIC_RATIO * scan_bytes, "bytes_per_launch": scan_bytes,
-                     "traffic_source": "ncu small-case ratio (profiles/k_ssm_scan_config3_small.md) x algorithmic bytes per launch"},
+                     "traffic_source": "ncu dram read+write of a 256-sequence k_ssm_scan launch (0.88x its algorithmic "
+                                       "bytes), scaled to this launch's sequences"},
         "e2e": {"value": world * tok * args.steps / t_wall, "unit": "tokens/s", "h2d_bytes_per_step": u.nbytes,
                 "d2h_bytes_per_step": u.nbytes},
         "gpu_launches": int(sum(s["launches"] for s in stats)), "clocks": clocks,
@@ -450,29 +503,24 @@ def bench_ssm(args, world, rank, local):
     return line, model
 
 
-def cpu_baseline_ssm(model, T: int = 96):
-    """The oracle port (tgo_ssm_forward: the reference VM's arithmetic over the same program,
-    pinned bit-exact to `tgc batch` in tests/test_ssm.py) on the host cores, one sequence per
-    thread; the cost per step does not depend on T."""
-    from oracle import tgo
-    d, keep = model.desc()
-    L = tgo.tgo()
-    threads = os.cpu_count() or 1
-    u = np.random.default_rng(3).standard_normal((threads, T, 256)).astype(np.float32)
-    out = np.zeros_like(u)
+SSM_REF_T = 256
 
-    def work(r):
-        L.tgo_ssm_forward(C.addressof(d), tgo.f32p(u[r]), T, out[r].ctypes.data_as(tgo.FP))
 
-    t0 = time.perf_counter()
-    th = [threading.Thread(target=work, args=(r,)) for r in range(threads)]
-    for t in th:
-        t.start()
-    for t in th:
-        t.join()
-    dt = time.perf_counter() - t0
-    return {"value": threads * T / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{threads} sequences x {T} steps (full config-3 blocks), one thread per sequence, {dt:.1f} s"}
+def cpu_baseline_ssm(S=None, runs: int = 1):
+    """The config-3 program on the reference's own VM (oracle/refvm.py SsmSample): one
+    sequence of SSM_REF_T steps per host core, all at once."""
+    from oracle import refvm
+    own = S is None
+    S = S or refvm.SsmSample(SSM_REF_T)
+    try:
+        t = statistics.median([S.run() for _ in range(runs)])
+        return {"value": S.threads * S.T / t, "unit": "tokens/s", "cores": S.threads, "kind": "reference",
+                "sample": f"the reference's VM (load_module, quantize_param --bits 8 --min-size 1, plan, vm_run_into) "
+                          f"on the config-3 program at full block widths, {S.T} steps per sequence, one sequence per "
+                          f"core on {S.threads} cores at once, {t:.2f} s (a scan step costs the same at every position)"}
+    finally:
+        if own:
+            S.close()
 
 
 # ---- config 2: weight-only dequant GEMM microbench ---------------------------------------------
@@ -484,11 +532,15 @@ GEMM_TC_TRAFFIC = {(256, 4): 12625920.0}
 def gemm_inputs(bits: int, M: int):
     """W codes uniform in [-8, 7] (int4) or [-127, 127] (int8), [N, K]; scale |N(0,0.02)|/7 or /127
     per output row; X [M, K] ~ N(0,1); seed 2. The reference op is tg_matmul_qa(o, q, bits, s, X^T, N, K, M)."""
-    from technograd_b200.tgir import pack_codes
     rng = np.random.default_rng(2)
     lo, hi = (-8, 8) if bits == 4 else (-127, 128)
     codes = rng.integers(lo, hi, size=GEMM_N * GEMM_K)
-    q = np.ascontiguousarray(pack_codes(codes, bits))
+    if bits == 8:
+        q = codes.astype(np.int8)
+    else:  # element i in byte i/2, low nibble first (runtime/tg_rt.h:124-129)
+        nib = (codes & 0xF).astype(np.uint8)
+        q = (nib[0::2] | (nib[1::2] << 4)).view(np.int8)
+    q = np.ascontiguousarray(q)
     s = (np.abs(rng.normal(0, 0.02, size=GEMM_N)) / (7 if bits == 4 else 127)).astype(np.float32)
     x = rng.standard_normal((M, GEMM_K), dtype=np.float32)
     return q, s, np.ascontiguousarray(x.T)  # b = X^T [K, M]
@@ -583,19 +635,18 @@ def bench_gemm(args, world, rank, local, M: int, bits: int):
     path = ("gemv_rows (CUDA cores)" if M <= 8 else
             "split_f32_t (activations -> bf16 hi/lo) + gemm_tc (tcgen05, codes expanded in the kernel)")
     line = {
-        "metric": f"int{bits} dequant GEMM [4096x4096] x [4096, M={M}] GEMMs/s (config 2)",
+        "metric": gemm_metric(bits, M)[0],
         "value": world * args.steps / t, "unit": "GEMM/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": sum(ms) / len(ms), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": f"int{bits} codes, f32 activations and accumulation" + ("" if M <= 8 else " (bf16 hi/lo split)"),
         "data": "synthetic (seed 2)",
-        "config": {"workload": f"config2 M={M} int{bits}", "M": M, "N": GEMM_N, "K": GEMM_K, "path": path,
-                   "l2": f"inputs larger than L2: step i uses weight copy i mod {ncopies} "
-                         f"({ncopies * q.nbytes >> 20} MB in all); the K steps run as one CUDA graph",
-                   "algorithmic_bytes": byts, "flops": flops},
+        "config": workload_config("gemm", args, M),
+        "breakdown": {"path": path, "weight_copies": ncopies, "weight_bytes_cycled": ncopies * q.nbytes,
+                      "algorithmic_bytes": byts, "flops": flops},
         "roofline": {"kernel": path, "bound": "hbm" if hbm else "tensor", "achieved": achieved, "peak": peak,
                      "unit": unit, "frac": achieved / peak, "peak_source": src + (" hbm_gbs" if hbm else " bf16 burst"),
                      "traffic": GEMM_TC_TRAFFIC.get((M, bits)),
-                     "traffic_source": "ncu dram bytes of one gemm_tc launch (profiles/gemm_tc_config2_m256.md)"
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gemm_tc launch at this M"
                      if (M, bits) in GEMM_TC_TRAFFIC else None},
         "e2e": {"value": world * args.steps / te, "unit": "GEMM/s", "h2d_bytes_per_step": b.nbytes,
                 "d2h_bytes_per_step": GEMM_N * M * 4},
@@ -712,15 +763,15 @@ def bench_lr(args, world, rank, local):
     with _lib.HostRegistered(rows, out_h, st_h):  # page-locked once, outside the timed region
         te = e2e()
     line = {
-        "metric": "latent_reasoner int8 batch rows/s (config 1)", "value": world * LR_ROWS * args.steps / t,
+        "metric": METRICS["lr"][0], "value": world * LR_ROWS * args.steps / t,
         "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": sum(ms) / len(ms), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config1 latent_reasoner int8 RTN --min-size 1", "rows_per_gpu": LR_ROWS,
-                   "think_steps_mean": float(steps_np.mean()), "l2": L2Flush.NOTE,
-                   "e2e_host_buffers": "page-locked with tg_cuda_host_register (direct DMA)",
-                   "e2e_pageable_rows_per_s": world * LR_ROWS * args.steps / te_pageable,
-                   "kernel": "generated for the program (NVRTC, sm_100a)" if spec else f"tape interpreter ({why})"},
+        "config": workload_config("lr", args),
+        "breakdown": {"think_steps_mean": float(steps_np.mean()),
+                      "e2e_host_buffers": "page-locked with tg_cuda_host_register (direct DMA)",
+                      "e2e_pageable_rows_per_s": world * LR_ROWS * args.steps / te_pageable,
+                      "kernel": "generated for the program (NVRTC, sm_100a)" if spec else f"tape interpreter ({why})"},
         "roofline": {"kernel": "tg_rowvm (generated for the program)" if spec else "vm_kernel (tape interpreter)",
                      "bound": "fp32", "achieved": achieved, "peak": FP32_NOMINAL_TFLOPS,
                      "unit": "TFLOP/s", "frac": achieved / FP32_NOMINAL_TFLOPS, "traffic": None,
@@ -752,59 +803,81 @@ def cpu_baseline_lr(rows: np.ndarray):
 
 # ---- the reference arm --------------------------------------------------------------------------
 
-def reference_arm(args, world, rank, local):
-    if rank != 0:
-        return None
-    if args.workload == "lr":
+def reference_arm(args) -> list:
+    """The reference's own CPU implementation of the path, timed on the host cores (no GPU,
+    no process group, nothing of technograd_b200): the lines for --workload (config 5 by
+    default), with the same metric, unit and config as this repository's arm."""
+    wl = "decode" if args.workload == "all" else args.workload
+    out = []
+
+    def emit(metric, unit, cfg, scaling, vals, walls, base):
+        v = statistics.median(vals)
+        base = dict(base, value=v)
+        out.append({"impl": "reference", "metric": metric, "value": v, "unit": unit, "n_gpus": 0, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": 1e3 * sum(walls) / len(walls), "higher_is_better": True,
+                    "scaling": scaling, "vs_baseline": None, "dtype": "f32 (int8/int4 codes, f32 accumulation)",
+                    "data": "synthetic", "config": cfg, "cpu_baseline": base,
+                    "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+
+    if wl == "lr":
         rows = lr_inputs(LR_ROWS)
+        if cpu_baseline_lr(rows) is None:
+            return [{"impl": "reference", "unavailable": "oracle/_ref/tgc was not built (needs the reference sources)"}]
         for _ in range(args.warmup):
             cpu_baseline_lr(rows)
-        vals, base = [], None
+        vals, walls, base = [], [], None
         for _ in range(args.steps):
+            t = time.perf_counter()
             base = cpu_baseline_lr(rows)
-            if base is None:
-                return {"impl": "reference", "unavailable": "oracle/_ref/tgc was not built (needs the reference sources)"}
+            walls.append(time.perf_counter() - t)
             vals.append(base["value"])
-        metric, unit, cfgw = "latent_reasoner int8 batch rows/s (config 1)", "rows/s", "config1 latent_reasoner int8 RTN --min-size 1"
-    elif args.workload == "gemm":
-        M, bits = args.m[0], args.bits
-        q, s, b = gemm_inputs(bits, M)
-        vals = [cpu_baseline_gemm(q, s, b, bits, M, budget_s=5.0)["value"] for _ in range(args.steps)]
-        base = cpu_baseline_gemm(q, s, b, bits, M, budget_s=5.0)
-        metric, unit = f"int{bits} dequant GEMM [4096x4096] x [4096, M={M}] GEMMs/s (config 2)", "GEMM/s"
-        cfgw = f"config2 M={M} int{bits}"
-    elif args.workload == "ssm":
-        from technograd_b200 import _lib, ssm
-        _lib.init(0, [local])
-        model = ssm.quantize_rtn_device(ssm.random_weights(ssm.CONFIG3, seed=3), ssm.CONFIG3, 8)
-        vals, base = [], None
-        for _ in range(args.steps):
-            base = cpu_baseline_ssm(model)
-            vals.append(base["value"])
-        metric, unit = "int8 stacked selective-SSM tokens/s (config 3)", "tokens/s"
-        cfgw = "config3 4 SSM blocks d_model 256, d_inner 512, d_state 16, conv 4: 1024 seqs x 4096 steps"
+        emit(*METRICS["lr"], workload_config("lr", args), "weak", vals, walls, base)
+    elif wl == "gemm":
+        for M in args.m:
+            q, s, b = gemm_inputs(args.bits, M)
+            for _ in range(args.warmup):
+                cpu_baseline_gemm(q, s, b, args.bits, M, budget_s=0.5)
+            vals, walls, base = [], [], None
+            for _ in range(args.steps):
+                t = time.perf_counter()
+                base = cpu_baseline_gemm(q, s, b, args.bits, M, budget_s=1.0)
+                walls.append(time.perf_counter() - t)
+                vals.append(base["value"])
+            emit(*gemm_metric(args.bits, M), workload_config("gemm", args, M), "weak", vals, walls, base)
+    elif wl == "ssm":
+        from oracle import refvm
+        S = refvm.SsmSample(SSM_REF_T)
+        try:
+            for _ in range(args.warmup):
+                S.run()
+            vals, walls, base = [], [], None
+            for _ in range(args.steps):
+                t = time.perf_counter()
+                base = cpu_baseline_ssm(S)
+                walls.append(time.perf_counter() - t)
+                vals.append(base["value"])
+        finally:
+            S.close()
+        emit(*METRICS["ssm"], workload_config("ssm", args), "strong", vals, walls, base)
     else:
-        # the model is generated on the GPU (same seeds as our arm), then the CPU port runs
-        from technograd_b200 import _lib, lm
-        _lib.init(0, [local])
-        pre = args.workload == "prefill"
-        built = lm.DeviceBuilt(lm.QWEN3_0_6B, bits=8 if pre else 4, method="rtn" if pre else "gptq", seed=4 if pre else 5)
-        vals, base = [], None
-        for _ in range(args.steps):
-            base = cpu_baseline_prefill(built) if pre else cpu_baseline_decode(built)
-            vals.append(base["value"])
-        if pre:
-            metric, unit = "int8 Qwen3-0.6B-shape batched prefill tokens/s (config 4)", "tokens/s"
-            cfgw = "config4 int8 RTN Qwen3-0.6B-shape prefill: 64 seqs x 512 tokens, last-position logits"
-        else:
-            metric, unit = "int4 Qwen3-0.6B-shape greedy decode tokens/s (config 5)", "tokens/s"
-            cfgw = "config5 int4 GPTQ Qwen3-0.6B-shape: 2048 seqs x 1024-token prompts + 256 decode steps"
-    v = statistics.median(vals)
-    base["value"] = v
-    return {"impl": "reference", "metric": metric, "value": v, "unit": unit, "n_gpus": 0, "steps": args.steps,
-            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": cfgw}, "cpu_baseline": base,
-            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        from oracle import refvm
+        pre = wl == "prefill"
+        P = ref_qwen3(PF_T if pre else PROMPT, 8 if pre else 4, not pre, 4 if pre else 5)
+        try:
+            for i in range(args.warmup):
+                P.run(refvm.PIECES[i % len(refvm.PIECES)])
+            P.times = {p: [] for p in refvm.PIECES}
+            walls = []
+            # one piece per step, in turn; at least one of each, so a forward can be assembled
+            for i in range(max(args.steps, len(refvm.PIECES))):
+                walls.append(P.run(refvm.PIECES[i % len(refvm.PIECES)]))
+            base = ref_qwen3_line(P, PF_T if pre else 1, "a 512-token prefill per sequence" if pre else
+                                  "1 generated token per sequence at the prompt's 1024-token prefix (a lower bound "
+                                  "of the cost: later tokens see up to 1280)")
+        finally:
+            P.close()
+        emit(*METRICS[wl], workload_config(wl, args), "strong", [base["value"]], walls, base)
+    return out
 
 
 def main():
@@ -812,7 +885,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="decode", choices=["decode", "lr", "prefill", "gemm", "ssm"])
+    ap.add_argument("--workload", default="all", choices=["all", "decode", "lr", "prefill", "gemm", "ssm"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     # shape overrides for small profiling captures; the line's config says when they were used
@@ -821,41 +894,55 @@ def main():
     ap.add_argument("--new", type=int, default=0)
     ap.add_argument("--layers", type=int, default=0)
     # config 2: batch sizes (one JSON line per M) and code width
-    ap.add_argument("--m", type=lambda v: [int(x) for x in v.split(",")], default=[1])
+    ap.add_argument("--m", type=lambda v: [int(x) for x in v.split(",")], default=[1, 16, 256, 4096])
     ap.add_argument("--bits", type=int, default=4, choices=[4, 8])
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    world, rank, local = dist_setup()
     if args.impl == "reference":
-        line = reference_arm(args, world, rank, local)
-    elif args.workload == "lr":
-        line, rows = bench_lr(args, world, rank, local)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_lr(rows)
-    elif args.workload == "ssm":
-        line, model = bench_ssm(args, world, rank, local)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_ssm(model)
-    elif args.workload == "prefill":
-        line, built = bench_prefill(args, world, rank, local)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_prefill(built)
-    elif args.workload == "gemm":
-        for M in args.m[:-1]:  # every M but the last prints here; the last takes the common path below
-            ln, data = bench_gemm(args, world, rank, local, M, args.bits)
-            if rank == 0 and world == 1 and not args.no_cpu_baseline:
-                ln["cpu_baseline"] = cpu_baseline_gemm(*data, args.bits, M)
-            if rank == 0:
-                print(json.dumps(ln), flush=True)
-        line, data = bench_gemm(args, world, rank, local, args.m[-1], args.bits)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_gemm(*data, args.bits, args.m[-1])
-    else:
-        line, built, _ = bench_decode(args, world, rank, local)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_decode(built)
-    if rank == 0 and line:
-        print(json.dumps(line), flush=True)
+        if int(os.environ.get("RANK", "0")) != 0:
+            return  # rank 0 alone times the reference; the others have no work
+        for line in reference_arm(args):
+            print(json.dumps(line), flush=True)
+        return
+    world, rank, local = dist_setup()
+    base = rank == 0 and world == 1 and not args.no_cpu_baseline
+    order = ["lr", "gemm", "ssm", "prefill", "decode"] if args.workload == "all" else [args.workload]
+    for wl in order:
+        lines = []
+        if wl == "lr":
+            line, rows = bench_lr(args, world, rank, local)
+            if base:
+                line["cpu_baseline"] = cpu_baseline_lr(rows)
+            lines.append(line)
+        elif wl == "gemm":
+            for M in args.m:
+                line, data = bench_gemm(args, world, rank, local, M, args.bits)
+                if base:
+                    line["cpu_baseline"] = cpu_baseline_gemm(*data, args.bits, M, budget_s=3.0)
+                lines.append(line)
+        elif wl == "ssm":
+            line, _ = bench_ssm(args, world, rank, local)
+            if base:
+                line["cpu_baseline"] = cpu_baseline_ssm()
+            lines.append(line)
+        elif wl == "prefill":
+            line, _ = bench_prefill(args, world, rank, local)
+            if base:
+                line["cpu_baseline"] = cpu_baseline_prefill()
+            lines.append(line)
+        else:
+            line, _, _ = bench_decode(args, world, rank, local)
+            if base:
+                line["cpu_baseline"] = cpu_baseline_decode()
+            lines.append(line)
+        if rank == 0:
+            for line in lines:
+                print(json.dumps(line), flush=True)
+        import gc
+
+        import torch
+        gc.collect()
+        torch.cuda.empty_cache()
     if world > 1:
         import torch.distributed as dist
         barrier(world)

@@ -41,10 +41,21 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("TG_REFERENCE", "/root/reference")
+
+
+def _reference() -> str:
+    """The reference checkout: $TG_REFERENCE, else a `reference` directory beside this repository."""
+    for d in (os.environ.get("TG_REFERENCE"), os.path.join(os.path.dirname(ROOT), "reference")):
+        if d and os.path.exists(os.path.join(d, "src", "vm.c")):
+            return d
+    sys.exit("make_golden.py: set TG_REFERENCE to the reference checkout (no src/vm.c found)")
+
+
+REF = _reference()
 sys.path.insert(0, ROOT)
 
 from oracle import tgo  # noqa: E402
+from oracle.refvm import emit_ssm  # noqa: E402
 
 
 def sh(*args, **kw) -> str:
@@ -263,53 +274,6 @@ def ssm_weights(cfg: dict, seed: int) -> dict:
         w[f"D_{b}"] = np.ones(DI, np.float32)
         w[f"Wo_{b}"] = g(DI, DM)
     return w
-
-
-def emit_ssm(cfg: dict, w: dict, outdir: str, T: int) -> str:
-    """The config-3 program in the reference's language: per block one scan over the steps
-    with the state h and the last three conv inputs as carries (include/tg_cuda.h
-    tg_cuda_ssm_desc states the arithmetic)."""
-    B, DM, DI, DS, R = (cfg[k] for k in ("blocks", "d_model", "d_inner", "d_state", "dt_rank"))
-    os.makedirs(os.path.join(outdir, "w"), exist_ok=True)
-    tables = {"Zh": np.zeros((DI, DS), np.float32), "Zc": np.zeros(DI, np.float32)}
-    for name, arr in list(w.items()) + list(tables.items()):
-        np.asarray(arr, dtype="<f4").tofile(os.path.join(outdir, "w", name + ".bin"))
-    lines = ["model ssm", ""]
-
-    def par(name, *shape):
-        lines.append(f'param {name} : f32[{", ".join(map(str, shape))}] = file("w/{name}.bin")')
-
-    par("nf", DM), par("Zh", DI, DS), par("Zc", DI)
-    for b in range(B):
-        par(f"nw_{b}", DM), par(f"Wx_{b}", DM, DI), par(f"Wz_{b}", DM, DI)
-        for i in range(4):
-            par(f"cw{i}_{b}", DI)
-        par(f"cb_{b}", DI), par(f"Wr_{b}", DI, R), par(f"WB_{b}", DI, DS), par(f"WC_{b}", DI, DS)
-        par(f"Wdt_{b}", R, DI), par(f"bdt_{b}", DI), par(f"A_{b}", DI, DS), par(f"D_{b}", DI), par(f"Wo_{b}", DI, DM)
-    lines += ["", f"def forward(u0: f32[{T}, {DM}]) -> f32[{T}, {DM}]:"]
-    for b in range(B):
-        lines += [f"    h{b} = Zh", f"    c1_{b} = Zc", f"    c2_{b} = Zc", f"    c3_{b} = Zc",
-                  f"    scan h{b}, c1_{b}, c2_{b}, c3_{b} over ut in u{b}:",
-                  f"        n = rmsnorm(ut) * nw_{b}",
-                  f"        xi = n @ Wx_{b}",
-                  f"        z = n @ Wz_{b}",
-                  f"        xc = c3_{b} * cw0_{b} + c2_{b} * cw1_{b} + c1_{b} * cw2_{b} + xi * cw3_{b} + cb_{b}",
-                  f"        c3_{b} = c2_{b}",
-                  f"        c2_{b} = c1_{b}",
-                  f"        c1_{b} = xi",
-                  "        xs = silu(xc)",
-                  f"        dt = softplus((xs @ Wr_{b}) @ Wdt_{b} + bdt_{b})",
-                  f"        bt = xs @ WB_{b}",
-                  f"        ct = xs @ WC_{b}",
-                  f"        e = exp(-(reshape(dt, {DI}, 1) * A_{b}))",
-                  f"        h{b} = e * h{b} + (1 - e) / A_{b} * outer(xs, bt)",
-                  f"        y = h{b} @ ct + D_{b} * xs",
-                  f"        emit u{b + 1} = ut + (y * silu(z)) @ Wo_{b}"]
-    lines.append(f"    return rmsnorm(u{B}) * nf")
-    path = os.path.join(outdir, "ssm.tg")
-    with open(path, "w") as f:
-        f.write("\n".join(lines) + "\n")
-    return path
 
 
 def nano_ssm(tgc: str) -> None:
