@@ -2,8 +2,8 @@
 tests/scan/nested_grad.tg, tests/attn/window.tg) and the programs of its sparse and
 memory tests (tests/memory/topk.tg, topk_pad.tg, scan.tg, sufmatch.tg; tests/quant/mlp.tg
 as f32 and quantized to int8 / int4, an spmm table) on the oracle VM and on the device
-row executor, against `tgc batch` output of the reference (tests/golden/programs); the
-reference's remaining stateless programs on the oracle VM.
+row executor, against `tgc batch` output of the reference (tests/golden/programs), and the
+reference's remaining stateless programs the same way.
 
 The oracle follows the reference's arithmetic order with the same libm, so it must
 agree bit for bit. The device path: values within 1e-4 + 1e-3 |ref|; think steps
@@ -91,7 +91,7 @@ def test_halt_step_counts(golden):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("name", NAMES)
+@pytest.mark.parametrize("name", NAMES + SMALL_NAMES)
 def test_device_executor_matches_tgc_batch(cuda, golden, name):
     m, rows, want, want_steps = fixture(golden, name)
     out, steps = Batch(m).run(rows)
