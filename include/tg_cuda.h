@@ -54,6 +54,16 @@ int tg_cuda_ngpus(void);
  * the kernel's status code (1, a timed-out full-barrier wait). Any other return means
  * the mechanism failed. The context stays usable. No reference counterpart. */
 int tg_cuda_selftest_wait(long long cycles, int *status);
+/* Test hook, no reference counterpart: the decoder's bf16 GEMM on device buffers,
+ * out = epilogue(sum over pairs q of a[pa[q]] [m, k] times b[pb[q]] [n, k] transposed),
+ * through the tile kernel (path 0) or the swapped-operand cluster kernel that the decode
+ * steps use (path 1). epi 0 stores (times scale[n] when scale is not NULL), 1 adds into
+ * out, 2 is SwiGLU: b's rows interleave blocks of 32 gate and 32 up channels, and
+ * out_hi/out_lo receive the bf16 hi/lo of silu(gate * scale) * (up * scale2), [m, n/2]
+ * with row stride ldo. Synchronous. */
+int tg_cuda_selftest_gemm(int path, const void *const *a, int na, const void *const *b, int nb, int npairs,
+			  const int *pa, const int *pb, int m, int n, int k, int epi, const float *scale,
+			  const float *scale2, float *out, long ldo, void *out_hi, void *out_lo, void *stream);
 /* Release every device resource the library holds. */
 void tg_cuda_shutdown(void);
 

@@ -22,7 +22,7 @@ OP = {name: i for i, name in enumerate(OPS)}
 PARAM, INPUT, TMP, STATE = 0, 1, 2, 3
 
 # Every entry point include/tg_cuda.h declares.
-SYMBOLS = ["tg_cuda_error", "tg_cuda_init", "tg_cuda_ngpus", "tg_cuda_selftest_wait", "tg_cuda_shutdown", "tg_cuda_matmul_q",
+SYMBOLS = ["tg_cuda_error", "tg_cuda_init", "tg_cuda_ngpus", "tg_cuda_selftest_wait", "tg_cuda_selftest_gemm", "tg_cuda_shutdown", "tg_cuda_matmul_q",
            "tg_cuda_matmul_qb_noalloc",
            "tg_cuda_quantize_rtn", "tg_cuda_gptq_prepare", "tg_cuda_quantize_gptq", "tg_cuda_gptq_free", "tg_cuda_load", "tg_cuda_batch", "tg_cuda_batch_device", "tg_cuda_free",
            "tg_cuda_host_register", "tg_cuda_host_unregister",
@@ -117,6 +117,8 @@ def lib() -> C.CDLL:
             "tg_cuda_init": ([i, C.POINTER(i)], i),
             "tg_cuda_ngpus": ([], i),
             "tg_cuda_selftest_wait": ([C.c_longlong, C.POINTER(i)], i),
+            "tg_cuda_selftest_gemm": ([i, C.POINTER(vp), i, C.POINTER(vp), i, i, C.POINTER(i), C.POINTER(i), i, i, i, i,
+                                       vp, vp, vp, C.c_long, vp, vp, vp], i),
             "tg_cuda_shutdown": ([], None),
             "tg_cuda_matmul_q": ([i, vp, vp, vp, i, vp, i, i, i, vp], i),
             "tg_cuda_matmul_qb_noalloc": ([vp, vp, vp, i, vp, i, i, i, vp], i),

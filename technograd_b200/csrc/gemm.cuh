@@ -48,6 +48,14 @@ struct GemmArgs {
 // 32 matching up rows), N = 2 * channels, output channels = N / 2.
 int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st);
 
+// Small batches (gemm_sk.cu): the same product with the weights in the MMA's 128-row slot
+// and K split over a thread-block cluster, summed in a fixed order. bf16 operands, epilogues
+// STORE / ADD / SWIGLU with scale_mode 0 or 2. gemm_sk_prepare sets the kernels' attributes
+// (once per device, outside any stream capture).
+bool gemm_sk_fits(const GemmArgs &p);
+int gemm_sk(const GemmOperands &ops, const GemmArgs &p, cudaStream_t st);
+int gemm_sk_prepare();
+
 int split_to_bf16(const float *src, long rows, long cols, long lds, bool transpose, __nv_bfloat16 *hi, __nv_bfloat16 *lo,
 		  long ldd, cudaStream_t st);
 int codes_to_bf16(const signed char *q, int bits, long rows, long cols, bool transpose, __nv_bfloat16 *dst, long ldd,

@@ -436,6 +436,7 @@ struct Engine {
 	long g_S = -1, g_kernels = 0;
 	int g_T = -1, g_nnew = -1;
 	bool g_prof = false;
+	bool small_gemm = true; // batches of 129-384 rows on gemm_sk (TG_CUDA_SMALL_GEMM=tile: the tile kernels)
 };
 
 enum { MK_DECODE = 1, MK_PREFILL = 2, MK_GEMM = 3 };
@@ -483,13 +484,19 @@ static void mark_end(Engine &g, int i)
 	if (i >= 0) ev_check(g, record(g, (g.capturing ? g.gmarks : g.marks)[i].b), "cudaEventRecord(mark end)");
 }
 
+// A layer's GEMM. Batches of 129-384 rows (a decode step of a 256-sequence wave) go to the
+// swapped-operand cluster kernel (gemm_sk.cu); measured per decode step of the full model
+// (28 layers), it takes 2.62 ms of GEMMs at 256 sequences against 2.88 ms for the tile
+// kernels, but 3.97 / 2.22 ms against 3.84 / 2.10 ms at 512 / 128, so other batches, and the
+// LM head's 151,936 columns, stay on the tile kernels. TG_CUDA_SMALL_GEMM=tile in the
+// environment at load time keeps every GEMM on the tile kernels (for comparisons).
 static int gemm_m(Engine &g, const GemmOperands &op, const GemmArgs &p0)
 {
 	GemmArgs p = p0;
-	p.partial = g.part.as<float>(); // split-K scratch for the small-batch decode GEMMs
+	p.partial = g.part.as<float>(); // split-K scratch for the tile kernel's small batches
 	p.partial_floats = (long)(g.part.bytes / sizeof(float));
 	int mk = mark_begin(g, MK_GEMM, 2.0 * p.M * p.N * p.K);
-	int rc = gemm(op, p, g.st);
+	int rc = g.small_gemm && p.M > 128 && p.M <= 384 && p.N <= 16384 && gemm_sk_fits(p) ? gemm_sk(op, p, g.st) : gemm(op, p, g.st);
 	mark_end(g, mk);
 	return rc;
 }
@@ -652,6 +659,11 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 	}
 	// kernel attributes are set here, never inside a graph capture
 	if (decode_smem(g) > 220 * 1024) return set_err(TG_CUDA_EINVAL, "max_len %d: decode scores exceed shared memory", max_len);
+	{
+		const char *e = getenv("TG_CUDA_SMALL_GEMM");
+		g.small_gemm = !(e && strcmp(e, "tile") == 0);
+	}
+	if ((rc = gemm_sk_prepare())) return rc;
 	TGC_CUDA(cudaFuncSetAttribute(k_attn_prefill_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FA_SMEM));
 	TGC_CUDA(cudaFuncSetAttribute(k_attn_decode<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_smem(g)));
 	TGC_CUDA(cudaFuncSetAttribute(k_attn_decode<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_smem(g)));
