@@ -2,6 +2,8 @@
 // selection, fault injection and small device helpers.
 #pragma once
 
+#include <utility>
+
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -67,6 +69,34 @@ struct DevBuf {
 	void release();
 	template <class T> T *as() const { return (T *)p; }
 };
+
+// Programmatic dependent launch. A kernel launched with the programmatic-serialization
+// attribute (launch_pdl) may start while the kernel before it on the stream is finishing;
+// pdl_wait() blocks the calling thread until that kernel has completed and its writes are
+// visible, so every thread calls it before it reads data a previous kernel may write or
+// writes data one may read. pdl_launch() lets the next such kernel start early. Both are
+// no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// L2 prefetch of a contiguous global range (16-byte aligned, bytes a multiple of 16). L2 is
+// where every device write lands first, so prefetching before pdl_wait reads no stale data.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes)
+{
+	asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((uint64_t)p), "r"(bytes) : "memory");
+}
+
+template <class... KArgs, class... Args>
+static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+				     Args &&...args)
+{
+	cudaLaunchConfig_t cfg = {};
+	cfg.gridDim = grid, cfg.blockDim = block, cfg.dynamicSmemBytes = smem, cfg.stream = st;
+	cudaLaunchAttribute attr[1];
+	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	attr[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = attr, cfg.numAttrs = 1;
+	return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Decoding of the reference's int4 packing: element e in byte e/2, low nibble first,
 // sign-extended (runtime/tg_rt.h:124-129).

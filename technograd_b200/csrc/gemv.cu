@@ -42,6 +42,13 @@ __global__ void __launch_bounds__(32 * KS) gemv_rows(float *__restrict__ o, cons
 	const int nchunks = k / CPC, cper = (nchunks + KS - 1) / KS;
 	const int c0 = ks * cper, c1 = min(nchunks, c0 + cper);
 	const signed char *qr = q + (long)min(row, m - 1) * row_bytes;
+	// this CTA's code rows into L2 while the kernel before it may still run (launched with
+	// programmatic serialization), then wait for it: the activations and the output may be its
+	const int r0 = blockIdx.x * 32, nr = min(32, m - r0);
+	if (threadIdx.x == 0 && nr > 0 && (row_bytes & 15) == 0 && ((uintptr_t)q & 15) == 0)
+		prefetch_l2(q + (long)r0 * row_bytes, (uint32_t)(nr * row_bytes));
+	pdl_wait();
+	pdl_launch();
 	if (SMB) {
 		for (int i = threadIdx.x; i < k * NB / 4; i += blockDim.x) sb4[i] = ((const float4 *)b)[i];
 		__syncthreads();
@@ -150,11 +157,10 @@ static int launch_rows_nb(float *o, const signed char *q, const float *s, const 
 			cudaFuncSetAttribute(gemv_rows<BITS, NB, KS, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
 			attr[dev] = true;
 		}
-		gemv_rows<BITS, NB, KS, true><<<grid, 32 * KS, smem, st>>>(o, q, s, b, m, k);
+		TGC_CUDA(launch_pdl(gemv_rows<BITS, NB, KS, true>, dim3(grid), dim3(32 * KS), smem, st, o, q, s, b, m, k));
 	} else {
-		gemv_rows<BITS, NB, KS, false><<<grid, 32 * KS, 0, st>>>(o, q, s, b, m, k);
+		TGC_CUDA(launch_pdl(gemv_rows<BITS, NB, KS, false>, dim3(grid), dim3(32 * KS), 0, st, o, q, s, b, m, k));
 	}
-	TGC_LAUNCH_CHECK();
 	return TG_CUDA_OK;
 }
 
