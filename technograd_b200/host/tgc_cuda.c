@@ -12,11 +12,17 @@
  * written with io_write_row, so text output is byte-compatible with the CPU path's format.
  *
  *   tgc_cuda [flags] batch MODEL DATA [-o OUT] --device cuda
+ *   tgc_cuda [flags] stream MODEL [SRC] [-o DST] --device cuda
+ *                                            row in, row out, flushed (src/serve.c:251-285):
+ *                                            each row runs through the micro-batcher
+ *                                            (tg_cuda_batcher_run), the compute of run_line
+ *                                            (src/serve.c:129-149); SRC/DST '-' or a file
  *   tgc_cuda cuda-kernel MODEL [-o OUT.cu]   the CUDA source generated for MODEL, compiled
  *                                            for sm_100a without a GPU (a build-time check)
  *   tgc_cuda <anything else>                 the reference's tgc, unchanged
  *
  * Built with the reference's sources (oracle/Makefile, target tgc_cuda). */
+#define _GNU_SOURCE /* getline */
 #include "tg.h"
 #include "tg_cuda.h"
 
@@ -31,6 +37,7 @@ int tgc_ref_main(int argc, char **argv); /* src/main.c's main */
 static void usage_cuda(void)
 {
 	fputs("usage: tgc batch <file> <data> [-o out] --device cuda\n"
+	      "       tgc stream <file> [src] [-o dst] --device cuda\n"
 	      "       tgc cuda-kernel <file> [-o out.cu]\n", stderr);
 	exit(2);
 }
@@ -181,6 +188,75 @@ static int batch_cuda(int argc, char **argv)
 	return tg_exit_status();
 }
 
+/* tgc stream on the GPUs: the loop of stream_main (src/serve.c:251-285) with run_line's
+ * compute (src/serve.c:129-149) handed to the micro-batcher. A row with a bad number or the
+ * wrong count gets the reference's `error:` line and the stream goes on; a row the device
+ * could not run gets `error: <the library's text>`. One reader thread submits one row at a
+ * time, so the batcher runs each row at once (max_wait 0); a server with many connections
+ * would let rows of different connections share batches. tcp:// endpoints stay with the
+ * reference's path. */
+static int stream_cuda(int argc, char **argv)
+{
+	const char *opath = NULL;
+	if (argc >= 5 && strcmp(argv[argc - 2], "-o") == 0) {
+		opath = argv[argc - 1];
+		argc -= 2;
+	}
+	if (argc != 3 && argc != 4) usage_cuda();
+	const char *src = argc == 4 ? argv[3] : "-";
+	if (strncmp(src, "tcp://", 6) == 0 || (opath && strncmp(opath, "tcp://", 6) == 0))
+		die(NULL, 0, "--device cuda: stream reads and writes '-' or files; tcp:// runs on the CPU path");
+	Module *m = load_module(argv[2]);
+	plan(m);
+	int per = 0;
+	for (int i = 0; i < m->ninputs; i++) per += shape_numel(&m->val[m->inputs[i]].sh);
+	const int n = shape_numel(&m->val[m->output].sh), nt = m->nthink ? m->nthink : 1;
+	tg_cuda_model *gpu = cuda_load(m);
+	tg_cuda_batcher *bt = NULL;
+	if (tg_cuda_batcher_new(gpu, 8192, 0, &bt)) die(NULL, 0, "--device cuda: %s", tg_cuda_error());
+	FILE *in = strcmp(src, "-") ? fopen(src, "r") : stdin;
+	if (!in) die(NULL, 0, "cannot open '%s'", src);
+	FILE *out = opath ? fopen(opath, "w") : stdout;
+	if (!out) die(NULL, 0, "cannot write '%s'", opath);
+	tg_signals();
+	float *row = xmalloc((size_t)(per ? per : 1) * sizeof *row), *o = xmalloc((size_t)n * sizeof *o);
+	int *steps = xmalloc((size_t)nt * sizeof *steps);
+	char *line = NULL;
+	size_t cap = 0;
+	long rows = 0;
+	double t0 = tr_now_ms();
+	while (!tg_stopping() && getline(&line, &cap, in) >= 0) {
+		const char *bad;
+		const int k = io_parse_row(line, NULL, 0, &bad);
+		if (k == 0) continue;
+		rows++;
+		if (k < 0) fprintf(out, "error: bad number near '%.20s'\n", bad);
+		else if (k != per) fprintf(out, "error: row has %d values, model %s needs %d\n", k, m->name, per);
+		else {
+			io_parse_row(line, row, per, &bad);
+			if (tg_cuda_batcher_run(bt, row, o, steps)) fprintf(out, "error: %s\n", tg_cuda_error());
+			else io_write_row(out, 0, o, n, steps, m->nthink);
+		}
+		if (fflush(out)) break; /* peer gone */
+	}
+	free(line);
+	if (in != stdin) fclose(in);
+	if (out != stdout && fclose(out)) die(NULL, 0, "write failed '%s'", opath);
+	if (tr_on(1)) {
+		tr_begin(1, "stream");
+		tr_num("rows", (double)rows);
+		tr_num("ms", tr_now_ms() - t0);
+		tr_end("%ld row(s) streamed on --device cuda", rows);
+	}
+	tg_cuda_batcher_free(bt);
+	tg_cuda_free(gpu);
+	tg_cuda_shutdown();
+	xfree(row);
+	xfree(o);
+	xfree(steps);
+	return tg_exit_status();
+}
+
 /* The kernel the library generates for MODEL, compiled for sm_100a: no GPU needed. */
 static int cuda_kernel(int argc, char **argv)
 {
@@ -257,7 +333,8 @@ int main(int argc, char **argv)
 		return cuda_kernel(n, argv);
 	}
 	if (!cuda) return tgc_ref_main(argc, orig); /* not ours: the reference, with its arguments untouched */
-	if (!cmd || strcmp(cmd, "batch") != 0) die(NULL, 0, "--device cuda applies to `tgc batch`");
+	if (!cmd || (strcmp(cmd, "batch") != 0 && strcmp(cmd, "stream") != 0))
+		die(NULL, 0, "--device cuda applies to `tgc batch` and `tgc stream`");
 	/* drop the -j/--log pairs the reference would have consumed: the GPU path has no CPU threads */
 	int n = 1;
 	for (int i = 1; i < k; i++) {
@@ -270,5 +347,5 @@ int main(int argc, char **argv)
 		argv[n++] = argv[i];
 	}
 	argv[n] = NULL;
-	return batch_cuda(n, argv);
+	return strcmp(cmd, "stream") == 0 ? stream_cuda(n, argv) : batch_cuda(n, argv);
 }

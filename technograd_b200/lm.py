@@ -48,8 +48,8 @@ class Model:
             keep.append(a)
             return a.ctypes.data_as(_lib.FP)
 
-        def qmat(codes: np.ndarray, scales: np.ndarray):
-            q = np.ascontiguousarray(tgir.pack_codes(codes, self.bits))
+        def qmat(q: np.ndarray, scales: np.ndarray):  # packed codes
+            q = np.ascontiguousarray(q, np.int8)
             s = np.ascontiguousarray(scales, np.float32)
             keep.extend([q, s])
             m = _lib.QMat()
@@ -57,9 +57,22 @@ class Model:
             m.s = s.ctypes.data_as(_lib.FP)
             return m
 
+        def packed_rows(p: QParam) -> np.ndarray | None:  # [rows, packed bytes per row], or None
+            per = p.shape[1] * self.bits // 8
+            if self.bits == 4 and p.shape[1] % 2:
+                return None  # a row ends inside a byte
+            return p.q[:p.shape[0] * per].reshape(p.shape[0], per)
+
+        def cat(names, axis):  # per-head params joined along the column (1) or row (0) axis
+            ps = [self.q[n] for n in names]
+            s = np.concatenate([p.s for p in ps])
+            rows = [packed_rows(p) for p in ps]
+            if all(r is not None for r in rows):  # join the packed bytes as they are
+                return qmat(np.concatenate(rows, axis=axis).ravel(), s)
+            return qmat(tgir.pack_codes(np.concatenate([p.codes() for p in ps], axis=axis), self.bits), s)
+
         def cat_cols(names):  # per-head [D, HD] params -> [D, n*HD], scales concatenated
-            codes = np.concatenate([self.q[n].codes() for n in names], axis=1)
-            return qmat(codes, np.concatenate([self.q[n].s for n in names]))
+            return cat(names, 1)
 
         d = _lib.LmDesc()
         d.layers, d.hidden, d.nq, d.nkv, d.head_dim, d.ffn, d.vocab = L, D, NQ, NKV, HD, FF, V
@@ -69,7 +82,7 @@ class Model:
         d.rope_theta = float(c["theta"])
         d.embed = f32p(self.f32["E"])
         d.final_norm = f32p(self.f32["lnf"])
-        d.lm_head = qmat(self.q["LM"].codes(), self.q["LM"].s)
+        d.lm_head = qmat(self.q["LM"].q, self.q["LM"].s)
         arrs = {k: (_lib.FP * L)() for k in ("ln1", "ln2", "qn", "kn")}
         mats = {k: (_lib.QMat * L)() for k in ("wq", "wk", "wv", "wo", "wg", "wu", "wd")}
         for l in range(L):
@@ -78,11 +91,9 @@ class Model:
             mats["wq"][l] = cat_cols([f"Wq_{l}_{h}" for h in range(NQ)])
             mats["wk"][l] = cat_cols([f"Wk_{l}_{j}" for j in range(NKV)])
             mats["wv"][l] = cat_cols([f"Wv_{l}_{j}" for j in range(NKV)])
-            wo_codes = np.concatenate([self.q[f"Wo_{l}_{h}"].codes() for h in range(NQ)], axis=0)  # [NQ*HD, D]
-            wo_s = np.concatenate([self.q[f"Wo_{l}_{h}"].s for h in range(NQ)])                  # [NQ*D]
-            mats["wo"][l] = qmat(wo_codes, wo_s)
+            mats["wo"][l] = cat([f"Wo_{l}_{h}" for h in range(NQ)], 0)  # [NQ*HD, D], scales [NQ*D]
             for k, n in (("wg", "Wg"), ("wu", "Wu"), ("wd", "Wd")):
-                mats[k][l] = qmat(self.q[f"{n}_{l}"].codes(), self.q[f"{n}_{l}"].s)
+                mats[k][l] = qmat(self.q[f"{n}_{l}"].q, self.q[f"{n}_{l}"].s)
         for k, v in arrs.items():
             setattr(d, k, C.cast(v, _lib.FPP))
         for k, v in mats.items():
@@ -92,10 +103,15 @@ class Model:
 
     @classmethod
     def from_tgir(cls, path: str, cfg: dict) -> "Model":
-        """A `tgc quantize`d Qwen3 program (optionally .gz)."""
-        op = gzip.open if path.endswith(".gz") else open
-        with op(path, "rt", encoding="utf-8") as f:
-            m = tgir.read(f.read())
+        """A `tgc quantize`d Qwen3 program. A plain file is read through a memory map with
+        its number lists parsed straight into arrays and the quantized params kept as their
+        packed codes (tgir.load), so a full-size model loads in memory proportional to its
+        codes; a .gz file is decompressed first."""
+        if path.endswith(".gz"):
+            with gzip.open(path, "rb") as f:
+                m = tgir.read(f.read())
+        else:
+            m = tgir.load(path)
         f32, q, bits = {}, {}, 0
         for v in m.vals:
             if v.kind != _lib.PARAM:

@@ -40,32 +40,69 @@ class Sym(str):
 
 
 _DECIMAL_BYTES = b"0123456789eE+-. \t\n\r\v\f"
-_BARE_SIGN = re.compile(rb"[+-](?![0-9.])")
+_SPACE = re.compile(rb"\s")
+_CHUNK = 1 << 25  # bytes of text parsed at a time
 
 
 def _plain_decimals(span) -> bool:
     """Whether a number list holds only decimal forms numpy parses as strtod does. Lists with
-    anything else (hex floats, inf/nan, symbols) or a bare sign go atom by atom."""
-    return not bytes(span).translate(None, _DECIMAL_BYTES) and _BARE_SIGN.search(span) is None
+    anything else (hex floats, inf/nan, symbols, a nested list or comment) or a bare sign go
+    atom by atom."""
+    if span.translate(None, _DECIMAL_BYTES):
+        return False
+    b = np.frombuffer(span, np.uint8)
+    sign = (b == 43) | (b == 45)  # '+' or '-'
+    if not sign.any():
+        return True
+    if sign[-1]:
+        return False
+    nx = b[1:]
+    number = (nx - np.uint8(48) <= 9) | (nx == 46)  # a digit (uint8 wrap) or '.' follows
+    return not (sign[:-1] & ~number).any()
 
 
-def _payload(span: bytes, head: str) -> np.ndarray:
-    """The numbers of a (data ...), (codes ...) or (scale ...) list, parsed in C. Codes are
-    integers (src/ir.c:478-509); data and scales are read as doubles and later rounded to
-    f32, as the reference's strtod + (float) does (src/sexp.c:112-121)."""
-    if not span.strip():
-        return np.zeros(0, np.int32 if head == "codes" else np.float64)
+def _parse_chunk(span: bytes, head: str) -> np.ndarray:
     with warnings.catch_warnings():
         warnings.simplefilter("error", DeprecationWarning)  # a partial parse is an error
         try:
             if head == "codes":
                 try:
-                    return np.fromstring(span, dtype=np.int32, sep=" ")
+                    c = np.fromstring(span, dtype=np.int32, sep=" ")
+                    return c.astype(np.int8) if c.size and -128 <= c.min() and c.max() <= 127 else c
                 except (ValueError, DeprecationWarning):
                     pass  # not plain integers: let the generic check below decide
             return np.fromstring(span, dtype=np.float64, sep=" ")
         except (ValueError, DeprecationWarning) as e:
             raise TgirError(f"bad number in ({head} ...)") from e
+
+
+def _payload(buf, start: int, end: int, head: str) -> np.ndarray | None:
+    """The numbers of the (data ...), (codes ...) or (scale ...) list whose text is
+    buf[start:end], parsed in C a few tens of MB at a time (split at whitespace), or None
+    when the list holds anything but plain decimals. Codes are integers (src/ir.c:478-509;
+    int8 when they fit); data and scales are read as doubles, as the reference's strtod
+    does (src/sexp.c:112-121), and rounded to f32 chunk by chunk as its (float) does, so a
+    list of hundreds of millions of numbers never exists as doubles or as one string."""
+    parts = []
+    s = start
+    while s < end:
+        e = min(end, s + _CHUNK)
+        if e < end:  # end the chunk at whitespace so that no number is split
+            m = _SPACE.search(buf, e, end)
+            e = m.start() if m else end
+        span = buf[s:e]
+        if not _plain_decimals(span):
+            return None
+        if span and not span.isspace():
+            x = _parse_chunk(span, head)
+            if x.dtype == np.float64 and head != "codes":
+                with np.errstate(over="ignore"):  # (float) of a double past the f32 range is inf, as in C
+                    x = x.astype(np.float32)
+            parts.append(x)
+        s = e
+    if not parts:
+        return np.zeros(0, np.int32 if head == "codes" else np.float32)
+    return parts[0] if len(parts) == 1 else np.concatenate(parts)
 
 
 def read_sexp(src, fast: bool = True) -> list:
@@ -87,10 +124,10 @@ def read_sexp(src, fast: bool = True) -> list:
                 end = buf.find(b")", pm.end())
                 if end < 0:
                     raise TgirError("unterminated list")
-                span = buf[pm.end():end]
-                if b"(" not in span and b";" not in span and _plain_decimals(span):
-                    head = pm.group(1).decode()
-                    stack[-1].append([Sym(head), _payload(span, head)])
+                head = pm.group(1).decode()
+                arr = _payload(buf, pm.end(), end, head)
+                if arr is not None:
+                    stack[-1].append([Sym(head), arr])
                     pos = end + 1
                     continue
         pos = m.end()
@@ -134,6 +171,15 @@ class PValue:
     @property
     def numel(self) -> int:
         return int(np.prod(self.shape)) if self.shape else 1
+
+    def dense(self) -> np.ndarray | None:
+        """The param's f32 values: its data, or for a quantized param code * scale of the
+        element's channel (src/ir.c:495-507, one f32 rounding), made on demand so that a
+        large quantized model is held as its codes only."""
+        if self.data is not None or not self.qbits:
+            return self.data
+        c2 = unpack_codes(self.q, self.qbits, self.numel).reshape(self.shape[0], -1).astype(np.float32)
+        return (c2 * (self.qs[:, None] if self.qaxis == 0 else self.qs[None, :])).astype(np.float32).ravel()
 
 
 @dataclass
@@ -198,11 +244,11 @@ def pack_codes(codes: np.ndarray, bits: int) -> np.ndarray:
         codes = codes.astype(np.int64)
     if bits == 8:
         return codes.astype(np.int8)
-    if codes.size % 2:
-        codes = np.concatenate([codes, [0]])
-    lo = codes[0::2] & 0x0F
-    hi = (codes[1::2] & 0x0F) << 4
-    return (lo | hi).astype(np.uint8).view(np.int8)
+    u = codes.astype(np.uint8)  # the low nibble survives the wrap
+    if u.size % 2:
+        u = np.concatenate([u, np.zeros(1, np.uint8)])
+    pair = u.reshape(-1, 2)
+    return ((pair[:, 0] & 0x0F) | (pair[:, 1] << 4)).view(np.int8)
 
 
 def unpack_codes(q: np.ndarray, bits: int, n: int) -> np.ndarray:
@@ -378,7 +424,7 @@ def read(src, fast: bool = True) -> Module:
                 raise TgirError("malformed quant axis (0 or 1, rank-2 param)")
             bits, axis = int(f[3][1]), int(f[3][2])
             with np.errstate(over="ignore"):  # (float) of a double past the f32 range is inf, as in C
-                sc = _numbers(f[3][3]).astype(np.float32)
+                sc = _numbers(f[3][3]).astype(np.float32, copy=False)
             codes = _numbers(f[3][4])
             if codes.dtype.kind == "f":
                 if not np.array_equal(codes, np.round(codes)):
@@ -388,21 +434,19 @@ def read(src, fast: bool = True) -> Module:
             if codes.size != n or sc.size != shape[axis]:
                 raise TgirError(f"param '{f[1]}': quant sizes")
             lim = 127 if bits == 8 else 7
-            if np.abs(codes).max(initial=0) > lim:
+            if codes.size and (codes.min() < -lim or codes.max() > lim):
                 raise TgirError(f"param '{f[1]}': code out of range")
             v = m.value(_lib.PARAM, shape, str(f[1]))
             pv = m.vals[v]
             pv.qbits, pv.qaxis = bits, axis
             pv.q = pack_codes(codes, bits)
-            pv.qs = sc
-            # data = code * scale of the element's channel (src/ir.c:495-507), one f32 rounding
-            c2 = codes.reshape(shape[0], -1).astype(np.float32)
-            pv.data = (c2 * (sc[:, None] if axis == 0 else sc[None, :])).astype(np.float32).ravel()
+            pv.qs = sc  # data (code * scale, src/ir.c:495-507) is made on demand: PValue.dense()
+            del codes
             rd.define(f[1], v)
         elif h in ("param", "state"):
             shape = _shape(f[2])
             with np.errstate(over="ignore"):
-                data = _numbers(f[3]).astype(np.float32)
+                data = _numbers(f[3]).astype(np.float32, copy=False)
             if data.size != int(np.prod(shape)):
                 raise TgirError(f"param '{f[1]}' needs {int(np.prod(shape))} values, has {data.size}")
             v = m.value(_lib.PARAM if h == "param" else _lib.STATE, shape, str(f[1]))
@@ -460,8 +504,9 @@ class CProgram:
             for d, n in enumerate(pv.shape):
                 cv.dim[d] = n
             cv.index = pv.index
-            if pv.data is not None:
-                arr = np.ascontiguousarray(pv.data, dtype=np.float32)
+            dense = pv.dense()
+            if dense is not None:
+                arr = np.ascontiguousarray(dense, dtype=np.float32)
                 self._keep.append(arr)
                 cv.data = arr.ctypes.data_as(_lib.FP)
             if pv.qbits:

@@ -153,3 +153,26 @@ def test_device_cuda_programs_match_fixtures(tmp_path, name):
     from technograd_b200.batch import load_samples
     rows = load_samples(os.path.join(PROGRAMS, f"{name}_rows.csv"), m.per)
     _check(path, rows, got, want, m.nout, m.nthink)
+
+
+@pytest.mark.gpu
+def test_stream_device_cuda_matches_reference_stream(tmp_path):
+    """`tgc stream --device cuda` (rows through the micro-batcher) against the reference's
+    `tgc stream` on the same lines: the same error lines for malformed rows, values within
+    tolerance and think steps under the 1e-6 rule for the rest."""
+    from technograd_b200 import tgir
+    rows = np.random.default_rng(13).integers(0, 2, size=(300, 8)).astype(np.float32)
+    lines = [",".join(f"{v:g}" for v in r) for r in rows]
+    lines[7], lines[100] = "1,2,x", "1,2,3"  # a bad number and a short row
+    (tmp_path / "in.csv").write_text("\n".join(lines) + "\n")
+    a = run(TGC_CUDA, "stream", LR, "in.csv", "-o", "gpu.txt", "--device", "cuda", cwd=tmp_path)
+    b = run(TGC, "stream", LR, "in.csv", "-o", "cpu.txt", cwd=tmp_path)
+    assert a.returncode == b.returncode == 0, a.stderr
+    got, want = (tmp_path / "gpu.txt").read_text().splitlines(), (tmp_path / "cpu.txt").read_text().splitlines()
+    assert len(got) == len(want) == 300
+    good = [i for i in range(300) if not want[i].startswith("error:")]
+    for i in set(range(300)) - set(good):
+        assert got[i] == want[i]
+    g = np.array([[float(x) for x in got[i].split(",")] for i in good])
+    w = np.array([[float(x) for x in want[i].split(",")] for i in good])
+    _check(LR, rows[good], g, w, 4, tgir.load(LR).nthink)

@@ -68,7 +68,7 @@ def test_codes_as_the_reference_reads_them(tmp_path, fast):
     want = tgc_values(tmp_path, src, len(codes))
     assert want is not None
     w = tgir.read(src, fast=fast).vals[0]
-    assert np.array_equal(np.zeros(len(codes), np.float32) + w.data.astype(np.float32), want)
+    assert np.array_equal(np.zeros(len(codes), np.float32) + w.dense().astype(np.float32), want)
     for bad in (["+", "1", "2"], ["1.5", "1", "2"], ["128", "1", "2"], ["nan", "1", "2"]):
         src = quant_model(bad)
         assert tgc_values(tmp_path, src, 3) is None

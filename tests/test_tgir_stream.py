@@ -70,7 +70,7 @@ def test_large_quantized_param_reads_in_bounded_memory(tmp_path):
     assert np.array_equal(w.q, tgir.pack_codes(codes, 4))
     assert np.array_equal(w.qs, scale)
     want = (codes.reshape(rows, cols).astype(np.float32) * scale[:, None]).ravel()
-    assert np.array_equal(w.data, want)
+    assert w.data is None and np.array_equal(w.dense(), want)  # dequantized on demand
     # arrays of the param: codes parsed as int32 (16.8 MB), data f32 (16.8 MB) and its
     # f32 codes (16.8 MB), packed codes (2.1 MB); one atom per number would need > 200 MB
     assert peak < 80 << 20, f"peak {peak >> 20} MB"
@@ -92,4 +92,39 @@ def test_non_integer_codes_are_rejected():
     src = ("(tgir 1 (model m) (param W (f32 2 2) (quant 8 0 (scale 0.5 0.5) (codes 1 2.5 3 4)))"
            " (input x (f32 2)) (block (%2 (f32 2) (matmul W x))) (output %2))")
     with pytest.raises(tgir.TgirError, match="integers"):
+        tgir.read(src)
+
+
+@pytest.mark.parametrize("chunk", [5, 64])
+def test_chunked_number_lists_match_generic(monkeypatch, chunk):
+    """Number lists parsed a few bytes at a time (split at whitespace) read exactly as the
+    generic reader reads them."""
+    monkeypatch.setattr(tgir, "_CHUNK", chunk)
+    for path in sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "programs", "*.tgir")))[:12]:
+        with open(path) as f:
+            src = f.read()
+        _same(tgir.load(path), tgir.read(src, fast=False))
+    src, codes, scale = _big_quant_src(16, 64)
+    m = tgir.read(src)
+    assert np.array_equal(m.vals[0].q, tgir.pack_codes(codes, 4)) and np.array_equal(m.vals[0].qs, scale)
+
+
+@pytest.mark.parametrize("chunk", [3, 1 << 20])
+@pytest.mark.parametrize("codes,bits", [("1 2 3 -128", 8), ("1 2 3 300", 8), ("1 -8 3 4", 4), ("1 8 3 4", 4)])
+def test_out_of_range_codes_are_rejected(monkeypatch, chunk, codes, bits):
+    monkeypatch.setattr(tgir, "_CHUNK", chunk)
+    src = (f"(tgir 1 (model m) (param W (f32 2 2) (quant {bits} 0 (scale 0.5 0.5) (codes {codes})))"
+           " (input x (f32 2)) (block (%2 (f32 2) (matmul W x))) (output %2))")
+    with pytest.raises(tgir.TgirError, match="out of range"):
+        tgir.read(src)
+
+
+@pytest.mark.parametrize("chunk", [2, 1 << 20])
+def test_a_bare_sign_at_a_chunk_end_goes_atom_by_atom(monkeypatch, chunk):
+    """'1 -' ends a chunk with a sign: not a plain decimal list, so the generic reader
+    decides (a bare sign is a symbol, src/sexp.c:112-121, and a symbol among numbers an
+    error)."""
+    monkeypatch.setattr(tgir, "_CHUNK", chunk)
+    src = "(tgir 1 (model m) (param p (f32 3) (data 1 - 2)) (input x (f32 3)) (block (%2 (f32 3) (add p x))) (output %2))"
+    with pytest.raises(tgir.TgirError, match="bad number"):
         tgir.read(src)
