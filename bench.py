@@ -71,9 +71,13 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
+    """nvidia-smi samples during the timed region. A timed region shorter than the 200 ms
+    sampling period is bracketed by a sample taken before it (first()) and by untimed repeats
+    of the same work after it (hold()), so the clocks it ran at are on record."""
 
     def __init__(self, gpu: int):
+        self.t0 = time.perf_counter()
+        self.held = None
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -83,6 +87,26 @@ class Clocks:
                                        "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
+
+    def first(self, timeout: float = 5.0) -> None:
+        """Waits for the sampler's first row (nvidia-smi takes a moment to start)."""
+        if self.p is None:
+            return
+        t = time.perf_counter()
+        while time.perf_counter() - t < timeout:
+            self.f.flush()
+            with open(self.f.name) as g:
+                if g.read().count("\n"):
+                    return
+            time.sleep(0.02)
+
+    def hold(self, work, min_s: float = 1.0) -> None:
+        """Repeats `work` (untimed) until the sampler has run for min_s seconds."""
+        n = 0
+        while time.perf_counter() - self.t0 < min_s:
+            work()
+            n += 1
+        self.held = n
 
     def stop(self) -> dict:
         if self.p is None:
@@ -104,8 +128,12 @@ class Clocks:
         mx = [v for v in (num(r[2]) for r in rows) if v is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+               "reasons": reasons, "samples": len(rows)}
+        if self.held is not None:
+            out["window"] = (f"a sample before the timed region, the region, and {self.held} untimed repeats of the "
+                             "same work right after it")
+        return out
 
 
 def dist_setup():
@@ -202,7 +230,9 @@ def workload_config(workload: str, args, M: int = 0) -> dict:
     if workload == "gemm":
         return {"workload": f"config2 M={M} int{args.bits}", "M": M, "N": GEMM_N, "K": GEMM_K,
                 "parallelism": "replicas (each rank its own GEMM)",
-                "l2": "inputs larger than L2: step i uses weight copy i mod n (together > 256 MB); the K steps run as one CUDA graph"}
+                "step": "one call on each of the weight copies in turn",
+                "l2": "inputs larger than L2: consecutive calls use different weight copies (together > 256 MB); the K "
+                      "steps run as one CUDA graph"}
     raise ValueError(workload)
 
 
@@ -578,17 +608,19 @@ def bench_gemm(args, world, rank, local, M: int, bits: int):
     for i in range(max(args.warmup, 2)):  # the first calls allocate the library's scratch
         call(do.data_ptr(), db.data_ptr(), i)
     torch.cuda.synchronize()
-    # the K timed steps, one call each on the next weight copy, captured as one CUDA graph so
-    # the per-call launch cost of the host is not timed
+    # a step is one call on each weight copy in turn (a stream of GEMMs, as a decoder issues
+    # them); the K timed steps are captured as one CUDA graph so the per-call launch cost of
+    # the host is not timed
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=side):
-        for i in range(args.steps):
+        for i in range(args.steps * ncopies):
             call(do.data_ptr(), db.data_ptr(), i)
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
     barrier(world)
     clk = Clocks(local)
+    clk.first()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     flush()
     torch.cuda.nvtx.range_push("timed")
@@ -597,6 +629,7 @@ def bench_gemm(args, world, rank, local, M: int, bits: int):
     e1.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
+    clk.hold(lambda: (graph.replay(), torch.cuda.synchronize()))
     barrier(world)
     clocks = clk.stop()
     ms = [e0.elapsed_time(e1) / args.steps] * args.steps
@@ -626,33 +659,35 @@ def bench_gemm(args, world, rank, local, M: int, bits: int):
     te = max_over_ranks(sum(wall), world)
     byts, flops = gemm_cost(bits, M)
     pk, src = peaks()
-    per = sum(ms) / 1e3 / args.steps
+    per = sum(ms) / 1e3 / args.steps / ncopies  # one GEMM
     hbm = M <= 16
     if hbm:
         achieved, peak, unit = byts / per / 1e9, pk["hbm_gbs"], "GB/s"
     else:
         achieved, peak, unit = flops / per / 1e12, pk["bf16_tflops"], "TFLOP/s"
-    path = ("gemv_rows (CUDA cores)" if M <= 8 else
+    path = ("gemv_bulk (code rows read coalesced into registers, CUDA cores, packed f32x2 FMAs)" if M <= 8 else
             "split_f32_t (activations -> bf16 hi/lo) + gemm_tc (tcgen05, codes expanded in the kernel)")
     line = {
         "metric": gemm_metric(bits, M)[0],
-        "value": world * args.steps / t, "unit": "GEMM/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "value": world * args.steps * ncopies / t, "unit": "GEMM/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup,
         "ms_per_step": sum(ms) / len(ms), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": f"int{bits} codes, f32 activations and accumulation" + ("" if M <= 8 else " (bf16 hi/lo split)"),
         "data": "synthetic (seed 2)",
         "config": workload_config("gemm", args, M),
-        "breakdown": {"path": path, "weight_copies": ncopies, "weight_bytes_cycled": ncopies * q.nbytes,
-                      "algorithmic_bytes": byts, "flops": flops},
+        "breakdown": {"path": path, "gemms_per_step": ncopies, "us_per_gemm": per * 1e6, "weight_copies": ncopies,
+                      "weight_bytes_cycled": ncopies * q.nbytes, "algorithmic_bytes": byts, "flops": flops},
         "roofline": {"kernel": path, "bound": "hbm" if hbm else "tensor", "achieved": achieved, "peak": peak,
                      "unit": unit, "frac": achieved / peak, "peak_source": src + (" hbm_gbs" if hbm else " bf16 burst"),
                      "traffic": GEMM_TC_TRAFFIC.get((M, bits)),
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gemm_tc launch at this M"
                      if (M, bits) in GEMM_TC_TRAFFIC else None},
         "e2e": {"value": world * args.steps / te, "unit": "GEMM/s", "h2d_bytes_per_step": b.nbytes,
-                "d2h_bytes_per_step": GEMM_N * M * 4},
+                "d2h_bytes_per_step": GEMM_N * M * 4,
+                "step": "one GEMM through tg_cuda_matmul_q: activations in from pinned host memory, the product out"},
         # GEMV: one kernel; tensor cores: the activation split, the GEMM, and the fixed-order
         # split-K reduction when fewer than 74 output tiles would leave SMs idle
-        "gpu_launches": args.steps * (1 if M <= 8 else 2 + (32 * -(-M // (256 if M >= 256 else 128)) * 2 <= 148)),
+        "gpu_launches": args.steps * ncopies * (1 if M <= 8 else 2 + (32 * -(-M // (256 if M >= 256 else 128)) * 2 <= 148)),
         "clocks": clocks,
     }
     return line, (q, s, b)
@@ -734,6 +769,7 @@ def bench_lr(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     clk = Clocks(local)
+    clk.first()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     for i in range(args.steps):
         flush()
@@ -741,6 +777,7 @@ def bench_lr(args, world, rank, local):
         step()
         ev[i][1].record(stream)
     torch.cuda.synchronize()
+    clk.hold(lambda: (step(), torch.cuda.synchronize()))
     barrier(world)
     clocks = clk.stop()
     ms = [a.elapsed_time(z) for a, z in ev]

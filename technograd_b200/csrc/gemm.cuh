@@ -61,5 +61,8 @@ int split_to_bf16(const float *src, long rows, long cols, long lds, bool transpo
 int codes_to_bf16(const signed char *q, int bits, long rows, long cols, bool transpose, __nv_bfloat16 *dst, long ldd,
 		  cudaStream_t st);
 int device_status_check(int *d_status, cudaStream_t st);
+// The per-device status word of the drop-in matmul calls (pinned, mapped; written only by a
+// kernel wait that timed out): an earlier call's timeout is reported, then cleared.
+int call_status_word(int dev, int **d_status);
 
 } // namespace tgc

@@ -911,8 +911,9 @@ int codes_to_bf16(const signed char *q, int bits, long rows, long cols, bool tra
 
 // ---- tg_cuda_matmul_q, large batch -------------------------------------------------------------
 
-// The drop-in call stays asynchronous: the GEMM's device status word is copied into a
-// pinned host word after each call, and a later call on the device reports it.
+// The drop-in call stays asynchronous: the kernels' status word is a pinned, mapped host
+// word that a wait which timed out writes directly, and a later call on the device reports
+// it (call_status_word; shared with the GEMV of gemv_bulk.cuh).
 struct TcScratch {
 	DevBuf buf, part;        // part: split-K partial sums of small-batch calls (64 MB)
 	int *h_status = nullptr; // pinned, mapped: the kernels' status word (written only by a wait that timed out)
@@ -930,6 +931,22 @@ int device_status_check(int *d_status, cudaStream_t st)
 	return TG_CUDA_OK;
 }
 
+int call_status_word(int dev, int **d_status)
+{
+	TcScratch &S = g_tc[dev];
+	if (!S.h_status) {
+		TGC_CUDA(cudaHostAlloc((void **)&S.h_status, sizeof(int), cudaHostAllocMapped));
+		*S.h_status = 0;
+		TGC_CUDA(cudaHostGetDevicePointer((void **)&S.d_status, S.h_status, 0));
+	}
+	if (int prev = *(volatile int *)S.h_status) { // an earlier call's kernel gave up waiting
+		*S.h_status = 0;
+		return set_err(TG_CUDA_EDEVICE, "a kernel of an earlier call on this device gave up waiting (status %d)", prev);
+	}
+	*d_status = S.d_status;
+	return TG_CUDA_OK;
+}
+
 int matmul_q_tc(int axis, float *o, const float *act, const signed char *q, int bits, const float *s, int m, int k, int n,
 		cudaStream_t st, bool *done)
 {
@@ -942,17 +959,9 @@ int matmul_q_tc(int axis, float *o, const float *act, const signed char *q, int 
 	long wrows = axis == 0 ? m : n;   // weight channels
 	long brows = axis == 0 ? n : m;   // activation rows (batch)
 	size_t wbytes = (size_t)wrows * k * 2, abytes = (size_t)brows * k * 2;
-	int rc;
-	if (!S.h_status) {
-		TGC_CUDA(cudaHostAlloc((void **)&S.h_status, sizeof(int), cudaHostAllocMapped));
-		*S.h_status = 0;
-		TGC_CUDA(cudaHostGetDevicePointer((void **)&S.d_status, S.h_status, 0));
-	}
-	if (int prev = *(volatile int *)S.h_status) { // an earlier call's kernel gave up waiting
-		*S.h_status = 0;
-		return set_err(TG_CUDA_EDEVICE, "a tensor-core kernel of an earlier call on this device gave up waiting (status %d)",
-			       prev);
-	}
+	int *d_status = nullptr;
+	int rc = call_status_word(dev, &d_status);
+	if (rc) return rc;
 	if ((rc = S.buf.ensure(wbytes + 2 * abytes + 256, dev))) return rc;
 	__nv_bfloat16 *wq = (__nv_bfloat16 *)S.buf.p;
 	__nv_bfloat16 *ahi = (__nv_bfloat16 *)((uint8_t *)S.buf.p + ((wbytes + 127) & ~(size_t)127));
@@ -967,7 +976,7 @@ int matmul_q_tc(int axis, float *o, const float *act, const signed char *q, int 
 	p.pa[0] = 0, p.pb[0] = 0, p.pa[1] = 0, p.pb[1] = 1;
 	p.epi = EPI_STORE;
 	p.out = o;
-	p.status = S.d_status; // no per-call reset or copy: a timeout writes the host word directly
+	p.status = d_status; // no per-call reset or copy: a timeout writes the host word directly
 	// small batches leave most SMs idle with one tile per weight slab: let gemm() split K
 	if ((rc = S.part.ensure((size_t)64 << 20, dev))) return rc;
 	p.partial = S.part.as<float>(), p.partial_floats = (long)((64 << 20) / sizeof(float));

@@ -2,9 +2,12 @@
 // small-batch regime of tg_matmul_qa / tg_matmul_qb (runtime/tg_rt.h:132-151),
 // where the op streams codes from HBM once and is bandwidth-bound.
 //
-//   gemv_rows : axis 0, o[i,j] = s[i] sum_p code(i*k+p) b[p*n+j], n <= 8.
-//               A lane owns a channel row and a warp one K slice of 32 rows;
-//               the activations of the slice are shared by the 32 lanes.
+//   gemv_bulk : axis 0, o[i,j] = s[i] sum_p code(i*k+p) b[p*n+j], n <= 8, when the
+//               activations fit in shared memory twice (gemv_bulk.cuh): warps read
+//               code rows coalesced into registers, one wave of CTAs over the SMs.
+//   gemv_rows : the same op for activations too large for that. A lane owns a
+//               channel row and a warp one K slice of 32 rows; the activations of
+//               the slice are shared by the 32 lanes.
 //   gemv_cols : axis 1, o[i,j] = s[j] sum_p a[i*k+p] code(p*n+j), m <= 8.
 //               A code row p is contiguous over channels j: each lane streams
 //               4 bytes (8 int4 / 4 int8 channels) of row p; the K axis is split
@@ -13,6 +16,8 @@
 //   qmm_exact : any shape; one thread per output, products summed serially in
 //               p order without contraction -- the reference's own rounding.
 #include "common.cuh"
+#include "gemm.cuh"
+#include "gemv_bulk.cuh"
 #include "gemv_cols.cuh"
 #include "kernels.cuh"
 
@@ -164,6 +169,63 @@ static int launch_rows_nb(float *o, const signed char *q, const float *s, const 
 	return TG_CUDA_OK;
 }
 
+// gemv_bulk: rows per CTA so that the grid is one wave over the SMs (a multiple of the rows
+// per warp, at most 16 warps); shared memory holds the activations twice.
+constexpr size_t GB_SMEM_MAX = 200 * 1024;
+
+static bool bulk_fits(int nb, int k) { return gemv_bulk_smem(nb, k) <= GB_SMEM_MAX; }
+
+template <int BITS, int NB, int NCHL>
+static int launch_bulk_nb(float *o, const signed char *q, const float *s, const float *b, int m, int k, cudaStream_t st)
+{
+	int dev = 0;
+	cudaGetDevice(&dev);
+	int *status = nullptr;
+	int rc = call_status_word(dev, &status);
+	if (rc) return rc;
+	static bool attr[64] = {};
+	if (!attr[dev]) {
+		TGC_CUDA(cudaFuncSetAttribute(gemv_bulk<BITS, NB, NCHL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GB_SMEM_MAX));
+		attr[dev] = true;
+	}
+	constexpr int RR = GemvBulkTile<NB>::RR;
+	const int sms = sm_count();
+	int rows = (m + sms - 1) / sms;
+	rows = rows < RR ? RR : rows > RR * GB_MAX_WARPS ? RR * GB_MAX_WARPS : (rows + RR - 1) / RR * RR;
+	const unsigned grid = (unsigned)((m + rows - 1) / rows);
+	const unsigned threads = (unsigned)(32 * (rows / RR));
+	TGC_CUDA(launch_pdl(gemv_bulk<BITS, NB, NCHL>, dim3(grid), dim3(threads), gemv_bulk_smem(NB, k), st, o, q, s, b, m, k, rows,
+			    status));
+	return TG_CUDA_OK;
+}
+
+template <int BITS>
+static int launch_bulk(int nb, float *o, const signed char *q, const float *s, const float *b, int m, int k, cudaStream_t st)
+{
+	// batches of one or two columns whose rows are exactly 32, 64, 96 or 128 chunks (k = 1024 ...
+	// 4096 int4, 512 ... 2048 int8) get the unrolled kernel without predicates
+	const int per_lane = k / (BITS == 8 ? 16 : 32) % 32 == 0 ? k / (BITS == 8 ? 16 : 32) / 32 : 0;
+#define GB_EXACT(NB)                                                                               \
+	switch (per_lane) {                                                                         \
+	case 1: return launch_bulk_nb<BITS, NB, 1>(o, q, s, b, m, k, st);                           \
+	case 2: return launch_bulk_nb<BITS, NB, 2>(o, q, s, b, m, k, st);                           \
+	case 3: return launch_bulk_nb<BITS, NB, 3>(o, q, s, b, m, k, st);                           \
+	case 4: return launch_bulk_nb<BITS, NB, 4>(o, q, s, b, m, k, st);                           \
+	default: return launch_bulk_nb<BITS, NB, 0>(o, q, s, b, m, k, st);                          \
+	}
+	switch (nb) {
+	case 1: GB_EXACT(1)
+	case 2: GB_EXACT(2)
+	case 3: return launch_bulk_nb<BITS, 3, 0>(o, q, s, b, m, k, st);
+	case 4: return launch_bulk_nb<BITS, 4, 0>(o, q, s, b, m, k, st);
+	case 5: return launch_bulk_nb<BITS, 5, 0>(o, q, s, b, m, k, st);
+	case 6: return launch_bulk_nb<BITS, 6, 0>(o, q, s, b, m, k, st);
+	case 7: return launch_bulk_nb<BITS, 7, 0>(o, q, s, b, m, k, st);
+	default: return launch_bulk_nb<BITS, 8, 0>(o, q, s, b, m, k, st);
+	}
+#undef GB_EXACT
+}
+
 template <int BITS>
 static int launch_rows(int nb, float *o, const signed char *q, const float *s, const float *b, int m, int k, cudaStream_t st)
 {
@@ -219,7 +281,8 @@ int matmul_q_gemv(int axis, float *o, const float *act, const signed char *q, in
 	*done = false;
 	bool aligned16 = ((uintptr_t)q & 15) == 0 && ((uintptr_t)act & 15) == 0;
 	if (axis == 0 && n <= 8 && aligned16 && k % (bits == 8 ? 16 : 32) == 0) {
-		int rc = bits == 8 ? launch_rows<8>(n, o, q, s, act, m, k, st) : launch_rows<4>(n, o, q, s, act, m, k, st);
+		int rc = bulk_fits(n, k) ? (bits == 8 ? launch_bulk<8>(n, o, q, s, act, m, k, st) : launch_bulk<4>(n, o, q, s, act, m, k, st))
+					 : (bits == 8 ? launch_rows<8>(n, o, q, s, act, m, k, st) : launch_rows<4>(n, o, q, s, act, m, k, st));
 		if (rc) return rc;
 		*done = true;
 	} else if (axis == 1 && m <= 8 && ((uintptr_t)q & 3) == 0 && n % (bits == 8 ? 4 : 8) == 0) {

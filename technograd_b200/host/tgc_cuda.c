@@ -225,7 +225,9 @@ static int stream_cuda(int argc, char **argv)
 	size_t cap = 0;
 	long rows = 0;
 	double t0 = tr_now_ms();
-	while (!tg_stopping() && getline(&line, &cap, in) >= 0) {
+	ssize_t len;
+	while (!tg_stopping() && (len = getline(&line, &cap, in)) >= 0) {
+		while (len > 0 && (line[len - 1] == '\n' || line[len - 1] == '\r')) line[--len] = 0; /* as serve.c's read_line */
 		const char *bad;
 		const int k = io_parse_row(line, NULL, 0, &bad);
 		if (k == 0) continue;

@@ -91,6 +91,45 @@ def test_matmul_q_tensor_cores_vs_oracle(cuda, axis, m, k, n, bits):
             np.testing.assert_allclose(got[j], want, rtol=RTOL, atol=ATOL)
 
 
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("m,k,n", [
+    # gemv_bulk: rows per CTA chosen for one wave (1 ... 16 warps), ragged last CTA, ragged
+    # last register block of a row, every batch width
+    (1, 4096, 1), (2, 32, 1), (3, 1056, 2), (147, 4096, 1), (148, 4096, 3), (149, 2048, 4), (4097, 4096, 1),
+    (4096, 4096, 5), (1000, 1056, 6), (300, 3072, 7), (16384, 1024, 8), (64, 25600, 1), (9, 12800, 2),
+    # activations too large for shared memory twice: gemv_rows
+    (256, 32768, 1), (100, 16384, 2),
+])
+def test_gemv_axis0_vs_oracle(cuda, m, k, n, bits):
+    rng = np.random.default_rng(m + k + n)
+    lim = 8 if bits == 4 else 127
+    codes = rng.integers(-lim, lim if bits == 8 else 8, size=m * k)
+    q = tgir.pack_codes(codes, bits)
+    s = (np.abs(rng.normal(0, 0.02, size=m)) / (7 if bits == 4 else 127)).astype(np.float32)
+    act = rng.normal(0, 1, size=k * n).astype(np.float32)
+    want = tgo.matmul_q(tgo.tgo(), "tgo_", 0, act, q, bits, s, m, k, n)
+    got = gpu_matmul_q(cuda, 0, act, q, bits, s, m, k, n)
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+    assert np.array_equal(got, gpu_matmul_q(cuda, 0, act, q, bits, s, m, k, n))  # fixed summation order
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_gemv_axis0_activation_range(cuda, bits):
+    """Activations from 1e-30 to 1e30 (the decode divides them by powers of two up to 2^12
+    while staging: exact outside the subnormal range, and below it the loss is far under
+    the absolute tolerance)."""
+    rng = np.random.default_rng(17)
+    m, k, n = 512, 2048, 1
+    codes = rng.integers(-7, 8, size=m * k)
+    q = tgir.pack_codes(codes, bits)
+    s = np.full(m, 1e-3, np.float32)
+    for scale in (1e-30, 1e-6, 1.0, 1e20, 1e30):
+        act = (rng.normal(0, 1, size=k * n) * scale).astype(np.float32)
+        want = tgo.matmul_q(tgo.tgo(), "tgo_", 0, act, q, bits, s, m, k, n)
+        got = gpu_matmul_q(cuda, 0, act, q, bits, s, m, k, n)
+        np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL * min(scale, 1.0))
+
+
 def test_matmul_q_edge_cases(cuda):
     # code -8 everywhere, k = 1, and a row count that is not a multiple of anything
     for axis, bits, m, k, n in ((0, 4, 3, 1, 1), (1, 4, 1, 1, 2), (0, 4, 5, 64, 2), (1, 8, 2, 5, 3)):

@@ -164,6 +164,7 @@ def test_stream_device_cuda_matches_reference_stream(tmp_path):
     rows = np.random.default_rng(13).integers(0, 2, size=(300, 8)).astype(np.float32)
     lines = [",".join(f"{v:g}" for v in r) for r in rows]
     lines[7], lines[100] = "1,2,x", "1,2,3"  # a bad number and a short row
+    lines[200] += "\r"  # a CRLF line ending
     (tmp_path / "in.csv").write_text("\n".join(lines) + "\n")
     a = run(TGC_CUDA, "stream", LR, "in.csv", "-o", "gpu.txt", "--device", "cuda", cwd=tmp_path)
     b = run(TGC, "stream", LR, "in.csv", "-o", "cpu.txt", cwd=tmp_path)
