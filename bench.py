@@ -556,7 +556,7 @@ def cpu_baseline_ssm(S=None, runs: int = 1):
 # ---- config 2: weight-only dequant GEMM microbench ---------------------------------------------
 GEMM_N = GEMM_K = 4096
 # DRAM bytes (read + write) of one gemm_tc launch, from an ncu capture: (M, bits) -> bytes
-GEMM_TC_TRAFFIC = {(256, 4): 12625920.0}
+GEMM_TRAFFIC = {(256, 4): 12625920.0, (1, 4): 8438016.0}  # ncu dram read + write of one launch
 
 
 def gemm_inputs(bits: int, M: int):
@@ -679,9 +679,9 @@ def bench_gemm(args, world, rank, local, M: int, bits: int):
                       "weight_bytes_cycled": ncopies * q.nbytes, "algorithmic_bytes": byts, "flops": flops},
         "roofline": {"kernel": path, "bound": "hbm" if hbm else "tensor", "achieved": achieved, "peak": peak,
                      "unit": unit, "frac": achieved / peak, "peak_source": src + (" hbm_gbs" if hbm else " bf16 burst"),
-                     "traffic": GEMM_TC_TRAFFIC.get((M, bits)),
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gemm_tc launch at this M"
-                     if (M, bits) in GEMM_TC_TRAFFIC else None},
+                     "traffic": GEMM_TRAFFIC.get((M, bits)),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of the path's main "
+                                       "kernel at this M" if (M, bits) in GEMM_TRAFFIC else None},
         "e2e": {"value": world * args.steps / te, "unit": "GEMM/s", "h2d_bytes_per_step": b.nbytes,
                 "d2h_bytes_per_step": GEMM_N * M * 4,
                 "step": "one GEMM through tg_cuda_matmul_q: activations in from pinned host memory, the product out"},
