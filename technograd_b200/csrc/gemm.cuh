@@ -1,6 +1,7 @@
 // gemm.cuh -- the tensor-core GEMM interface used inside the library.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -64,5 +65,8 @@ int device_status_check(int *d_status, cudaStream_t st);
 // The per-device status word of the drop-in matmul calls (pinned, mapped; written only by a
 // kernel wait that timed out): an earlier call's timeout is reported, then cleared.
 int call_status_word(int dev, int **d_status);
+// A TMA map of a bf16 [rows, K] matrix (row stride ld elements): boxes of 64 columns x
+// box_rows rows, 128-byte swizzle (the K-major operand layout of the UMMA descriptors).
+int bf16_tile_map(CUtensorMap *m, const void *base, long rows, long K, long ld, int box_rows);
 
 } // namespace tgc

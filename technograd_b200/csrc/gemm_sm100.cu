@@ -599,6 +599,12 @@ static int make_map(CUtensorMap *m, const void *base, long rows, long K, long ld
 }
 
 // f32 or bf16 [rows, cols] output (row pitch ld elements), box of box_x x 128 rows, 128-byte swizzle.
+int bf16_tile_map(CUtensorMap *m, const void *base, long rows, long K, long ld, int box_rows)
+{
+	int rc = get_encode();
+	return rc ? rc : make_map(m, base, rows, K, ld, box_rows);
+}
+
 static int make_out_map(CUtensorMap *m, CUtensorMapDataType dt, int esize, const void *base, long rows, long cols, long ld,
 			int box_x)
 {

@@ -401,6 +401,7 @@ __global__ void k_argmax(const float *__restrict__ logits, int V, int *__restric
 
 struct Layer {
 	DevBuf wqkv, sqkv, wo_hi, wo_lo, wgu, sg, su, wd, sd, ln1, ln2, qn, kn;
+	CUtensorMap kmap, vmap; // the layer's K and V bf16 cache planes as [slot * NKV * max_len][128] (prefill attention)
 };
 
 struct Engine {
@@ -437,6 +438,7 @@ struct Engine {
 	int g_T = -1, g_nnew = -1;
 	bool g_prof = false;
 	bool small_gemm = true; // batches of 129-384 rows on gemm_sk (TG_CUDA_SMALL_GEMM=tile: the tile kernels)
+	bool prefill_tma = true; // k_attn_prefill_tma (TG_CUDA_PREFILL=staged: k_attn_prefill_tc)
 };
 
 enum { MK_DECODE = 1, MK_PREFILL = 2, MK_GEMM = 3 };
@@ -663,8 +665,20 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 		const char *e = getenv("TG_CUDA_SMALL_GEMM");
 		g.small_gemm = !(e && strcmp(e, "tile") == 0);
 	}
+	{
+		const char *e = getenv("TG_CUDA_PREFILL");
+		g.prefill_tma = !(e && strcmp(e, "staged") == 0);
+	}
+	for (int l = 0; l < g.L; l++) { // TMA maps of the cache planes, boxes of 64 dims x 64 positions
+		const size_t lo = (size_t)l * max_seqs * NKV * (size_t)max_len * HD;
+		const long rows = (long)max_seqs * NKV * max_len;
+		if ((rc = bf16_tile_map(&g.layers[l]->kmap, g.kh.as<__nv_bfloat16>() + lo, rows, HD, HD, FA_K)) ||
+		    (rc = bf16_tile_map(&g.layers[l]->vmap, g.vh.as<__nv_bfloat16>() + lo, rows, HD, HD, FA_K)))
+			return rc;
+	}
 	if ((rc = gemm_sk_prepare())) return rc;
 	TGC_CUDA(cudaFuncSetAttribute(k_attn_prefill_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FA_SMEM));
+	TGC_CUDA(cudaFuncSetAttribute(k_attn_prefill_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FB_SMEM));
 	TGC_CUDA(cudaFuncSetAttribute(k_attn_decode<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_smem(g)));
 	TGC_CUDA(cudaFuncSetAttribute(k_attn_decode<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_smem(g)));
 	TGC_CUDA(cudaMemsetAsync(g.status.p, 0, 64, g.st));
@@ -712,9 +726,15 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 		if (!decode) {
 			dim3 grid((T + FA_Q - 1) / FA_Q, NQ, (unsigned)S);
 			int mk = mark_begin(g, MK_PREFILL, 4.0 * HD * (double)T * (T + 1) / 2 * NQ * S);
-			k_attn_prefill_tc<<<grid, FA_THREADS, FA_SMEM, g.st>>>(g.q.as<float>(), kcc, vcc, T, NQ, NKV, slot0, g.max_len,
-									       g.scale, g.ahi.as<__nv_bfloat16>(),
-									       g.alo.as<__nv_bfloat16>(), status);
+			if (g.prefill_tma)
+				k_attn_prefill_tma<<<grid, FB_THREADS, FB_SMEM, g.st>>>(g.q.as<float>(), Y.kmap, Y.vmap, kcc.q, vcc.q, T, NQ,
+											NKV, slot0, g.max_len, g.scale,
+											g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>(),
+											status);
+			else
+				k_attn_prefill_tc<<<grid, FA_THREADS, FA_SMEM, g.st>>>(g.q.as<float>(), kcc, vcc, T, NQ, NKV, slot0,
+										       g.max_len, g.scale, g.ahi.as<__nv_bfloat16>(),
+										       g.alo.as<__nv_bfloat16>(), status);
 			mark_end(g, mk);
 		} else {
 			// the key count (position + 1) is read on the device; bytes = per-key part * len + the rest
