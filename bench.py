@@ -43,6 +43,7 @@ from __future__ import annotations
 
 import argparse
 import ctypes as C
+import faulthandler
 import json
 import os
 import re
@@ -266,21 +267,29 @@ def bench_decode(args, world, rank, local):
 
     for i in range(args.warmup):
         step(i)
-    eng.profile(True)
+    # The timed steps run without the engine's per-kernel profiling events: an event between two
+    # kernels of the captured decode step breaks their programmatic overlap and costs time of
+    # its own. The breakdown and the roofline come from one profiled step of the same kind
+    # right after the timed region.
+    eng.profile(False)
     barrier(world)
     clk = Clocks(local)
-    dev_ms, wall, stats = [], [], []
+    dev_ms, wall, launches = [], [], 0
     torch.cuda.nvtx.range_push("timed")  # lets a profiler restrict its launch list to the timed steps
     for i in range(args.steps):
         t = time.perf_counter()
         tok = step(args.warmup + i)
         wall.append(time.perf_counter() - t)
         s = eng.stats()
-        stats.append(s)
         dev_ms.append(s["device_ms"])
+        launches += s["launches"]
     torch.cuda.nvtx.range_pop()
     barrier(world)
     clocks = clk.stop()
+    eng.profile(True)
+    step(args.warmup + args.steps)
+    stats = [eng.stats()]
+    eng.profile(False)
     t_dev = max_over_ranks(sum(dev_ms) / 1e3, world)
     t_wall = max_over_ranks(sum(wall), world)
     tokens_step = wave * new
@@ -292,10 +301,10 @@ def bench_decode(args, world, rank, local):
     achieved = dec_bytes / (dec_ms / 1e3) / 1e9
     gemm_tf = sum(s["gemm_flops"] for s in stats) / (sum(s["gemm_ms"] for s in stats) / 1e3) / 1e12
     pre_tf = sum(s["attn_prefill_flops"] for s in stats) / (sum(s["attn_prefill_ms"] for s in stats) / 1e3) / 1e12
-    tot_ms = sum(dev_ms)
+    tot_ms = sum(s["device_ms"] for s in stats)  # the profiled step
     line = {
         "metric": METRICS["decode"][0], "value": value, "unit": "tokens/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sum(dev_ms) / len(dev_ms),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
         "data": "synthetic: random-init weights N(0,0.02), uniform-random prompt ids (seed 5)",
         "config": workload_config("decode", args),
@@ -305,7 +314,11 @@ def bench_decode(args, world, rank, local):
                                   f"{wave} seqs x {prompt + new - 1} positions",
                       "share_of_step": {"attn_decode": dec_ms / tot_ms, "gemm": sum(s["gemm_ms"] for s in stats) / tot_ms,
                                         "attn_prefill": sum(s["attn_prefill_ms"] for s in stats) / tot_ms},
-                      "gemm_tflops": gemm_tf, "attn_prefill_tflops_f32": pre_tf, "build_s": t_build},
+                      "gemm_tflops": gemm_tf, "attn_prefill_tflops_f32": pre_tf, "build_s": t_build,
+                      "profiled_step_ms": tot_ms,
+                      "profiled_step": "shares, TFLOP/s and the roofline: one step with per-kernel CUDA events right "
+                                       "after the timed region (the timed steps run without them, so the decode "
+                                       "step's kernels overlap by programmatic dependent launch)"},
         "roofline": {"kernel": "k_attn_decode (KV-cache attention)", "bound": "hbm", "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "peak_source": src,
                      # ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_attn_decode launch over 64
@@ -317,7 +330,7 @@ def bench_decode(args, world, rank, local):
                      "ms_per_launch": dec_ms / max(dec_launches, 1)},
         "e2e": {"value": world * tokens_step * args.steps / t_wall, "unit": "tokens/s",
                 "h2d_bytes_per_step": wave * prompt * 4, "d2h_bytes_per_step": wave * new * 4},
-        "gpu_launches": int(sum(s["launches"] for s in stats)), "clocks": clocks,
+        "gpu_launches": int(launches), "clocks": clocks,
     }
     return line, built, tok
 
@@ -379,21 +392,27 @@ def bench_prefill(args, world, rank, local):
     eng = lm.Engine(built, max_seqs=shard, max_len=T, devices=[local])
     for _ in range(args.warmup):
         eng.forward(ids)
-    eng.profile(True)
+    # timed without the per-kernel profiling events; the breakdown and the roofline come from
+    # one profiled forward right after the timed region
+    eng.profile(False)
     barrier(world)
     clk = Clocks(local)
-    dev_ms, wall, stats = [], [], []
+    dev_ms, wall, launches = [], [], 0
     torch.cuda.nvtx.range_push("timed")
     for _ in range(args.steps):
         t = time.perf_counter()
         eng.forward(ids)
         wall.append(time.perf_counter() - t)
         s = eng.stats()
-        stats.append(s)
         dev_ms.append(s["device_ms"])
+        launches += s["launches"]
     torch.cuda.nvtx.range_pop()
     barrier(world)
     clocks = clk.stop()
+    eng.profile(True)
+    eng.forward(ids)
+    stats = [eng.stats()]
+    eng.profile(False)
     t_dev = max_over_ranks(sum(dev_ms) / 1e3, world)
     t_wall = max_over_ranks(sum(wall), world)
     tok = shard * T
@@ -401,24 +420,27 @@ def bench_prefill(args, world, rank, local):
     gemm_ms = sum(s["gemm_ms"] for s in stats)
     gemm_fl = sum(s["gemm_flops"] for s in stats)
     achieved = gemm_fl / (gemm_ms / 1e3) / 1e12
-    tot_ms = sum(dev_ms)
+    tot_ms = sum(s["device_ms"] for s in stats)  # the profiled forward
     line = {
         "metric": METRICS["prefill"][0], "value": world * tok * args.steps / t_dev,
-        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sum(dev_ms) / len(dev_ms),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
         "data": "synthetic: random-init weights N(0,0.02), uniform-random ids (seed 4)",
         "config": workload_config("prefill", args),
         "breakdown": {"seqs_per_gpu": shard,
                       "share_of_step": {"gemm": gemm_ms / tot_ms, "attn_prefill": sum(s["attn_prefill_ms"] for s in stats) / tot_ms},
                       "attn_prefill_tflops_f32": sum(s["attn_prefill_flops"] for s in stats) /
-                      max(sum(s["attn_prefill_ms"] for s in stats) / 1e3, 1e-9) / 1e12, "build_s": t_build},
+                      max(sum(s["attn_prefill_ms"] for s in stats) / 1e3, 1e-9) / 1e12, "build_s": t_build,
+                      "profiled_step_ms": tot_ms,
+                      "profiled_step": "shares, TFLOP/s and the roofline: one forward with per-kernel CUDA events "
+                                       "right after the timed region (the timed forwards run without them)"},
         "roofline": {"kernel": "gemm_tc (tcgen05 dequant GEMM, all linear layers)", "bound": "tensor",
                      "achieved": achieved, "peak": pk["bf16_tflops_sustained"] if "bf16_tflops_sustained" in pk
                      else pk["bf16_tflops"], "unit": "TFLOP/s", "peak_source": src + " bf16 sustained",
                      "traffic": None, "flops_per_launch": gemm_fl / max(sum(s["gemm_launches"] for s in stats), 1)},
         "e2e": {"value": world * tok * args.steps / t_wall, "unit": "tokens/s", "h2d_bytes_per_step": ids.nbytes,
                 "d2h_bytes_per_step": shard * cfg["vocab"] * 4},
-        "gpu_launches": int(sum(s["launches"] for s in stats)), "clocks": clocks,
+        "gpu_launches": int(launches), "clocks": clocks,
     }
     line["roofline"]["frac"] = achieved / line["roofline"]["peak"]
     return line, built
@@ -475,19 +497,24 @@ def bench_ssm(args, world, rank, local):
     dout = torch.empty_like(du)
     for _ in range(args.warmup):
         eng.forward_device(du.data_ptr(), S, T, dout.data_ptr())
-    eng.profile(True)
+    # timed without the per-kernel profiling events; the breakdown and the roofline come from
+    # one profiled forward right after the timed region
+    eng.profile(False)
     barrier(world)
     clk = Clocks(local)
-    dev_ms, stats = [], []
+    dev_ms, launches = [], 0
     torch.cuda.nvtx.range_push("timed")
     for _ in range(args.steps):
         eng.forward_device(du.data_ptr(), S, T, dout.data_ptr())
         s = eng.stats()
-        stats.append(s)
         dev_ms.append(s["device_ms"])
+        launches += s["launches"]
     torch.cuda.nvtx.range_pop()
     barrier(world)
     clocks = clk.stop()
+    eng.profile(True)
+    eng.forward_device(du.data_ptr(), S, T, dout.data_ptr())
+    stats = [eng.stats()]
     t_dev = max_over_ranks(sum(dev_ms) / 1e3, world)
     # e2e: host (pinned) rows in, host rows out, through tg_cuda_ssm_forward
     hu = torch.from_numpy(u).pin_memory()
@@ -504,7 +531,7 @@ def bench_ssm(args, world, rank, local):
     tok = S * T
     scan_ms = sum(s["scan_ms"] for s in stats)
     gemm_ms = sum(s["gemm_ms"] for s in stats)
-    tot_ms = sum(dev_ms)
+    tot_ms = sum(s["device_ms"] for s in stats)  # the profiled forward
     pk, src = peaks()
     scan_tf = sum(s["scan_flops"] for s in stats) / (scan_ms / 1e3) / 1e12
     gemm_tf = sum(s["gemm_flops"] for s in stats) / (gemm_ms / 1e3) / 1e12
@@ -514,12 +541,14 @@ def bench_ssm(args, world, rank, local):
     scan_bytes = float(S * 64 * (cfg["d_inner"] * 12 + (cfg["dt_rank"] + 2 * cfg["d_state"]) * 4))
     line = {
         "metric": METRICS["ssm"][0], "value": world * tok * args.steps / t_dev,
-        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / args.steps,
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sum(dev_ms) / len(dev_ms),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
         "data": "synthetic: random-init weights N(0,0.02) int8 RTN, inputs N(0,1) (seed 3)",
         "config": workload_config("ssm", args),
         "breakdown": {"seqs_per_gpu": S, "chunk": 64, "share_of_step": {"scan": scan_ms / tot_ms, "gemm": gemm_ms / tot_ms},
-                      "gemm_tflops": gemm_tf, "build_s": t_build},
+                      "gemm_tflops": gemm_tf, "build_s": t_build, "profiled_step_ms": tot_ms,
+                      "profiled_step": "shares, TFLOP/s and the roofline: one forward with per-kernel CUDA events "
+                                       "right after the timed region (the timed forwards run without them)"},
         "roofline": {"kernel": "k_ssm_scan (FP32 pipe + SFU)", "bound": "fp32", "achieved": scan_tf,
                      "peak": FP32_NOMINAL_TFLOPS, "unit": "TFLOP/s", "frac": scan_tf / FP32_NOMINAL_TFLOPS,
                      "peak_source": "nominal FP32 SIMT (148 SMs x 128 lanes x FMA x 1965 MHz); not in MEASURED_PEAKS",
@@ -528,7 +557,7 @@ def bench_ssm(args, world, rank, local):
                                        "bytes), scaled to this launch's sequences"},
         "e2e": {"value": world * tok * args.steps / t_wall, "unit": "tokens/s", "h2d_bytes_per_step": u.nbytes,
                 "d2h_bytes_per_step": u.nbytes},
-        "gpu_launches": int(sum(s["launches"] for s in stats)), "clocks": clocks,
+        "gpu_launches": int(launches), "clocks": clocks,
     }
     return line, model
 
@@ -935,6 +964,7 @@ def main():
     ap.add_argument("--bits", type=int, default=4, choices=[4, 8])
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    faulthandler.enable()  # a fatal signal (abort, segfault) prints the Python stack of every thread
     if args.impl == "reference":
         if int(os.environ.get("RANK", "0")) != 0:
             return  # rank 0 alone times the reference; the others have no work

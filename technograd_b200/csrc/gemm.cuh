@@ -43,6 +43,9 @@ struct GemmArgs {
 	int cbits, cside;
 	long cld;
 	int raw_bytes; // set by gemm(): bytes of one K block of codes (TMA-loaded into each ring stage)
+	// launch with programmatic stream serialization (the kernels wait for the one before them
+	// with griddepcontrol.wait before touching memory; only the decoder's captured step sets it)
+	int pdl;
 };
 
 // Launch on stream. SwiGLU: B rows come in blocks of 64 (32 gate rows then the

@@ -52,6 +52,7 @@ struct SkArgs {
 	__nv_bfloat16 *out_hi, *out_lo;
 	int kper;                      // K blocks per cluster rank
 	int *status;
+	int pdl;                       // launched with programmatic stream serialization
 };
 
 __device__ __forceinline__ uint32_t cluster_rank()
@@ -128,6 +129,8 @@ __global__ void __launch_bounds__(192, 1) gemm_sk(const __grid_constant__ SkMaps
 	__syncthreads();
 	tc_fence_after();
 	const uint32_t tmem = *tslot;
+	pdl_wait(); // the kernel before it (with programmatic launch) has completed: inputs ready
+	pdl_launch();
 
 	if (warp == 0) { // ---- producer
 		if (lane == 0)
@@ -363,6 +366,11 @@ static cudaLaunchConfig_t sk_config(const SkArgs &p, int S, int body, cudaStream
 	attr[0].val.clusterDim.z = (unsigned)S;
 	cfg.attrs = attr;
 	cfg.numAttrs = 1;
+	if (p.pdl) {
+		attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+		attr[1].val.programmaticStreamSerializationAllowed = 1;
+		cfg.numAttrs = 2;
+	}
 	return cfg;
 }
 
@@ -371,7 +379,7 @@ static int sk_launch(const SkMaps &maps, const SkArgs &p, int S, cudaStream_t st
 {
 	const int body = sk_body(NB, STAGES, p.nw, p.nx, S);
 	if (body > SK_RING) return set_err(TG_CUDA_EINVAL, "gemm_sk: %d bytes of shared memory", body);
-	cudaLaunchAttribute attr[1];
+	cudaLaunchAttribute attr[2];
 	cudaLaunchConfig_t cfg = sk_config<NB, STAGES, EPI>(p, S, body, st, attr);
 	TGC_CUDA(cudaLaunchKernelEx(&cfg, gemm_sk<NB, STAGES, EPI>, maps, p));
 	return TG_CUDA_OK;
@@ -404,7 +412,7 @@ static int sk_occ_one(SkOcc &o, int nw)
 		const int S = 1 << ls, body = sk_body(NB, STAGES, nw, 2, S);
 		int n = 0;
 		if (body <= SK_RING) {
-			cudaLaunchAttribute attr[1];
+			cudaLaunchAttribute attr[2];
 			cudaLaunchConfig_t cfg = sk_config<NB, STAGES, EPI_STORE>(p, S, body, nullptr, attr);
 			TGC_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_sk<NB, STAGES, EPI_STORE>, &cfg));
 		}
@@ -505,6 +513,7 @@ int gemm_sk(const GemmOperands &ops, const GemmArgs &p, cudaStream_t st)
 	a.scale2 = p.scale2;
 	a.out = p.out, a.ldo = p.ldo, a.out_hi = p.out_hi, a.out_lo = p.out_lo, a.status = p.status;
 	a.kper = sh.kper;
+	a.pdl = p.pdl;
 	for (int j = 0; j < p.nb; j++)
 		if ((rc = sk_map(&maps.w[j], ops.b[j], p.N, p.K, ops.ldb, SK_W))) return rc;
 	for (int i = 0; i < p.na; i++)

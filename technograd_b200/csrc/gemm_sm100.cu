@@ -121,6 +121,8 @@ __global__ void __launch_bounds__(320, 1) gemm_tc(const __grid_constant__ TmaMap
 	__syncthreads();
 	tc_fence_after();
 	const uint32_t tmem = *tslot;
+	pdl_wait(); // the kernel before it (with programmatic launch) has completed: inputs ready
+	pdl_launch();
 
 	if (warp == 0 && lane == 0) { // ---- producer
 		// the codes of this CTA's whole K range into L2 up front, 256 contiguous bytes per row
@@ -646,8 +648,12 @@ static int launch_bn(const TmaMaps &maps, const GemmArgs &p, cudaStream_t st)
 		attr_set[dev] = true;
 	}
 	dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, p.kb_per_split ? (unsigned)(((p.K + BK - 1) / BK + p.kb_per_split - 1) / p.kb_per_split) : 1u);
-	gemm_tc<BN, STAGES, EPI><<<grid, 320, smem, st>>>(maps, p);
-	TGC_LAUNCH_CHECK();
+	if (p.pdl) {
+		TGC_CUDA(launch_pdl(gemm_tc<BN, STAGES, EPI>, grid, dim3(320), smem, st, maps, p));
+	} else {
+		gemm_tc<BN, STAGES, EPI><<<grid, 320, smem, st>>>(maps, p);
+		TGC_LAUNCH_CHECK();
+	}
 	return TG_CUDA_OK;
 }
 
@@ -684,6 +690,8 @@ static int launch_split(int BN, int stages, const TmaMaps &maps, const GemmArgs 
 template <int EPI>
 __global__ void k_split_reduce(const float *__restrict__ part, int splits, long mpad, int M, int N, GemmArgs p)
 {
+	pdl_wait();
+	pdl_launch();
 	long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
 	const int outc = EPI == EPI_SWIGLU ? N / 2 : N;
 	if (t >= (long)M * outc) return;
@@ -776,10 +784,14 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 		if ((rc = launch_split(BN, stages, maps, q, grid, st))) return rc;
 		const long outs = (long)p.M * (p.epi == EPI_SWIGLU ? p.N / 2 : p.N);
 		const unsigned blocks = (unsigned)((outs + 255) / 256);
-		if (p.epi == EPI_SWIGLU) k_split_reduce<EPI_SWIGLU><<<blocks, 256, 0, st>>>(p.partial, splits, q.mpad, p.M, p.N, p);
-		else if (p.epi == EPI_ADD) k_split_reduce<EPI_ADD><<<blocks, 256, 0, st>>>(p.partial, splits, q.mpad, p.M, p.N, p);
-		else k_split_reduce<EPI_STORE><<<blocks, 256, 0, st>>>(p.partial, splits, q.mpad, p.M, p.N, p);
-		TGC_LAUNCH_CHECK();
+		auto reduce = p.epi == EPI_SWIGLU ? k_split_reduce<EPI_SWIGLU> : p.epi == EPI_ADD ? k_split_reduce<EPI_ADD>
+											     : k_split_reduce<EPI_STORE>;
+		if (p.pdl) {
+			TGC_CUDA(launch_pdl(reduce, dim3(blocks), dim3(256), 0, st, (const float *)p.partial, splits, q.mpad, p.M, p.N, p));
+		} else {
+			reduce<<<blocks, 256, 0, st>>>(p.partial, splits, q.mpad, p.M, p.N, p);
+			TGC_LAUNCH_CHECK();
+		}
 		return TG_CUDA_OK;
 	}
 	// the output goes through TMA when its pitch and base allow; the tile is staged in the

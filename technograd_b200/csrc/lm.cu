@@ -89,6 +89,8 @@ __global__ void k_wo_prescale(const signed char *__restrict__ q, const float *__
 __global__ void k_embed(const float *__restrict__ ids, const int *__restrict__ tok, long M, const float *__restrict__ E,
 			int V, int D, float *__restrict__ h)
 {
+	pdl_wait(); // programmatic dependent launch inside the decode step (no-op otherwise)
+	pdl_launch();
 	long r = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
 	int lane = threadIdx.x & 31;
 	if (r >= M) return;
@@ -109,6 +111,8 @@ __global__ void k_embed(const float *__restrict__ ids, const int *__restrict__ t
 __global__ void k_rmsnorm_split(const float *__restrict__ x, long M, int D, const float *__restrict__ w, float eps,
 				int last_T, __nv_bfloat16 *__restrict__ hi, __nv_bfloat16 *__restrict__ lo)
 {
+	pdl_wait(); // programmatic dependent launch inside the decode step (no-op otherwise)
+	pdl_launch();
 	long r = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
 	int lane = threadIdx.x & 31;
 	if (r >= M) return;
@@ -134,6 +138,8 @@ __global__ void k_qk_rope(const float *__restrict__ qkv, long M, int T, int pos0
 			  const float *__restrict__ cosT, const float *__restrict__ sinT, float *__restrict__ q_out,
 			  KvPlane kc, KvPlane vc, int slot0, int max_len)
 {
+	pdl_wait(); // programmatic dependent launch inside the decode step (no-op otherwise)
+	pdl_launch();
 	constexpr int HD = 128;
 	long gw = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
 	int lane = threadIdx.x & 31;
@@ -197,6 +203,8 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 						     int NKV, int slot0, int max_len, float scale, __nv_bfloat16 *__restrict__ ohi,
 						     __nv_bfloat16 *__restrict__ olo)
 {
+	pdl_wait(); // programmatic dependent launch inside the decode step (no-op otherwise)
+	pdl_launch();
 	constexpr int HD = 128;
 	constexpr int DU = 8; // positions a warp loads per step (8 x 384 bytes in flight)
 	static_assert(DU == 8, "the score butterfly reduces exactly 8 positions");
@@ -342,6 +350,8 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 __global__ void k_argmax(const float *__restrict__ logits, int V, int *__restrict__ tok, int *__restrict__ out, int ld_out,
 			 int col, const int *__restrict__ dpos, int T)
 {
+	pdl_wait(); // programmatic dependent launch inside the decode step (no-op otherwise)
+	pdl_launch();
 	if (dpos) col = *dpos - T + 1; // decode: the token fed at position pos yields output column pos - T + 1
 	const float *x = logits + (long)blockIdx.x * V;
 	float best = -INFINITY;
@@ -439,6 +449,11 @@ struct Engine {
 	bool g_prof = false;
 	bool small_gemm = true; // batches of 129-384 rows on gemm_sk (TG_CUDA_SMALL_GEMM=tile: the tile kernels)
 	bool prefill_tma = true; // k_attn_prefill_tma (TG_CUDA_PREFILL=staged: k_attn_prefill_tc)
+	// while the decode step is captured without profiling marks: kernels are launched with
+	// programmatic stream serialization, so each one's launch and prologue overlap the tail of
+	// the one before it (every kernel of the step waits for its predecessor, pdl_wait, before
+	// it touches memory); TG_CUDA_PDL=0 turns it off
+	bool pdl = false, pdl_enabled = true;
 };
 
 enum { MK_DECODE = 1, MK_PREFILL = 2, MK_GEMM = 3 };
@@ -486,6 +501,15 @@ static void mark_end(Engine &g, int i)
 	if (i >= 0) ev_check(g, record(g, (g.capturing ? g.gmarks : g.marks)[i].b), "cudaEventRecord(mark end)");
 }
 
+// A launch on the engine's stream, with programmatic stream serialization while g.pdl.
+template <class... KArgs, class... Args>
+static cudaError_t launch_k(Engine &g, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, Args &&...args)
+{
+	if (g.pdl) return launch_pdl(kernel, grid, block, smem, g.st, std::forward<Args>(args)...);
+	kernel<<<grid, block, smem, g.st>>>(std::forward<Args>(args)...);
+	return cudaGetLastError();
+}
+
 // A layer's GEMM. Batches of 129-384 rows (a decode step of a 256-sequence wave) go to the
 // swapped-operand cluster kernel (gemm_sk.cu); measured per decode step of the full model
 // (28 layers), it takes 2.62 ms of GEMMs at 256 sequences against 2.88 ms for the tile
@@ -495,6 +519,7 @@ static void mark_end(Engine &g, int i)
 static int gemm_m(Engine &g, const GemmOperands &op, const GemmArgs &p0)
 {
 	GemmArgs p = p0;
+	p.pdl = g.pdl ? 1 : 0;
 	p.partial = g.part.as<float>(); // split-K scratch for the tile kernel's small batches
 	p.partial_floats = (long)(g.part.bytes / sizeof(float));
 	int mk = mark_begin(g, MK_GEMM, 2.0 * p.M * p.N * p.K);
@@ -668,6 +693,8 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 	{
 		const char *e = getenv("TG_CUDA_PREFILL");
 		g.prefill_tma = !(e && strcmp(e, "staged") == 0);
+		e = getenv("TG_CUDA_PDL");
+		g.pdl_enabled = !(e && strcmp(e, "0") == 0);
 	}
 	for (int l = 0; l < g.L; l++) { // TMA maps of the cache planes, boxes of 64 dims x 64 positions
 		const size_t lo = (size_t)l * max_seqs * NKV * (size_t)max_len * HD;
@@ -712,17 +739,18 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 		const KvPlane vc{ g.vh.as<__nv_bfloat16>() + lo, g.vq.as<signed char>() + lo };
 		const KvPlaneC kcc{ kc.h, kc.q }, vcc{ vc.h, vc.q };
 		g.launches += 3; // two norms and the q/k rope of this layer
-		k_rmsnorm_split<<<warps_grid, 256, 0, g.st>>>(g.h.as<float>(), M, D, Y.ln1.as<float>(), g.eps, 0,
-							     g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>());
+		TGC_CUDA(launch_k(g, k_rmsnorm_split, dim3(warps_grid), dim3(256), 0, (const float *)g.h.as<float>(), M, D,
+				  (const float *)Y.ln1.as<float>(), g.eps, 0, g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>()));
 		GemmOperands op;
 		op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = Y.wqkv.p, op.lda = D, op.ldb = D;
 		GemmArgs p = gemm_args((int)M, g.HQKV(), D, EPI_STORE);
 		p.scale = Y.sqkv.as<float>(), p.scale_mode = 2, p.out = g.qkv.as<float>(), p.ldo = g.HQKV(), p.status = status;
 		if ((rc = gemm_m(g, op, p))) return rc;
 		long heads = M * (NQ + 2 * NKV);
-		k_qk_rope<<<(unsigned)((heads * 32 + 255) / 256), 256, 0, g.st>>>(
-			g.qkv.as<float>(), M, T, pos0, decode ? g.dpos.as<int>() : nullptr, NQ, NKV, g.eps, Y.qn.as<float>(),
-			Y.kn.as<float>(), g.cosT.as<float>(), g.sinT.as<float>(), g.q.as<float>(), kc, vc, slot0, g.max_len);
+		TGC_CUDA(launch_k(g, k_qk_rope, dim3((unsigned)((heads * 32 + 255) / 256)), dim3(256), 0, (const float *)g.qkv.as<float>(),
+				  M, T, pos0, (const int *)(decode ? g.dpos.as<int>() : nullptr), NQ, NKV, g.eps,
+				  (const float *)Y.qn.as<float>(), (const float *)Y.kn.as<float>(), (const float *)g.cosT.as<float>(),
+				  (const float *)g.sinT.as<float>(), g.q.as<float>(), kc, vc, slot0, g.max_len));
 		if (!decode) {
 			dim3 grid((T + FA_Q - 1) / FA_Q, NQ, (unsigned)S);
 			int mk = mark_begin(g, MK_PREFILL, 4.0 * HD * (double)T * (T + 1) / 2 * NQ * S);
@@ -743,13 +771,13 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 			// per key: K and V rows of 3-byte elements
 			int mk = mark_begin(g, MK_DECODE, (double)S * NQ * HD * 4 * 2, (double)S * NKV * HD * 3 * 2);
 			if (NQ / NKV == 2)
-				k_attn_decode<2><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kcc, vcc, 0, g.dpos.as<int>(), NQ, NKV, slot0,
-									  g.max_len, g.scale, g.ahi.as<__nv_bfloat16>(),
-									  g.alo.as<__nv_bfloat16>());
+				TGC_CUDA(launch_k(g, k_attn_decode<2>, grid, dim3(256), smem, (const float *)g.q.as<float>(), kcc, vcc, 0,
+						  (const int *)g.dpos.as<int>(), NQ, NKV, slot0, g.max_len, g.scale,
+						  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>()));
 			else
-				k_attn_decode<1><<<grid, 256, smem, g.st>>>(g.q.as<float>(), kcc, vcc, 0, g.dpos.as<int>(), NQ, NKV, slot0,
-									  g.max_len, g.scale, g.ahi.as<__nv_bfloat16>(),
-									  g.alo.as<__nv_bfloat16>());
+				TGC_CUDA(launch_k(g, k_attn_decode<1>, grid, dim3(256), smem, (const float *)g.q.as<float>(), kcc, vcc, 0,
+						  (const int *)g.dpos.as<int>(), NQ, NKV, slot0, g.max_len, g.scale,
+						  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>()));
 			mark_end(g, mk);
 		}
 		TGC_LAUNCH_CHECK();
@@ -761,8 +789,8 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 		p.pa[0] = 0, p.pb[0] = 0, p.pa[1] = 0, p.pb[1] = 1, p.pa[2] = 1, p.pb[2] = 0;
 		p.out = g.h.as<float>(), p.ldo = D, p.status = status;
 		if ((rc = gemm_m(g, op, p))) return rc;
-		k_rmsnorm_split<<<warps_grid, 256, 0, g.st>>>(g.h.as<float>(), M, D, Y.ln2.as<float>(), g.eps, 0,
-							     g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>());
+		TGC_CUDA(launch_k(g, k_rmsnorm_split, dim3(warps_grid), dim3(256), 0, (const float *)g.h.as<float>(), M, D,
+				  (const float *)Y.ln2.as<float>(), g.eps, 0, g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>()));
 		op = GemmOperands();
 		op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = Y.wgu.p, op.lda = D, op.ldb = D;
 		p = gemm_args((int)M, 2 * FF, D, EPI_SWIGLU);
@@ -783,8 +811,8 @@ static int head(Engine &g, long S, int T)
 {
 	int rc;
 	g.launches++;
-	k_rmsnorm_split<<<(unsigned)((S * 32 + 255) / 256), 256, 0, g.st>>>(g.h.as<float>(), S, g.D, g.lnf.as<float>(), g.eps, T,
-									    g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>());
+	TGC_CUDA(launch_k(g, k_rmsnorm_split, dim3((unsigned)((S * 32 + 255) / 256)), dim3(256), 0, (const float *)g.h.as<float>(), S,
+			  g.D, (const float *)g.lnf.as<float>(), g.eps, T, g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>()));
 	TGC_LAUNCH_CHECK();
 	GemmOperands op;
 	op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = g.lmw.p, op.lda = g.D, op.ldb = g.D;
@@ -827,20 +855,25 @@ static int prefill(Engine &g, const float *ids_host, long S, int T, int slot0, f
 // One decode step for S sequences whose fed token sits at position *dpos: embed the last
 // tokens, every layer against the KV cache, the LM head, argmax into column *dpos - T + 1
 // of out_tok, then *dpos += 1. Launch arguments do not depend on the step.
-__global__ void k_bump(int *pos) { pos[0] += 1; }
+__global__ void k_bump(int *pos)
+{
+	pdl_wait();
+	pdl_launch();
+	pos[0] += 1;
+}
 
 static int decode_step(Engine &g, long S, int T, int nnew)
 {
 	int rc;
 	g.launches++;
-	k_embed<<<(unsigned)((S * 32 + 255) / 256), 256, 0, g.st>>>(nullptr, g.tok.as<int>(), S, g.E.as<float>(), g.V, g.D,
-								     g.h.as<float>());
+	TGC_CUDA(launch_k(g, k_embed, dim3((unsigned)((S * 32 + 255) / 256)), dim3(256), 0, (const float *)nullptr,
+			  (const int *)g.tok.as<int>(), S, (const float *)g.E.as<float>(), g.V, g.D, g.h.as<float>()));
 	if ((rc = run_layers(g, S, 1, 0, 0, true))) return rc;
 	if ((rc = head(g, S, 1))) return rc;
 	g.launches += 2;
-	k_argmax<<<(unsigned)S, 1024, 0, g.st>>>(g.logits.as<float>(), g.V, g.tok.as<int>(), g.out_tok.as<int>(), nnew, 0,
-						 g.dpos.as<int>(), T);
-	k_bump<<<1, 1, 0, g.st>>>(g.dpos.as<int>());
+	TGC_CUDA(launch_k(g, k_argmax, dim3((unsigned)S), dim3(1024), 0, (const float *)g.logits.as<float>(), g.V, g.tok.as<int>(),
+			  g.out_tok.as<int>(), nnew, 0, (const int *)g.dpos.as<int>(), T));
+	TGC_CUDA(launch_k(g, k_bump, dim3(1), dim3(1), 0, g.dpos.as<int>()));
 	TGC_LAUNCH_CHECK();
 	return TG_CUDA_OK;
 }
@@ -859,7 +892,9 @@ static int decode_graph(Engine &g, long S, int T, int nnew)
 	cudaGraph_t graph = nullptr;
 	TGC_CUDA(cudaStreamBeginCapture(g.st, cudaStreamCaptureModeThreadLocal));
 	g.capturing = true;
+	g.pdl = g.pdl_enabled && !g.prof; // profiling marks between kernels would break the overlap anyway
 	int rc = decode_step(g, S, T, nnew);
+	g.pdl = false;
 	g.capturing = false;
 	cudaError_t e = cudaStreamEndCapture(g.st, &graph);
 	g.g_kernels = g.launches - before;
