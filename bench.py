@@ -62,6 +62,7 @@ sys.path.insert(0, ROOT)
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # 74.4: 148 SMs x 128 FP32 lanes x FMA x 1965 MHz
 TOTAL_SEQS, PROMPT, NEW, WAVE = 2048, 1024, 257, 512
+SMALL_SEQS = 8  # sequences per GPU of the small-wave decode line (its products: dequant GEMVs over int4 codes)
 
 
 def peaks():
@@ -193,6 +194,8 @@ def barrier(world: int) -> None:
 
 METRICS = {
     "decode": ("int4 Qwen3-0.6B-shape greedy decode tokens/s (config 5)", "tokens/s"),
+    "decode_small": ("int4 Qwen3-0.6B-shape greedy decode tokens/s, 8 sequences per GPU (config 5 shape, small wave)",
+                     "tokens/s"),
     "prefill": ("int8 Qwen3-0.6B-shape batched prefill tokens/s (config 4)", "tokens/s"),
     "ssm": ("int8 stacked selective-SSM tokens/s (config 3)", "tokens/s"),
     "lr": ("latent_reasoner int8 batch rows/s (config 1)", "rows/s"),
@@ -213,6 +216,15 @@ def workload_config(workload: str, args, M: int = 0) -> dict:
                 "seqs": total, "prompt": prompt, "new_tokens_per_seq": new, "max_seqs_per_wave": WAVE,
                 "parallelism": "sequences sharded over ranks, waves of <= 512 per GPU",
                 "l2": "inputs larger than L2 (the KV cache, tens of GB, is streamed every decode step)"}
+    if workload == "decode_small":
+        per, prompt, new, layers = args.seqs or SMALL_SEQS, args.prompt or PROMPT, args.new or NEW, args.layers or 28
+        full = (per, prompt, new, layers) == (SMALL_SEQS, PROMPT, NEW, 28)
+        return {"workload": "config5 int4 GPTQ Qwen3-0.6B-shape, small wave: 8 seqs per GPU x 1024-token prompts + 256 "
+                            "decode steps" if full else
+                f"REDUCED config5 small wave: {per} seqs per GPU x {prompt} + {new - 1} steps, {layers} layers",
+                "seqs_per_gpu": per, "prompt": prompt, "new_tokens_per_seq": new,
+                "parallelism": "each rank its own sequences (one wave)",
+                "l2": "inputs larger than L2 (the KV cache, up to 1.8 GB, and 0.3 GB of codes are streamed every decode step)"}
     if workload == "prefill":
         seqs, T, layers = args.seqs or PF_SEQS, args.prompt or PF_T, args.layers or 28
         return {"workload": "config4 int8 RTN Qwen3-0.6B-shape prefill: 64 seqs x 512 tokens, last-position logits"
@@ -243,14 +255,17 @@ def decode_ids(total: int, prompt: int) -> np.ndarray:
     return np.random.default_rng(5).integers(0, 151936, size=(total, prompt)).astype(np.float32)
 
 
-def bench_decode(args, world, rank, local):
+def bench_decode(args, world, rank, local, small: bool = False):
+    """Config 5: 2048 sequences over the ranks in waves of up to 512 per GPU; small: 8
+    sequences per GPU in one wave, whose products run as dequant GEMVs over the int4 codes."""
     import torch
 
     from technograd_b200 import _lib, lm
     _lib.init(0, [local])
     torch.cuda.set_device(local)
     cfg = dict(lm.QWEN3_0_6B, layers=args.layers or lm.QWEN3_0_6B["layers"])
-    total, prompt, new = args.seqs or TOTAL_SEQS, args.prompt or PROMPT, args.new or NEW
+    total = (args.seqs or SMALL_SEQS) * world if small else args.seqs or TOTAL_SEQS
+    prompt, new = args.prompt or PROMPT, args.new or NEW
     t0 = time.perf_counter()
     built = lm.DeviceBuilt(cfg, bits=4, method="gptq", seed=5)
     t_build = time.perf_counter() - t0
@@ -302,12 +317,17 @@ def bench_decode(args, world, rank, local):
     gemm_tf = sum(s["gemm_flops"] for s in stats) / (sum(s["gemm_ms"] for s in stats) / 1e3) / 1e12
     pre_tf = sum(s["attn_prefill_flops"] for s in stats) / (sum(s["attn_prefill_ms"] for s in stats) / 1e3) / 1e12
     tot_ms = sum(s["device_ms"] for s in stats)  # the profiled step
+    # the decode steps' products: the weight operands they read (int4 codes + scales for the
+    # GEMVs of waves of up to 8 sequences, else the bf16 copies) per decode step, against HBM
+    wb, wms = sum(s["decode_gemm_weight_bytes"] for s in stats), sum(s["decode_gemm_ms"] for s in stats)
+    wl = "decode_small" if small else "decode"
     line = {
-        "metric": METRICS["decode"][0], "value": value, "unit": "tokens/s",
+        "metric": METRICS[wl][0], "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sum(dev_ms) / len(dev_ms),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (bf16 hi/lo tensor-core split)",
+        "higher_is_better": True, "scaling": "weak" if small else "strong", "vs_baseline": None,
+        "dtype": "f32 (bf16 hi/lo tensor-core split; f32 FMA in the small-wave GEMVs)",
         "data": "synthetic: random-init weights N(0,0.02), uniform-random prompt ids (seed 5)",
-        "config": workload_config("decode", args),
+        "config": workload_config(wl, args),
         "breakdown": {"seqs_per_step_per_gpu": wave, "steps_for_full_job": nwaves,
                       "kv_cache": f"24-bit elements (bf16 + remainder byte, within 2^-16 of f32), "
                                   f"{wave * (prompt + new - 1) * cfg['layers'] * 8 * 128 * 6 / 1e9:.0f} GB per GPU at "
@@ -315,6 +335,10 @@ def bench_decode(args, world, rank, local):
                       "share_of_step": {"attn_decode": dec_ms / tot_ms, "gemm": sum(s["gemm_ms"] for s in stats) / tot_ms,
                                         "attn_prefill": sum(s["attn_prefill_ms"] for s in stats) / tot_ms},
                       "gemm_tflops": gemm_tf, "attn_prefill_tflops_f32": pre_tf, "build_s": t_build,
+                      "decode_weights": {
+                          "form": "int4 codes, dequant GEMVs" if wave <= 8 else "bf16 copies of the codes, tensor-core GEMMs",
+                          "bytes_per_decode_step": wb / max(new - 1, 1), "ms_per_decode_step": wms / max(new - 1, 1),
+                          "gbs": wb / max(wms, 1e-9) / 1e6, "frac_of_hbm": wb / max(wms, 1e-9) / 1e6 / pk["hbm_gbs"]},
                       "profiled_step_ms": tot_ms,
                       "profiled_step": "shares, TFLOP/s and the roofline: one step with per-kernel CUDA events right "
                                        "after the timed region (the timed steps run without them, so the decode "
@@ -942,7 +966,8 @@ def reference_arm(args) -> list:
                                   "of the cost: later tokens see up to 1280)")
         finally:
             P.close()
-        emit(*METRICS[wl], workload_config(wl, args), "strong", [base["value"]], walls, base)
+        emit(*METRICS[wl], workload_config(wl, args), "weak" if wl == "decode_small" else "strong", [base["value"]], walls,
+             base)
     return out
 
 
@@ -951,7 +976,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="all", choices=["all", "decode", "lr", "prefill", "gemm", "ssm"])
+    ap.add_argument("--workload", default="all", choices=["all", "decode", "decode_small", "lr", "prefill", "gemm", "ssm"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     # shape overrides for small profiling captures; the line's config says when they were used
@@ -973,7 +998,8 @@ def main():
         return
     world, rank, local = dist_setup()
     base = rank == 0 and world == 1 and not args.no_cpu_baseline
-    order = ["lr", "gemm", "ssm", "prefill", "decode"] if args.workload == "all" else [args.workload]
+    order = ["lr", "gemm", "ssm", "prefill", "decode_small", "decode"] if args.workload == "all" else [args.workload]
+    ref_decode = None  # the reference's per-token cost is the same for both decode lines: timed once
     for wl in order:
         lines = []
         if wl == "lr":
@@ -998,9 +1024,10 @@ def main():
                 line["cpu_baseline"] = cpu_baseline_prefill()
             lines.append(line)
         else:
-            line, _, _ = bench_decode(args, world, rank, local)
+            line, _, _ = bench_decode(args, world, rank, local, small=wl == "decode_small")
             if base:
-                line["cpu_baseline"] = cpu_baseline_decode()
+                ref_decode = ref_decode or cpu_baseline_decode()
+                line["cpu_baseline"] = ref_decode
             lines.append(line)
         if rank == 0:
             for line in lines:

@@ -279,6 +279,10 @@ typedef struct {
 	double gemm_ms;            /* tensor-core GEMMs */
 	double gemm_flops;         /* 2 M N K per GEMM (the useful work, not the bf16 hi/lo passes) */
 	long gemm_launches;
+	double gemm_weight_bytes;  /* the weight operands the GEMMs read: bf16 tiles, or packed codes
+	                              (+ scales) for the batches that dequantize in the kernel */
+	double decode_gemm_ms;     /* the part of gemm_ms spent in the decode steps */
+	double decode_gemm_weight_bytes; /* the part of gemm_weight_bytes read by the decode steps */
 } tg_cuda_lm_stats;
 int tg_cuda_lm_profile(tg_cuda_lm *g, int enable);
 int tg_cuda_lm_get_stats(const tg_cuda_lm *g, tg_cuda_lm_stats *out);

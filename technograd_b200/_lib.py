@@ -98,7 +98,8 @@ class LmStats(C.Structure):
     _fields_ = [("device_ms", C.c_double), ("launches", C.c_long), ("attn_decode_ms", C.c_double),
                 ("attn_decode_bytes", C.c_double), ("attn_decode_launches", C.c_long), ("attn_prefill_ms", C.c_double),
                 ("attn_prefill_flops", C.c_double), ("gemm_ms", C.c_double), ("gemm_flops", C.c_double),
-                ("gemm_launches", C.c_long)]
+                ("gemm_launches", C.c_long), ("gemm_weight_bytes", C.c_double),
+                ("decode_gemm_ms", C.c_double), ("decode_gemm_weight_bytes", C.c_double)]
 
 
 _lib = None

@@ -43,6 +43,12 @@ struct GemmArgs {
 	int cbits, cside;
 	long cld;
 	int raw_bytes; // set by gemm(): bytes of one K block of codes (TMA-loaded into each ring stage)
+	// Scaled dequant (cside 2 with nb 2): B[0] and B[1] are both built from the codes, as the
+	// bf16 hi and lo parts of code * cscale[(k / cgroup) * cscale_ld + n] (weights whose scale
+	// changes along K, such as per-head o_proj scales); cgroup a multiple of 64
+	const float *cscale;
+	int cgroup;
+	long cscale_ld;
 	// launch with programmatic stream serialization (the kernels wait for the one before them
 	// with griddepcontrol.wait before touching memory; only the decoder's captured step sets it)
 	int pdl;

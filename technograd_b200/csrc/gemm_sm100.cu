@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(320, 1) gemm_tc(const __grid_constant__ TmaMap
 		for (int i = 0; i < p.na; i++)
 			if (!(i == 0 && p.cside == 1)) tma_prefetch_desc(&maps.a[i]);
 		for (int i = 0; i < p.nb; i++)
-			if (!(i == 0 && p.cside == 2)) tma_prefetch_desc(&maps.b[i]);
+			if (!(p.cside == 2 && (i == 0 || p.cscale))) tma_prefetch_desc(&maps.b[i]);
 		if (p.cside) {
 			tma_prefetch_desc(&maps.c);
 			tma_prefetch_desc(&maps.cpf);
@@ -139,9 +139,10 @@ __global__ void __launch_bounds__(320, 1) gemm_tc(const __grid_constant__ TmaMap
 				mbar_expect_tx(&rawf[s], p.raw_bytes);
 				tma_load_2d(st + ops_bytes, &maps.c, &rawf[s], (kb0 + kb) * kbytes, p.cside == 1 ? m0 : n0);
 			}
-			mbar_expect_tx(&full[s], ops_bytes - (p.cside == 1 ? A_TILE : p.cside == 2 ? B_TILE : 0));
+			const int cb = p.cside == 2 ? (p.cscale ? 2 : 1) : 0; // B tiles the converters build
+			mbar_expect_tx(&full[s], ops_bytes - (p.cside == 1 ? A_TILE : cb * B_TILE));
 			for (int i = p.cside == 1 ? 1 : 0; i < p.na; i++) tma_load_2d(st + i * A_TILE, &maps.a[i], &full[s], (kb0 + kb) * BK, m0);
-			for (int j = p.cside == 2 ? 1 : 0; j < p.nb; j++)
+			for (int j = cb; j < p.nb; j++)
 				tma_load_2d(st + p.na * A_TILE + j * B_TILE, &maps.b[j], &full[s], (kb0 + kb) * BK, n0);
 		}
 	} else if (warp == 1 && lane == 0) { // ---- MMA issuer
@@ -202,9 +203,18 @@ __global__ void __launch_bounds__(320, 1) gemm_tc(const __grid_constant__ TmaMap
 				uint8_t *slot = stg + (p.cside == 1 ? 0 : p.na * A_TILE);
 				const uint8_t *raw = stg + ops_bytes;
 				uint4 vv[4];
+				float sc[4];
 #pragma unroll
-				for (int i = 0; i < 4; i++)
-					if (et + i * 256 < chunks) vv[i] = *(const uint4 *)(raw + (et + i * 256) * 16);
+				for (int i = 0; i < 4; i++) {
+					const int it = et + i * 256;
+					if (it < chunks) {
+						vv[i] = *(const uint4 *)(raw + it * 16);
+						if (p.cscale) { // the scale of this chunk's row in this K block's group
+							const int n = n0 + it / cpr;
+							sc[i] = n < p.N ? p.cscale[(long)((kb0 + kb) * BK / p.cgroup) * p.cscale_ld + n] : 0.0f;
+						}
+					}
+				}
 #pragma unroll
 				for (int i = 0; i < 4; i++) {
 					const int it = et + i * 256;
@@ -213,7 +223,39 @@ __global__ void __launch_bounds__(320, 1) gemm_tc(const __grid_constant__ TmaMap
 					uint8_t *dst = smem_row(slot, rr);
 					const uint4 v = vv[i];
 					const uint32_t w[4] = { v.x, v.y, v.z, v.w };
-					if (p.cbits == 8) { // 16 codes -> swizzle units 2c, 2c + 1
+					if (p.cscale) {
+						// hi and lo of code * scale (f32, rounded once), as the load-time split
+						// of the same product: hi into B[0], lo into B[1] at the same offsets
+						uint8_t *dlo = dst + B_TILE;
+						const int upw = p.cbits == 8 ? 2 : 4;   // bf16 pairs per code word
+						const int u0 = p.cbits == 8 ? 2 * c : 4 * c; // first 16-byte unit
+#pragma unroll
+						for (int j = 0; j < 4; j++) {
+							uint32_t h[4];
+							if (p.cbits == 8) int8x4_bf16(w[j], h);
+							else int4x8_bf16(w[j], h);
+							uint32_t hh[4], ll[4];
+#pragma unroll
+							for (int e = 0; e < 4; e++) {
+								if (e >= upw) break;
+								const float a = __fmul_rn(__uint_as_float(h[e] << 16), sc[i]);
+								const float b = __fmul_rn(__uint_as_float(h[e] & 0xFFFF0000u), sc[i]);
+								const uint32_t ah = bf16_bits(a), bh = bf16_bits(b);
+								hh[e] = ah | (bh << 16);
+								ll[e] = bf16_bits(__fsub_rn(a, __uint_as_float(ah << 16))) |
+									(bf16_bits(__fsub_rn(b, __uint_as_float(bh << 16))) << 16);
+							}
+							if (p.cbits == 8) { // word j = codes 4j..4j+3: half of unit u0 + j / 2
+								const int off = (((u0 + (j >> 1)) ^ sw) << 4) + (j & 1) * 8;
+								*(uint2 *)(dst + off) = make_uint2(hh[0], hh[1]);
+								*(uint2 *)(dlo + off) = make_uint2(ll[0], ll[1]);
+							} else {
+								const int off = ((u0 + j) ^ sw) << 4;
+								*(uint4 *)(dst + off) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+								*(uint4 *)(dlo + off) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+							}
+						}
+					} else if (p.cbits == 8) { // 16 codes -> swizzle units 2c, 2c + 1
 						uint32_t h[8];
 #pragma unroll
 						for (int j = 0; j < 4; j++) int8x4_bf16(w[j], h + 2 * j);
@@ -728,6 +770,8 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 	if (p.cside && (p.cside > 2 || !p.codes || (p.cbits != 8 && p.cbits != 4) || p.K % BK || p.cld % 16 ||
 			((uintptr_t)p.codes & 15) || (p.cside == 1 && p.pa[0] != 0 && p.na < 1)))
 		return set_err(TG_CUDA_EINVAL, "gemm: in-kernel dequant needs K %% 64 == 0 and 16-byte aligned code rows");
+	if (p.cscale && (p.cside != 2 || p.nb != 2 || p.cgroup <= 0 || p.cgroup % BK || p.cscale_ld < p.N))
+		return set_err(TG_CUDA_EINVAL, "gemm: scaled dequant needs the codes as B, two B operands and K groups of 64k");
 	int sms = 148, dev = 0;
 	cudaGetDevice(&dev);
 	cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -753,7 +797,7 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 	for (int i = 0; i < p.na; i++)
 		if (!(i == 0 && p.cside == 1) && (rc = make_map(&maps.a[i], ops.a[i], p.M, p.K, ops.lda, BM))) return rc;
 	for (int j = 0; j < p.nb; j++)
-		if (!(j == 0 && p.cside == 2) && (rc = make_map(&maps.b[j], ops.b[j], p.N, p.K, ops.ldb, BN))) return rc;
+		if (!(p.cside == 2 && (j == 0 || p.cscale)) && (rc = make_map(&maps.b[j], ops.b[j], p.N, p.K, ops.ldb, BN))) return rc;
 	// as many ring stages (2..4; 6 for the narrow tile) as fit in 220 KB of shared memory
 	const int stage = stage_of(BN);
 	const int stages = std::min(BN == 32 ? 6 : 4, std::max(2, (220 * 1024) / stage));

@@ -37,6 +37,7 @@
 #include "attn_tc.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
+#include "gemv_dec.cuh"
 #include "kernels.cuh"
 #include "tc.cuh"
 
@@ -68,6 +69,25 @@ __global__ void k_codes_gu(const signed char *__restrict__ qg, const signed char
 	dst[row * D + p] = __float2bfloat16_rn(v);
 }
 
+// [K, N] codes (x @ W layout, int4 two per flat index pair, low nibble first) -> K-major rows
+// of codes packed the same way: source column n becomes row row0 + (n / blk) * 2 blk + off +
+// n % blk (blk = N: row row0 + n; blk 32 with off 0 / 32: the gate/up interleave of k_codes_gu).
+// One thread per output byte. These rows feed the small-batch GEMV and the GEMM's in-kernel
+// dequant.
+__global__ void k_codes_T(const signed char *__restrict__ q, int bits, long K, long N, long blk, long off, long row0,
+			  uint8_t *__restrict__ dst, long ld)
+{
+	const long kbytes = bits == 8 ? K : K / 2;
+	long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+	if (t >= N * kbytes) return;
+	const long n = t / kbytes, j = t % kbytes;
+	const long row = row0 + (n / blk) * 2 * blk + off + n % blk;
+	uint8_t b;
+	if (bits == 8) b = (uint8_t)q[j * N + n];
+	else b = (uint8_t)((qcode(q, 4, 2 * j * N + n) & 15) | ((qcode(q, 4, (2 * j + 1) * N + n) & 15) << 4));
+	dst[row * ld + j] = b;
+}
+
 // o_proj: stacked per-head codes [NQ*HD, D] with scales s[h*D + n] -> B[n][h*HD + p] =
 // code * s, split hi/lo (the dequantized value the program's param holds, src/ir.c:503-507).
 __global__ void k_wo_prescale(const signed char *__restrict__ q, const float *__restrict__ s, int bits, int KO, int HD,
@@ -84,6 +104,23 @@ __global__ void k_wo_prescale(const signed char *__restrict__ q, const float *__
 }
 
 // ---- per-token kernels ----------------------------------------------------------------------
+
+// SwiGLU of the small-batch GEMV's gate/up sums [M][2 FF] (rows in k_codes_gu's interleaved
+// order) with the per-channel scales, split to bf16 hi/lo [M][FF]: the arithmetic of the
+// GEMM's SwiGLU epilogue on the same sums.
+__global__ void k_swiglu_split(const float *__restrict__ gu, long M, int FF, const float *__restrict__ sg,
+			       const float *__restrict__ su, __nv_bfloat16 *__restrict__ hi, __nv_bfloat16 *__restrict__ lo)
+{
+	pdl_wait(); // programmatic dependent launch inside the decode step (no-op otherwise)
+	pdl_launch();
+	const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+	if (t >= M * FF) return;
+	const long j = t / FF;
+	const int f = (int)(t % FF);
+	const float *r = gu + j * 2 * FF + (f / 32) * 64 + f % 32;
+	const float gs = r[0] * sg[f], us = r[32] * su[f];
+	split_bf16(__fmul_rn(__fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs))), us), hi[t], lo[t]); // silu(g) * u
+}
 
 // h[r] = E[round(ids[r])] or zeros out of range (take, runtime/tg_rt.h:316-322). One warp per row.
 __global__ void k_embed(const float *__restrict__ ids, const int *__restrict__ tok, long M, const float *__restrict__ E,
@@ -411,6 +448,9 @@ __global__ void k_argmax(const float *__restrict__ logits, int V, int *__restric
 
 struct Layer {
 	DevBuf wqkv, sqkv, wo_hi, wo_lo, wgu, sg, su, wd, sd, ln1, ln2, qn, kn;
+	// the same weights as packed codes [out][in] (small batches read these: a quarter (int4) or
+	// half (int8) of the bf16 bytes), and o_proj's per-head scales [NQ][D]
+	DevBuf cqkv, cgu, cd, co, so;
 	CUtensorMap kmap, vmap; // the layer's K and V bf16 cache planes as [slot * NKV * max_len][128] (prefill attention)
 };
 
@@ -420,6 +460,16 @@ struct Engine {
 	int L, D, NQ, NKV, HD, FF, V, bits, max_seqs, max_len;
 	float eps, scale;
 	DevBuf E, lnf, lmw, lms, cosT, sinT;
+	DevBuf clm; // LM head codes [V][D] packed
+	// Batches of at most gemv_rows rows (decode steps of waves of up to 8 sequences) run the
+	// layers' products as dequant GEMVs over the packed codes (gemv_dec); batches of at most
+	// codes_rows rows run the tensor-core GEMM with the codes expanded in the kernel; the rest
+	// read the bf16 copies. TG_CUDA_GEMV_ROWS / TG_CUDA_CODES_ROWS set them at load.
+	long gemv_rows = 8, codes_rows = 0;
+	bool codes = false; // packed codes built
+	DevBuf gus;         // the GEMV's gate/up sums [gemv_rows][2 FF] before SwiGLU
+	bool use_gemv(long M) const { return codes && M <= gemv_rows; }
+	bool use_codes(long M) const { return codes && M <= codes_rows; }
 	std::vector<std::unique_ptr<Layer>> layers;
 	DevBuf kh, kq, vh, vq; // the KV cache: bf16 and residual-byte planes (kv.cuh)
 	// activations
@@ -522,12 +572,17 @@ static int gemm_m(Engine &g, const GemmOperands &op, const GemmArgs &p0)
 	p.pdl = g.pdl ? 1 : 0;
 	p.partial = g.part.as<float>(); // split-K scratch for the tile kernel's small batches
 	p.partial_floats = (long)(g.part.bytes / sizeof(float));
-	int mk = mark_begin(g, MK_GEMM, 2.0 * p.M * p.N * p.K);
+	// the weight operand's bytes: codes (+ per-head scales) or bf16 tiles, + the epilogue's scales
+	const double wbytes = (p.cside == 2 ? (double)p.N * p.cld + (p.cscale ? 4.0 * p.N * (p.K / p.cgroup) : 0.0)
+					    : 2.0 * p.nb * p.N * p.K) + (p.scale ? 4.0 * p.N : 0.0);
+	int mk = mark_begin(g, MK_GEMM, 2.0 * p.M * p.N * p.K, wbytes);
 	int rc = g.small_gemm && p.M > 128 && p.M <= 384 && p.N <= 16384 && gemm_sk_fits(p) ? gemm_sk(op, p, g.st) : gemm(op, p, g.st);
 	mark_end(g, mk);
 	return rc;
 }
 
+// The times of n marks into t. keys > 0: the marks of one replay of the decode-step graph, whose
+// attention reads keys positions per sequence; keys == 0: marks of directly launched kernels.
 static void add_marks(Engine &g, tg_cuda_lm_stats &t, const std::vector<Engine::Mark> &v, size_t n, double keys)
 {
 	for (size_t i = 0; i < n; i++) {
@@ -538,7 +593,10 @@ static void add_marks(Engine &g, tg_cuda_lm_stats &t, const std::vector<Engine::
 			t.attn_decode_ms += e, t.attn_decode_bytes += v[i].work + v[i].work_len * keys, t.attn_decode_launches++;
 			break;
 		case MK_PREFILL: t.attn_prefill_ms += e, t.attn_prefill_flops += v[i].work; break;
-		case MK_GEMM: t.gemm_ms += e, t.gemm_flops += v[i].work, t.gemm_launches++; break;
+		case MK_GEMM:
+			t.gemm_ms += e, t.gemm_flops += v[i].work, t.gemm_weight_bytes += v[i].work_len, t.gemm_launches++;
+			if (keys > 0) t.decode_gemm_ms += e, t.decode_gemm_weight_bytes += v[i].work_len; // a decode step's
+			break;
 		}
 	}
 }
@@ -610,27 +668,51 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 			}
 		if ((rc = upload(g.cosT, c.data(), c.size() * 4, dev, g.st)) || (rc = upload(g.sinT, s.data(), s.size() * 4, dev, g.st))) return rc;
 	}
-	DevBuf tmpq, tmpq2, tmps;
-	auto codes_T = [&](const tg_cuda_qmat &m, long rows, long cols, __nv_bfloat16 *dst, long ldd) -> int {
-		// [rows=in, cols=out] codes -> dst[out][in]
+	{
+		const char *e = getenv("TG_CUDA_GEMV_ROWS");
+		if (e) g.gemv_rows = std::min(atol(e), 8L);
+		e = getenv("TG_CUDA_CODES_ROWS");
+		if (e) g.codes_rows = std::min(atol(e), 128L);
+		// whole K blocks of 64 (the GEMM's dequant) and per-head scale groups of them
+		g.codes = (g.gemv_rows > 0 || g.codes_rows > 0) && (bits == 4 || bits == 8) && D % 64 == 0 &&
+			  ((long)NQ * HD) % 64 == 0 && FF % 64 == 0 && HD % 64 == 0;
+	}
+	const long cpb = bits == 8 ? 1 : 2; // codes per byte
+	DevBuf tmpq, tmpq2;
+	// the uploaded codes [K, N] (in src) -> packed K-major rows of cdst (when codes are kept)
+	auto pack_T = [&](const DevBuf &src, long K, long N, long blk, long off, long row0, DevBuf &cdst) -> int {
+		if (!g.codes) return TG_CUDA_OK;
+		const long n = N * (K / cpb);
+		k_codes_T<<<(unsigned)((n + 255) / 256), 256, 0, g.st>>>(src.as<signed char>(), bits, K, N, blk, off, row0,
+									  cdst.as<uint8_t>(), K / cpb);
+		TGC_LAUNCH_CHECK();
+		return TG_CUDA_OK;
+	};
+	auto codes_T = [&](const tg_cuda_qmat &m, long rows, long cols, __nv_bfloat16 *dst, long ldd, DevBuf *cdst = nullptr,
+			   long row0 = 0) -> int {
+		// [rows=in, cols=out] codes -> dst[out][in] (and the packed codes into cdst rows row0..)
 		int r;
 		if ((r = upload(tmpq, m.q, qbytes(rows * cols, bits), dev, g.st))) return r;
 		if ((r = codes_to_bf16(tmpq.as<signed char>(), bits, rows, cols, true, dst, ldd, g.st))) return r;
+		if (cdst && (r = pack_T(tmpq, rows, cols, cols, 0, row0, *cdst))) return r;
 		TGC_CUDA(cudaStreamSynchronize(g.st));
 		return TG_CUDA_OK;
 	};
+	auto calloc_ = [&](DevBuf &b, long rows, long K) -> int { return g.codes ? b.alloc((size_t)rows * (K / cpb), dev) : TG_CUDA_OK; };
 	// LM head [D, V] -> [V][D]
-	if ((rc = g.lmw.alloc((size_t)V * D * 2, dev)) || (rc = codes_T(d->lm_head, D, V, g.lmw.as<__nv_bfloat16>(), D)) ||
+	if ((rc = g.lmw.alloc((size_t)V * D * 2, dev)) || (rc = calloc_(g.clm, V, D)) ||
+	    (rc = codes_T(d->lm_head, D, V, g.lmw.as<__nv_bfloat16>(), D, &g.clm)) ||
 	    (rc = upload(g.lms, d->lm_head.s, (size_t)V * 4, dev, g.st)))
 		return rc;
 	for (int l = 0; l < g.L; l++) {
 		g.layers.emplace_back(new Layer);
 		Layer &Y = *g.layers.back();
 		const int HQKV = g.HQKV();
-		if ((rc = Y.wqkv.alloc((size_t)HQKV * D * 2, dev))) return rc;
+		if ((rc = Y.wqkv.alloc((size_t)HQKV * D * 2, dev)) || (rc = calloc_(Y.cqkv, HQKV, D))) return rc;
 		__nv_bfloat16 *w = Y.wqkv.as<__nv_bfloat16>();
-		if ((rc = codes_T(d->wq[l], D, NQ * HD, w, D)) || (rc = codes_T(d->wk[l], D, NKV * HD, w + (size_t)NQ * HD * D, D)) ||
-		    (rc = codes_T(d->wv[l], D, NKV * HD, w + (size_t)(NQ + NKV) * HD * D, D)))
+		if ((rc = codes_T(d->wq[l], D, NQ * HD, w, D, &Y.cqkv, 0)) ||
+		    (rc = codes_T(d->wk[l], D, NKV * HD, w + (size_t)NQ * HD * D, D, &Y.cqkv, (long)NQ * HD)) ||
+		    (rc = codes_T(d->wv[l], D, NKV * HD, w + (size_t)(NQ + NKV) * HD * D, D, &Y.cqkv, (long)(NQ + NKV) * HD)))
 			return rc;
 		{
 			std::vector<float> s(HQKV);
@@ -642,11 +724,13 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 		// o_proj: pre-scaled hi/lo [D][NQ*HD]
 		const long KO = (long)NQ * HD;
 		if ((rc = Y.wo_hi.alloc((size_t)D * KO * 2, dev)) || (rc = Y.wo_lo.alloc((size_t)D * KO * 2, dev)) ||
-		    (rc = upload(tmpq, d->wo[l].q, qbytes(KO * D, bits), dev, g.st)) || (rc = upload(tmps, d->wo[l].s, (size_t)NQ * D * 4, dev, g.st)))
+		    (rc = calloc_(Y.co, D, KO)) || (rc = upload(tmpq, d->wo[l].q, qbytes(KO * D, bits), dev, g.st)) ||
+		    (rc = upload(Y.so, d->wo[l].s, (size_t)NQ * D * 4, dev, g.st)))
 			return rc;
-		k_wo_prescale<<<(unsigned)((KO * D + 255) / 256), 256, 0, g.st>>>(tmpq.as<signed char>(), tmps.as<float>(), bits, (int)KO,
+		k_wo_prescale<<<(unsigned)((KO * D + 255) / 256), 256, 0, g.st>>>(tmpq.as<signed char>(), Y.so.as<float>(), bits, (int)KO,
 										      HD, D, Y.wo_hi.as<__nv_bfloat16>(), Y.wo_lo.as<__nv_bfloat16>());
 		TGC_LAUNCH_CHECK();
+		if ((rc = pack_T(tmpq, KO, D, D, 0, 0, Y.co))) return rc;
 		TGC_CUDA(cudaStreamSynchronize(g.st));
 		// gate/up interleaved [2FF][D]
 		if ((rc = Y.wgu.alloc((size_t)2 * FF * D * 2, dev)) || (rc = upload(tmpq, d->wg[l].q, qbytes((long)D * FF, bits), dev, g.st)) ||
@@ -655,10 +739,13 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 		k_codes_gu<<<(unsigned)((2L * D * FF + 255) / 256), 256, 0, g.st>>>(tmpq.as<signed char>(), tmpq2.as<signed char>(), bits, D,
 										      FF, Y.wgu.as<__nv_bfloat16>());
 		TGC_LAUNCH_CHECK();
+		if ((rc = calloc_(Y.cgu, 2L * FF, D)) || (rc = pack_T(tmpq, D, FF, 32, 0, 0, Y.cgu)) || (rc = pack_T(tmpq2, D, FF, 32, 32, 0, Y.cgu)))
+			return rc;
 		TGC_CUDA(cudaStreamSynchronize(g.st));
 		if ((rc = upload(Y.sg, d->wg[l].s, (size_t)FF * 4, dev, g.st)) || (rc = upload(Y.su, d->wu[l].s, (size_t)FF * 4, dev, g.st))) return rc;
 		// down [FF, D] -> [D][FF]
-		if ((rc = Y.wd.alloc((size_t)D * FF * 2, dev)) || (rc = codes_T(d->wd[l], FF, D, Y.wd.as<__nv_bfloat16>(), FF)) ||
+		if ((rc = Y.wd.alloc((size_t)D * FF * 2, dev)) || (rc = calloc_(Y.cd, D, FF)) ||
+		    (rc = codes_T(d->wd[l], FF, D, Y.wd.as<__nv_bfloat16>(), FF, &Y.cd)) ||
 		    (rc = upload(Y.sd, d->wd[l].s, (size_t)D * 4, dev, g.st)))
 			return rc;
 		if ((rc = upload(Y.ln1, d->ln1[l], (size_t)D * 4, dev, g.st)) || (rc = upload(Y.ln2, d->ln2[l], (size_t)D * 4, dev, g.st)) ||
@@ -680,6 +767,7 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 	    (rc = g.status.alloc(64, dev)))
 		return rc;
 	if ((rc = g.dpos.alloc(16, dev))) return rc;
+	if (g.codes && g.gemv_rows > 0 && (rc = g.gus.alloc((size_t)g.gemv_rows * 2 * FF * 4, dev))) return rc;
 	{ // split-K partial sums of the decode GEMMs: up to 16 splits of a 128-row-padded batch
 		long mpad = ((long)max_seqs + 127) / 128 * 128, nmax = std::max<long>(g.HQKV(), std::max<long>(2L * FF, D));
 		if ((rc = g.part.alloc((size_t)16 * mpad * nmax * sizeof(float), dev))) return rc;
@@ -703,7 +791,7 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 		    (rc = bf16_tile_map(&g.layers[l]->vmap, g.vh.as<__nv_bfloat16>() + lo, rows, HD, HD, FA_K)))
 			return rc;
 	}
-	if ((rc = gemm_sk_prepare())) return rc;
+	if ((rc = gemm_sk_prepare()) || (rc = gemv_dec_prepare())) return rc;
 	TGC_CUDA(cudaFuncSetAttribute(k_attn_prefill_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FA_SMEM));
 	TGC_CUDA(cudaFuncSetAttribute(k_attn_prefill_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FB_SMEM));
 	TGC_CUDA(cudaFuncSetAttribute(k_attn_decode<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_smem(g)));
@@ -711,6 +799,29 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 	TGC_CUDA(cudaMemsetAsync(g.status.p, 0, 64, g.st));
 	TGC_CUDA(cudaStreamSynchronize(g.st));
 	return TG_CUDA_OK;
+}
+
+// B[0] (the weights, [N][K]) from packed codes expanded in the kernel instead of the bf16 copy
+static void codes_b(const Engine &g, GemmArgs &p, const DevBuf &c)
+{
+	p.codes = c.as<signed char>(), p.cbits = g.bits, p.cside = 2, p.cld = (long)p.K * g.bits / 8;
+}
+
+// A product of a batch of at most 8 rows: out[j][n] (+)= s * sum_k (hi + lo)[j][k] code(n, k)
+// as a dequant GEMV over the packed codes [N][K] (group > 0: per-(K group, n) scales).
+static int gemv_m(Engine &g, const DevBuf &codes, const void *hi, const void *lo, long lda, long M, int N, int K, const float *s,
+		  int group, long s_ld, float *out, long ldo, int epi)
+{
+	GemvDecArgs a;
+	memset(&a, 0, sizeof a);
+	a.hi = (const __nv_bfloat16 *)hi, a.lo = (const __nv_bfloat16 *)lo, a.lda = lda, a.nb = (int)M;
+	a.q = codes.as<signed char>(), a.m = N, a.k = K, a.bits = g.bits;
+	a.s = s, a.group = group, a.s_ld = s_ld, a.out = out, a.ldo = ldo, a.epi = epi;
+	const double wbytes = (double)N * K * g.bits / 8 + (s ? 4.0 * N * (group ? K / group : 1) : 0.0);
+	int mk = mark_begin(g, MK_GEMM, 2.0 * M * N * K, wbytes);
+	int rc = gemv_dec(a, g.st, g.pdl);
+	mark_end(g, mk);
+	return rc;
 }
 
 static GemmArgs gemm_args(int M, int N, int K, int epi)
@@ -732,6 +843,10 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 	const long S = M / T;
 	int *status = g.status.as<int>();
 	const unsigned warps_grid = (unsigned)((M * 32 + 255) / 256);
+	// the weights' form: GEMVs over codes (batches of up to 8 rows), the GEMM with the codes
+	// expanded in the kernel, or the GEMM on the bf16 copies
+	const bool gv = g.use_gemv(M), cw = !gv && g.use_codes(M);
+	const long KO = (long)NQ * HD;
 	for (int l = 0; l < g.L; l++) {
 		Layer &Y = *g.layers[l];
 		const size_t lo = (size_t)l * g.max_seqs * NKV * (size_t)g.max_len * HD; // this layer's first element
@@ -742,10 +857,18 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 		TGC_CUDA(launch_k(g, k_rmsnorm_split, dim3(warps_grid), dim3(256), 0, (const float *)g.h.as<float>(), M, D,
 				  (const float *)Y.ln1.as<float>(), g.eps, 0, g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>()));
 		GemmOperands op;
-		op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = Y.wqkv.p, op.lda = D, op.ldb = D;
-		GemmArgs p = gemm_args((int)M, g.HQKV(), D, EPI_STORE);
-		p.scale = Y.sqkv.as<float>(), p.scale_mode = 2, p.out = g.qkv.as<float>(), p.ldo = g.HQKV(), p.status = status;
-		if ((rc = gemm_m(g, op, p))) return rc;
+		GemmArgs p;
+		if (gv) {
+			if ((rc = gemv_m(g, Y.cqkv, g.xhi.p, g.xlo.p, D, M, g.HQKV(), D, Y.sqkv.as<float>(), 0, 0, g.qkv.as<float>(), g.HQKV(),
+					 GD_STORE)))
+				return rc;
+		} else {
+			op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = Y.wqkv.p, op.lda = D, op.ldb = D;
+			p = gemm_args((int)M, g.HQKV(), D, EPI_STORE);
+			p.scale = Y.sqkv.as<float>(), p.scale_mode = 2, p.out = g.qkv.as<float>(), p.ldo = g.HQKV(), p.status = status;
+			if (cw) codes_b(g, p, Y.cqkv);
+			if ((rc = gemm_m(g, op, p))) return rc;
+		}
 		long heads = M * (NQ + 2 * NKV);
 		TGC_CUDA(launch_k(g, k_qk_rope, dim3((unsigned)((heads * 32 + 255) / 256)), dim3(256), 0, (const float *)g.qkv.as<float>(),
 				  M, T, pos0, (const int *)(decode ? g.dpos.as<int>() : nullptr), NQ, NKV, g.eps,
@@ -781,26 +904,47 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 			mark_end(g, mk);
 		}
 		TGC_LAUNCH_CHECK();
-		// o_proj with the residual: h += attn @ Wo (hi*hi + hi*lo + lo*hi)
-		op = GemmOperands();
-		op.a[0] = g.ahi.p, op.a[1] = g.alo.p, op.b[0] = Y.wo_hi.p, op.b[1] = Y.wo_lo.p, op.lda = (long)NQ * HD, op.ldb = (long)NQ * HD;
-		p = gemm_args((int)M, D, NQ * HD, EPI_ADD);
-		p.nb = 2, p.npairs = 3;
-		p.pa[0] = 0, p.pb[0] = 0, p.pa[1] = 0, p.pb[1] = 1, p.pa[2] = 1, p.pb[2] = 0;
-		p.out = g.h.as<float>(), p.ldo = D, p.status = status;
-		if ((rc = gemm_m(g, op, p))) return rc;
+		// o_proj with the residual: h += attn @ Wo (hi*hi + hi*lo + lo*hi; the GEMV: per-head scales)
+		if (gv) {
+			if ((rc = gemv_m(g, Y.co, g.ahi.p, g.alo.p, KO, M, D, (int)KO, Y.so.as<float>(), HD, D, g.h.as<float>(), D, GD_ADD)))
+				return rc;
+		} else {
+			op = GemmOperands();
+			op.a[0] = g.ahi.p, op.a[1] = g.alo.p, op.b[0] = Y.wo_hi.p, op.b[1] = Y.wo_lo.p, op.lda = KO, op.ldb = KO;
+			p = gemm_args((int)M, D, (int)KO, EPI_ADD);
+			p.nb = 2, p.npairs = 3;
+			p.pa[0] = 0, p.pb[0] = 0, p.pa[1] = 0, p.pb[1] = 1, p.pa[2] = 1, p.pb[2] = 0;
+			p.out = g.h.as<float>(), p.ldo = D, p.status = status;
+			if (cw) { // hi and lo of code * per-head scale, built in the kernel
+				codes_b(g, p, Y.co);
+				p.cscale = Y.so.as<float>(), p.cgroup = HD, p.cscale_ld = D;
+			}
+			if ((rc = gemm_m(g, op, p))) return rc;
+		}
 		TGC_CUDA(launch_k(g, k_rmsnorm_split, dim3(warps_grid), dim3(256), 0, (const float *)g.h.as<float>(), M, D,
 				  (const float *)Y.ln2.as<float>(), g.eps, 0, g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>()));
+		if (gv) { // gate/up sums, then SwiGLU with the channel scales
+			if ((rc = gemv_m(g, Y.cgu, g.xhi.p, g.xlo.p, D, M, 2 * FF, D, nullptr, 0, 0, g.gus.as<float>(), 2L * FF, GD_STORE)))
+				return rc;
+			g.launches++;
+			TGC_CUDA(launch_k(g, k_swiglu_split, dim3((unsigned)((M * FF + 255) / 256)), dim3(256), 0, (const float *)g.gus.as<float>(),
+					  M, FF, (const float *)Y.sg.as<float>(), (const float *)Y.su.as<float>(), g.ghi.as<__nv_bfloat16>(),
+					  g.glo.as<__nv_bfloat16>()));
+			if ((rc = gemv_m(g, Y.cd, g.ghi.p, g.glo.p, FF, M, D, FF, Y.sd.as<float>(), 0, 0, g.h.as<float>(), D, GD_ADD))) return rc;
+			continue;
+		}
 		op = GemmOperands();
 		op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = Y.wgu.p, op.lda = D, op.ldb = D;
 		p = gemm_args((int)M, 2 * FF, D, EPI_SWIGLU);
 		p.scale = Y.sg.as<float>(), p.scale2 = Y.su.as<float>(), p.out_hi = g.ghi.as<__nv_bfloat16>(),
 		p.out_lo = g.glo.as<__nv_bfloat16>(), p.ldo = FF, p.status = status;
+		if (cw) codes_b(g, p, Y.cgu);
 		if ((rc = gemm_m(g, op, p))) return rc;
 		op = GemmOperands();
 		op.a[0] = g.ghi.p, op.a[1] = g.glo.p, op.b[0] = Y.wd.p, op.lda = FF, op.ldb = FF;
 		p = gemm_args((int)M, D, FF, EPI_ADD);
 		p.scale = Y.sd.as<float>(), p.scale_mode = 2, p.out = g.h.as<float>(), p.ldo = D, p.status = status;
+		if (cw) codes_b(g, p, Y.cd);
 		if ((rc = gemm_m(g, op, p))) return rc;
 	}
 	return TG_CUDA_OK;
@@ -814,10 +958,14 @@ static int head(Engine &g, long S, int T)
 	TGC_CUDA(launch_k(g, k_rmsnorm_split, dim3((unsigned)((S * 32 + 255) / 256)), dim3(256), 0, (const float *)g.h.as<float>(), S,
 			  g.D, (const float *)g.lnf.as<float>(), g.eps, T, g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>()));
 	TGC_LAUNCH_CHECK();
+	// the head stays on the tensor cores even for a handful of sequences: a GEMV over its
+	// 151,936 rows measured 230 us a step at 8 sequences (FMA and shared-memory bound), the
+	// GEMM tens of microseconds
 	GemmOperands op;
 	op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = g.lmw.p, op.lda = g.D, op.ldb = g.D;
 	GemmArgs p = gemm_args((int)S, g.V, g.D, EPI_STORE);
 	p.scale = g.lms.as<float>(), p.scale_mode = 2, p.out = g.logits.as<float>(), p.ldo = g.V, p.status = g.status.as<int>();
+	if (g.use_codes(S)) codes_b(g, p, g.clm);
 	if ((rc = gemm_m(g, op, p))) return rc;
 	return TG_CUDA_OK;
 }
@@ -1063,6 +1211,8 @@ extern "C" int tg_cuda_lm_get_stats(const tg_cuda_lm *g, tg_cuda_lm_stats *out)
 		out->attn_decode_launches += t.attn_decode_launches;
 		out->attn_prefill_ms += t.attn_prefill_ms, out->attn_prefill_flops += t.attn_prefill_flops;
 		out->gemm_ms += t.gemm_ms, out->gemm_flops += t.gemm_flops, out->gemm_launches += t.gemm_launches;
+		out->gemm_weight_bytes += t.gemm_weight_bytes;
+		out->decode_gemm_ms += t.decode_gemm_ms, out->decode_gemm_weight_bytes += t.decode_gemm_weight_bytes;
 	}
 	return TG_CUDA_OK;
 }

@@ -76,6 +76,51 @@ def test_generate_teacher_forced(micro):
     assert match / total >= 0.999 or total - match <= 1
 
 
+def test_code_weights_match_bf16_weights(micro, monkeypatch):
+    """With TG_CUDA_CODES_ROWS=128 the tensor-core GEMMs of at most 128 rows read the weights
+    as packed codes, expanded inside the GEMM (o_proj: the hi/lo of code * per-head scale, as
+    the load-time copy holds them); the bf16 copies give the same bits. Prefill of 3 x 40 =
+    120 rows (every GEMM on codes), of 3 x 60 (180 rows: the layers on bf16, the 3-row head on
+    codes), and greedy decode of 3 rows (the GEMVs off in both engines)."""
+    rng = np.random.default_rng(9)
+    short = rng.integers(0, MICRO["vocab"], size=(3, 40)).astype(np.float32)
+    long_ = rng.integers(0, MICRO["vocab"], size=(3, 60)).astype(np.float32)
+    monkeypatch.setenv("TG_CUDA_GEMV_ROWS", "0")
+    res = {}
+    for rows in ("128", "0"):
+        monkeypatch.setenv("TG_CUDA_CODES_ROWS", rows)
+        eng = lm.Engine(micro, max_seqs=4, max_len=72)
+        eng.profile(True)
+        a = eng.forward(short)
+        wb = eng.stats()["gemm_weight_bytes"]
+        b = eng.forward(long_)
+        t = eng.generate(short, 8)
+        res[rows] = (a, b, t, wb)
+    for i in range(2):
+        assert np.array_equal(res["128"][i].view(np.uint32), res["0"][i].view(np.uint32))
+    assert np.array_equal(res["128"][2], res["0"][2])
+    # codes: a quarter (int4) or half (int8) of the bf16 bytes, o_proj's two planes included
+    assert 0 < res["128"][3] < (0.3 if micro.bits == 4 else 0.55) * res["0"][3]
+
+
+@pytest.mark.parametrize("S,T", [(1, 1), (5, 1), (1, 8), (2, 4), (8, 1)])
+def test_gemv_batches_vs_oracle(micro, S, T):
+    """Batches of at most 8 rows (S x T) run every layer product as a dequant GEMV over the
+    packed codes (1, 5 and 8 rows: the 1-, 8- and 8-column kernels, padding included); logits
+    against the oracle."""
+    ids = np.random.default_rng(100 + S * T).integers(0, MICRO["vocab"], size=(S, T)).astype(np.float32)
+    eng = lm.Engine(micro, max_seqs=8, max_len=16)
+    eng.profile(True)
+    got = eng.forward(ids)
+    st = eng.stats()
+    np.testing.assert_allclose(got, oracle_logits(micro, ids), rtol=RTOL, atol=ATOL)
+    # the layers' weight bytes are the codes' (+ scales); the head reads its bf16 copy
+    D, FF, V, HQ = MICRO["hidden"], MICRO["ffn"], MICRO["vocab"], MICRO["nq"] * MICRO["head_dim"]
+    HQKV = (MICRO["nq"] + 2 * MICRO["nkv"]) * MICRO["head_dim"]
+    want = MICRO["layers"] * (HQKV * D + D * HQ + 2 * FF * D + D * FF) * micro.bits / 8 + V * D * 2
+    assert want <= st["gemm_weight_bytes"] < 1.1 * want
+
+
 def test_generate_consistent_with_prefill(micro):
     """The decode path (KV cache, one token per step) agrees with a fresh prefill of the same
     prefix: every token is the prefill's argmax, or (both paths being within the logit

@@ -101,6 +101,27 @@ def test_config5_prefill_and_decode_vs_oracle(config5):
     assert bad == 0, f"{bad} of {checked} greedy tokens differ from the oracle's argmax beyond the tie tolerance"
 
 
+def test_config5_small_wave_gemv_vs_oracle(config5):
+    """A wave of 6 sequences: every decode step's layer products run as dequant GEMVs over the
+    int4 codes (the 3072-wide down projection, o_proj's per-head scales). Sequences 0 and 5 of
+    bench.py's first prompts: the prefill's logits and three greedy tokens, as above."""
+    built, (desc, keep) = config5
+    S, T, NEW = 6, 1024, 3
+    ids = np.random.default_rng(5).integers(0, V, size=(2048, T)).astype(np.float32)[:S]
+    eng = lm.Engine(built, max_seqs=S, max_len=T + NEW - 1)
+    logits = eng.forward(ids)
+    tok = eng.generate(ids, NEW)
+    bad = 0
+    for s in (0, 5):
+        want = oracle_logits(desc, ids[s])
+        np.testing.assert_allclose(logits[s], want, rtol=RTOL, atol=ATOL, err_msg=f"sequence {s}")
+        for step in range(NEW):
+            if step:
+                want = oracle_logits(desc, np.concatenate([ids[s], tok[s, :step].astype(np.float32)]))
+            bad += not argmax_ok(int(tok[s, step]), want)
+    assert bad == 0, f"{bad} greedy tokens differ from the oracle's argmax beyond the tie tolerance"
+
+
 def test_config4_prefill_vs_oracle(cuda):
     built = lm.DeviceBuilt(lm.QWEN3_0_6B, bits=8, method="rtn", seed=4)
     desc, keep = built.desc()
