@@ -356,6 +356,17 @@ def bench_decode(args, world, rank, local, small: bool = False):
                 "h2d_bytes_per_step": wave * prompt * 4, "d2h_bytes_per_step": wave * new * 4},
         "gpu_launches": int(launches), "clocks": clocks,
     }
+    if small:
+        # a small wave's step is dominated by its products (the layers' GEMVs over int4 codes
+        # and the LM head): their weight bytes per launch against HBM
+        nl = sum(s["gemm_launches"] for s in stats)
+        line["roofline"] = {"kernel": "gemv_dec (decode-step layer products over int4 codes) and the LM head's GEMM",
+                            "bound": "hbm", "achieved": wb / max(wms, 1e-9) / 1e6, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                            "frac": wb / max(wms, 1e-9) / 1e6 / pk["hbm_gbs"], "peak_source": src, "traffic": None,
+                            "bytes_per_launch": sum(s["gemm_weight_bytes"] for s in stats) / max(nl, 1),
+                            "note": "latency-bound: about 10 us a launch for 1-4 MB of codes; the attention line of "
+                                    "this step is in breakdown.attn_decode"}
+        line["breakdown"]["attn_decode"] = {"gbs": achieved, "ms_per_launch": dec_ms / max(dec_launches, 1)}
     return line, built, tok
 
 

@@ -4,7 +4,7 @@
 // are copied into shared memory by 16-byte cp.async copies, all in flight at once (with the
 // warps' first code loads), then each value hi + lo (exact in f32), divided by the place value
 // of its code, is written into the swizzled chunk layout the decode reads. The CTA then takes
-// blocks of `rows` consecutive code rows in turn (RR rows per warp, as gemv_bulk): each warp
+// blocks of `rows` consecutive code rows in turn (RR rows per warp): each warp
 // streams its rows' 16-byte code chunks (lane j: chunks j, j + 32, ...), the next register
 // block (or the next row block's first) in flight while it computes one, and sums over the
 // warp with a fixed butterfly (deterministic). Grouped scales: a chunk lies inside one group,
@@ -22,6 +22,12 @@
 namespace tgc {
 
 constexpr size_t GD_SMEM_MAX = 200 * 1024;
+// Rows per warp and code chunks per lane and row in one register block. More rows than
+// gemv_bulk's tile: every staged activation read from shared memory then feeds RR rows, which
+// is what bounds a batch of 4 or 8 columns.
+template <int NB> struct GemvDecTile {
+	static constexpr int RR = NB <= 4 ? 4 : 2, BLK = NB <= 2 ? 2 : 1;
+};
 constexpr int GD_THREADS = 32 * GB_MAX_WARPS;
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src)
@@ -39,7 +45,7 @@ template <int BITS, int NB, int EPI, bool GROUPED>
 __global__ void __launch_bounds__(GD_THREADS, 1) gemv_dec_k(const GemvDecArgs a)
 {
 	using S = GemvBulkShape<BITS, NB>;
-	constexpr int RR = GemvBulkTile<NB>::RR, BLK = GemvBulkTile<NB>::BLK;
+	constexpr int RR = GemvDecTile<NB>::RR, BLK = GemvDecTile<NB>::BLK;
 	extern __shared__ __align__(128) unsigned char smem[];
 	float *sbf = (float *)smem;
 	const float4 *sb = (const float4 *)smem;
@@ -66,14 +72,54 @@ __global__ void __launch_bounds__(GD_THREADS, 1) gemv_dec_k(const GemvDecArgs a)
 	pdl_wait(); // the activations come from the kernel ahead of this one
 	pdl_launch();
 	// the live activation rows into shared memory, 16 bytes per copy, all in flight at once
-	for (int i = threadIdx.x; i < 2 * a.nb * k8; i += blockDim.x) {
-		const int row = i / k8, p8 = i - row * k8, plane = row >= a.nb, j = row - plane * a.nb;
-		cp_async16(raw + ((size_t)(plane * NB + j) * a.k + 8 * p8), (plane ? a.lo : a.hi) + (long)j * a.lda + 8 * p8);
-	}
+	const bool norm = a.x != nullptr;
+	float *rawf = (float *)raw; // norm: the f32 rows x[j]
+	const int k4 = a.k / 4;
+	if (norm)
+		for (int i = threadIdx.x; i < a.nb * k4; i += blockDim.x) {
+			const int j = i / k4, p4 = i - j * k4;
+			cp_async16(rawf + (size_t)j * a.k + 4 * p4, a.x + (long)j * a.lda + 4 * p4);
+		}
+	else
+		for (int i = threadIdx.x; i < 2 * a.nb * k8; i += blockDim.x) {
+			const int row = i / k8, p8 = i - row * k8, plane = row >= a.nb, j = row - plane * a.nb;
+			cp_async16(raw + ((size_t)(plane * NB + j) * a.k + 8 * p8), (plane ? a.lo : a.hi) + (long)j * a.lda + 8 * p8);
+		}
 	uint4 qa[RR][BLK]; // this warp's first register block, in flight with the copies
 	load_block(qa, blockIdx.x, 0);
 	cp_async_wait_all();
 	__syncthreads();
+	if (norm) {
+		// 1 / rms of row j by warp j, in the rmsnorm kernel's order (lane-strided FMAs, then a
+		// butterfly), so each activation is the value that kernel computes
+		__shared__ float rinv[NB];
+		if (w < a.nb) {
+			const float *xr = rawf + (size_t)w * a.k;
+			float ss = 0.0f;
+			for (int i = lane; i < a.k; i += 32) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+			for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+			if (lane == 0) rinv[w] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.k), a.eps)));
+		}
+		__syncthreads();
+		// activation (j, p) = (x * inv) * nw, placed as below (a float4 of positions per item)
+		for (int i = threadIdx.x; i < NB * k4; i += blockDim.x) {
+			const int j = i / k4, p0 = 4 * (i - j * k4);
+			float4 xv = make_float4(0.f, 0.f, 0.f, 0.f), wv = xv;
+			float inv = 0.0f;
+			if (j < a.nb) {
+				xv = *(const float4 *)(rawf + (size_t)j * a.k + p0);
+				wv = __ldg((const float4 *)(a.nw + p0));
+				inv = rinv[j];
+			}
+			const float xs[4] = { xv.x, xv.y, xv.z, xv.w }, ws[4] = { wv.x, wv.y, wv.z, wv.w };
+#pragma unroll
+			for (int e = 0; e < 4; e++) {
+				const int p = p0 + e, c = p / S::CPC, pc = p % S::CPC, f = pc * NB + j;
+				sbf[4 * (c * S::UPC + S::swz(c, f >> 2)) + (f & 3)] = __fmul_rn(__fmul_rn(xs[e], inv), ws[e]) * S::place(pc);
+			}
+		}
+	} else
 	// activation (j, p) = hi + lo (exact) -> chunk c = p / CPC, float f = (p % CPC) * NB + j of
 	// the chunk's units, divided by its code's place value; rows j >= nb stage as zeros
 	for (int i = threadIdx.x; i < NB * k8; i += blockDim.x) {
@@ -174,8 +220,10 @@ __global__ void __launch_bounds__(GD_THREADS, 1) gemv_dec_k(const GemvDecArgs a)
 bool gemv_dec_fits(const GemvDecArgs &a)
 {
 	return a.nb >= 1 && a.nb <= 8 && (a.bits == 4 || a.bits == 8) && a.m >= 1 && a.k >= 32 && a.k % 32 == 0 &&
-	       !((uintptr_t)a.q & 15) && gemv_dec_smem(8, a.k) <= GD_SMEM_MAX && a.lda % 8 == 0 && !((uintptr_t)a.hi & 15) &&
-	       !((uintptr_t)a.lo & 15) && (a.group == 0 || (a.s && a.group % 32 == 0));
+	       !((uintptr_t)a.q & 15) && gemv_dec_smem(8, a.k) <= GD_SMEM_MAX &&
+	       (a.x ? a.nw && a.lda % 4 == 0 && !((uintptr_t)a.x & 15) && !((uintptr_t)a.nw & 15)
+		    : a.lda % 8 == 0 && !((uintptr_t)a.hi & 15) && !((uintptr_t)a.lo & 15)) &&
+	       (a.group == 0 || (a.s && a.group % 32 == 0));
 }
 
 static int sms_of_device()
@@ -190,7 +238,7 @@ static int sms_of_device()
 template <int BITS, int NB, int EPI, bool G>
 static int launch(GemvDecArgs a, cudaStream_t st, bool pdl)
 {
-	constexpr int RR = GemvBulkTile<NB>::RR;
+	constexpr int RR = GemvDecTile<NB>::RR;
 	const int sms = sms_of_device();
 	// rows per block: the rows over the SMs (a multiple of RR, at most 16 warps' worth); one CTA
 	// per SM stages the activations once (all 16 warps copy and convert) and takes blocks in turn

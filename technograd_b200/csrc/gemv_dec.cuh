@@ -15,6 +15,10 @@ enum { GD_STORE = 0, GD_ADD = 1 };
 
 struct GemvDecArgs {
 	const __nv_bfloat16 *hi, *lo; // activation rows j < nb, row stride lda elements
+	// or, with x set: the activations are rmsnorm(x[j]) * nw (f32 rows of stride lda; the
+	// arithmetic of the decoder's rmsnorm kernel), and hi / lo are not read
+	const float *x, *nw;
+	float eps;
 	long lda;
 	int nb;                       // 1..8
 	const signed char *q;         // codes [m][k]
@@ -30,7 +34,7 @@ struct GemvDecArgs {
 
 // Whether gemv_dec takes this shape: k a multiple of 32 codes (one 16-byte int4 chunk, two of
 // int8) and at most 3200 (8 rows' activations, as copied and as staged, in shared memory),
-// 16-byte aligned code rows and activation rows (lda a multiple of 8).
+// 16-byte aligned code rows and activation rows (lda a multiple of 8 for hi / lo, of 4 for x).
 bool gemv_dec_fits(const GemvDecArgs &a);
 // Launch on st, with programmatic stream serialization when pdl.
 int gemv_dec(GemvDecArgs a, cudaStream_t st, bool pdl);

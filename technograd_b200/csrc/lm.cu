@@ -234,11 +234,16 @@ __global__ void k_qk_rope(const float *__restrict__ qkv, long M, int T, int pos0
 // CTA = (kv head, sequence); the GRP query heads sharing that kv head are done together.
 // Scores: each warp takes every 8th position, a lane holds 4 dims; softmax in shared memory;
 // values: each warp accumulates its positions, warps are summed through shared memory.
+// Grid (NKV, S, splits). With one split a CTA covers every key and writes the normalised
+// output. With more (small waves, whose (kv head, sequence) grid leaves most SMs idle), split
+// z covers a range of keys (a multiple of 64) and writes, per query head, its maximum score,
+// its sum of exp(score - max) and its unnormalised sum of exp(score - max) * v into split_out
+// ([S][NQ][splits][HD + 2]: the HD sums, then max and sum); k_attn_combine finishes.
 template <int GRP>
 __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q, KvPlaneC kc, KvPlaneC vc, int len,
 						     const int *__restrict__ dpos, int NQ,
 						     int NKV, int slot0, int max_len, float scale, __nv_bfloat16 *__restrict__ ohi,
-						     __nv_bfloat16 *__restrict__ olo)
+						     __nv_bfloat16 *__restrict__ olo, float *__restrict__ split_out)
 {
 	pdl_wait(); // programmatic dependent launch inside the decode step (no-op otherwise)
 	pdl_launch();
@@ -247,6 +252,9 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 	static_assert(DU == 8, "the score butterfly reduces exactly 8 positions");
 	extern __shared__ float sm[];
 	if (dpos) len = *dpos + 1; // keys 0..pos, the new token's own included
+	const int nsp = gridDim.z, sp = blockIdx.z;
+	const int chunk = nsp == 1 ? len : ((len + nsp - 1) / nsp + 63) & ~63;
+	const int k0 = min(len, sp * chunk), k1 = min(len, k0 + chunk); // this CTA's keys [k0, k1)
 	float *sc = sm;                               // [GRP][max_len rounded up]
 	float *red = sc + GRP * ((max_len + 3) & ~3); // [8][GRP][HD]
 	__shared__ float wmax[8][GRP], wsum[8][GRP];
@@ -261,12 +269,12 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 	float mx[GRP];
 #pragma unroll
 	for (int g = 0; g < GRP; g++) mx[g] = -INFINITY;
-	for (int p0 = warp * DU; p0 < len; p0 += 8 * DU) {
+	for (int p0 = k0 + warp * DU; p0 < k1; p0 += 8 * DU) {
 		uint2 khv[DU];
 		uint32_t kqv[DU];
 #pragma unroll
 		for (int u = 0; u < DU; u++) {
-			const bool in = p0 + u < len;
+			const bool in = p0 + u < k1;
 			khv[u] = in ? *(const uint2 *)(kh + (long)(p0 + u) * HD) : make_uint2(0u, 0u);
 			kqv[u] = in ? *(const uint32_t *)(kq + (long)(p0 + u) * HD) : 0u;
 		}
@@ -298,7 +306,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 			float v = (up ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, up ? v2[0] : v2[1], 4);
 			v += __shfl_xor_sync(0xffffffffu, v, 2);
 			v += __shfl_xor_sync(0xffffffffu, v, 1);
-			if (p0 + pu < len) {
+			if (p0 + pu < k1) {
 				v = __fmul_rn(v, scale);
 				if ((lane & 3) == 0) sc[g * ((max_len + 3) & ~3) + p0 + pu] = v;
 				mx[g] = fmaxf(mx[g], v);
@@ -323,7 +331,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 	float part[GRP];
 #pragma unroll
 	for (int g = 0; g < GRP; g++) part[g] = 0.0f;
-	for (int p = threadIdx.x; p < len; p += 256)
+	for (int p = k0 + threadIdx.x; p < k1; p += 256)
 #pragma unroll
 		for (int g = 0; g < GRP; g++) {
 			float e = expf(sc[g * stride + p] - gmax[g]);
@@ -345,12 +353,12 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 	float4 acc[GRP];
 #pragma unroll
 	for (int g = 0; g < GRP; g++) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-	for (int p0 = warp * DU; p0 < len; p0 += 8 * DU) {
+	for (int p0 = k0 + warp * DU; p0 < k1; p0 += 8 * DU) {
 		uint2 vhv[DU];
 		uint32_t vqv[DU];
 #pragma unroll
 		for (int u = 0; u < DU; u++) {
-			const bool in = p0 + u < len;
+			const bool in = p0 + u < k1;
 			vhv[u] = in ? *(const uint2 *)(vh + (long)(p0 + u) * HD) : make_uint2(0u, 0u);
 			vqv[u] = in ? *(const uint32_t *)(vq + (long)(p0 + u) * HD) : 0u;
 		}
@@ -359,7 +367,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 		for (int u = 0; u < DU; u++) vv[u] = kv_decode4(vhv[u], vqv[u]);
 #pragma unroll
 		for (int u = 0; u < DU; u++) {
-			if (p0 + u >= len) break;
+			if (p0 + u >= k1) break;
 #pragma unroll
 			for (int g = 0; g < GRP; g++) {
 				float e = sc[g * stride + p0 + u];
@@ -377,10 +385,42 @@ __global__ void __launch_bounds__(256) k_attn_decode(const float *__restrict__ q
 		int g = i / HD, d = i % HD;
 		float v = 0.0f;
 		for (int w = 0; w < 8; w++) v += red[((long)w * GRP + g) * HD + d];
+		if (nsp > 1) { // this split's partial sums (an empty range: max -inf, sums 0)
+			float *pp = split_out + (((long)s * NQ + kvh * GRP + g) * nsp + sp) * (HD + 2);
+			pp[d] = v;
+			if (d == 0) pp[HD] = gmax[g], pp[HD + 1] = gsum[g];
+			continue;
+		}
 		v = v / gsum[g];
 		long o = (long)s * NQ * HD + (long)(kvh * GRP + g) * HD + d;
 		split_bf16(v, ohi[o], olo[o]);
 	}
+}
+
+// The splits of k_attn_decode for one (query head, sequence) -- grid (NQ, S), 128 threads, a
+// dimension each: with M the largest split maximum, out = sum_z acc_z e^(m_z - M) /
+// sum_z l_z e^(m_z - M), summed in split order; then split to bf16 hi/lo as the one-split
+// kernel writes it.
+__global__ void __launch_bounds__(128) k_attn_combine(const float *__restrict__ part, int nsp, int NQ,
+						      __nv_bfloat16 *__restrict__ ohi, __nv_bfloat16 *__restrict__ olo)
+{
+	pdl_wait(); // programmatic dependent launch inside the decode step (no-op otherwise)
+	pdl_launch();
+	constexpr int HD = 128;
+	const int qh = blockIdx.x, s = blockIdx.y, d = threadIdx.x;
+	const float *pp = part + ((long)s * NQ + qh) * nsp * (HD + 2);
+	float M = -INFINITY;
+	for (int z = 0; z < nsp; z++) M = fmaxf(M, pp[z * (HD + 2) + HD]);
+	float L = 0.0f, v = 0.0f;
+	for (int z = 0; z < nsp; z++) {
+		const float *pz = pp + z * (HD + 2);
+		if (pz[HD + 1] == 0.0f) continue; // no keys in this split
+		const float w = expf(pz[HD] - M);
+		L = fmaf(pz[HD + 1], w, L);
+		v = fmaf(pz[d], w, v);
+	}
+	const long o = ((long)s * NQ + qh) * HD + d;
+	split_bf16(v / L, ohi[o], olo[o]);
 }
 
 // First index of the row maximum (greedy decode).
@@ -468,6 +508,11 @@ struct Engine {
 	long gemv_rows = 8, codes_rows = 0;
 	bool codes = false; // packed codes built
 	DevBuf gus;         // the GEMV's gate/up sums [gemv_rows][2 FF] before SwiGLU
+	// decode attention of small waves split over key ranges (k_attn_decode / k_attn_combine):
+	// partial sums [seqs][NQ][splits][HD + 2] for up to split_seqs sequences
+	DevBuf apart;
+	long split_seqs = 0;
+	int sms = 148;
 	bool use_gemv(long M) const { return codes && M <= gemv_rows; }
 	bool use_codes(long M) const { return codes && M <= codes_rows; }
 	std::vector<std::unique_ptr<Layer>> layers;
@@ -768,6 +813,15 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 		return rc;
 	if ((rc = g.dpos.alloc(16, dev))) return rc;
 	if (g.codes && g.gemv_rows > 0 && (rc = g.gus.alloc((size_t)g.gemv_rows * 2 * FF * 4, dev))) return rc;
+	cudaDeviceGetAttribute(&g.sms, cudaDevAttrMultiProcessorCount, dev);
+	{ // waves whose (kv head, sequence) grid fills at most half the SMs split the decode attention
+		const char *e = getenv("TG_CUDA_DECODE_SPLIT");
+		g.split_seqs = e && strcmp(e, "0") == 0 ? 0 : std::min<long>(max_seqs, g.sms / (2L * NKV));
+		if (g.split_seqs > 0 && HD == 128 &&
+		    (rc = g.apart.alloc((size_t)g.split_seqs * NQ * 8 * (HD + 2) * sizeof(float), dev)))
+			return rc;
+		if (HD != 128) g.split_seqs = 0;
+	}
 	{ // split-K partial sums of the decode GEMMs: up to 16 splits of a 128-row-padded batch
 		long mpad = ((long)max_seqs + 127) / 128 * 128, nmax = std::max<long>(g.HQKV(), std::max<long>(2L * FF, D));
 		if ((rc = g.part.alloc((size_t)16 * mpad * nmax * sizeof(float), dev))) return rc;
@@ -809,12 +863,14 @@ static void codes_b(const Engine &g, GemmArgs &p, const DevBuf &c)
 
 // A product of a batch of at most 8 rows: out[j][n] (+)= s * sum_k (hi + lo)[j][k] code(n, k)
 // as a dequant GEMV over the packed codes [N][K] (group > 0: per-(K group, n) scales).
+// With x set, the activations are rmsnorm(x) * nw, computed in the GEMV (hi / lo unused).
 static int gemv_m(Engine &g, const DevBuf &codes, const void *hi, const void *lo, long lda, long M, int N, int K, const float *s,
-		  int group, long s_ld, float *out, long ldo, int epi)
+		  int group, long s_ld, float *out, long ldo, int epi, const float *x = nullptr, const float *nw = nullptr)
 {
 	GemvDecArgs a;
 	memset(&a, 0, sizeof a);
 	a.hi = (const __nv_bfloat16 *)hi, a.lo = (const __nv_bfloat16 *)lo, a.lda = lda, a.nb = (int)M;
+	a.x = x, a.nw = nw, a.eps = g.eps;
 	a.q = codes.as<signed char>(), a.m = N, a.k = K, a.bits = g.bits;
 	a.s = s, a.group = group, a.s_ld = s_ld, a.out = out, a.ldo = ldo, a.epi = epi;
 	const double wbytes = (double)N * K * g.bits / 8 + (s ? 4.0 * N * (group ? K / group : 1) : 0.0);
@@ -853,14 +909,15 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 		const KvPlane kc{ g.kh.as<__nv_bfloat16>() + lo, g.kq.as<signed char>() + lo };
 		const KvPlane vc{ g.vh.as<__nv_bfloat16>() + lo, g.vq.as<signed char>() + lo };
 		const KvPlaneC kcc{ kc.h, kc.q }, vcc{ vc.h, vc.q };
-		g.launches += 3; // two norms and the q/k rope of this layer
-		TGC_CUDA(launch_k(g, k_rmsnorm_split, dim3(warps_grid), dim3(256), 0, (const float *)g.h.as<float>(), M, D,
-				  (const float *)Y.ln1.as<float>(), g.eps, 0, g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>()));
+		g.launches += gv ? 1 : 3; // the q/k rope and (but for the GEMVs, which norm themselves) two norms
+		if (!gv)
+			TGC_CUDA(launch_k(g, k_rmsnorm_split, dim3(warps_grid), dim3(256), 0, (const float *)g.h.as<float>(), M, D,
+					  (const float *)Y.ln1.as<float>(), g.eps, 0, g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>()));
 		GemmOperands op;
 		GemmArgs p;
-		if (gv) {
-			if ((rc = gemv_m(g, Y.cqkv, g.xhi.p, g.xlo.p, D, M, g.HQKV(), D, Y.sqkv.as<float>(), 0, 0, g.qkv.as<float>(), g.HQKV(),
-					 GD_STORE)))
+		if (gv) { // rmsnorm(h) * ln1 in the GEMV
+			if ((rc = gemv_m(g, Y.cqkv, nullptr, nullptr, D, M, g.HQKV(), D, Y.sqkv.as<float>(), 0, 0, g.qkv.as<float>(), g.HQKV(),
+					 GD_STORE, g.h.as<float>(), Y.ln1.as<float>())))
 				return rc;
 		} else {
 			op.a[0] = g.xhi.p, op.a[1] = g.xlo.p, op.b[0] = Y.wqkv.p, op.lda = D, op.ldb = D;
@@ -893,14 +950,25 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 			dim3 grid(NKV, (unsigned)S);
 			// per key: K and V rows of 3-byte elements
 			int mk = mark_begin(g, MK_DECODE, (double)S * NQ * HD * 4 * 2, (double)S * NKV * HD * 3 * 2);
+			// a small wave: key ranges over more CTAs (2 per SM at most), at least 64 keys each
+			const int nsp = S <= g.split_seqs
+						? (int)std::max<long>(1, std::min<long>({ 8L, 2L * g.sms / (NKV * S), (long)g.max_len / 64 }))
+						: 1;
+			grid.z = nsp;
+			float *part = nsp > 1 ? g.apart.as<float>() : nullptr;
 			if (NQ / NKV == 2)
 				TGC_CUDA(launch_k(g, k_attn_decode<2>, grid, dim3(256), smem, (const float *)g.q.as<float>(), kcc, vcc, 0,
 						  (const int *)g.dpos.as<int>(), NQ, NKV, slot0, g.max_len, g.scale,
-						  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>()));
+						  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>(), part));
 			else
 				TGC_CUDA(launch_k(g, k_attn_decode<1>, grid, dim3(256), smem, (const float *)g.q.as<float>(), kcc, vcc, 0,
 						  (const int *)g.dpos.as<int>(), NQ, NKV, slot0, g.max_len, g.scale,
+						  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>(), part));
+			if (nsp > 1) {
+				g.launches++;
+				TGC_CUDA(launch_k(g, k_attn_combine, dim3(NQ, (unsigned)S), dim3(128), 0, (const float *)part, nsp, NQ,
 						  g.ahi.as<__nv_bfloat16>(), g.alo.as<__nv_bfloat16>()));
+			}
 			mark_end(g, mk);
 		}
 		TGC_LAUNCH_CHECK();
@@ -921,10 +989,12 @@ static int run_layers(Engine &g, long M, int T, int pos0, int slot0, bool decode
 			}
 			if ((rc = gemm_m(g, op, p))) return rc;
 		}
-		TGC_CUDA(launch_k(g, k_rmsnorm_split, dim3(warps_grid), dim3(256), 0, (const float *)g.h.as<float>(), M, D,
-				  (const float *)Y.ln2.as<float>(), g.eps, 0, g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>()));
-		if (gv) { // gate/up sums, then SwiGLU with the channel scales
-			if ((rc = gemv_m(g, Y.cgu, g.xhi.p, g.xlo.p, D, M, 2 * FF, D, nullptr, 0, 0, g.gus.as<float>(), 2L * FF, GD_STORE)))
+		if (!gv)
+			TGC_CUDA(launch_k(g, k_rmsnorm_split, dim3(warps_grid), dim3(256), 0, (const float *)g.h.as<float>(), M, D,
+					  (const float *)Y.ln2.as<float>(), g.eps, 0, g.xhi.as<__nv_bfloat16>(), g.xlo.as<__nv_bfloat16>()));
+		if (gv) { // gate/up sums of rmsnorm(h) * ln2, then SwiGLU with the channel scales
+			if ((rc = gemv_m(g, Y.cgu, nullptr, nullptr, D, M, 2 * FF, D, nullptr, 0, 0, g.gus.as<float>(), 2L * FF, GD_STORE,
+					 g.h.as<float>(), Y.ln2.as<float>())))
 				return rc;
 			g.launches++;
 			TGC_CUDA(launch_k(g, k_swiglu_split, dim3((unsigned)((M * FF + 255) / 256)), dim3(256), 0, (const float *)g.gus.as<float>(),

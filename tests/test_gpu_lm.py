@@ -121,6 +121,24 @@ def test_gemv_batches_vs_oracle(micro, S, T):
     assert want <= st["gemm_weight_bytes"] < 1.1 * want
 
 
+@pytest.mark.parametrize("T", [500, 20])
+def test_decode_split_keys_teacher_forced(micro, T):
+    """Waves that fill few SMs split each decode step's attention over key ranges of 64k keys
+    (here 3 sequences x 2 KV heads: 8 ranges at max_len 600) and combine the ranges' maxima,
+    sums and partial outputs. T = 500: every range used, the last one partly; T = 20: one range
+    holds every key and seven are empty. Greedy tokens teacher-forced against the oracle."""
+    rng = np.random.default_rng(21)
+    S, nnew = 3, 5
+    ids = rng.integers(0, MICRO["vocab"], size=(S, T)).astype(np.float32)
+    tok = lm.Engine(micro, max_seqs=S, max_len=600).generate(ids, nnew)
+    for step in range(nnew):
+        want = oracle_logits(micro, np.concatenate([ids, tok[:, :step].astype(np.float32)], axis=1))
+        for s in range(S):
+            if tok[s, step] != want[s].argmax():
+                top2 = np.sort(want[s])[-2:]
+                assert top2[1] - top2[0] <= ATOL + RTOL * abs(top2[1]), f"seq {s} step {step}"
+
+
 def test_generate_consistent_with_prefill(micro):
     """The decode path (KV cache, one token per step) agrees with a fresh prefill of the same
     prefix: every token is the prefill's argmax, or (both paths being within the logit
