@@ -133,7 +133,7 @@ typedef struct {
 	int bits, gptq, ncal;
 } HQuant;
 
-/* quantize_param of params lo..hi-1 (each param is independent: the calls share nothing) */
+/* quantize_param of params lo..hi-1 (on the calling thread: see ref_vm_load) */
 static void h_quant(void *ctx, int lo, int hi, int tid)
 {
 	(void)tid;
@@ -170,7 +170,11 @@ void *ref_vm_load(const char *path, int bits, int gptq, int min_size, int ncal)
 		for (int i = 0; i < s.n; i++)
 			if (s.p[i].K <= 2048) h_hessian(s.p[i].K, ncal);
 	HQuant hq = { m, &s, bits, gptq, ncal };
-	par_for(s.n, 1, h_quant, &hq); /* quantization is setup, not timed: spread over the cores */
+	/* on this thread only: quantize_param allocates through the reference's allocator, whose
+	 * block list has no lock (src/util.c:21-75), and par_for workers must not allocate
+	 * (src/par.c:11-12); run from workers it corrupted that list now and then, and the
+	 * process aborted while stderr pointed at /dev/null */
+	h_quant(&hq, 0, s.n, 0);
 	fflush(stderr);
 	if (keep >= 0 && nul >= 0) dup2(keep, 2);
 	if (keep >= 0) close(keep);
