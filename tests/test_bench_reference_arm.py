@@ -65,3 +65,25 @@ def test_qwen3_pieces_run_on_the_reference_vm(tmp_path, piece):
     sec = (C.c_double * 2)()
     assert R.ref_vm_run(mod, 3, 2, sec) >= 1
     assert sec[0] > 0 and sec[1] > 0
+
+
+def test_every_workload_has_a_metric_and_config():
+    """Both arms name each workload's metric and config from the same static tables; reduced
+    shapes (profiling overrides) say so in the config."""
+    import argparse
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("bench_static", os.path.join(ROOT, "bench.py"))
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    args = argparse.Namespace(seqs=0, prompt=0, new=0, layers=0, bits=4)
+    for wl in ("decode", "decode_small", "prefill", "ssm", "lr"):
+        metric, unit = b.METRICS[wl]
+        assert metric and unit in ("tokens/s", "rows/s")
+        cfg = b.workload_config(wl, args)
+        assert cfg["workload"].startswith("config"), (wl, cfg)
+    assert b.workload_config("decode_small", args)["seqs_per_gpu"] == b.SMALL_SEQS
+    assert b.workload_config("gemm", args, 16)["M"] == 16
+    small = argparse.Namespace(seqs=2, prompt=64, new=3, layers=2, bits=4)
+    for wl in ("decode", "decode_small", "prefill", "ssm"):
+        assert b.workload_config(wl, small)["workload"].startswith("REDUCED"), wl
