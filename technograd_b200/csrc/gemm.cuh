@@ -49,6 +49,9 @@ struct GemmArgs {
 	const float *cscale;
 	int cgroup;
 	long cscale_ld;
+	// the decoder's batches of 2-4 M tiles (waves of up to 512 sequences): tiles as wide as
+	// the output allows, the K range split over the SMs, instead of 64-wide tiles
+	int wide;
 	// launch with programmatic stream serialization (the kernels wait for the one before them
 	// with griddepcontrol.wait before touching memory; only the decoder's captured step sets it)
 	int pdl;

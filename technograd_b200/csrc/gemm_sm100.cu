@@ -779,7 +779,7 @@ int gemm(const GemmOperands &ops, GemmArgs p, cudaStream_t st)
 	// each CTA then streams a narrower slab of the weights and no K split may be needed.
 	const long mtiles = (p.M + BM - 1) / BM;
 	int BN = p.epi == EPI_SWIGLU || p.N >= 256 ? 256 : 128;
-	if (((p.N + BN - 1) / BN) * mtiles * 2 <= sms && p.N % 64 == 0 && mtiles <= 4) BN = 64;
+	if (((p.N + BN - 1) / BN) * mtiles * 2 <= sms && p.N % 64 == 0 && mtiles <= (p.wide ? 1 : 4)) BN = 64;
 	if (p.N <= 32 && p.epi != EPI_SWIGLU) BN = 32; // a batch of up to 32 (drop-in axis 0): one narrow MMA
 	// In-kernel dequant adds the raw code block to each stage; keep at least 3 stages of
 	// TMA in flight rather than the widest tile

@@ -543,6 +543,7 @@ struct Engine {
 	int g_T = -1, g_nnew = -1;
 	bool g_prof = false;
 	bool small_gemm = true; // batches of 129-384 rows on gemm_sk (TG_CUDA_SMALL_GEMM=tile: the tile kernels)
+	bool wide_tiles = true; // GemmArgs::wide for the tile kernels (TG_CUDA_WIDE_TILES=0: 64-wide tiles up to 4 M tiles)
 	bool prefill_tma = true; // k_attn_prefill_tma (TG_CUDA_PREFILL=staged: k_attn_prefill_tc)
 	// while the decode step is captured without profiling marks: kernels are launched with
 	// programmatic stream serialization, so each one's launch and prologue overlap the tail of
@@ -615,6 +616,7 @@ static int gemm_m(Engine &g, const GemmOperands &op, const GemmArgs &p0)
 {
 	GemmArgs p = p0;
 	p.pdl = g.pdl ? 1 : 0;
+	p.wide = g.wide_tiles ? 1 : 0;
 	p.partial = g.part.as<float>(); // split-K scratch for the tile kernel's small batches
 	p.partial_floats = (long)(g.part.bytes / sizeof(float));
 	// the weight operand's bytes: codes (+ per-head scales) or bf16 tiles, + the epilogue's scales
@@ -837,6 +839,8 @@ static int load_engine(Engine &g, const tg_cuda_lm_desc *d, int dev, int max_seq
 		g.prefill_tma = !(e && strcmp(e, "staged") == 0);
 		e = getenv("TG_CUDA_PDL");
 		g.pdl_enabled = !(e && strcmp(e, "0") == 0);
+		e = getenv("TG_CUDA_WIDE_TILES");
+		g.wide_tiles = !(e && strcmp(e, "0") == 0);
 	}
 	for (int l = 0; l < g.L; l++) { // TMA maps of the cache planes, boxes of 64 dims x 64 positions
 		const size_t lo = (size_t)l * max_seqs * NKV * (size_t)max_len * HD;

@@ -122,6 +122,23 @@ def test_config5_small_wave_gemv_vs_oracle(config5):
     assert bad == 0, f"{bad} greedy tokens differ from the oracle's argmax beyond the tie tolerance"
 
 
+def test_config5_full_wave_decode_vs_oracle(config5):
+    """A whole 512-sequence wave, config 5's wave size, with 16-token prompts (so the oracle
+    side stays small): the decode steps' GEMMs run at M = 512 on the tile kernels (tiles as
+    wide as the output allows, the K range split over the SMs). Sequences 0, 255 and 511:
+    three greedy tokens teacher-forced against the oracle."""
+    built, (desc, keep) = config5
+    S, T, NEW = 512, 16, 3
+    ids = np.random.default_rng(55).integers(0, V, size=(S, T)).astype(np.float32)
+    tok = lm.Engine(built, max_seqs=S, max_len=T + NEW - 1).generate(ids, NEW)
+    bad = 0
+    for s in (0, 255, 511):
+        for step in range(NEW):
+            want = oracle_logits(desc, np.concatenate([ids[s], tok[s, :step].astype(np.float32)]))
+            bad += not argmax_ok(int(tok[s, step]), want)
+    assert bad == 0, f"{bad} greedy tokens differ from the oracle's argmax beyond the tie tolerance"
+
+
 def test_config4_prefill_vs_oracle(cuda):
     built = lm.DeviceBuilt(lm.QWEN3_0_6B, bits=8, method="rtn", seed=4)
     desc, keep = built.desc()
