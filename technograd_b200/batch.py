@@ -182,16 +182,20 @@ def _g9(v) -> str:
     return f"{v:.9g}"
 
 
-def write_rows(path: str | None, out: np.ndarray, steps: np.ndarray) -> None:
-    if path and is_binary(path):
-        out.astype("<f4").tofile(path)
-        return
+def _text_rows(out: np.ndarray, steps: np.ndarray) -> str:
     lines = []
     for r in range(out.shape[0]):
         vals = ",".join(_g9(v) for v in out[r])
         extra = "".join(f",{int(s)}" for s in steps[r])
         lines.append(vals + extra)
-    text = "\n".join(lines) + ("\n" if lines else "")
+    return "\n".join(lines) + ("\n" if lines else "")
+
+
+def write_rows(path: str | None, out: np.ndarray, steps: np.ndarray) -> None:
+    if path and is_binary(path):
+        out.astype("<f4").tofile(path)
+        return
+    text = _text_rows(out, steps)
     if path:
         with open(path, "w", encoding="utf-8") as f:
             f.write(text)
@@ -199,12 +203,13 @@ def write_rows(path: str | None, out: np.ndarray, steps: np.ndarray) -> None:
         sys.stdout.write(text)
 
 
-def _writable(path: str) -> bool:
-    if os.path.isdir(path):
-        return False
-    if os.path.exists(path):
-        return os.access(path, os.W_OK)
-    return os.access(os.path.dirname(os.path.abspath(path)), os.W_OK)
+def _open_out(path: str):
+    """src/main.c:64-68 open_out: the output file, created (or truncated) once the samples
+    have validated and before any compute (src/main.c:414-419); 'cannot write' otherwise."""
+    try:
+        return open(path, "wb") if is_binary(path) else open(path, "w", encoding="utf-8")
+    except OSError as e:
+        raise ValueError(f"cannot write '{path}'") from e
 
 
 def main(argv=None) -> int:
@@ -221,14 +226,21 @@ def main(argv=None) -> int:
     except OSError as e:
         raise ValueError(f"cannot open '{a.model}'") from e
     rows = load_samples(a.data, m.per, m.name)  # everything validated before compute or output
-    if a.out and not _writable(a.out):  # src/main.c:64-68, checked without creating the file
-        raise ValueError(f"cannot write '{a.out}'")
-    b = Batch(m, a.gpus)
-    out, steps = b.run(rows)
+    f = _open_out(a.out) if a.out else None
     try:
-        write_rows(a.out, out, steps)
-    except OSError as e:
-        raise ValueError(f"write failed '{a.out}'") from e
+        b = Batch(m, a.gpus)
+        out, steps = b.run(rows)
+        try:
+            if f is None:
+                sys.stdout.write(_text_rows(out, steps))
+            else:
+                f.write(out.astype("<f4").tobytes() if is_binary(a.out) else _text_rows(out, steps))
+                f.close()  # src/main.c:71-74 close_out: an error here is 'write failed'
+        except OSError as e:
+            raise ValueError(f"write failed '{a.out}'") from e
+    finally:
+        if f is not None and not f.closed:
+            f.close()
     if a.v:
         ms = (time.perf_counter() - t0) * 1e3
         sys.stderr.write(f"[batch] {rows.shape[0]} row(s) in {ms:.2f} ms on {_lib.lib().tg_cuda_ngpus()} GPU(s)\n")
