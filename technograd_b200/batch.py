@@ -14,7 +14,6 @@ from __future__ import annotations
 
 import argparse
 import ctypes as C
-import os
 import re
 import sys
 import time
