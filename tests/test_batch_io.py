@@ -181,3 +181,28 @@ def test_unwritable_output_fails_before_compute(tmp_path):
         r = subprocess.run([sys.executable, "-m", "technograd_b200.batch", str(mp), str(dp), "-o", str(bad)],
                            capture_output=True, text=True, timeout=120, cwd=ROOT)
         assert r.returncode == 1 and r.stderr.startswith("error: cannot write '"), r.stderr
+
+
+@pytest.mark.parametrize("suffix", [".csv", ".bin"])
+def test_main_writes_what_write_rows_writes(tmp_path, monkeypatch, suffix):
+    """The output the CLI opens before compute (src/main.c:414-419) holds exactly what
+    write_rows writes for the same rows, as text or as binary f32; the device is stubbed."""
+    mp, dp = tmp_path / "m.tgir", tmp_path / "rows.csv"
+    mp.write_text(IDENT)
+    dp.write_text("1 2\n3 4\n")
+    out = np.array([[0.5, -1.25], [3.0, 1e-9]], np.float32)
+    steps = np.zeros((2, 0), np.int32)
+
+    class Stub:
+        def __init__(self, module, gpus=0):
+            pass
+
+        def run(self, rows):
+            assert rows.shape[0] == 2
+            return out, steps
+
+    monkeypatch.setattr(batch, "Batch", Stub)
+    got, want = tmp_path / ("got" + suffix), tmp_path / ("want" + suffix)
+    assert batch.main([str(mp), str(dp), "-o", str(got)]) == 0
+    batch.write_rows(str(want), out, steps)
+    assert got.read_bytes() == want.read_bytes()
